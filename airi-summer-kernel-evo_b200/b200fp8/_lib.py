@@ -1,0 +1,159 @@
+"""ctypes binding of libb200fp8.so (the C ABI declared in include/b200fp8.h).
+
+The library is built in-tree (``make -C airi-summer-kernel-evo_b200``) and loaded from
+this package directory.  There is no fallback: if the shared object is missing or fails
+to load, every op raises.  The CPU oracle under ``oracle/`` is test infrastructure and is
+never reached from here.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libb200fp8.so")
+
+B2F_OK = 0
+B2F_ERR_ARG = 1
+B2F_ERR_UNSUPPORTED = 2
+B2F_ERR_CUDA = 3
+B2F_ERR_TIMEOUT = 4
+B2F_ERR_NCCL = 5
+
+DTYPE_F32 = 0
+DTYPE_BF16 = 1
+DTYPE_E4M3 = 2
+
+ACT_NONE = 0
+ACT_RELU = 1
+ACT_GELU_TANH = 2
+ACT_LEAKY_RELU = 3
+ACT_SILU = 4
+
+GEMM_STORE = 0
+GEMM_ROWSUM = 1
+
+NORM_RMS = 0
+NORM_LAYER = 1
+
+
+class B2FError(RuntimeError):
+    """Raised when a b2f_* entry point returns a non-zero status."""
+
+    def __init__(self, code: int, message: str):
+        super().__init__(f"b200fp8 error {code}: {message}")
+        self.code = code
+
+
+class GemmArgs(ctypes.Structure):
+    """Mirror of ``b2f_gemm_args`` (include/b200fp8.h)."""
+
+    _fields_ = [
+        ("m", ctypes.c_int), ("n", ctypes.c_int), ("k", ctypes.c_int),
+        ("a", ctypes.c_void_p), ("lda", ctypes.c_longlong),
+        ("b", ctypes.c_void_p), ("ldb", ctypes.c_longlong),
+        ("alpha", ctypes.c_float), ("alpha_ptr", ctypes.c_void_p),
+        ("bias", ctypes.c_void_p),
+        ("pre_mul", ctypes.c_float), ("pre_add", ctypes.c_float),
+        ("act", ctypes.c_int), ("act_param", ctypes.c_float),
+        ("post_mul", ctypes.c_float),
+        ("residual", ctypes.c_void_p), ("residual_dtype", ctypes.c_int),
+        ("residual_ld", ctypes.c_longlong), ("residual_scale", ctypes.c_float),
+        ("out", ctypes.c_void_p), ("out_dtype", ctypes.c_int),
+        ("out_ld", ctypes.c_longlong), ("out_scale", ctypes.c_float),
+        ("amax", ctypes.c_void_p),
+        ("mode", ctypes.c_int),
+        ("tile_n", ctypes.c_int),
+    ]
+
+
+class NormArgs(ctypes.Structure):
+    """Mirror of ``b2f_norm_args`` (include/b200fp8.h)."""
+
+    _fields_ = [
+        ("rows", ctypes.c_int), ("cols", ctypes.c_int),
+        ("x", ctypes.c_void_p), ("x_dtype", ctypes.c_int), ("x_scale", ctypes.c_float),
+        ("x_ld", ctypes.c_longlong),
+        ("residual", ctypes.c_void_p), ("residual_dtype", ctypes.c_int),
+        ("residual_ld", ctypes.c_longlong),
+        ("weight", ctypes.c_void_p), ("bias", ctypes.c_void_p),
+        ("weight_dtype", ctypes.c_int), ("weight_offset", ctypes.c_float),
+        ("kind", ctypes.c_int), ("eps", ctypes.c_float),
+        ("h_out", ctypes.c_void_p), ("h_dtype", ctypes.c_int), ("h_ld", ctypes.c_longlong),
+        ("y_out", ctypes.c_void_p), ("y_ld", ctypes.c_longlong),
+        ("q_out", ctypes.c_void_p), ("q_ld", ctypes.c_longlong),
+        ("q_scale", ctypes.c_float), ("dynamic_scale", ctypes.c_int),
+        ("amax", ctypes.c_void_p), ("scale_out", ctypes.c_void_p),
+    ]
+
+
+class Op(ctypes.Structure):
+    """Mirror of ``b2f_op``."""
+
+    _fields_ = [
+        ("name", ctypes.c_char_p),
+        ("abi_version", ctypes.c_int),
+        ("fn", ctypes.c_void_p),
+        ("signature", ctypes.c_char_p),
+    ]
+
+
+# Every symbol include/b200fp8.h declares (checked by the CPU test suite).
+EXPORTED_SYMBOLS = (
+    "b2f_version", "b2f_last_error", "b2f_num_sms", "b2f_status_read",
+    "b2f_debug_bounded_wait", "b2f_gemm_args_init", "b2f_gemm_fp8", "b2f_gemm_pair_capacity",
+    "b2f_norm_args_init", "b2f_norm_quant",
+    "b2f_registry_lookup", "b2f_registry_size", "b2f_registry_at",
+)
+
+_lib = None
+
+
+def _declare(lib: ctypes.CDLL) -> None:
+    vp = ctypes.c_void_p
+    lib.b2f_version.restype = ctypes.c_int
+    lib.b2f_last_error.restype = ctypes.c_char_p
+    lib.b2f_num_sms.restype = ctypes.c_int
+    lib.b2f_status_read.argtypes = [ctypes.c_int]
+    lib.b2f_status_read.restype = ctypes.c_int
+    lib.b2f_debug_bounded_wait.argtypes = [ctypes.c_ulonglong, vp]
+    lib.b2f_debug_bounded_wait.restype = ctypes.c_int
+    lib.b2f_gemm_args_init.argtypes = [ctypes.POINTER(GemmArgs)]
+    lib.b2f_gemm_args_init.restype = None
+    lib.b2f_gemm_fp8.argtypes = [ctypes.POINTER(GemmArgs), vp]
+    lib.b2f_gemm_fp8.restype = ctypes.c_int
+    lib.b2f_gemm_pair_capacity.restype = ctypes.c_int
+    lib.b2f_norm_args_init.argtypes = [ctypes.POINTER(NormArgs)]
+    lib.b2f_norm_args_init.restype = None
+    lib.b2f_norm_quant.argtypes = [ctypes.POINTER(NormArgs), vp]
+    lib.b2f_norm_quant.restype = ctypes.c_int
+    lib.b2f_registry_lookup.argtypes = [ctypes.c_char_p]
+    lib.b2f_registry_lookup.restype = ctypes.POINTER(Op)
+    lib.b2f_registry_size.restype = ctypes.c_int
+    lib.b2f_registry_at.argtypes = [ctypes.c_int]
+    lib.b2f_registry_at.restype = ctypes.POINTER(Op)
+
+
+def lib() -> ctypes.CDLL:
+    """Load (once) and return the shared library; raises if it is missing."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(
+                f"libb200fp8.so not built at {LIB_PATH}; run `make -C airi-summer-kernel-evo_b200`"
+                " or __graft_entry__.build()")
+        handle = ctypes.CDLL(LIB_PATH)
+        _declare(handle)
+        _lib = handle
+    return _lib
+
+
+def check(code: int) -> None:
+    if code != B2F_OK:
+        msg = lib().b2f_last_error().decode(errors="replace")
+        raise B2FError(code, msg)
+
+
+def device_status(reset: bool = False) -> int:
+    """Device status word (0 = ok; B2F_DEV_* codes after a bounded wait expired)."""
+    return int(lib().b2f_status_read(1 if reset else 0))

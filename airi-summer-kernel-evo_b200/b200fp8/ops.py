@@ -1,0 +1,163 @@
+"""Torch-facing wrappers of the C-ABI ops.
+
+Tensors are passed to libb200fp8.so as raw device pointers plus shapes; the kernels run
+on torch's current CUDA stream.  float8_e4m3fn tensors (or uint8 views of them) carry
+FP8 data; a per-tensor scale ``s`` means ``value = stored * s``.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import torch
+
+from . import _lib
+from ._lib import GemmArgs, check
+
+_ACTS = {
+    None: _lib.ACT_NONE, "none": _lib.ACT_NONE, "relu": _lib.ACT_RELU,
+    "gelu_tanh": _lib.ACT_GELU_TANH, "leaky_relu": _lib.ACT_LEAKY_RELU,
+    "silu": _lib.ACT_SILU,
+}
+
+_DT = {
+    torch.float32: _lib.DTYPE_F32,
+    torch.bfloat16: _lib.DTYPE_BF16,
+    torch.float8_e4m3fn: _lib.DTYPE_E4M3,
+    torch.uint8: _lib.DTYPE_E4M3,
+}
+
+
+def _stream() -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _check_cuda(*tensors: Optional[torch.Tensor]) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise ValueError("b200fp8 ops take CUDA tensors only (no CPU fallback)")
+
+
+def _fp8_rows(t: torch.Tensor, name: str) -> None:
+    if t.dtype not in (torch.float8_e4m3fn, torch.uint8):
+        raise TypeError(f"{name} must be float8_e4m3fn (or its uint8 storage)")
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise ValueError(f"{name} must be a row-major 2-D tensor")
+
+
+def gemm_fp8(a: torch.Tensor, b_nk: torch.Tensor, *, scale_a: float = 1.0,
+             scale_b: float = 1.0, alpha_tensor: Optional[torch.Tensor] = None,
+             bias: Optional[torch.Tensor] = None, pre_mul: float = 1.0,
+             pre_add: float = 0.0, act: Optional[str] = None, act_param: float = 0.0,
+             post_mul: float = 1.0, residual: Optional[torch.Tensor] = None,
+             residual_scale: float = 1.0, out: Optional[torch.Tensor] = None,
+             out_dtype: torch.dtype = torch.bfloat16, out_scale: float = 1.0,
+             amax: Optional[torch.Tensor] = None, rowsum: bool = False,
+             tile_n: int = 0) -> torch.Tensor:
+    """out = epilogue(scale_a*scale_b * A . B_nk^T)  (see b2f_gemm_fp8).
+
+    ``out_scale`` is the quantisation scale of an e4m3 output (stored = v / out_scale).
+    With ``rowsum=True`` the output is f32 [M] holding sum over columns of v / out_scale.
+    """
+    _check_cuda(a, b_nk, bias, residual, out, amax, alpha_tensor)
+    _fp8_rows(a, "a")
+    _fp8_rows(b_nk, "b_nk")
+    m, k = a.shape
+    n, k2 = b_nk.shape
+    if k != k2:
+        raise ValueError(f"K mismatch: {k} vs {k2}")
+    if rowsum:
+        if out is None:
+            out = torch.zeros((m,), device=a.device, dtype=torch.float32)
+        out_dtype = torch.float32
+    elif out is None:
+        out = torch.empty((m, n), device=a.device, dtype=out_dtype)
+    args = GemmArgs()
+    _lib.lib().b2f_gemm_args_init(ctypes.byref(args))
+    args.m, args.n, args.k = m, n, k
+    args.a, args.lda = a.data_ptr(), a.stride(0)
+    args.b, args.ldb = b_nk.data_ptr(), b_nk.stride(0)
+    args.alpha = float(scale_a) * float(scale_b)
+    args.alpha_ptr = _ptr(alpha_tensor)
+    if bias is not None:
+        if bias.dtype != torch.float32 or not bias.is_contiguous():
+            raise TypeError("bias must be contiguous float32")
+    args.bias = _ptr(bias)
+    args.pre_mul, args.pre_add = pre_mul, pre_add
+    args.act = _ACTS[act]
+    args.act_param = act_param
+    args.post_mul = post_mul
+    if residual is not None:
+        if residual.dim() != 2 or residual.stride(1) != 1:
+            raise ValueError("residual must be row-major 2-D")
+        args.residual = residual.data_ptr()
+        args.residual_dtype = _DT[residual.dtype]
+        args.residual_ld = residual.stride(0)
+        args.residual_scale = residual_scale
+    args.out = out.data_ptr()
+    args.out_dtype = _DT[out.dtype]
+    args.out_ld = out.stride(0) if out.dim() == 2 else 1
+    args.out_scale = out_scale
+    args.amax = _ptr(amax)
+    args.mode = _lib.GEMM_ROWSUM if rowsum else _lib.GEMM_STORE
+    args.tile_n = tile_n
+    check(_lib.lib().b2f_gemm_fp8(ctypes.byref(args), _stream()))
+    return out
+
+
+def norm_quant(x: torch.Tensor, weight: torch.Tensor, *, kind: str = "rms",
+               bias: Optional[torch.Tensor] = None, weight_offset: float = 0.0,
+               eps: float = 1e-6, x_scale: float = 1.0,
+               residual: Optional[torch.Tensor] = None,
+               h_out: Optional[torch.Tensor] = None, y_out: Optional[torch.Tensor] = None,
+               q_out: Optional[torch.Tensor] = None, q_scale: Optional[float] = None,
+               amax: Optional[torch.Tensor] = None,
+               scale_out: Optional[torch.Tensor] = None):
+    """Residual-add + RMSNorm/LayerNorm + e4m3 quantisation (see b2f_norm_quant).
+
+    ``q_scale=None`` selects the dynamic per-tensor scale amax(|y|)/448, returned in
+    ``scale_out`` (f32 [1]).  Returns ``(q_out, scale_out)``.
+    """
+    _check_cuda(x, weight, bias, residual, h_out, y_out, q_out, amax, scale_out)
+    if x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError("x must be row-major 2-D")
+    rows, cols = x.shape
+    if q_out is None:
+        q_out = torch.empty((rows, cols), device=x.device, dtype=torch.float8_e4m3fn)
+    dynamic = q_scale is None
+    if dynamic:
+        if amax is None:
+            amax = torch.zeros(1, device=x.device, dtype=torch.float32)
+        if scale_out is None:
+            scale_out = torch.empty(1, device=x.device, dtype=torch.float32)
+    args = _lib.NormArgs()
+    _lib.lib().b2f_norm_args_init(ctypes.byref(args))
+    args.rows, args.cols = rows, cols
+    args.x, args.x_dtype, args.x_scale, args.x_ld = x.data_ptr(), _DT[x.dtype], x_scale, x.stride(0)
+    if residual is not None:
+        args.residual, args.residual_dtype = residual.data_ptr(), _DT[residual.dtype]
+        args.residual_ld = residual.stride(0)
+    if weight.dtype not in (torch.float32, torch.bfloat16):
+        raise TypeError("weight must be f32 or bf16")
+    if bias is not None and bias.dtype != weight.dtype:
+        raise TypeError("bias dtype must match weight dtype")
+    args.weight, args.bias = weight.data_ptr(), _ptr(bias)
+    args.weight_dtype, args.weight_offset = _DT[weight.dtype], weight_offset
+    args.kind = {"rms": _lib.NORM_RMS, "layer": _lib.NORM_LAYER}[kind]
+    args.eps = eps
+    if h_out is not None:
+        args.h_out, args.h_dtype, args.h_ld = h_out.data_ptr(), _DT[h_out.dtype], h_out.stride(0)
+    if y_out is not None:
+        if y_out.dtype != torch.bfloat16:
+            raise TypeError("y_out must be bf16")
+        args.y_out, args.y_ld = y_out.data_ptr(), y_out.stride(0)
+    args.q_out, args.q_ld = q_out.data_ptr(), q_out.stride(0)
+    args.q_scale = 1.0 if dynamic else float(q_scale)
+    args.dynamic_scale = 1 if dynamic else 0
+    args.amax, args.scale_out = _ptr(amax), _ptr(scale_out)
+    check(_lib.lib().b2f_norm_quant(ctypes.byref(args), _stream()))
+    return q_out, scale_out

@@ -1,0 +1,238 @@
+// Host launcher of the tcgen05 e4m3 GEMM (C ABI: b2f_gemm_fp8).
+#include <cstring>
+#include <string>
+
+#include "gemm_fp8.cuh"
+#include "host_common.h"
+
+namespace b2f {
+
+namespace {
+
+thread_local int g_pair_capacity = 0;  // co-resident CTA pairs seen by the last pair launch
+
+// Output tensor map for the epilogue's TMA stores: the output viewed as bytes
+// [m, n * esize] with 32-row x 128-byte boxes in the 128B swizzle layout.
+int encode_out_map(const b2f_gemm_args* a, const EpilogueParams& ep, CUtensorMap* map) {
+  std::memset(map, 0, sizeof(*map));
+  if (!ep.out_vec || ep.mode != kModeStore) return B2F_OK;
+  const int esz = a->out_dtype == B2F_DTYPE_F32 ? 4 : (a->out_dtype == B2F_DTYPE_BF16 ? 2 : 1);
+  const unsigned long long dims[2] = {(unsigned long long)a->n * esz, (unsigned long long)a->m};
+  const unsigned long long strides[1] = {(unsigned long long)a->out_ld * esz};
+  const unsigned int box[2] = {128, 32};
+  std::string err;
+  if (!encode_tmap(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a->out, dims, strides, box,
+                   CU_TENSOR_MAP_SWIZZLE_128B, &err))
+    return fail(B2F_ERR_ARG, "gemm_fp8: output tensor map: " + err);
+  return B2F_OK;
+}
+
+EpilogueParams make_epilogue(const b2f_gemm_args* a) {
+  EpilogueParams ep;
+  ep.alpha = a->alpha;
+  ep.alpha_ptr = a->alpha_ptr;
+  ep.bias = a->bias;
+  ep.pre_mul = a->pre_mul;
+  ep.pre_add = a->pre_add;
+  ep.act = a->act;
+  ep.act_param = a->act_param;
+  ep.post_mul = a->post_mul;
+  ep.residual = a->residual;
+  ep.res_dtype = a->residual_dtype;
+  ep.res_ld = a->residual_ld;
+  ep.res_scale = a->residual_scale;
+  ep.out = a->out;
+  ep.out_dtype = a->out_dtype;
+  ep.out_ld = a->out_ld;
+  ep.out_inv_scale = 1.0f / a->out_scale;
+  ep.amax = a->amax;
+  ep.mode = a->mode;
+  const int esz = a->out_dtype == B2F_DTYPE_F32 ? 4 : (a->out_dtype == B2F_DTYPE_BF16 ? 2 : 1);
+  const int rsz =
+      a->residual_dtype == B2F_DTYPE_F32 ? 4 : (a->residual_dtype == B2F_DTYPE_BF16 ? 2 : 1);
+  ep.out_vec = (((uintptr_t)a->out) % 16 == 0) && ((a->out_ld * esz) % 16 == 0);
+  ep.res_vec = a->residual == nullptr ||
+               ((((uintptr_t)a->residual) % 16 == 0) && ((a->residual_ld * rsz) % 16 == 0));
+  return ep;
+}
+
+template <int BN>
+int launch_gemm(const b2f_gemm_args* a, const EpilogueParams& ep, cudaStream_t stream) {
+  using Cfg = GemmCfg<BN>;
+  CUtensorMap ta, tb;
+  std::string err;
+  {
+    const unsigned long long dims[2] = {(unsigned long long)a->k, (unsigned long long)a->m};
+    const unsigned long long strides[1] = {(unsigned long long)a->lda};
+    const unsigned int box[2] = {Cfg::BK, Cfg::BM};
+    if (!encode_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a->a, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_128B, &err))
+      return fail(B2F_ERR_ARG, "gemm_fp8: A tensor map: " + err);
+  }
+  {
+    const unsigned long long dims[2] = {(unsigned long long)a->k, (unsigned long long)a->n};
+    const unsigned long long strides[1] = {(unsigned long long)a->ldb};
+    const unsigned int box[2] = {Cfg::BK, (unsigned int)BN};
+    if (!encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a->b, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_128B, &err))
+      return fail(B2F_ERR_ARG, "gemm_fp8: B tensor map: " + err);
+  }
+  GemmShape shape{a->m, a->n, a->k};
+
+  const int num_tiles = ((a->m + Cfg::BM - 1) / Cfg::BM) * ((a->n + BN - 1) / BN);
+  const int sms = sm_count();
+  if (sms <= 0) return fail(B2F_ERR_CUDA, "gemm_fp8: cannot query SM count");
+  const int grid = num_tiles < sms ? num_tiles : sms;
+  auto kern = gemm_fp8_kernel<BN>;
+  static thread_local int attr_dev = -1;
+  int dev = 0;
+  B2F_CUDA_TRY(cudaGetDevice(&dev));
+  if (attr_dev != dev) {
+    B2F_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      Cfg::SMEM_BYTES));
+    attr_dev = dev;
+  }
+  CUtensorMap to;
+  if (int rc = encode_out_map(a, ep, &to)) return rc;
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, to, shape, ep);
+  B2F_CUDA_TRY(cudaGetLastError());
+  return B2F_OK;
+}
+
+int launch_gemm_pair(const b2f_gemm_args* a, const EpilogueParams& ep, cudaStream_t stream) {
+  using Cfg = Gemm2Cfg;
+  CUtensorMap ta, tb;
+  std::string err;
+  {
+    const unsigned long long dims[2] = {(unsigned long long)a->k, (unsigned long long)a->m};
+    const unsigned long long strides[1] = {(unsigned long long)a->lda};
+    const unsigned int box[2] = {Cfg::BK, Cfg::BM};
+    if (!encode_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a->a, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_128B, &err))
+      return fail(B2F_ERR_ARG, "gemm_fp8: A tensor map: " + err);
+  }
+  {
+    const unsigned long long dims[2] = {(unsigned long long)a->k, (unsigned long long)a->n};
+    const unsigned long long strides[1] = {(unsigned long long)a->ldb};
+    const unsigned int box[2] = {Cfg::BK, Cfg::BN / 2};
+    if (!encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a->b, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_128B, &err))
+      return fail(B2F_ERR_ARG, "gemm_fp8: B tensor map: " + err);
+  }
+  GemmShape shape{a->m, a->n, a->k};
+  const int num_tiles = ((a->m + 255) / 256) * ((a->n + Cfg::BN - 1) / Cfg::BN);
+  static thread_local int cached_dev = -1, cached_pairs = 0;
+  int dev = 0;
+  B2F_CUDA_TRY(cudaGetDevice(&dev));
+  if (cached_dev != dev) {
+    B2F_CUDA_TRY(cudaFuncSetAttribute(gemm_fp8_pair_kernel,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      Cfg::SMEM_BYTES));
+    cudaLaunchConfig_t probe = {};
+    probe.gridDim = dim3(2 * 256, 1, 1);
+    probe.blockDim = dim3(Cfg::THREADS, 1, 1);
+    probe.dynamicSmemBytes = Cfg::SMEM_BYTES;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2; attr.val.clusterDim.y = 1; attr.val.clusterDim.z = 1;
+    probe.attrs = &attr;
+    probe.numAttrs = 1;
+    int clusters = 0;
+    B2F_CUDA_TRY(cudaOccupancyMaxActiveClusters(&clusters, gemm_fp8_pair_kernel, &probe));
+    if (clusters <= 0) return fail(B2F_ERR_UNSUPPORTED, "gemm_fp8: no co-resident CTA pairs");
+    cached_pairs = clusters;
+    cached_dev = dev;
+  }
+  g_pair_capacity = cached_pairs;
+  const int pairs = num_tiles < cached_pairs ? num_tiles : cached_pairs;
+  CUtensorMap to;
+  if (int rc = encode_out_map(a, ep, &to)) return rc;
+  gemm_fp8_pair_kernel<<<2 * pairs, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, to, shape,
+                                                                             ep);
+  B2F_CUDA_TRY(cudaGetLastError());
+  return B2F_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+}  // namespace b2f
+
+extern "C" {
+
+void b2f_gemm_args_init(b2f_gemm_args* a) {
+  if (a == nullptr) return;
+  *a = b2f_gemm_args{};
+  a->alpha = 1.0f;
+  a->pre_mul = 1.0f;
+  a->pre_add = 0.0f;
+  a->act = B2F_ACT_NONE;
+  a->act_param = 0.0f;
+  a->post_mul = 1.0f;
+  a->residual_dtype = B2F_DTYPE_BF16;
+  a->residual_scale = 1.0f;
+  a->out_dtype = B2F_DTYPE_BF16;
+  a->out_scale = 1.0f;
+  a->mode = B2F_GEMM_STORE;
+  a->tile_n = 0;
+}
+
+int b2f_gemm_pair_capacity(void) { return b2f::g_pair_capacity; }
+
+int b2f_gemm_fp8(const b2f_gemm_args* a, b2f_stream_t stream) {
+  using namespace b2f;
+  if (a == nullptr) return fail(B2F_ERR_ARG, "gemm_fp8: null args");
+  if (a->m <= 0 || a->n <= 0 || a->k <= 0) return fail(B2F_ERR_ARG, "gemm_fp8: empty shape");
+  if (a->a == nullptr || a->b == nullptr || a->out == nullptr)
+    return fail(B2F_ERR_ARG, "gemm_fp8: null tensor");
+  if (a->k % 16 != 0) return fail(B2F_ERR_ARG, "gemm_fp8: k must be a multiple of 16");
+  if (a->lda < a->k || a->ldb < a->k || a->lda % 16 || a->ldb % 16)
+    return fail(B2F_ERR_ARG, "gemm_fp8: lda/ldb must be >= k and multiples of 16");
+  if (!aligned16(a->a) || !aligned16(a->b))
+    return fail(B2F_ERR_ARG, "gemm_fp8: A and B must be 16-byte aligned");
+  if (a->out_dtype < 0 || a->out_dtype > 2 || a->residual_dtype < 0 || a->residual_dtype > 2)
+    return fail(B2F_ERR_ARG, "gemm_fp8: bad dtype");
+  if (a->act < 0 || a->act > 4) return fail(B2F_ERR_ARG, "gemm_fp8: bad activation");
+  if (a->mode != B2F_GEMM_STORE && a->mode != B2F_GEMM_ROWSUM)
+    return fail(B2F_ERR_ARG, "gemm_fp8: bad mode");
+  if (a->mode == B2F_GEMM_ROWSUM && a->out_dtype != B2F_DTYPE_F32)
+    return fail(B2F_ERR_ARG, "gemm_fp8: ROWSUM needs an f32 output");
+  if (a->mode == B2F_GEMM_STORE && a->out_ld < a->n)
+    return fail(B2F_ERR_ARG, "gemm_fp8: out_ld < n");
+  if (a->out_scale == 0.0f) return fail(B2F_ERR_ARG, "gemm_fp8: out_scale must be non-zero");
+  const int esz = a->out_dtype == B2F_DTYPE_F32 ? 4 : (a->out_dtype == B2F_DTYPE_BF16 ? 2 : 1);
+  if (((uintptr_t)a->out) % esz != 0) return fail(B2F_ERR_ARG, "gemm_fp8: misaligned out");
+  if (a->residual != nullptr && a->residual_ld < a->n)
+    return fail(B2F_ERR_ARG, "gemm_fp8: residual_ld < n");
+  if (a->bias != nullptr && ((uintptr_t)a->bias) % 16 != 0)
+    return fail(B2F_ERR_ARG, "gemm_fp8: bias must be 16-byte aligned");
+  cudaStream_t s = (cudaStream_t)stream;
+  int tn = a->tile_n;
+  if (tn == 0) {
+    // Small-N or few-tile problems use 128-wide tiles to fill the 148 SMs.
+    const int sms = sm_count();
+    const long long tiles256 = (long long)((a->m + 127) / 128) * ((a->n + 255) / 256);
+    const long long pair_tiles = (long long)((a->m + 255) / 256) * ((a->n + 255) / 256);
+    if (a->m > 128 && pair_tiles >= sms / 2) tn = 512;  // CTA-pair 256x256 tiles
+    else tn = (tiles256 < sms) ? 128 : 256;
+  }
+  const EpilogueParams ep = make_epilogue(a);
+  if (tn == 512) return launch_gemm_pair(a, ep, s);
+  if (tn == 256) return launch_gemm<256>(a, ep, s);
+  if (tn == 128) return launch_gemm<128>(a, ep, s);
+  return fail(B2F_ERR_ARG, "gemm_fp8: tile_n must be 0, 128, 256 or 512 (CTA pair)");
+}
+
+}  // extern "C"
+
+#ifdef B2F_TRACE
+extern "C" int b2f_trace_read(void* host, unsigned long long bytes, int reset) {
+  if (bytes > sizeof(b2f::g_trace)) bytes = sizeof(b2f::g_trace);
+  if (cudaMemcpyFromSymbol(host, b2f::g_trace, bytes) != cudaSuccess) return -1;
+  if (reset) {
+    static unsigned long long zeros[160 * 64] = {};
+    cudaMemcpyToSymbol(b2f::g_trace, zeros, sizeof(zeros));
+  }
+  return 0;
+}
+#endif

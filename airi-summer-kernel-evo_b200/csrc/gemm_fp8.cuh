@@ -1,0 +1,695 @@
+// Persistent warp-specialised e4m3 x e4m3 -> f32 GEMM on 5th-generation tensor cores.
+//
+//   C[M,N] = epilogue( (A[M,K] . B[N,K]^T) * alpha )
+//
+// A and B are K-major (row-major [rows, K] bytes), exactly the `matrix_a` / `matrix_b_nk`
+// operands of the reference's square-GEMM and GEMM+epilogue tasks
+// (tasks/level1_01_square_matrix_multiplication_fp8/starter.py:125-138,
+//  tasks/level2_76_gemm_add_relu_fp8/starter.py:148-169).
+//
+// Roles (192 threads, one CTA per SM, grid = min(#tiles, #SMs)):
+//   warp 0   TMA producer: streams 128-byte K blocks of A (128 rows) and B (BN rows) into
+//            a STAGES-deep ring of 128B-swizzled shared-memory slots.
+//   warp 1   allocates TMEM (2 accumulators x BN f32 columns), then one thread issues
+//            tcgen05.mma.kind::f8f6f4 (M=128, N=BN, K=32) four times per K block and
+//            releases each slot with tcgen05.commit.
+//   warps 2-5 epilogue: tcgen05.ld 32 columns at a time from the accumulator, apply the
+//            fused epilogue in registers and store.  Double-buffered accumulators let the
+//            epilogue of tile i overlap the main loop of tile i+1.
+#pragma once
+#include "common.cuh"
+
+namespace b2f {
+
+#ifdef B2F_TRACE
+// Debug-only timeline: per CTA, per tile (first 8), globaltimer stamps of each role.
+__device__ unsigned long long g_trace[160][8][8];
+#define B2F_STAMP(tile, slot)                                                   \
+  do {                                                                          \
+    if ((tile) < 8 && blockIdx.x < 160) g_trace[blockIdx.x][(tile)][(slot)] = globaltimer(); \
+  } while (0)
+#else
+#define B2F_STAMP(tile, slot) do {} while (0)
+#endif
+
+enum : int { kOutF32 = 0, kOutBF16 = 1, kOutE4M3 = 2 };
+enum : int { kActNone = 0, kActRelu = 1, kActGeluTanh = 2, kActLeakyRelu = 3, kActSilu = 4 };
+enum : int { kModeStore = 0, kModeRowSum = 1 };
+
+struct EpilogueParams {
+  float alpha;             // scale_a * scale_b
+  const float* alpha_ptr;  // optional device scalar multiplied into alpha (may be null)
+  const float* bias;       // [N] f32, may be null
+  float pre_mul, pre_add;  // v = (alpha*acc + bias)*pre_mul + pre_add
+  int act;                 // activation applied after the affine step
+  float act_param;         // LeakyReLU negative slope
+  float post_mul;          // v *= post_mul after the activation
+  const void* residual;    // optional [M, res_ld] tensor added after post_mul
+  int res_dtype;           // kOutF32 / kOutBF16 / kOutE4M3
+  long long res_ld;
+  float res_scale;         // residual value = stored * res_scale
+  void* out;               // output [M, out_ld]  (RowSum mode: f32 [M])
+  int out_dtype;
+  long long out_ld;
+  float out_inv_scale;     // stored = v * out_inv_scale (quantised outputs)
+  float* amax;             // optional: atomic max of |v| over the whole output
+  int mode;                // kModeStore / kModeRowSum
+  int out_vec;             // out base and row pitch 16-byte aligned: vector stores
+  int res_vec;             // residual base and row pitch 16-byte aligned: vector loads
+};
+
+struct GemmShape {
+  int M, N, K;
+};
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+  // 0.5 x (1 + tanh( sqrt(2/pi) (x + 0.044715 x^3) )), as torch's approximate="tanh".
+  const float k0 = 0.7978845608028654f;
+  const float k1 = 0.044715f;
+  float u = k0 * (x + k1 * x * x * x);
+  return 0.5f * x * (1.0f + tanhf(u));
+}
+
+// Activation selected at compile time: a runtime switch inside the element loop gets
+// if-converted into evaluating every activation for every element.
+template <int ACT>
+__device__ __forceinline__ float act_fn(float v, float p) {
+  if constexpr (ACT == kActRelu) return fmaxf(v, 0.0f);
+  else if constexpr (ACT == kActGeluTanh) return gelu_tanh(v);
+  else if constexpr (ACT == kActLeakyRelu) return v >= 0.0f ? v : v * p;
+  else if constexpr (ACT == kActSilu) return v / (1.0f + expf(-v));
+  else return v;
+}
+
+template <int ACT>
+__device__ __forceinline__ void act_affine32(float (&v)[32], float pre_mul, float pre_add,
+                                             float p, float post_mul) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = act_fn<ACT>(fmaf(v[j], pre_mul, pre_add), p) * post_mul;
+}
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int BM = 128;
+  static constexpr int BK = 128;  // bytes of K per stage = one 128B swizzle row
+  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static constexpr int A_BYTES = BM * BK;
+  static constexpr int B_BYTES = BN * BK;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;  // two accumulators
+  static constexpr int SMEM_BYTES =
+      STAGES * STAGE_BYTES + 4 * 8192 /*epilogue staging*/ + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int THREADS = 192;
+};
+
+// Tile order: groups of GROUP_M row-blocks sweep all column blocks, so the CTAs that run
+// concurrently share A rows and B columns in L2.
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
+  constexpr int GROUP_M = 8;
+  const int per_group = GROUP_M * num_n;
+  const int g = t / per_group;
+  const int first_m = g * GROUP_M;
+  const int gsize = min(num_m - first_m, GROUP_M);
+  const int r = t - g * per_group;
+  mb = first_m + r % gsize;
+  nb = r / gsize;
+}
+
+// Epilogue math for 32 consecutive columns of one row: scale, bias, affine, activation,
+// residual; tracks |v| (amax) and the row sum.  Returns the f32 values before the store.
+__device__ __forceinline__ void epi_values(const EpilogueParams& ep, float alpha, int row,
+                                           int col0, int M, int N, const uint32_t (&acc)[32],
+                                           float (&v)[32], float& rowsum, float& amax_local) {
+  const bool row_ok = row < M;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(acc[j]) * alpha;
+  if (ep.bias != nullptr) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      const int c = col0 + j;
+      if (c + 3 < N) {
+        float4 b = *reinterpret_cast<const float4*>(ep.bias + c);
+        v[j] += b.x; v[j + 1] += b.y; v[j + 2] += b.z; v[j + 3] += b.w;
+      } else {
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (c + u < N) v[j + u] += ep.bias[c + u];
+      }
+    }
+  }
+  switch (ep.act) {  // uniform branch, once per 32 columns
+    case kActRelu: act_affine32<kActRelu>(v, ep.pre_mul, ep.pre_add, ep.act_param, ep.post_mul); break;
+    case kActGeluTanh: act_affine32<kActGeluTanh>(v, ep.pre_mul, ep.pre_add, ep.act_param, ep.post_mul); break;
+    case kActLeakyRelu: act_affine32<kActLeakyRelu>(v, ep.pre_mul, ep.pre_add, ep.act_param, ep.post_mul); break;
+    case kActSilu: act_affine32<kActSilu>(v, ep.pre_mul, ep.pre_add, ep.act_param, ep.post_mul); break;
+    default: act_affine32<kActNone>(v, ep.pre_mul, ep.pre_add, ep.act_param, ep.post_mul); break;
+  }
+  const bool in_n = row_ok && (col0 + 32 <= N);
+  if (ep.residual != nullptr && row_ok) {
+    const bool full = in_n && ep.res_vec;
+    if (ep.res_dtype == kOutBF16) {
+      const __nv_bfloat16* rp =
+          reinterpret_cast<const __nv_bfloat16*>(ep.residual) + (long long)row * ep.res_ld + col0;
+      if (full) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          uint4 q = *reinterpret_cast<const uint4*>(rp + j);
+          float2 a = unpack_bf16x2(q.x), b = unpack_bf16x2(q.y), c = unpack_bf16x2(q.z),
+                 d = unpack_bf16x2(q.w);
+          v[j] += a.x * ep.res_scale; v[j + 1] += a.y * ep.res_scale;
+          v[j + 2] += b.x * ep.res_scale; v[j + 3] += b.y * ep.res_scale;
+          v[j + 4] += c.x * ep.res_scale; v[j + 5] += c.y * ep.res_scale;
+          v[j + 6] += d.x * ep.res_scale; v[j + 7] += d.y * ep.res_scale;
+        }
+      } else {
+        for (int j = 0; j < 32; ++j)
+          if (col0 + j < N) v[j] += __bfloat162float(rp[j]) * ep.res_scale;
+      }
+    } else if (ep.res_dtype == kOutF32) {
+      const float* rp = reinterpret_cast<const float*>(ep.residual) + (long long)row * ep.res_ld + col0;
+      if (full) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          float4 q = *reinterpret_cast<const float4*>(rp + j);
+          v[j] += q.x * ep.res_scale; v[j + 1] += q.y * ep.res_scale;
+          v[j + 2] += q.z * ep.res_scale; v[j + 3] += q.w * ep.res_scale;
+        }
+      } else {
+        for (int j = 0; j < 32; ++j)
+          if (col0 + j < N) v[j] += rp[j] * ep.res_scale;
+      }
+    } else {
+      const uint8_t* rp = reinterpret_cast<const uint8_t*>(ep.residual) + (long long)row * ep.res_ld + col0;
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < N) v[j] += e4m3_to_f32(rp[j]) * ep.res_scale;
+    }
+  }
+  if (ep.amax != nullptr && row_ok) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (col0 + j < N) amax_local = fmaxf(amax_local, fabsf(v[j]));
+  }
+  if (ep.mode == kModeRowSum && row_ok) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (col0 + j < N) rowsum += v[j];
+  }
+}
+
+// Packs 32 f32 values into the output type: 16 (f32: 32, e4m3: 8) 32-bit words.
+__device__ __forceinline__ void epi_pack(const EpilogueParams& ep, const float (&v)[32],
+                                         uint32_t (&w)[32]) {
+  const float s = ep.out_inv_scale;
+  if (ep.out_dtype == kOutBF16) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) w[j] = pack_bf16x2(v[2 * j] * s, v[2 * j + 1] * s);
+  } else if (ep.out_dtype == kOutF32) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(v[j] * s);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      w[j] = uint32_t(f32x2_to_e4m3x2(v[4 * j] * s, v[4 * j + 1] * s)) |
+             (uint32_t(f32x2_to_e4m3x2(v[4 * j + 2] * s, v[4 * j + 3] * s)) << 16);
+  }
+}
+
+// Fallback store for outputs whose base or row pitch is not 16-byte aligned.
+__device__ __forceinline__ void epi_store_direct(const EpilogueParams& ep, int row, int col0,
+                                                 int N, const float (&v)[32]) {
+  const float s = ep.out_inv_scale;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if (col0 + j >= N) continue;
+    const long long o = (long long)row * ep.out_ld + col0 + j;
+    if (ep.out_dtype == kOutBF16)
+      reinterpret_cast<__nv_bfloat16*>(ep.out)[o] = __float2bfloat16_rn(v[j] * s);
+    else if (ep.out_dtype == kOutF32)
+      reinterpret_cast<float*>(ep.out)[o] = v[j] * s;
+    else
+      reinterpret_cast<uint8_t*>(ep.out)[o] =
+          static_cast<uint8_t>(f32x2_to_e4m3x2(v[j] * s, 0.0f) & 0xFF);
+  }
+}
+
+// Bytes per output element and columns per 128-byte staging row.
+__device__ __forceinline__ int out_esize(int dt) { return dt == kOutF32 ? 4 : (dt == kOutBF16 ? 2 : 1); }
+
+// Drains one 128 x BN accumulator (this warp: 32 TMEM lanes = 32 rows) through the fused
+// epilogue.  Output goes through a per-warp, double-buffered 32 x 128-byte shared-memory
+// staging tile in the 128B-swizzle layout and leaves with TMA bulk-tensor stores (full
+// 128-byte lines, clipped at the M/N edges by the TMA unit).  `stage` points at this
+// warp's 2 x 4 KB staging area (1024-byte aligned).
+template <int BN>
+__device__ __forceinline__ void epilogue_tile(const EpilogueParams& ep, const CUtensorMap* tmap_out,
+                                              float alpha, uint32_t t_row, int row, int row0,
+                                              int col_base, int M, int N, uint8_t* stage,
+                                              int& buf, float& rowsum, float& amax_local) {
+  const int lane = threadIdx.x & 31;
+  if (ep.mode == kModeRowSum) {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      float v[32];
+      tmem_ld32(t_row + c * 32, r);
+      const int col0 = col_base + c * 32;
+      if (col0 < N) epi_values(ep, alpha, row, col0, M, N, r, v, rowsum, amax_local);
+    }
+    return;
+  }
+  if (!ep.out_vec) {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      float v[32];
+      tmem_ld32(t_row + c * 32, r);
+      const int col0 = col_base + c * 32;
+      if (col0 < N) {
+        epi_values(ep, alpha, row, col0, M, N, r, v, rowsum, amax_local);
+        if (row < M) epi_store_direct(ep, row, col0, N, v);
+      }
+    }
+    return;
+  }
+  const int esz = out_esize(ep.out_dtype);
+  const int cw = 128 / esz;     // columns per 128-byte staging row
+  const int subs = cw / 32;     // tcgen05.ld x32 per staging chunk (f32 1, bf16 2, e4m3 4)
+#pragma unroll 1
+  for (int c0 = 0; c0 < BN; c0 += cw) {
+    if (col_base + c0 >= N) break;
+    uint8_t* sbuf = stage + buf * 4096;
+    // The store issued two chunks ago from this buffer must have finished reading it.
+    if (lane == 0) bulk_wait_read<1>();
+    __syncwarp();
+#pragma unroll 1
+    for (int sub = 0; sub < subs; ++sub) {
+      uint32_t r[32];
+      float v[32];
+      uint32_t w[32];
+      tmem_ld32(t_row + c0 + sub * 32, r);
+      epi_values(ep, alpha, row, col_base + c0 + sub * 32, M, N, r, v, rowsum, amax_local);
+      epi_pack(ep, v, w);
+      // this sub-chunk covers 16-byte granules [sub*g, sub*g + g) of the 128-byte row
+      const int g = 8 / subs;
+      uint8_t* rowp = sbuf + lane * 128;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (u < g) {
+          const int gi = sub * g + u;
+          uint4 q = make_uint4(w[4 * u], w[4 * u + 1], w[4 * u + 2], w[4 * u + 3]);
+          *reinterpret_cast<uint4*>(rowp + ((gi ^ (lane & 7)) << 4)) = q;
+        }
+      }
+    }
+    fence_async_shared();
+    __syncwarp();
+#if !defined(B2F_EXP) || B2F_EXP != 4
+    if (lane == 0) {
+      tma_store_2d(tmap_out, sbuf, (col_base + c0) * esz, row0);
+      bulk_commit();
+    }
+#endif
+    buf ^= 1;
+  }
+}
+
+template <int BN>
+__global__ void __launch_bounds__(192, 1)
+    gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                    const __grid_constant__ CUtensorMap tmap_b,
+                    const __grid_constant__ CUtensorMap tmap_out, const GemmShape shape,
+                    const EpilogueParams ep) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte alignment for the 128B-swizzle atoms.
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* smem_a = smem;
+  uint8_t* smem_b = smem + STAGES * Cfg::A_BYTES;
+  uint8_t* smem_stage = smem + STAGES * Cfg::STAGE_BYTES;  // 4 warps x 2 x 4 KB
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem_stage + 4 * 8192);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;   // [2]
+  uint64_t* tempty_bar = tfull_bar + 2;       // [2]
+  uint64_t* drain_bar = tempty_bar + 2;       // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int M = shape.M, N = shape.N, K = shape.K;
+  const int num_m = (M + Cfg::BM - 1) / Cfg::BM;
+  const int num_n = (N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (K + Cfg::BK - 1) / Cfg::BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 4);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+    if (ep.out_vec && ep.mode == kModeStore) tma_prefetch_desc(&tmap_out);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer
+#if defined(B2F_EXP) && B2F_EXP == 3
+      const uint64_t pol_a = policy_evict_normal();
+      const uint64_t pol_b = policy_evict_normal();
+#else
+      const uint64_t pol_a = policy_evict_last();
+      const uint64_t pol_b = policy_evict_last();
+#endif
+      int stage = 0;
+      uint32_t phase = 0;
+      long long issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        int mb, nb;
+        tile_coords(t, num_m, num_n, mb, nb);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, kDevTimeoutProducer, abort_flag)) {
+            ok = false;
+            break;
+          }
+          if (kb == 0) B2F_STAMP((t - (int)blockIdx.x) / (int)gridDim.x, 0);
+          mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
+          tma_load_2d(smem_a + stage * Cfg::A_BYTES, &tmap_a, &full_bar[stage], kb * Cfg::BK,
+                      mb * Cfg::BM, pol_a);
+          tma_load_2d(smem_b + stage * Cfg::B_BYTES, &tmap_b, &full_bar[stage], kb * Cfg::BK,
+                      nb * BN, pol_b);
+          ++issued;
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      // Drain: every issued copy must have landed before the CTA may exit.
+      const long long pending = issued < STAGES ? issued : STAGES;
+      for (long long i = 0; i < pending; ++i) {
+        if (--stage < 0) { stage = STAGES - 1; phase ^= 1; }
+        uint64_t t0 = globaltimer();
+        while (!mbar_test(&full_bar[stage], phase)) {
+          if (globaltimer() - t0 > B2F_WAIT_NS) { record_error(kDevTimeoutDrain); break; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ MMA issuer
+      constexpr uint32_t idesc = make_idesc_f8(Cfg::BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, kDevTimeoutMma, abort_flag)) break;
+        B2F_STAMP(it, 1);
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, kDevTimeoutMma, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem_a + stage * Cfg::A_BYTES);
+          const uint32_t b_addr = smem_u32(smem_b + stage * Cfg::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < Cfg::BK / 32; ++k) {
+            const uint64_t ad = make_sdesc_sw128(a_addr + k * 32, 1024);
+            const uint64_t bd = make_sdesc_sw128(b_addr + k * 32, 1024);
+            mma_f8(d_tmem, ad, bd, idesc, (kb | k) != 0);
+          }
+          mma_commit(&empty_bar[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (ok) mma_commit(&tfull_bar[acc]);
+        B2F_STAMP(it, 2);
+      }
+      // Drain: wait until every issued MMA retired before TMEM is released.
+      mma_commit(drain_bar);
+      uint64_t t0 = globaltimer();
+      while (!mbar_test(drain_bar, 0)) {
+        if (globaltimer() - t0 > B2F_WAIT_NS) { record_error(kDevTimeoutDrain); break; }
+      }
+    }
+  } else {
+    // -------------------------------------------------------------- epilogue
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    uint8_t* stage = smem_stage + (warp - 2) * 8192;
+    int buf = 0;
+    float alpha = ep.alpha;
+    if (ep.alpha_ptr != nullptr) alpha *= *ep.alpha_ptr;
+    float amax_local = 0.0f;
+    int it = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
+      int mb, nb;
+      tile_coords(t, num_m, num_n, mb, nb);
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      if (!mbar_wait(&tfull_bar[acc], acc_phase, kDevTimeoutEpilogue, abort_flag)) break;
+      if (warp == 2 && lane == 0) B2F_STAMP(it, 3);
+      tc_fence_after();
+      const int row0 = mb * Cfg::BM + q * 32;
+      const int row = row0 + lane;
+      float rowsum = 0.0f;
+      const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
+      epilogue_tile<BN>(ep, &tmap_out, alpha, t_row, row, row0, nb * BN, M, N, stage, buf,
+                        rowsum, amax_local);
+      tc_fence_before();
+      __syncwarp();
+      if (warp == 2 && lane == 0) B2F_STAMP(it, 4);
+      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      if (ep.mode == kModeRowSum && row < M)
+        atomicAdd(reinterpret_cast<float*>(ep.out) + row, rowsum * ep.out_inv_scale);
+    }
+    if (lane == 0) bulk_wait_all();  // output stores complete before the CTA exits
+    if (ep.amax != nullptr) {
+      amax_local = warp_max(amax_local);
+      if (lane == 0) atomic_max_nonneg(ep.amax, amax_local);
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+
+// ---------------------------------------------------------------------------------------
+// CTA-pair variant (cluster of 2, tcgen05 cta_group::2): the pair owns a 256 x 256 output
+// tile.  CTA r loads A rows [128 r, 128 r + 128) and B rows [128 r, 128 r + 128) of the
+// tile; the leader (r = 0) issues M=256, N=256, K=32 MMAs that read both CTAs' shared
+// memory, and each CTA's TMEM receives its own 128 rows x 256 columns.  Per SM this moves
+// half the B bytes of the single-CTA kernel for the same MMA work.  TMA loads are plain
+// (no multicast); only tcgen05.commit multicasts its arrive to both CTAs.
+struct Gemm2Cfg {
+  static constexpr int BM = 128;   // rows per CTA (256 per pair)
+  static constexpr int BN = 256;   // columns per pair tile (128 B rows per CTA)
+  static constexpr int BK = 128;
+  static constexpr int STAGES = 6;
+  static constexpr int A_BYTES = BM * BK;
+  static constexpr int B_BYTES = (BN / 2) * BK;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 4 * 8192 + 1024 + 256;
+  static constexpr int THREADS = 192;
+};
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+    gemm_fp8_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                         const __grid_constant__ CUtensorMap tmap_b,
+                         const __grid_constant__ CUtensorMap tmap_out, const GemmShape shape,
+                         const EpilogueParams ep) {
+  using Cfg = Gemm2Cfg;
+  constexpr int STAGES = Cfg::STAGES;
+  constexpr int BN = Cfg::BN;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* smem_a = smem;
+  uint8_t* smem_b = smem + STAGES * Cfg::A_BYTES;
+  uint8_t* smem_stage = smem + STAGES * Cfg::STAGE_BYTES;  // 4 warps x 2 x 4 KB
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem_stage + 4 * 8192);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;  // [2]
+  uint64_t* tempty_bar = tfull_bar + 2;      // [2]  (leader's are used)
+  uint64_t* drain_bar = tempty_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int M = shape.M, N = shape.N, K = shape.K;
+  const int num_m = (M + 2 * Cfg::BM - 1) / (2 * Cfg::BM);
+  const int num_n = (N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (K + Cfg::BK - 1) / Cfg::BK;
+  const int pair = blockIdx.x >> 1;
+  const int num_pairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 8);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+    if (ep.out_vec && ep.mode == kModeStore) tma_prefetch_desc(&tmap_out);
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer (both CTAs)
+      const uint64_t pol = policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0;
+      long long issued = 0;
+      bool ok = true;
+      for (int t = pair; t < num_tiles && ok; t += num_pairs) {
+        int mb, nb;
+        tile_coords(t, num_m, num_n, mb, nb);
+        const int row_a = mb * 2 * Cfg::BM + rank * Cfg::BM;
+        const int row_b = nb * BN + rank * (BN / 2);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, kDevTimeoutProducer, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = map_to_rank(&full_bar[stage], 0);
+          if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * Cfg::STAGE_BYTES);
+          tma_load_2d_pair(smem_a + stage * Cfg::A_BYTES, &tmap_a, fb, kb * Cfg::BK, row_a, pol);
+          tma_load_2d_pair(smem_b + stage * Cfg::B_BYTES, &tmap_b, fb, kb * Cfg::BK, row_b, pol);
+          ++issued;
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      if (rank == 0) {
+        const long long pending = issued < STAGES ? issued : STAGES;
+        for (long long i = 0; i < pending; ++i) {
+          if (--stage < 0) { stage = STAGES - 1; phase ^= 1; }
+          const uint64_t t0 = globaltimer();
+          while (!mbar_test(&full_bar[stage], phase)) {
+            if (globaltimer() - t0 > B2F_WAIT_NS) { record_error(kDevTimeoutDrain); break; }
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ------------------------------------------------------------ MMA issuer (leader)
+      constexpr uint32_t idesc = make_idesc_f8(2 * Cfg::BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int t = pair; t < num_tiles && ok; t += num_pairs, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, kDevTimeoutMma, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, kDevTimeoutMma, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem_a + stage * Cfg::A_BYTES);
+          const uint32_t b_addr = smem_u32(smem_b + stage * Cfg::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < Cfg::BK / 32; ++k) {
+            const uint64_t ad = make_sdesc_sw128(a_addr + k * 32, 1024);
+            const uint64_t bd = make_sdesc_sw128(b_addr + k * 32, 1024);
+            mma_f8_pair(d_tmem, ad, bd, idesc, (kb | k) != 0);
+          }
+          mma_commit_pair(&empty_bar[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (ok) mma_commit_pair(&tfull_bar[acc]);
+      }
+      mma_commit_pair(drain_bar);
+      const uint64_t t0 = globaltimer();
+      while (!mbar_test(drain_bar, 0)) {
+        if (globaltimer() - t0 > B2F_WAIT_NS) { record_error(kDevTimeoutDrain); break; }
+      }
+    }
+  } else {
+    // -------------------------------------------------------------- epilogue (both CTAs)
+    const int q = warp & 3;
+    uint8_t* stage = smem_stage + (warp - 2) * 8192;
+    int buf = 0;
+    float alpha = ep.alpha;
+    if (ep.alpha_ptr != nullptr) alpha *= *ep.alpha_ptr;
+    float amax_local = 0.0f;
+    int it = 0;
+    for (int t = pair; t < num_tiles; t += num_pairs, ++it) {
+      int mb, nb;
+      tile_coords(t, num_m, num_n, mb, nb);
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      if (!mbar_wait(&tfull_bar[acc], acc_phase, kDevTimeoutEpilogue, abort_flag)) break;
+      tc_fence_after();
+      const int row0 = mb * 2 * Cfg::BM + rank * Cfg::BM + q * 32;
+      const int row = row0 + lane;
+      float rowsum = 0.0f;
+      const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
+      epilogue_tile<BN>(ep, &tmap_out, alpha, t_row, row, row0, nb * BN, M, N, stage, buf,
+                        rowsum, amax_local);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(map_to_rank(&tempty_bar[acc], 0));
+      if (ep.mode == kModeRowSum && row < M)
+        atomicAdd(reinterpret_cast<float*>(ep.out) + row, rowsum * ep.out_inv_scale);
+    }
+    if (lane == 0) bulk_wait_all();  // output stores complete before the CTA exits
+    if (ep.amax != nullptr) {
+      amax_local = warp_max(amax_local);
+      if (lane == 0) atomic_max_nonneg(ep.amax, amax_local);
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+}  // namespace b2f

@@ -1,0 +1,30 @@
+// Host-side helpers shared by the C-ABI translation units: error reporting, SM count,
+// and TMA descriptor encoding through the driver entry point (no link-time libcuda
+// dependency, so the library also loads on machines without a GPU driver).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <string>
+
+#include "../../include/b200fp8.h"
+
+namespace b2f {
+
+void set_error(const std::string& msg);
+int fail(int code, const std::string& msg);
+int cuda_fail(cudaError_t e, const char* what);
+int sm_count();
+
+// Encode a 2-D (or 3-D) tiled tensor map for an 8- or 16-bit row-major tensor.
+// dims/strides are innermost first; strides are in bytes for dims 1..rank-1.
+bool encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
+                 const unsigned long long* dims, const unsigned long long* strides_bytes,
+                 const unsigned int* box, CUtensorMapSwizzle swizzle, std::string* err);
+
+#define B2F_CUDA_TRY(expr)                                   \
+  do {                                                       \
+    cudaError_t _e = (expr);                                 \
+    if (_e != cudaSuccess) return ::b2f::cuda_fail(_e, #expr); \
+  } while (0)
+
+}  // namespace b2f

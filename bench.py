@@ -1,0 +1,453 @@
+#!/usr/bin/env python
+"""Benchmark of the b200fp8 hot path (one JSON line on rank 0).
+
+Default workload: square FP8 GEMM C = A . B^T, M=N=K=8192, e4m3
+inputs quantised from N(0,1) with per-tensor amax scales, f32 accumulation, bf16 output.
+A "step" is one GEMM over one input set.  Under torchrun each rank computes its own
+8192-column shard of C = A . [B_0 .. B_{N-1}]^T (weak scaling, no communication).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload gemm|gemm_bias_relu|norm|gpt2|qwen] [--n 8192]
+
+--impl reference times the reference's own computation of the path on the host cores:
+the evaluator's ``torch._scaled_mm(a_fp8, b_fp8.t(), scale_a, scale_b, out_dtype=f32)``
+call (tasks/level1_01_square_matrix_multiplication_fp8/starter.py:125-138) run on CPU,
+with a bf16 cast of the result, each step on a bounded row sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "airi-summer-kernel-evo_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+L2_BYTES = 126 * 1024 * 1024
+
+
+def _peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "basis": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+                "basis": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.t_start = None
+        self.t_end = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu=timestamp,{self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def mark(self, which: str):
+        setattr(self, which, time.time())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out = ""
+        rows = []
+        for line in out.splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 10:
+                continue
+            try:
+                rows.append({"sm": float(parts[2]), "max": float(parts[3]),
+                             "hw": parts[6], "hwt": parts[7], "swt": parts[8], "pcap": parts[9]})
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        under = [r for r in rows if r["sm"] > 0.5 * r["max"]] or rows
+        reasons = set()
+        for r in under:
+            if r["hw"] == "Active":
+                reasons.add("hw_slowdown")
+            if r["hwt"] == "Active":
+                reasons.add("hw_thermal_slowdown")
+            if r["swt"] == "Active":
+                reasons.add("sw_thermal_slowdown")
+            if r["pcap"] == "Active":
+                reasons.add("sw_power_cap")
+        return {"sm_mhz": statistics.median(r["sm"] for r in under),
+                "sm_max_mhz": max(r["max"] for r in rows), "reasons": sorted(reasons),
+                "samples": len(under)}
+
+
+def _dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def _max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ------------------------------------------------------------------ workloads
+def _fp8_inputs(shape, gen, scale=1.0):
+    x = torch.randn(shape, generator=gen, dtype=torch.float32) * scale
+    amax = float(x.abs().max())
+    s = amax / 448.0
+    return (x / s).to(torch.float8_e4m3fn), s
+
+
+class GemmWorkload:
+    """Square FP8 GEMM or GEMM+bias+ReLU."""
+
+    def __init__(self, n: int, rank: int, bias_relu: bool = False, m: int = None):
+        self.n = n
+        self.m = m if m is not None else n
+        self.k = n
+        self.bias_relu = bias_relu
+        g = torch.Generator("cpu").manual_seed(20260726 + rank)
+        xscale = 0.1 if bias_relu else 1.0
+        a, self.sa = _fp8_inputs((self.m, self.k), g, xscale)
+        b, self.sb = _fp8_inputs((self.n, self.k), g, xscale)
+        self.bias_cpu = (torch.randn((self.n,), generator=g) * 0.02) if bias_relu else None
+        self.a_cpu, self.b_cpu = a, b
+        self.flops = 2.0 * self.m * self.n * self.k
+        self.algo_bytes = self.m * self.k + self.n * self.k + self.m * self.n * 2 + (
+            4 * self.n if bias_relu else 0)
+        # Rotate input sets so every step streams operands from HBM, not L2.
+        per_set = self.m * self.k + self.n * self.k
+        self.nsets = max(1, -(-3 * L2_BYTES // per_set)) if per_set < 2 * L2_BYTES else 2
+        self.nsets = min(self.nsets, 8)
+        self.sets = []
+        for i in range(self.nsets):
+            self.sets.append((a.cuda(), b.cuda()))
+        self.bias = self.bias_cpu.cuda() if bias_relu else None
+        self.out = torch.empty((self.m, self.n), device="cuda", dtype=torch.bfloat16)
+        self.i = 0
+        self.name = ("gemm_bias_relu_fp8" if bias_relu else "square_gemm_fp8")
+
+    def config(self):
+        return {"workload": f"{self.name} M={self.m} N={self.n} K={self.k} e4m3->bf16",
+                "M": self.m, "N": self.n, "K": self.k, "out_dtype": "bf16",
+                "inputs": "N(0,1)" + ("x0.1" if self.bias_relu else "") + " amax-scaled e4m3",
+                "l2": f"{self.nsets} rotating input sets "
+                      f"({self.nsets * (self.m * self.k + self.n * self.k) / 2**20:.0f} MiB) > 126 MiB L2"}
+
+    def step(self):
+        from b200fp8 import ops
+        a, b = self.sets[self.i % self.nsets]
+        self.i += 1
+        if self.bias_relu:
+            ops.gemm_fp8(a, b, scale_a=self.sa, scale_b=self.sb, bias=self.bias, act="relu",
+                         out=self.out)
+        else:
+            ops.gemm_fp8(a, b, scale_a=self.sa, scale_b=self.sb, out=self.out)
+        return 1  # launches
+
+    # ---------------- end-to-end through the public API with host buffers
+    def e2e_setup(self):
+        self.h_a = self.a_cpu.view(torch.uint8).pin_memory()
+        self.h_b = self.b_cpu.view(torch.uint8).pin_memory()
+        self.h_out = torch.empty((self.m, self.n), dtype=torch.bfloat16).pin_memory()
+        self.d_a = torch.empty_like(self.h_a, device="cuda")
+        self.d_b = torch.empty_like(self.h_b, device="cuda")
+
+    def e2e_step(self):
+        from b200fp8 import ops
+        self.d_a.copy_(self.h_a, non_blocking=True)
+        self.d_b.copy_(self.h_b, non_blocking=True)
+        if self.bias_relu:
+            ops.gemm_fp8(self.d_a, self.d_b, scale_a=self.sa, scale_b=self.sb, bias=self.bias,
+                         act="relu", out=self.out)
+        else:
+            ops.gemm_fp8(self.d_a, self.d_b, scale_a=self.sa, scale_b=self.sb, out=self.out)
+        self.h_out.copy_(self.out, non_blocking=True)
+
+    def e2e_bytes(self):
+        return self.h_a.numel() + self.h_b.numel(), self.h_out.numel() * 2
+
+    # ---------------- CPU baseline (oracle, bounded row sample)
+    def cpu_sample(self, target_s: float):
+        from oracle import gemm as og
+        threads = len(os.sched_getaffinity(0))
+        torch.set_num_threads(threads)
+        rows = 64
+        t = 0.0
+        while True:
+            t0 = time.perf_counter()
+            v = og.cpu_fast_scaled_mm(self.a_cpu[:rows], self.b_cpu, self.sa, self.sb)
+            if self.bias_relu:
+                v = torch.relu(v + self.bias_cpu)
+            v.to(torch.bfloat16)
+            t = time.perf_counter() - t0
+            if t > target_s / 4 or rows >= self.m:
+                break
+            rows = min(self.m, rows * 4)
+        tflops = 2.0 * rows * self.n * self.k / t / 1e12
+        return {"value": tflops, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                "sample": f"{rows} of {self.m} rows of the same GEMM ({2.0*rows*self.n*self.k/1e9:.1f} GFLOP), "
+                          f"f32 dequantise + torch.matmul on CPU, {t:.2f} s"}
+
+
+def run_ours(args):
+    world, rank, local = _dist()
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    from b200fp8 import _lib, device_status  # noqa: F401  (fails loudly without the .so)
+
+    wl_name = args.workload
+    if wl_name in ("gemm", "gemm_bias_relu"):
+        if wl_name == "gemm":
+            wl = GemmWorkload(args.n, rank)
+        else:
+            wl = GemmWorkload(8192, rank, bias_relu=True, m=128)
+        metric = "TFLOP/s"
+        unit = "TFLOP/s"
+    else:
+        raise SystemExit(f"unknown workload {wl_name}")
+
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        wl.step()
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(torch.cuda.current_device() if world == 1 else local)
+    if rank == 0:
+        sampler.start()
+        time.sleep(0.3)
+    # Untimed soak (~1 s of the same steps) so the clocks the sampler sees, and the
+    # timed region, are the sustained under-load state rather than an idle-clock burst.
+    t_soak = time.time()
+    while time.time() - t_soak < args.soak_seconds:
+        for _ in range(8):
+            wl.step()
+        torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    _barrier(world)
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    launches = 0
+    for i in range(args.steps):
+        ev[i][0].record(stream)
+        launches += wl.step()
+        ev[i][1].record(stream)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    _barrier(world)
+    clocks = sampler.stop() if rank == 0 else None
+    total_ms = _max_over_ranks(t0.elapsed_time(t1), world)
+    per_launch_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
+    per_launch_ms = _max_over_ranks(per_launch_ms, world)
+    ms_per_step = total_ms / args.steps
+    value = wl.flops * world / (ms_per_step * 1e-3) / 1e12
+    status = device_status()
+
+    # end-to-end through the public op with pinned host buffers
+    wl.e2e_setup()
+    for _ in range(2):
+        wl.e2e_step()
+    torch.cuda.synchronize()
+    _barrier(world)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(3, min(args.steps, 20))
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        wl.e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = _max_over_ranks(e0.elapsed_time(e1) / e2e_steps, world)
+    h2d, d2h = wl.e2e_bytes()
+
+    # cuBLASLt FP8 (torch._scaled_mm) on the same operands: a library reference point.
+    cublas = None
+    if wl_name == "gemm":
+        try:
+            a, b = wl.sets[0]
+            sa = torch.tensor(wl.sa, device="cuda")
+            sb = torch.tensor(wl.sb, device="cuda")
+            for _ in range(3):
+                torch._scaled_mm(a, b.t(), scale_a=sa, scale_b=sb, out_dtype=torch.bfloat16)
+            torch.cuda.synchronize()
+            c0 = torch.cuda.Event(enable_timing=True)
+            c1 = torch.cuda.Event(enable_timing=True)
+            reps = 10
+            c0.record()
+            for j in range(reps):
+                a, b = wl.sets[j % wl.nsets]
+                torch._scaled_mm(a, b.t(), scale_a=sa, scale_b=sb, out_dtype=torch.bfloat16)
+            c1.record()
+            torch.cuda.synchronize()
+            cublas = wl.flops / (c0.elapsed_time(c1) / reps * 1e-3) / 1e12
+        except Exception as exc:  # report, never fail the bench on the side measurement
+            cublas = f"unavailable: {type(exc).__name__}"
+
+    peaks = _peaks()
+    fp8_peak = 2.0 * peaks["bf16_tflops"]
+    achieved = wl.flops / (per_launch_ms * 1e-3) / 1e12
+    out = {
+        "metric": f"{metric} ({wl.name}, whole job)", "value": round(value, 2), "unit": unit,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 in, f32 accumulate, bf16 out",
+        "data": "synthetic (seeded N(0,1), per-tensor amax e4m3 scales)",
+        "config": dict(wl.config(), parallelism=f"N-sharded columns x{world} (no communication)"),
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1),
+                     "peak": round(fp8_peak, 1), "unit": "TFLOP/s",
+                     "frac": round(achieved / fp8_peak, 4),
+                     "peak_basis": f"2 x {peaks['basis']} cuBLAS bf16 burst "
+                                   f"({peaks['bf16_tflops']} TFLOP/s); e4m3 dense rate is 2x bf16",
+                     "traffic": None, "kernel": "gemm_fp8_kernel<256>",
+                     "per_launch_ms": round(per_launch_ms, 5),
+                     "algorithmic_bytes": wl.algo_bytes},
+        "e2e": {"value": round(wl.flops * world / (e2e_ms * 1e-3) / 1e12, 3), "unit": unit,
+                "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h,
+                "path": "b200fp8.ops.gemm_fp8 with pinned host A,B -> device, C -> host"},
+        "gpu_launches": launches,
+        "clocks": clocks,
+        "device_status": status,
+        "cublaslt_fp8_tflops_same_shape": (round(cublas, 1) if isinstance(cublas, float) else cublas),
+    }
+    traffic_path = os.path.join(ROOT, "profiles", "gemm_fp8_traffic.json")
+    if os.path.exists(traffic_path):
+        try:
+            with open(traffic_path) as f:
+                tr = json.load(f)
+            if tr.get("n") == wl.n:
+                out["roofline"]["traffic"] = tr.get("traffic_bytes_per_launch")
+        except Exception:
+            pass
+    if rank == 0 and world == 1:
+        out["cpu_baseline"] = wl.cpu_sample(target_s=args.cpu_seconds)
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    """Reference arm: the reference evaluator's own _scaled_mm math on the host cores."""
+    world, rank, _ = _dist()
+    if rank != 0:
+        return
+    from oracle import gemm as og
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    n = args.n
+    g = torch.Generator("cpu").manual_seed(20260726)
+    b, sb = _fp8_inputs((n, n), g)
+    if args.ref_rows > 0:
+        rows = args.ref_rows
+    else:
+        # The reference's CPU _scaled_mm is scalar: calibrate on one row, then size each
+        # step so that warmup + steps take about two minutes in total.
+        a1, sa1 = _fp8_inputs((1, n), g)
+        t0 = time.perf_counter()
+        og.reference_scaled_mm_cpu(a1, b, sa1, sb)
+        t_row = max(time.perf_counter() - t0, 1e-4)
+        rows = int(max(1, min(n, 120.0 / (args.steps + args.warmup) / t_row)))
+    a, sa = _fp8_inputs((rows, n), g)
+    step = lambda: og.reference_scaled_mm_cpu(a, b, sa, sb).to(torch.bfloat16)  # noqa: E731
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / args.steps
+    flops = 2.0 * rows * n * n
+    value = flops / dt / 1e12
+    out = {
+        "impl": "reference", "metric": "TFLOP/s (square_gemm_fp8, whole job)",
+        "value": round(value, 5), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 in, f32 accumulate, bf16 out",
+        "data": "synthetic (seeded N(0,1), per-tensor amax e4m3 scales)",
+        "config": {"workload": f"square_gemm_fp8 M=N=K={n} e4m3->bf16 (row sample)",
+                   "M": n, "N": n, "K": n, "parallelism": "host cores of rank 0"},
+        "cpu_baseline": {"value": round(value, 5), "unit": "TFLOP/s", "cores": threads,
+                         "kind": "port",
+                         "sample": f"{rows} of {n} rows per step: torch._scaled_mm(a, b.t(), "
+                                   "scale_a, scale_b, out_dtype=f32) on CPU, the reference "
+                                   "evaluator's call (level1_01 starter.py:125-138)"},
+        "e2e": {"value": round(value, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__,
+                                 formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="gemm")
+    ap.add_argument("--n", type=int, default=8192)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--ref-rows", type=int, default=0,
+                    help="rows per reference step (0 = sized for a ~2 minute run)")
+    ap.add_argument("--soak-seconds", type=float, default=1.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,194 @@
+/*
+ * b200fp8 — C ABI of the B200-native FP8 kernel library (libb200fp8.so).
+ *
+ * The reference (bulatsharif/airi-summer-kernel-evo) exposes its kernels as CuTe-DSL
+ * `@cute.jit` entry points that an evaluator compiles and calls with evaluator-owned
+ * tensors.  Each entry point below replaces one of those interfaces; the comment above
+ * every function names the reference interface (file:line, relative to the reference
+ * repository root).
+ *
+ * Conventions
+ *  - Every pointer is a device pointer owned by the caller (the reference's evaluator
+ *    owns every buffer the same way, tasks/model_gpt2_small_transformer_block_fp8/TASK.md:46-49).
+ *  - FP8 tensors are raw float8_e4m3fn bytes; a stored byte q means the value q * scale.
+ *  - Row-major storage with an explicit leading dimension (elements) per matrix.
+ *  - `stream` is a cudaStream_t passed as void*.  Calls are asynchronous on it.
+ *  - Return value: B2F_OK or a B2F_ERR_* code; b2f_last_error() gives a message for the
+ *    calling thread.  No C++ exception crosses this ABI.
+ *  - Kernels never trap.  Every internal wait is bounded; an expired wait sets the device
+ *    status word, which b2f_status_read() returns (B2F_DEV_* codes).
+ */
+#ifndef B200FP8_H_
+#define B200FP8_H_
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B2F_ABI_VERSION 1
+
+typedef void* b2f_stream_t;
+
+enum b2f_status {
+  B2F_OK = 0,
+  B2F_ERR_ARG = 1,
+  B2F_ERR_UNSUPPORTED = 2,
+  B2F_ERR_CUDA = 3,
+  B2F_ERR_TIMEOUT = 4,
+  B2F_ERR_NCCL = 5
+};
+
+enum b2f_dtype { B2F_DTYPE_F32 = 0, B2F_DTYPE_BF16 = 1, B2F_DTYPE_E4M3 = 2 };
+
+enum b2f_act {
+  B2F_ACT_NONE = 0,
+  B2F_ACT_RELU = 1,
+  B2F_ACT_GELU_TANH = 2,
+  B2F_ACT_LEAKY_RELU = 3,
+  B2F_ACT_SILU = 4
+};
+
+enum b2f_gemm_mode { B2F_GEMM_STORE = 0, B2F_GEMM_ROWSUM = 1 };
+
+/* Device status word codes (b2f_status_read). */
+enum b2f_dev_status {
+  B2F_DEV_OK = 0,
+  B2F_DEV_TIMEOUT_PRODUCER = 1,
+  B2F_DEV_TIMEOUT_MMA = 2,
+  B2F_DEV_TIMEOUT_EPILOGUE = 3,
+  B2F_DEV_TIMEOUT_DRAIN = 4,
+  B2F_DEV_BAD_ARGS = 5
+};
+
+/* Library ABI version (B2F_ABI_VERSION of the build). */
+int b2f_version(void);
+
+/* Message describing the last error returned to the calling thread ("" if none). */
+const char* b2f_last_error(void);
+
+/* Number of SMs on the current device (cached per device), or -1. */
+int b2f_num_sms(void);
+
+/* Read (and with reset != 0, clear) the device status word of the current device. */
+int b2f_status_read(int reset);
+
+/* Test hook: launch one kernel that waits on an mbarrier nothing arrives on, with a
+ * bounded wait of `wait_ns`; it must record B2F_DEV_TIMEOUT_EPILOGUE and return. */
+int b2f_debug_bounded_wait(unsigned long long wait_ns, b2f_stream_t stream);
+
+/* ------------------------------------------------------------------ GEMM
+ * out = epilogue(alpha * (A . B^T))
+ *   A: e4m3 [m, lda], K-major; B: e4m3 [n, ldb], K-major (the reference's `matrix_b_nk`).
+ *   v = (alpha * acc [* *alpha_ptr] + bias[col]) * pre_mul + pre_add
+ *   v = act(v) * post_mul
+ *   v += residual[row, col] * residual_scale           (optional)
+ *   STORE : out[row, col] = v / out_scale  in out_dtype (e4m3 uses RN + saturation)
+ *   ROWSUM: out[row] += sum_col(v) / out_scale  (out is f32 [m], zeroed by the caller)
+ *   amax (optional): *amax = max(*amax, |v|) over the written elements.
+ * Replaces: square_gemm (tasks/level1_01_square_matrix_multiplication_fp8/starter.py:29-37,
+ *   reference math :125-138), gemm_add_relu (tasks/level2_76_gemm_add_relu_fp8/starter.py,
+ *   reference math :148-169) and the epilogue family tasks/level2_{09,12,14,40,63}_* /
+ *   starter.py:116-126, the QKV projection tasks/model_gpt2_small_qkv_projection_fp8/
+ *   starter.py:151-158 and every `_cute_harness_scaled_linear` of the block tasks.
+ * Requirements: lda, ldb multiples of 16; k multiple of 16; 16-byte aligned A, B.
+ */
+typedef struct b2f_gemm_args {
+  int m, n, k;
+  const void* a;
+  long long lda;
+  const void* b;
+  long long ldb;
+  float alpha;
+  const float* alpha_ptr;
+  const float* bias;
+  float pre_mul, pre_add;
+  int act;
+  float act_param;
+  float post_mul;
+  const void* residual;
+  int residual_dtype;
+  long long residual_ld;
+  float residual_scale;
+  void* out;
+  int out_dtype;
+  long long out_ld;
+  float out_scale;
+  float* amax;
+  int mode;
+  int tile_n; /* 0 = automatic, else 128 or 256 */
+} b2f_gemm_args;
+
+/* Fill `args` with neutral defaults (alpha 1, pre_mul 1, post_mul 1, out_scale 1, bf16 out). */
+void b2f_gemm_args_init(b2f_gemm_args* args);
+
+int b2f_gemm_fp8(const b2f_gemm_args* args, b2f_stream_t stream);
+
+/* Co-resident CTA pairs the last CTA-pair GEMM launch on this thread used (0 = none yet). */
+int b2f_gemm_pair_capacity(void);
+
+/* ------------------------------------------------------------------ norm + quantise
+ * h = x * x_scale + residual          (x: bf16 / f32 / e4m3; residual optional, bf16 / f32)
+ * RMS  : y = h * rsqrt(mean(h^2) + eps) * (weight + weight_offset)
+ * LAYER: y = (h - mean) * rsqrt(var(h) + eps) * weight + bias
+ * q = e4m3(y / s): s = q_scale (static) or, with dynamic_scale, s = amax(|bf16(y)|) / 448
+ *     written to *scale_out (the kernel also leaves amax(|y|) in *amax).
+ * Optional outputs: h_out (the updated residual stream; when bf16 the norm uses the
+ * bf16-rounded h), y_out (bf16 normalised rows).
+ * Replaces: residual_rmsnorm (cute_kernels/fused_residual_rmsnorm_fp8/submission.py:57-106,
+ *   formula :139-145), the Qwen rms_norm step (tasks/model_qwen35_4b_full_attention_block_fp8/
+ *   starter.py:167-171, used at :347-348 and :402-403), the GPT-2 LayerNorm steps
+ *   (tasks/model_gpt2_small_transformer_block_fp8/starter.py:407-416, 461-470) and
+ *   layer_norm (tasks/level1_40_layer_norm_fp8/starter.py).
+ * Requirements: cols % 8 == 0, cols <= 4096, 16-byte aligned rows.
+ */
+enum b2f_norm_kind { B2F_NORM_RMS = 0, B2F_NORM_LAYER = 1 };
+
+typedef struct b2f_norm_args {
+  int rows, cols;
+  const void* x;
+  int x_dtype;
+  float x_scale;
+  long long x_ld;
+  const void* residual;
+  int residual_dtype;
+  long long residual_ld;
+  const void* weight;
+  const void* bias;
+  int weight_dtype;
+  float weight_offset;
+  int kind;
+  float eps;
+  void* h_out;
+  int h_dtype;
+  long long h_ld;
+  void* y_out;
+  long long y_ld;
+  void* q_out;
+  long long q_ld;
+  float q_scale;
+  int dynamic_scale;
+  float* amax;
+  float* scale_out;
+} b2f_norm_args;
+
+void b2f_norm_args_init(b2f_norm_args* args);
+int b2f_norm_quant(const b2f_norm_args* args, b2f_stream_t stream);
+
+/* ------------------------------------------------------------------ op registry */
+typedef struct b2f_op {
+  const char* name;      /* e.g. "gemm_fp8" */
+  int abi_version;
+  void* fn;              /* pointer to the b2f_* entry point */
+  const char* signature; /* human-readable argument struct name */
+} b2f_op;
+
+/* Look up an op by name; NULL if unknown. */
+const b2f_op* b2f_registry_lookup(const char* name);
+/* Number of registered ops and indexed access (for enumeration). */
+int b2f_registry_size(void);
+const b2f_op* b2f_registry_at(int index);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* B200FP8_H_ */

@@ -1,0 +1,140 @@
+"""Parity of the tcgen05 e4m3 GEMM (b2f_gemm_fp8) with the CPU oracle.
+
+Bars: bf16 outputs within 1 bf16 rounding of the oracle's f32 value (rel 2^-8) plus a
+small absolute slack for f32 accumulation order; e4m3 outputs within 1 e4m3 ulp; f32
+outputs within rel 1e-5 + atol 1e-4 * sqrt(K).
+"""
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+
+from helpers import e4m3_ulp_diff, fp8_amax, gen, randn
+from oracle import gemm as og
+
+pytestmark = pytest.mark.gpu
+
+
+def _ops():
+    from b200fp8 import ops
+    return ops
+
+
+def _close_bf16(out, ref, k):
+    err = (out.float().cpu() - ref).abs()
+    tol = ref.abs() * 2.0 ** -7 + 1e-5 * math.sqrt(k)
+    bad = err > tol
+    assert not bad.any(), f"{int(bad.sum())} mismatches, max err {float(err.max())}"
+
+
+@pytest.mark.parametrize("m,n,k", [
+    (128, 256, 128), (128, 128, 256), (256, 512, 1024), (1000, 777, 528),
+    (8, 40, 64), (384, 2304, 768), (1024, 1024, 4096),
+])
+@pytest.mark.parametrize("tile_n", [0, 128, 256, 512])
+def test_gemm_bf16_out(m, n, k, tile_n):
+    g = gen(20260726 + m + n + k)
+    a, sa = fp8_amax((m, k), g)
+    b, sb = fp8_amax((n, k), g)
+    ref = og.scaled_mm(a, b, sa, sb)
+    out = _ops().gemm_fp8(a.cuda(), b.cuda(), scale_a=sa, scale_b=sb, tile_n=tile_n)
+    torch.cuda.synchronize()
+    _close_bf16(out, ref, k)
+
+
+def test_gemm_f32_out_reference_task_scales():
+    # level1_01 convention: A, B ~ U(0,1)*448 -> e4m3, output f32 * (1/448)^2.
+    g = gen(20260726)
+    n = 512
+    sa = 1.0 / 448.0
+    a = (torch.rand((n, n), generator=g) * 448.0).to(torch.float8_e4m3fn)
+    b = (torch.rand((n, n), generator=g) * 448.0).to(torch.float8_e4m3fn)
+    ref = og.scaled_mm(a, b, sa, sa)
+    out = _ops().gemm_fp8(a.cuda(), b.cuda(), scale_a=sa, scale_b=sa, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    err = (out.cpu() - ref).abs().max().item()
+    assert err <= 0.125 * 1e-2, err  # reference threshold is 0.125 full-abs
+
+
+@pytest.mark.parametrize("variant", ["relu76", "sub_mul_relu09", "leaky12", "scale40",
+                                     "relu_div63", "gelu", "silu"])
+def test_gemm_epilogues(variant):
+    m, n, k = 256, 384, 512
+    g = gen(20260727)
+    a, sa = fp8_amax((m, k), g)
+    b, sb = fp8_amax((n, k), g, 0.1)
+    bias = randn((n,), g, 0.02)
+    kw = dict(bias=bias)
+    if variant == "relu76":
+        kw.update(act="relu")
+    elif variant == "sub_mul_relu09":
+        kw.update(pre_mul=1.5, pre_add=-3.0, act="relu")
+    elif variant == "leaky12":
+        kw.update(pre_mul=2.0, act="leaky_relu", act_param=0.1)
+    elif variant == "scale40":
+        kw.update(pre_mul=1.5)
+    elif variant == "relu_div63":
+        kw.update(act="relu", post_mul=0.5)
+    elif variant == "gelu":
+        kw.update(act="gelu_tanh")
+    elif variant == "silu":
+        kw.update(act="silu")
+    ref = og.gemm_epilogue(a, b, sa, sb, **kw)
+    kwg = dict(kw)
+    kwg["bias"] = bias.cuda()
+    out = _ops().gemm_fp8(a.cuda(), b.cuda(), scale_a=sa, scale_b=sb,
+                          out_dtype=torch.float32, **kwg)
+    torch.cuda.synchronize()
+    err = (out.cpu() - ref).abs()
+    assert float(err.max()) < 1e-4 * (1 + float(ref.abs().max())), float(err.max())
+
+
+def test_gemm_rowsum_level2_14():
+    m, n, k = 256, 1024, 512
+    g = gen(20260727)
+    a, sa = fp8_amax((m, k), g)
+    b, sb = fp8_amax((n, k), g, 0.1)
+    ref = og.gemm_epilogue(a, b, sa, sb, post_mul=0.5, rowsum=True, out_scale=1.0 / 1.5)
+    out = _ops().gemm_fp8(a.cuda(), b.cuda(), scale_a=sa, scale_b=sb, post_mul=0.5,
+                          rowsum=True, out_scale=1.0 / 1.5)
+    torch.cuda.synchronize()
+    err = (out.cpu() - ref).abs().max().item()
+    assert err < 1e-3 * (1 + ref.abs().max().item()), err
+
+
+@pytest.mark.parametrize("res_dtype", [torch.bfloat16, torch.float32])
+def test_gemm_residual_requant_e4m3(res_dtype):
+    m, n, k = 512, 768, 768
+    g = gen(20260801)
+    a, sa = fp8_amax((m, k), g)
+    b, sb = fp8_amax((n, k), g, 0.02)
+    res = randn((m, n), g).to(res_dtype)
+    bias = randn((n,), g, 0.02)
+    out_scale = 1.0 / 64.0
+    v = og.gemm_epilogue(a, b, sa, sb, bias=bias, residual=res, out_scale=out_scale)
+    ref_q = v.to(torch.float8_e4m3fn)
+    amax = torch.zeros(1, device="cuda")
+    out = _ops().gemm_fp8(a.cuda(), b.cuda(), scale_a=sa, scale_b=sb, bias=bias.cuda(),
+                          residual=res.cuda(), out_dtype=torch.float8_e4m3fn,
+                          out_scale=out_scale, amax=amax)
+    torch.cuda.synchronize()
+    d = e4m3_ulp_diff(out.cpu(), ref_q)
+    assert int(d.max()) <= 1
+    assert float((d > 0).float().mean()) < 0.01
+    ref_amax = float((v * out_scale).abs().max())
+    assert abs(float(amax.cpu()) - ref_amax) <= 1e-5 * ref_amax
+
+
+def test_gemm_rejects_bad_args():
+    from b200fp8 import B2FError
+    a = torch.zeros((128, 100), dtype=torch.uint8, device="cuda")
+    b = torch.zeros((128, 100), dtype=torch.uint8, device="cuda")
+    with pytest.raises(B2FError):
+        _ops().gemm_fp8(a, b)  # K=100 is not a multiple of 16
+
+
+def test_status_word_clean_after_gemms():
+    from b200fp8 import device_status
+    assert device_status() == 0
