@@ -87,6 +87,36 @@ class NormArgs(ctypes.Structure):
     ]
 
 
+class AttnArgs(ctypes.Structure):
+    """Mirror of ``b2f_attn_args`` (include/b200fp8.h)."""
+
+    _fields_ = [
+        ("batch", ctypes.c_int), ("seq", ctypes.c_int), ("hq", ctypes.c_int),
+        ("hkv", ctypes.c_int), ("head_dim", ctypes.c_int), ("causal", ctypes.c_int),
+        ("q", ctypes.c_void_p), ("q_ld", ctypes.c_longlong), ("q_scale", ctypes.c_float),
+        ("k", ctypes.c_void_p), ("k_ld", ctypes.c_longlong), ("k_scale", ctypes.c_float),
+        ("v", ctypes.c_void_p), ("v_ld", ctypes.c_longlong), ("v_scale", ctypes.c_float),
+        ("sm_scale", ctypes.c_float),
+        ("gate", ctypes.c_void_p), ("gate_dtype", ctypes.c_int), ("gate_ld", ctypes.c_longlong),
+        ("gate_head_stride", ctypes.c_longlong), ("gate_scale", ctypes.c_float),
+        ("ctx", ctypes.c_void_p), ("ctx_ld", ctypes.c_longlong), ("ctx_scale", ctypes.c_float),
+    ]
+
+
+class RopeArgs(ctypes.Structure):
+    """Mirror of ``b2f_rope_args`` (include/b200fp8.h)."""
+
+    _fields_ = [
+        ("rows", ctypes.c_int), ("heads", ctypes.c_int), ("head_dim", ctypes.c_int),
+        ("in", ctypes.c_void_p), ("in_ld", ctypes.c_longlong),
+        ("in_head_stride", ctypes.c_longlong), ("in_scale", ctypes.c_float),
+        ("weight", ctypes.c_void_p), ("weight_offset", ctypes.c_float), ("eps", ctypes.c_float),
+        ("cos", ctypes.c_void_p), ("sin", ctypes.c_void_p), ("rotary_dim", ctypes.c_int),
+        ("seq", ctypes.c_int),
+        ("out", ctypes.c_void_p), ("out_ld", ctypes.c_longlong), ("out_scale", ctypes.c_float),
+    ]
+
+
 class Op(ctypes.Structure):
     """Mirror of ``b2f_op``."""
 
@@ -102,7 +132,8 @@ class Op(ctypes.Structure):
 EXPORTED_SYMBOLS = (
     "b2f_version", "b2f_last_error", "b2f_num_sms", "b2f_status_read",
     "b2f_debug_bounded_wait", "b2f_gemm_args_init", "b2f_gemm_fp8", "b2f_gemm_pair_capacity",
-    "b2f_norm_args_init", "b2f_norm_quant",
+    "b2f_norm_args_init", "b2f_norm_quant", "b2f_attn_args_init", "b2f_attention_fp8",
+    "b2f_head_norm_rope", "b2f_fp8_to_bf16",
     "b2f_registry_lookup", "b2f_registry_size", "b2f_registry_at",
 )
 
@@ -127,6 +158,15 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.b2f_norm_args_init.restype = None
     lib.b2f_norm_quant.argtypes = [ctypes.POINTER(NormArgs), vp]
     lib.b2f_norm_quant.restype = ctypes.c_int
+    lib.b2f_attn_args_init.argtypes = [ctypes.POINTER(AttnArgs)]
+    lib.b2f_attn_args_init.restype = None
+    lib.b2f_attention_fp8.argtypes = [ctypes.POINTER(AttnArgs), vp]
+    lib.b2f_attention_fp8.restype = ctypes.c_int
+    lib.b2f_head_norm_rope.argtypes = [ctypes.POINTER(RopeArgs), vp]
+    lib.b2f_head_norm_rope.restype = ctypes.c_int
+    lib.b2f_fp8_to_bf16.argtypes = [vp, ctypes.c_longlong, vp, ctypes.c_longlong, ctypes.c_int,
+                                    ctypes.c_int, ctypes.c_float, vp]
+    lib.b2f_fp8_to_bf16.restype = ctypes.c_int
     lib.b2f_registry_lookup.argtypes = [ctypes.c_char_p]
     lib.b2f_registry_lookup.restype = ctypes.POINTER(Op)
     lib.b2f_registry_size.restype = ctypes.c_int

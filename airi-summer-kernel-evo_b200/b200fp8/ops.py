@@ -161,3 +161,81 @@ def norm_quant(x: torch.Tensor, weight: torch.Tensor, *, kind: str = "rms",
     args.amax, args.scale_out = _ptr(amax), _ptr(scale_out)
     check(_lib.lib().b2f_norm_quant(ctypes.byref(args), _stream()))
     return q_out, scale_out
+
+
+def attention_fp8(q: torch.Tensor, k: torch.Tensor, v_bf16: torch.Tensor, *, batch: int,
+                  heads: int, kv_heads: int, head_dim: int, causal: bool = True,
+                  q_scale: float = 1.0, k_scale: float = 1.0, v_scale: float = 1.0,
+                  sm_scale: float = 0.0, gate: Optional[torch.Tensor] = None,
+                  gate_scale: float = 1.0, gate_head_stride: Optional[int] = None,
+                  ctx: Optional[torch.Tensor] = None, ctx_scale: float = 1.0) -> torch.Tensor:
+    """Fused attention (see b2f_attention_fp8).  q/k are e4m3 2-D [T, cols] views with head h
+    at column h*head_dim (row pitch = stride(0)); v_bf16 is bf16 [T, cols]; returns the e4m3
+    context [T, heads*head_dim]."""
+    _check_cuda(q, k, v_bf16, gate, ctx)
+    _fp8_rows(q, "q")
+    _fp8_rows(k, "k")
+    if v_bf16.dtype != torch.bfloat16 or v_bf16.dim() != 2 or v_bf16.stride(1) != 1:
+        raise TypeError("v must be a row-major bf16 2-D tensor")
+    t = q.shape[0]
+    if t % batch:
+        raise ValueError("token count must be batch * seq")
+    if ctx is None:
+        ctx = torch.empty((t, heads * head_dim), device=q.device, dtype=torch.float8_e4m3fn)
+    a = _lib.AttnArgs()
+    _lib.lib().b2f_attn_args_init(ctypes.byref(a))
+    a.batch, a.seq, a.hq, a.hkv, a.head_dim = batch, t // batch, heads, kv_heads, head_dim
+    a.causal = 1 if causal else 0
+    a.q, a.q_ld, a.q_scale = q.data_ptr(), q.stride(0), q_scale
+    a.k, a.k_ld, a.k_scale = k.data_ptr(), k.stride(0), k_scale
+    a.v, a.v_ld, a.v_scale = v_bf16.data_ptr(), v_bf16.stride(0), v_scale
+    a.sm_scale = sm_scale
+    if gate is not None:
+        if gate.dim() != 2 or gate.stride(1) != 1:
+            raise ValueError("gate must be row-major 2-D")
+        a.gate, a.gate_dtype, a.gate_ld = gate.data_ptr(), _DT[gate.dtype], gate.stride(0)
+        a.gate_head_stride = head_dim if gate_head_stride is None else gate_head_stride
+        a.gate_scale = gate_scale
+    a.ctx, a.ctx_ld, a.ctx_scale = ctx.data_ptr(), ctx.stride(0), ctx_scale
+    check(_lib.lib().b2f_attention_fp8(ctypes.byref(a), _stream()))
+    return ctx
+
+
+def head_norm_rope(x: torch.Tensor, *, heads: int, head_dim: int, in_scale: float,
+                   out_scale: float, head_stride: Optional[int] = None,
+                   weight: Optional[torch.Tensor] = None, weight_offset: float = 1.0,
+                   eps: float = 1e-6, cos: Optional[torch.Tensor] = None,
+                   sin: Optional[torch.Tensor] = None, rotary_dim: int = 0, seq: int = 0,
+                   out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Per-head RMSNorm (w + weight_offset) + rotate-half RoPE + e4m3 requantisation."""
+    _check_cuda(x, weight, cos, sin, out)
+    _fp8_rows(x, "x")
+    rows = x.shape[0]
+    if out is None:
+        out = torch.empty((rows, heads * head_dim), device=x.device, dtype=torch.float8_e4m3fn)
+    a = _lib.RopeArgs()
+    a.rows, a.heads, a.head_dim = rows, heads, head_dim
+    setattr(a, "in", x.data_ptr())
+    a.in_ld = x.stride(0)
+    a.in_head_stride = head_dim if head_stride is None else head_stride
+    a.in_scale = in_scale
+    if weight is not None and weight.dtype != torch.float32:
+        raise TypeError("weight must be f32")
+    a.weight, a.weight_offset, a.eps = _ptr(weight), weight_offset, eps
+    a.cos, a.sin, a.rotary_dim, a.seq = _ptr(cos), _ptr(sin), rotary_dim, seq
+    a.out, a.out_ld, a.out_scale = out.data_ptr(), out.stride(0), out_scale
+    check(_lib.lib().b2f_head_norm_rope(ctypes.byref(a), _stream()))
+    return out
+
+
+def fp8_to_bf16(x: torch.Tensor, scale: float = 1.0,
+                out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """bf16 copy of an e4m3 [rows, cols] view (exact), times ``scale``."""
+    _check_cuda(x, out)
+    _fp8_rows(x, "x")
+    rows, cols = x.shape
+    if out is None:
+        out = torch.empty((rows, cols), device=x.device, dtype=torch.bfloat16)
+    check(_lib.lib().b2f_fp8_to_bf16(x.data_ptr(), x.stride(0), out.data_ptr(), out.stride(0),
+                                     rows, cols, scale, _stream()))
+    return out

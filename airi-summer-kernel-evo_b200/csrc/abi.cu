@@ -113,6 +113,9 @@ namespace {
 const b2f_op g_ops[] = {
     {"gemm_fp8", B2F_ABI_VERSION, (void*)&b2f_gemm_fp8, "b2f_gemm_args"},
     {"norm_quant", B2F_ABI_VERSION, (void*)&b2f_norm_quant, "b2f_norm_args"},
+    {"attention_fp8", B2F_ABI_VERSION, (void*)&b2f_attention_fp8, "b2f_attn_args"},
+    {"head_norm_rope", B2F_ABI_VERSION, (void*)&b2f_head_norm_rope, "b2f_rope_args"},
+    {"fp8_to_bf16", B2F_ABI_VERSION, (void*)&b2f_fp8_to_bf16, "(in, in_ld, out, out_ld, rows, cols, scale)"},
 };
 }
 

@@ -1,0 +1,500 @@
+// Fused FP8 attention on 5th-generation tensor cores (C ABI: b2f_attention_fp8).
+//
+// One CTA owns 128 queries of one (sequence, query head):
+//   S_j  = Q . K_j^T            tcgen05.mma kind::f8f6f4 (e4m3 x e4m3 -> f32 in TMEM)
+//   P_j  = exp2(S_j * scale*log2e - m)  in registers, online softmax with lazy rescaling
+//          (the running max only moves when it grows by more than 2^8), P rounded to bf16
+//   O   += P_j . V_j            tcgen05.mma kind::f16 (bf16 x bf16 -> f32 in TMEM);
+//                               V is bf16 (exact image of the e4m3 values) read MN-major
+//   ctx  = e4m3( O / l * sigmoid(gate) / ctx_scale )   fused epilogue
+// Roles (192 threads): warp 0 TMA producer (Q once, K/V ring), warp 1 MMA issuer,
+// warps 2-5 softmax + epilogue (one query row per thread).  S is double-buffered in TMEM
+// so Q.K_{j+1}^T runs while the softmax of tile j is computed.  Causal tiles above the
+// diagonal are never visited; GQA maps query head h to KV head h / (Hq / Hkv).
+//
+// Reference math: tasks/model_gpt2_small_transformer_block_fp8/starter.py:428-453 (GPT-2),
+// tasks/model_qwen35_4b_full_attention_block_fp8/starter.py:354-392 (Qwen, gated GQA),
+// tasks/model_qwen35_4b_vision_block_fp8/starter.py:327-345 (non-causal).
+#include <cstring>
+#include <string>
+
+#include "common.cuh"
+#include "host_common.h"
+
+namespace b2f {
+namespace {
+
+struct AttnParams {
+  int seq, batch, hq, hkv;
+  int causal;
+  float qk_scale_log2;  // q_scale * k_scale * sm_scale * log2(e)
+  const void* gate;     // optional [T, gate_ld], e4m3 or bf16
+  int gate_dtype;
+  long long gate_ld;
+  long long gate_hstride;
+  float gate_scale;
+  uint8_t* ctx;         // e4m3 [T, ctx_ld], head h at column h * D
+  long long ctx_ld;
+  float ctx_inv_scale;
+  float v_scale;        // V bf16 values are multiplied by v_scale in the epilogue
+};
+
+__device__ __forceinline__ uint64_t make_sdesc(uint32_t addr, uint32_t layout, uint32_t lbo,
+                                               uint32_t sbo) {
+  uint64_t d = 0;
+  d |= uint64_t((addr >> 4) & 0x3FFF);
+  d |= uint64_t((lbo >> 4) & 0x3FFF) << 16;
+  d |= uint64_t((sbo >> 4) & 0x3FFF) << 32;
+  d |= uint64_t(1) << 46;
+  d |= uint64_t(layout & 7) << 61;
+  return d;
+}
+
+template <int D>
+struct AttnCfg {
+  static constexpr int BQ = 128;
+  static constexpr int BKV = (D == 256) ? 64 : 128;
+  static constexpr int ST = (D == 256) ? 2 : 3;
+  // e4m3 operand tiles: rows of min(D,128) bytes, D/128 k-blocks (1 for D=64)
+  static constexpr int KB = (D >= 128) ? D / 128 : 1;
+  static constexpr int ROWB = (D >= 128) ? 128 : D;
+  static constexpr uint32_t LAYOUT8 = (ROWB == 128) ? 2u : 4u;  // SW128 / SW64
+  static constexpr uint32_t SBO8 = 8 * ROWB;
+  static constexpr int Q_BYTES = BQ * D;
+  static constexpr int K_BYTES = BKV * D;
+  static constexpr int V_BYTES = BKV * D * 2;  // bf16
+  static constexpr int P_BYTES = BQ * BKV * 2;  // bf16
+  static constexpr int STAGE_BYTES = K_BYTES + V_BYTES;
+  static constexpr int SMEM_BYTES = Q_BYTES + ST * STAGE_BYTES + P_BYTES + 1024 + 512;
+  static constexpr int S_COLS = BKV;
+  static constexpr int O_COL = 2 * BKV;
+  static constexpr int TMEM_COLS = 512;
+  static_assert(2 * BKV + D <= 512, "TMEM budget");
+};
+
+template <int D>
+__global__ void __launch_bounds__(192, 1)
+    attention_kernel(const __grid_constant__ CUtensorMap tm_q,
+                     const __grid_constant__ CUtensorMap tm_k,
+                     const __grid_constant__ CUtensorMap tm_v, const AttnParams p) {
+  using C = AttnCfg<D>;
+  constexpr int BQ = C::BQ, BKV = C::BKV, ST = C::ST;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sq = smem;
+  uint8_t* skv = sq + C::Q_BYTES;
+  uint8_t* sp = skv + ST * C::STAGE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sp + C::P_BYTES);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = kv_full + ST;
+  uint64_t* s_full = kv_empty + ST;  // [2]
+  uint64_t* s_free = s_full + 2;     // [2]
+  uint64_t* p_full = s_free + 2;
+  uint64_t* pv_done = p_full + 1;
+  uint64_t* drain = pv_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_qt = (p.seq + BQ - 1) / BQ;
+  const int qt = n_qt - 1 - blockIdx.x;  // longest causal rows first
+  const int h = blockIdx.y;
+  const int b = blockIdx.z;
+  const int hk = h / (p.hq / p.hkv);
+  const int q0 = qt * BQ;
+  const int kv_end = p.causal ? min(p.seq, q0 + BQ) : p.seq;
+  const int nkv = (kv_end + BKV - 1) / BKV;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);
+    }
+    mbar_init(p_full, 4);
+    mbar_init(pv_done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------------------------- producer
+      const uint64_t pol = policy_evict_last();
+      mbar_arrive_expect_tx(q_full, C::Q_BYTES);
+      for (int kb = 0; kb < C::KB; ++kb)
+        tma_load_3d(sq + kb * BQ * C::ROWB, &tm_q, q_full, h * D + kb * 128, q0, b, pol);
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      for (int j = 0; j < nkv; ++j) {
+        if (!mbar_wait(&kv_empty[stage], phase ^ 1, kDevTimeoutProducer, abort_flag)) break;
+        uint8_t* sk = skv + stage * C::STAGE_BYTES;
+        uint8_t* sv = sk + C::K_BYTES;
+        mbar_arrive_expect_tx(&kv_full[stage], C::STAGE_BYTES);
+        for (int kb = 0; kb < C::KB; ++kb)
+          tma_load_3d(sk + kb * BKV * C::ROWB, &tm_k, &kv_full[stage], hk * D + kb * 128,
+                      j * BKV, b, pol);
+        for (int vb = 0; vb < D / 64; ++vb)
+          tma_load_3d(sv + vb * BKV * 128, &tm_v, &kv_full[stage], hk * D + vb * 64, j * BKV, b,
+                      pol);
+        ++issued;
+        if (++stage == ST) { stage = 0; phase ^= 1; }
+      }
+      // drain outstanding copies before the CTA may exit
+      const int pending = issued < ST ? issued : ST;
+      for (int i = 0; i < pending; ++i) {
+        if (--stage < 0) { stage = ST - 1; phase ^= 1; }
+        const uint64_t t0 = globaltimer();
+        while (!mbar_test(&kv_full[stage], phase))
+          if (globaltimer() - t0 > B2F_WAIT_NS) { record_error(kDevTimeoutDrain); break; }
+      }
+      {
+        const uint64_t t0 = globaltimer();
+        while (!mbar_test(q_full, 0))
+          if (globaltimer() - t0 > B2F_WAIT_NS) { record_error(kDevTimeoutDrain); break; }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------------------------------------------------------- MMA issuer
+      constexpr uint32_t idesc_s = make_idesc_f8(BQ, BKV);
+      constexpr uint32_t idesc_pv = make_idesc_bf16(BQ, D, 1);
+      bool ok = mbar_wait(q_full, 0, kDevTimeoutMma, abort_flag);
+      const uint32_t q_addr = smem_u32(sq);
+      auto issue_s = [&](int j) -> bool {
+        const int st = j % ST;
+        const uint32_t ph = (j / ST) & 1;
+        if (!mbar_wait(&kv_full[st], ph, kDevTimeoutMma, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(skv + st * C::STAGE_BYTES);
+        const uint32_t d_s = tmem + (j & 1) * C::S_COLS;
+#pragma unroll
+        for (int kb = 0; kb < C::KB; ++kb) {
+#pragma unroll
+          for (int k = 0; k < C::ROWB / 32; ++k) {
+            const uint64_t ad =
+                make_sdesc(q_addr + kb * BQ * C::ROWB + k * 32, C::LAYOUT8, 16, C::SBO8);
+            const uint64_t bd =
+                make_sdesc(k_addr + kb * BKV * C::ROWB + k * 32, C::LAYOUT8, 16, C::SBO8);
+            mma_f8(d_s, ad, bd, idesc_s, (kb | k) != 0);
+          }
+        }
+        mma_commit(&s_full[j & 1]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      if (ok && nkv > 1) ok = issue_s(1);
+      const uint32_t p_addr = smem_u32(sp);
+      for (int j = 0; j < nkv && ok; ++j) {
+        if (!mbar_wait(p_full, j & 1, kDevTimeoutMma, abort_flag)) break;
+        tc_fence_after();
+        const int st = j % ST;
+        const uint32_t v_addr = smem_u32(skv + st * C::STAGE_BYTES + C::K_BYTES);
+#pragma unroll
+        for (int kb = 0; kb < BKV / 64; ++kb) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t ad = make_sdesc(p_addr + kb * BQ * 128 + k * 32, 2, 16, 1024);
+            const uint64_t bd = make_sdesc(v_addr + (kb * 4 + k) * 2048, 2, BKV * 128, 1024);
+            mma_bf16(tmem + C::O_COL, ad, bd, idesc_pv, (j | kb | k) != 0);
+          }
+        }
+        mma_commit(pv_done);
+        mma_commit(&kv_empty[st]);
+        if (j + 2 < nkv) {
+          if (!mbar_wait(&s_free[j & 1], (j >> 1) & 1, kDevTimeoutMma, abort_flag)) break;
+          if (!issue_s(j + 2)) break;
+        }
+      }
+      mma_commit(drain);
+      const uint64_t t0 = globaltimer();
+      while (!mbar_test(drain, 0))
+        if (globaltimer() - t0 > B2F_WAIT_NS) { record_error(kDevTimeoutDrain); break; }
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax + epilogue
+    const int qd = warp & 3;
+    const int r = qd * 32 + lane;  // row within the tile == TMEM lane
+    const int qi = q0 + r;         // query index within the sequence
+    const uint32_t t_lane = tmem + (uint32_t(qd * 32) << 16);
+    float m_used = -INFINITY;
+    float l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkv; ++j) {
+      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, kDevTimeoutEpilogue, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[BKV];
+#pragma unroll
+      for (int c = 0; c < BKV / 32; ++c) {
+        uint32_t raw[32];
+        tmem_ld32(t_lane + (j & 1) * C::S_COLS + c * 32, raw);
+#pragma unroll
+        for (int u = 0; u < 32; ++u) s[c * 32 + u] = __uint_as_float(raw[u]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[j & 1]);
+      const int k0 = j * BKV;
+      const bool need_mask = (k0 + BKV > p.seq) || (p.causal && k0 + BKV - 1 > q0);
+      float mt = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < BKV; ++c) {
+        float x = s[c] * p.qk_scale_log2;
+        if (need_mask) {
+          const int kidx = k0 + c;
+          if (kidx >= p.seq || (p.causal && kidx > qi)) x = -INFINITY;
+        }
+        s[c] = x;
+        mt = fmaxf(mt, x);
+      }
+      // lazy rescaling: keep the reference max unless the row max grew by more than 8
+      float corr = 1.0f;
+      bool rescale = false;
+      if (mt > m_used + 8.0f) {
+        if (m_used != -INFINITY) {
+          corr = exp2f(m_used - mt);
+          rescale = true;
+        }
+        m_used = mt;
+      }
+      const float mref = (m_used == -INFINITY) ? 0.0f : m_used;
+      float lt = 0.f;
+      uint32_t pk[BKV / 2];
+#pragma unroll
+      for (int c = 0; c < BKV; c += 2) {
+        const float e0 = exp2f(s[c] - mref);
+        const float e1 = exp2f(s[c + 1] - mref);
+        const __nv_bfloat162 bb = __floats2bfloat162_rn(e0, e1);
+        // the row sum uses the bf16-rounded weights, exactly what the P.V MMA sees
+        const float2 rb = __bfloat1622float2(bb);
+        lt += rb.x + rb.y;
+        pk[c / 2] = *reinterpret_cast<const uint32_t*>(&bb);
+      }
+      if (j > 0) {
+        if (!mbar_wait(pv_done, (j - 1) & 1, kDevTimeoutEpilogue, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (rescale) {
+#pragma unroll 1
+          for (int c = 0; c < D; c += 16) {
+            uint32_t o[16];
+            tmem_ld16(t_lane + C::O_COL + c, o);
+#pragma unroll
+            for (int u = 0; u < 16; ++u) o[u] = __float_as_uint(__uint_as_float(o[u]) * corr);
+            tmem_st16(t_lane + C::O_COL + c, o);
+          }
+          tmem_st_wait();
+        }
+      }
+      l = l * corr + lt;
+      // P row -> shared memory, K-major 128B-swizzled bf16 (64 keys per 128-byte row)
+#pragma unroll
+      for (int g = 0; g < BKV / 8; ++g) {
+        const int kb = g >> 3, gi = g & 7;
+        uint8_t* dst = sp + kb * BQ * 128 + r * 128 + ((gi ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4*>(dst) =
+            make_uint4(pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
+      }
+      fence_async_shared();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    // ---------------------------------------------------------------- epilogue
+    if (ok && mbar_wait(pv_done, (nkv - 1) & 1, kDevTimeoutEpilogue, abort_flag)) {
+      tc_fence_after();
+      const long long row = (long long)b * p.seq + qi;
+      const bool valid = qi < p.seq;
+      const float inv_l = (l > 0.f) ? p.v_scale / l : 0.f;
+#pragma unroll 1
+      for (int c = 0; c < D; c += 32) {
+        uint32_t o[32];
+        tmem_ld32(t_lane + C::O_COL + c, o);
+        if (!valid) continue;
+        float v[32];
+#pragma unroll
+        for (int u = 0; u < 32; ++u) v[u] = __uint_as_float(o[u]) * inv_l;
+        if (p.gate != nullptr) {
+          const long long go = row * p.gate_ld + (long long)h * p.gate_hstride + c;
+          if (p.gate_dtype == kE4M3) {
+            const uint8_t* gp = reinterpret_cast<const uint8_t*>(p.gate) + go;
+#pragma unroll
+            for (int u = 0; u < 32; u += 16) {
+              const uint4 q = *reinterpret_cast<const uint4*>(gp + u);
+              const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                const float2 a = e4m3x2_to_f32x2(w[t] & 0xFFFF);
+                const float2 bb = e4m3x2_to_f32x2(w[t] >> 16);
+                const float gv[4] = {a.x, a.y, bb.x, bb.y};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float gg = gv[e] * p.gate_scale;
+                  v[u + 4 * t + e] *= 1.0f / (1.0f + expf(-gg));
+                }
+              }
+            }
+          } else {
+            const __nv_bfloat16* gp = reinterpret_cast<const __nv_bfloat16*>(p.gate) + go;
+#pragma unroll
+            for (int u = 0; u < 32; ++u) {
+              const float gg = __bfloat162float(gp[u]) * p.gate_scale;
+              v[u] *= 1.0f / (1.0f + expf(-gg));
+            }
+          }
+        }
+        uint32_t w[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t)
+          w[t] = uint32_t(f32x2_to_e4m3x2(v[4 * t] * p.ctx_inv_scale,
+                                          v[4 * t + 1] * p.ctx_inv_scale)) |
+                 (uint32_t(f32x2_to_e4m3x2(v[4 * t + 2] * p.ctx_inv_scale,
+                                           v[4 * t + 3] * p.ctx_inv_scale))
+                  << 16);
+        uint8_t* dst = p.ctx + row * p.ctx_ld + (long long)h * D + c;
+        *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(dst + 16) = make_uint4(w[4], w[5], w[6], w[7]);
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+template <int D>
+int launch_attention(const b2f_attn_args* a, cudaStream_t stream) {
+  using C = AttnCfg<D>;
+  CUtensorMap tq, tk, tv;
+  std::string err;
+  const CUtensorMapSwizzle sw8 =
+      (C::ROWB == 128) ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  {
+    const unsigned long long dims[3] = {(unsigned long long)a->hq * D, (unsigned long long)a->seq,
+                                        (unsigned long long)a->batch};
+    const unsigned long long strides[2] = {(unsigned long long)a->q_ld,
+                                           (unsigned long long)a->q_ld * a->seq};
+    const unsigned int box[3] = {(unsigned int)C::ROWB, (unsigned int)C::BQ, 1};
+    if (!encode_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, a->q, dims, strides, box, sw8, &err))
+      return fail(B2F_ERR_ARG, "attention: Q tensor map: " + err);
+  }
+  {
+    const unsigned long long dims[3] = {(unsigned long long)a->hkv * D, (unsigned long long)a->seq,
+                                        (unsigned long long)a->batch};
+    const unsigned long long strides[2] = {(unsigned long long)a->k_ld,
+                                           (unsigned long long)a->k_ld * a->seq};
+    const unsigned int box[3] = {(unsigned int)C::ROWB, (unsigned int)C::BKV, 1};
+    if (!encode_tmap(&tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, a->k, dims, strides, box, sw8, &err))
+      return fail(B2F_ERR_ARG, "attention: K tensor map: " + err);
+  }
+  {
+    const unsigned long long dims[3] = {(unsigned long long)a->hkv * D, (unsigned long long)a->seq,
+                                        (unsigned long long)a->batch};
+    const unsigned long long strides[2] = {(unsigned long long)a->v_ld * 2,
+                                           (unsigned long long)a->v_ld * 2 * a->seq};
+    const unsigned int box[3] = {64, (unsigned int)C::BKV, 1};
+    if (!encode_tmap(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a->v, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_128B, &err))
+      return fail(B2F_ERR_ARG, "attention: V tensor map: " + err);
+  }
+  AttnParams p;
+  p.seq = a->seq; p.batch = a->batch; p.hq = a->hq; p.hkv = a->hkv;
+  p.causal = a->causal;
+  const float sm = a->sm_scale > 0.f ? a->sm_scale : 1.0f / sqrtf((float)D);
+  p.qk_scale_log2 = a->q_scale * a->k_scale * sm * 1.4426950408889634f;
+  p.gate = a->gate; p.gate_dtype = a->gate_dtype; p.gate_ld = a->gate_ld;
+  p.gate_hstride = a->gate_head_stride; p.gate_scale = a->gate_scale;
+  p.ctx = reinterpret_cast<uint8_t*>(a->ctx); p.ctx_ld = a->ctx_ld;
+  p.ctx_inv_scale = 1.0f / a->ctx_scale;
+  p.v_scale = a->v_scale;
+  static thread_local int attr_dev[3] = {-1, -1, -1};
+  const int slot = D == 64 ? 0 : (D == 128 ? 1 : 2);
+  int dev = 0;
+  B2F_CUDA_TRY(cudaGetDevice(&dev));
+  if (attr_dev[slot] != dev) {
+    B2F_CUDA_TRY(cudaFuncSetAttribute(attention_kernel<D>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+    attr_dev[slot] = dev;
+  }
+  dim3 grid((a->seq + C::BQ - 1) / C::BQ, a->hq, a->batch);
+  attention_kernel<D><<<grid, 192, C::SMEM_BYTES, stream>>>(tq, tk, tv, p);
+  B2F_CUDA_TRY(cudaGetLastError());
+  return B2F_OK;
+}
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+}  // namespace b2f
+
+extern "C" {
+
+void b2f_attn_args_init(b2f_attn_args* a) {
+  if (a == nullptr) return;
+  *a = b2f_attn_args{};
+  a->causal = 1;
+  a->q_scale = a->k_scale = a->v_scale = 1.0f;
+  a->gate_dtype = B2F_DTYPE_E4M3;
+  a->gate_scale = 1.0f;
+  a->ctx_scale = 1.0f;
+}
+
+int b2f_attention_fp8(const b2f_attn_args* a, b2f_stream_t stream) {
+  using namespace b2f;
+  if (a == nullptr) return fail(B2F_ERR_ARG, "attention: null args");
+  if (a->batch <= 0 || a->seq <= 0 || a->hq <= 0 || a->hkv <= 0)
+    return fail(B2F_ERR_ARG, "attention: empty shape");
+  if (a->hq % a->hkv != 0) return fail(B2F_ERR_ARG, "attention: hq must be a multiple of hkv");
+  const int d = a->head_dim;
+  if (d != 64 && d != 128 && d != 256)
+    return fail(B2F_ERR_UNSUPPORTED, "attention: head_dim must be 64, 128 or 256");
+  if (a->q == nullptr || a->k == nullptr || a->v == nullptr || a->ctx == nullptr)
+    return fail(B2F_ERR_ARG, "attention: null tensor");
+  if (!al16(a->q) || !al16(a->k) || !al16(a->v) || !al16(a->ctx))
+    return fail(B2F_ERR_ARG, "attention: tensors must be 16-byte aligned");
+  if (a->q_ld % 16 || a->k_ld % 16 || (a->v_ld * 2) % 16 || a->ctx_ld % 16 ||
+      a->q_ld < (long long)a->hq * d || a->k_ld < (long long)a->hkv * d ||
+      a->v_ld < (long long)a->hkv * d || a->ctx_ld < (long long)a->hq * d)
+    return fail(B2F_ERR_ARG,
+                "attention: row pitches must cover the heads and be 16-byte multiples");
+  if (a->gate != nullptr) {
+    const int gs = a->gate_dtype == B2F_DTYPE_BF16 ? 2 : 1;
+    if (a->gate_dtype != B2F_DTYPE_BF16 && a->gate_dtype != B2F_DTYPE_E4M3)
+      return fail(B2F_ERR_ARG, "attention: gate must be e4m3 or bf16");
+    if (!al16(a->gate) || (a->gate_ld * gs) % 16 || (a->gate_head_stride * gs) % 16)
+      return fail(B2F_ERR_ARG, "attention: gate must be 16-byte aligned");
+  }
+  if (!(a->ctx_scale > 0.f)) return fail(B2F_ERR_ARG, "attention: ctx_scale must be > 0");
+  cudaStream_t s = (cudaStream_t)stream;
+  if (d == 64) return launch_attention<64>(a, s);
+  if (d == 128) return launch_attention<128>(a, s);
+  return launch_attention<256>(a, s);
+}
+
+}  // extern "C"

@@ -1,0 +1,165 @@
+// Attention operand preparation (C ABI: b2f_head_norm_rope, b2f_fp8_to_bf16).
+//
+// b2f_head_norm_rope: one warp per (token, head) row of D e4m3 values:
+//   x = stored * in_scale; y = x * rsqrt(mean(x^2) + eps) * (w + w_offset)   (optional)
+//   rotate-half RoPE on the first rotary_dim dims with cos/sin[pos], pos = token % seq
+//   out = e4m3(y / out_scale) into a dense [T, H * D] tensor.
+// Reference: _cute_harness_rms_norm / _cute_harness_apply_rope
+// (tasks/model_qwen35_4b_full_attention_block_fp8/starter.py:167-183, applied at :365-376).
+//
+// b2f_fp8_to_bf16: copies an e4m3 column block to bf16 (the exact image of the e4m3
+// values: bf16 holds every e4m3 value), used for the V operand of the P.V MMA.
+#include <string>
+
+#include "common.cuh"
+#include "host_common.h"
+
+namespace b2f {
+namespace {
+
+struct RopeParams {
+  const uint8_t* in;
+  long long in_ld, in_hstride;
+  float in_scale;
+  const float* weight;  // [D] f32 or null (no norm)
+  float w_offset, eps;
+  const float* cos;     // [seq, rotary] f32 or null (no RoPE)
+  const float* sin;
+  int rotary, seq;
+  uint8_t* out;
+  long long out_ld;
+  float out_inv_scale;
+  int rows, heads;
+};
+
+template <int D>
+__global__ void __launch_bounds__(256) head_norm_rope_kernel(const RopeParams p) {
+  constexpr int E = D / 32;  // elements per lane
+  const int warp_global = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (warp_global >= p.rows * p.heads) return;
+  const int t = warp_global / p.heads;
+  const int h = warp_global - t * p.heads;
+  const uint8_t* src = p.in + (long long)t * p.in_ld + (long long)h * p.in_hstride + lane * E;
+  float x[E];
+#pragma unroll
+  for (int e = 0; e < E; e += 2) {
+    const float2 v = e4m3x2_to_f32x2(*reinterpret_cast<const uint16_t*>(src + e));
+    x[e] = v.x * p.in_scale;
+    x[e + 1] = v.y * p.in_scale;
+  }
+  if (p.weight != nullptr) {
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) ss += x[e] * x[e];
+    ss = warp_sum(ss);
+    const float inv = rsqrtf(ss / float(D) + p.eps);
+#pragma unroll
+    for (int e = 0; e < E; ++e) x[e] = x[e] * inv * (p.weight[lane * E + e] + p.w_offset);
+  }
+  if (p.cos != nullptr) {
+    const int pos = t % p.seq;
+    const int half = p.rotary / 2;
+    const int off = half / E;  // lane distance between rotation partners
+    float y[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      const int i = lane * E + e;
+      const int src_lane = (i < half) ? lane + off : lane - off;
+      const float partner = __shfl_sync(0xffffffffu, x[e], src_lane & 31);
+      if (i < p.rotary) {
+        const float rh = (i < half) ? -partner : partner;
+        y[e] = x[e] * p.cos[(long long)pos * p.rotary + i] +
+               rh * p.sin[(long long)pos * p.rotary + i];
+      } else {
+        y[e] = x[e];
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < E; ++e) x[e] = y[e];
+  }
+  uint8_t* dst = p.out + (long long)t * p.out_ld + (long long)h * D + lane * E;
+#pragma unroll
+  for (int e = 0; e < E; e += 2)
+    *reinterpret_cast<uint16_t*>(dst + e) =
+        f32x2_to_e4m3x2(x[e] * p.out_inv_scale, x[e + 1] * p.out_inv_scale);
+}
+
+__global__ void fp8_to_bf16_kernel(const uint8_t* in, long long in_ld, __nv_bfloat16* out,
+                                   long long out_ld, int rows, int cols, float scale) {
+  const int vec_per_row = cols / 8;
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)rows * vec_per_row) return;
+  const int r = int(i / vec_per_row);
+  const int c = int(i - (long long)r * vec_per_row) * 8;
+  const uint2 q = *reinterpret_cast<const uint2*>(in + (long long)r * in_ld + c);
+  const float2 a = e4m3x2_to_f32x2(q.x & 0xFFFF), b = e4m3x2_to_f32x2(q.x >> 16),
+               cc = e4m3x2_to_f32x2(q.y & 0xFFFF), d = e4m3x2_to_f32x2(q.y >> 16);
+  uint4 o;
+  o.x = pack_bf16x2(a.x * scale, a.y * scale);
+  o.y = pack_bf16x2(b.x * scale, b.y * scale);
+  o.z = pack_bf16x2(cc.x * scale, cc.y * scale);
+  o.w = pack_bf16x2(d.x * scale, d.y * scale);
+  *reinterpret_cast<uint4*>(out + (long long)r * out_ld + c) = o;
+}
+
+}  // namespace
+}  // namespace b2f
+
+extern "C" {
+
+int b2f_head_norm_rope(const b2f_rope_args* a, b2f_stream_t stream) {
+  using namespace b2f;
+  if (a == nullptr) return fail(B2F_ERR_ARG, "head_norm_rope: null args");
+  if (a->rows <= 0 || a->heads <= 0) return fail(B2F_ERR_ARG, "head_norm_rope: empty shape");
+  const int d = a->head_dim;
+  if (d != 64 && d != 128 && d != 256)
+    return fail(B2F_ERR_UNSUPPORTED, "head_norm_rope: head_dim must be 64, 128 or 256");
+  if (a->in == nullptr || a->out == nullptr) return fail(B2F_ERR_ARG, "head_norm_rope: null tensor");
+  if (a->cos != nullptr) {
+    if (a->sin == nullptr || a->seq <= 0)
+      return fail(B2F_ERR_ARG, "head_norm_rope: cos needs sin and seq");
+    const int e = d / 32;
+    if (a->rotary_dim <= 0 || a->rotary_dim > d || a->rotary_dim % (2 * e) != 0)
+      return fail(B2F_ERR_ARG, "head_norm_rope: rotary_dim must be a multiple of 2*head_dim/32");
+  }
+  if (((a->in_ld | a->in_head_stride | a->out_ld) & 1) || ((uintptr_t)a->in & 1) ||
+      ((uintptr_t)a->out & 1))
+    return fail(B2F_ERR_ARG, "head_norm_rope: 2-byte alignment required");
+  if (!(a->out_scale > 0.f)) return fail(B2F_ERR_ARG, "head_norm_rope: out_scale must be > 0");
+  RopeParams p;
+  p.in = reinterpret_cast<const uint8_t*>(a->in);
+  p.in_ld = a->in_ld; p.in_hstride = a->in_head_stride; p.in_scale = a->in_scale;
+  p.weight = a->weight; p.w_offset = a->weight_offset; p.eps = a->eps;
+  p.cos = a->cos; p.sin = a->sin; p.rotary = a->rotary_dim;
+  p.seq = a->seq > 0 ? a->seq : a->rows;
+  p.out = reinterpret_cast<uint8_t*>(a->out); p.out_ld = a->out_ld;
+  p.out_inv_scale = 1.0f / a->out_scale;
+  p.rows = a->rows; p.heads = a->heads;
+  const long long warps = (long long)a->rows * a->heads;
+  const int grid = (int)((warps + 7) / 8);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (d == 64) head_norm_rope_kernel<64><<<grid, 256, 0, s>>>(p);
+  else if (d == 128) head_norm_rope_kernel<128><<<grid, 256, 0, s>>>(p);
+  else head_norm_rope_kernel<256><<<grid, 256, 0, s>>>(p);
+  B2F_CUDA_TRY(cudaGetLastError());
+  return B2F_OK;
+}
+
+int b2f_fp8_to_bf16(const void* in, long long in_ld, void* out, long long out_ld, int rows,
+                    int cols, float scale, b2f_stream_t stream) {
+  using namespace b2f;
+  if (rows <= 0 || cols <= 0) return fail(B2F_ERR_ARG, "fp8_to_bf16: empty shape");
+  if (in == nullptr || out == nullptr) return fail(B2F_ERR_ARG, "fp8_to_bf16: null tensor");
+  if (cols % 8 || in_ld % 8 || out_ld % 8 || ((uintptr_t)in & 7) || ((uintptr_t)out & 15))
+    return fail(B2F_ERR_ARG, "fp8_to_bf16: cols/ld multiples of 8, aligned tensors required");
+  const long long n = (long long)rows * (cols / 8);
+  const int grid = (int)((n + 255) / 256);
+  fp8_to_bf16_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<const uint8_t*>(in), in_ld, reinterpret_cast<__nv_bfloat16*>(out), out_ld,
+      rows, cols, scale);
+  B2F_CUDA_TRY(cudaGetLastError());
+  return B2F_OK;
+}
+
+}  // extern "C"

@@ -174,6 +174,82 @@ typedef struct b2f_norm_args {
 void b2f_norm_args_init(b2f_norm_args* args);
 int b2f_norm_quant(const b2f_norm_args* args, b2f_stream_t stream);
 
+/* ------------------------------------------------------------------ attention
+ * ctx[t, h*D:(h+1)*D] = e4m3( softmax(q_h k_g^T * sm_scale [causal]) v_g * sigmoid(gate) / ctx_scale )
+ *   tokens t = b * seq + s (attention stays inside each sequence); g = h / (hq / hkv) (GQA)
+ *   q: e4m3 [T, q_ld], head h at column h*D, value = stored * q_scale
+ *   k: e4m3 [T, k_ld], head g at column g*D, value = stored * k_scale
+ *   v: bf16 [T, v_ld], head g at column g*D, value = stored * v_scale
+ *   gate (optional): e4m3 or bf16 [T, gate_ld], head h at column h*gate_head_stride,
+ *         value = stored * gate_scale
+ *   sm_scale <= 0 selects 1/sqrt(D).
+ * Replaces: the attention step of gpt2_transformer_block (reference math
+ *   tasks/model_gpt2_small_transformer_block_fp8/starter.py:428-453), attention_kernel of
+ *   qwen35_full_attention_block (tasks/model_qwen35_4b_full_attention_block_fp8/starter.py:
+ *   40-49, reference math :354-392) and the vision block's non-causal attention
+ *   (tasks/model_qwen35_4b_vision_block_fp8/starter.py:327-345).
+ * Requirements: head_dim 64, 128 or 256; 16-byte aligned rows.
+ */
+typedef struct b2f_attn_args {
+  int batch, seq, hq, hkv, head_dim;
+  int causal;
+  const void* q;
+  long long q_ld;
+  float q_scale;
+  const void* k;
+  long long k_ld;
+  float k_scale;
+  const void* v;
+  long long v_ld;
+  float v_scale;
+  float sm_scale;
+  const void* gate;
+  int gate_dtype;
+  long long gate_ld;
+  long long gate_head_stride;
+  float gate_scale;
+  void* ctx;
+  long long ctx_ld;
+  float ctx_scale;
+} b2f_attn_args;
+
+void b2f_attn_args_init(b2f_attn_args* args);
+int b2f_attention_fp8(const b2f_attn_args* args, b2f_stream_t stream);
+
+/* ------------------------------------------------------------------ attention operand prep
+ * Per (token, head): x = in * in_scale; optional RMSNorm x * rsqrt(mean(x^2)+eps) *
+ * (weight + weight_offset); optional rotate-half RoPE on the first rotary_dim dims with
+ * cos/sin [seq, rotary_dim] at position token % seq; out = e4m3(y / out_scale) into
+ * [rows, out_ld] with head h at column h*D.
+ * Replaces: q_headnorm / k_headnorm (kernel_evo_archive/best_kernels/qwen-no-prof/
+ *   submission.py:368-449; reference math tasks/model_qwen35_4b_full_attention_block_fp8/
+ *   starter.py:167-183 and :365-376).
+ */
+typedef struct b2f_rope_args {
+  int rows, heads, head_dim;
+  const void* in;
+  long long in_ld;
+  long long in_head_stride;
+  float in_scale;
+  const float* weight;
+  float weight_offset;
+  float eps;
+  const float* cos;
+  const float* sin;
+  int rotary_dim;
+  int seq;
+  void* out;
+  long long out_ld;
+  float out_scale;
+} b2f_rope_args;
+
+int b2f_head_norm_rope(const b2f_rope_args* args, b2f_stream_t stream);
+
+/* out (bf16) = in (e4m3 bytes) * scale, [rows, cols] with row pitches in elements.
+ * Produces the bf16 V operand of b2f_attention_fp8 (exact: bf16 holds every e4m3 value). */
+int b2f_fp8_to_bf16(const void* in, long long in_ld, void* out, long long out_ld, int rows,
+                    int cols, float scale, b2f_stream_t stream);
+
 /* ------------------------------------------------------------------ op registry */
 typedef struct b2f_op {
   const char* name;      /* e.g. "gemm_fp8" */

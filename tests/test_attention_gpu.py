@@ -1,0 +1,121 @@
+"""Parity of the fused tcgen05 attention (b2f_attention_fp8) and its operand prep
+(b2f_head_norm_rope, b2f_fp8_to_bf16) with the CPU oracle.
+
+Bar for the e4m3 context, in value space against the oracle's unquantised f32 context:
+  |ctx - ref| <= half an e4m3 step at |ref|  (the requantisation itself)
+               + 2^-7 * max|v|               (P is rounded to bf16 before the P.V MMA,
+                                              the reference keeps f32; f32 sum order)
+and at least 95% of the stored e4m3 codes equal the oracle's requantised codes.
+An e4m3 "ulp" count is not used: near-zero contexts change sign under tiny absolute
+errors, which spans many codes without being a meaningful error.
+"""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from helpers import e4m3_ulp_diff, gen
+from oracle import attention as oatt
+
+pytestmark = pytest.mark.gpu
+
+
+def _ops():
+    from b200fp8 import ops
+    return ops
+
+
+def e4m3_half_step(x: torch.Tensor) -> torch.Tensor:
+    """Half the spacing of e4m3 values around |x| (x in stored units)."""
+    a = x.abs().clamp_min(2.0 ** -6)
+    return torch.exp2(torch.floor(torch.log2(a)) - 3.0) * 0.5
+
+
+def assert_ctx_close(ctx_q, ref_f32, scale, vmax):
+    got = ctx_q.cpu().float()
+    ref_units = ref_f32 / scale
+    bound = e4m3_half_step(ref_units) + 2.0 ** -7 * vmax / scale
+    err = (got - ref_units).abs()
+    bad = err > bound
+    assert not bad.any(), f"{int(bad.sum())} elements out of bound, max err {float(err.max())}"
+    same = (ctx_q.cpu().view(torch.uint8) == ref_units.to(torch.float8_e4m3fn).view(torch.uint8))
+    assert float(same.float().mean()) >= 0.95, float(same.float().mean())
+
+
+def _qkv(t, hq, hkv, d, g, scale=1 / 64.0):
+    q = (torch.randn((t, hq * d), generator=g) * 1.5 / scale).to(torch.float8_e4m3fn)
+    k = (torch.randn((t, hkv * d), generator=g) * 1.5 / scale).to(torch.float8_e4m3fn)
+    v = (torch.randn((t, hkv * d), generator=g) / scale).to(torch.float8_e4m3fn)
+    return q, k, v
+
+
+@pytest.mark.parametrize("batch,seq,hq,hkv,d,causal", [
+    (1, 128, 1, 1, 64, True), (2, 256, 2, 2, 64, True), (1, 128, 12, 12, 64, True),
+    (1, 384, 4, 2, 128, True), (2, 128, 16, 4, 256, True), (1, 128, 16, 16, 64, False),
+    (1, 200, 2, 1, 128, True), (1, 256, 4, 1, 128, False), (1, 1024, 2, 2, 64, True),
+    (1, 512, 2, 1, 256, True),
+])
+def test_attention_matches_oracle(batch, seq, hq, hkv, d, causal):
+    g = gen(1000 + seq + hq + d)
+    s = 1 / 64.0
+    t = batch * seq
+    q, k, v = _qkv(t, hq, hkv, d, g, s)
+    vf = v.float().view(t, hkv, d) * s
+    ref = oatt.attention(q.float().view(t, hq, d) * s, k.float().view(t, hkv, d) * s, vf,
+                         batch=batch, causal=causal).reshape(t, hq * d)
+    ops = _ops()
+    ctx = ops.attention_fp8(q.cuda(), k.cuda(), ops.fp8_to_bf16(v.cuda()), batch=batch,
+                            heads=hq, kv_heads=hkv, head_dim=d, causal=causal, q_scale=s,
+                            k_scale=s, v_scale=s, ctx_scale=s)
+    torch.cuda.synchronize()
+    assert_ctx_close(ctx, ref, s, float(vf.abs().max()))
+
+
+def test_attention_gated_interleaved_qwen_reference_layout():
+    # tasks/model_qwen35_4b_full_attention_block_fp8: q_gate [T, 16, 2, 256]; gate = half 1,
+    # scores / 16 (sqrt(256)), causal, GQA 16/4, ctx * sigmoid(gate)
+    t, hq, hkv, d = 128, 16, 4, 256
+    g = gen(20260801)
+    s = 1 / 64.0
+    qg = (torch.randn((t, hq * 2 * d), generator=g) / s).to(torch.float8_e4m3fn)
+    k = (torch.randn((t, hkv * d), generator=g) / s).to(torch.float8_e4m3fn)
+    v = (torch.randn((t, hkv * d), generator=g) / s).to(torch.float8_e4m3fn)
+    qh = qg.float().view(t, hq, 2, d) * s
+    vf = v.float().view(t, hkv, d) * s
+    ref = oatt.attention(qh[:, :, 0], k.float().view(t, hkv, d) * s, vf, batch=1, causal=True,
+                         gate=qh[:, :, 1], sm_scale=1 / 16.0).reshape(t, hq * d)
+    ops = _ops()
+    qgc = qg.cuda()
+    q_dense = qgc.view(t, hq, 2, d)[:, :, 0].contiguous().view(t, hq * d)
+    ctx = ops.attention_fp8(q_dense, k.cuda(), ops.fp8_to_bf16(v.cuda()), batch=1, heads=hq,
+                            kv_heads=hkv, head_dim=d, q_scale=s, k_scale=s, v_scale=s,
+                            gate=qgc[:, d:], gate_scale=s, gate_head_stride=2 * d, ctx_scale=s)
+    torch.cuda.synchronize()
+    assert_ctx_close(ctx, ref, s, float(vf.abs().max()))
+
+
+@pytest.mark.parametrize("d,rot", [(256, 64), (128, 128), (64, 64)])
+def test_head_norm_rope(d, rot):
+    t, h, seq = 256, 4, 128
+    g = gen(7 + d)
+    s = 1 / 64.0
+    x = (torch.randn((t, h * d), generator=g) / s).to(torch.float8_e4m3fn)
+    w = torch.randn((d,), generator=g) * 0.02
+    cos, sin = oatt.rope_tables(seq, rot, 1e6, batch=t // seq)
+    ref = oatt.head_rmsnorm_rope(x.float().view(t, h, d) * s, w, cos, sin, rot)
+    ref_q = (ref.reshape(t, h * d) / s).to(torch.float8_e4m3fn)
+    out = _ops().head_norm_rope(x.cuda(), heads=h, head_dim=d, in_scale=s, out_scale=s,
+                                weight=w.cuda(), cos=cos[:seq].contiguous().cuda(),
+                                sin=sin[:seq].contiguous().cuda(), rotary_dim=rot, seq=seq)
+    torch.cuda.synchronize()
+    diff = e4m3_ulp_diff(out.cpu(), ref_q)
+    assert int(diff.max()) <= 1
+    assert float((diff > 0).float().mean()) < 0.01
+
+
+def test_fp8_to_bf16_exact():
+    g = gen(3)
+    x = (torch.randn((64, 256), generator=g) * 50).to(torch.float8_e4m3fn)
+    out = _ops().fp8_to_bf16(x.cuda(), scale=1 / 64.0)
+    torch.cuda.synchronize()
+    assert torch.equal(out.cpu(), (x.float() / 64.0).to(torch.bfloat16))
