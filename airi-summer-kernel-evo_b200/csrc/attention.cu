@@ -237,10 +237,10 @@ __global__ void __launch_bounds__(192, 1)
     float l = 0.f;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
-      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, kDevTimeoutEpilogue, abort_flag)) {
-        ok = false;
-        break;
-      }
+      // tcgen05.ld/st are warp-collective: every lane must take the same path.
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[j & 1], (j >> 1) & 1, kDevTimeoutEpilogue,
+                                             abort_flag));
+      if (!ok) break;
       tc_fence_after();
       float s[BKV];
 #pragma unroll
@@ -290,12 +290,13 @@ __global__ void __launch_bounds__(192, 1)
         pk[c / 2] = *reinterpret_cast<const uint32_t*>(&bb);
       }
       if (j > 0) {
-        if (!mbar_wait(pv_done, (j - 1) & 1, kDevTimeoutEpilogue, abort_flag)) {
-          ok = false;
-          break;
-        }
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait(pv_done, (j - 1) & 1, kDevTimeoutEpilogue, abort_flag));
+        if (!ok) break;
         tc_fence_after();
-        if (rescale) {
+        // The rescale decision is per row; the TMEM round trip runs for the whole warp
+        // (lanes that need no rescale multiply by corr == 1).
+        if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
           for (int c = 0; c < D; c += 16) {
             uint32_t o[16];
@@ -322,7 +323,9 @@ __global__ void __launch_bounds__(192, 1)
       if (lane == 0) mbar_arrive(p_full);
     }
     // ---------------------------------------------------------------- epilogue
-    if (ok && mbar_wait(pv_done, (nkv - 1) & 1, kDevTimeoutEpilogue, abort_flag)) {
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (nkv - 1) & 1, kDevTimeoutEpilogue,
+                                                  abort_flag));
+    if (ok) {
       tc_fence_after();
       const long long row = (long long)b * p.seq + qi;
       const bool valid = qi < p.seq;

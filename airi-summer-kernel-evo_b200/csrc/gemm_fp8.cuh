@@ -464,7 +464,10 @@ __global__ void __launch_bounds__(192, 1)
       tile_coords(t, num_m, num_n, mb, nb);
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
-      if (!mbar_wait(&tfull_bar[acc], acc_phase, kDevTimeoutEpilogue, abort_flag)) break;
+      // tcgen05.ld is warp-collective: the whole warp leaves together or not at all.
+      if (!__all_sync(0xffffffffu,
+                      mbar_wait(&tfull_bar[acc], acc_phase, kDevTimeoutEpilogue, abort_flag)))
+        break;
       if (warp == 2 && lane == 0) B2F_STAMP(it, 3);
       tc_fence_after();
       const int row0 = mb * Cfg::BM + q * 32;
@@ -662,7 +665,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       tile_coords(t, num_m, num_n, mb, nb);
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
-      if (!mbar_wait(&tfull_bar[acc], acc_phase, kDevTimeoutEpilogue, abort_flag)) break;
+      // tcgen05.ld is warp-collective: the whole warp leaves together or not at all.
+      if (!__all_sync(0xffffffffu,
+                      mbar_wait(&tfull_bar[acc], acc_phase, kDevTimeoutEpilogue, abort_flag)))
+        break;
       tc_fence_after();
       const int row0 = mb * 2 * Cfg::BM + rank * Cfg::BM + q * 32;
       const int row = row0 + lane;
