@@ -53,6 +53,7 @@ class GemmArgs(ctypes.Structure):
         ("a", ctypes.c_void_p), ("lda", ctypes.c_longlong),
         ("b", ctypes.c_void_p), ("ldb", ctypes.c_longlong),
         ("alpha", ctypes.c_float), ("alpha_ptr", ctypes.c_void_p),
+        ("col_scale", ctypes.c_void_p),
         ("bias", ctypes.c_void_p),
         ("pre_mul", ctypes.c_float), ("pre_add", ctypes.c_float),
         ("act", ctypes.c_int), ("act_param", ctypes.c_float),
@@ -133,7 +134,7 @@ EXPORTED_SYMBOLS = (
     "b2f_version", "b2f_last_error", "b2f_num_sms", "b2f_status_read",
     "b2f_debug_bounded_wait", "b2f_gemm_args_init", "b2f_gemm_fp8", "b2f_gemm_pair_capacity",
     "b2f_norm_args_init", "b2f_norm_quant", "b2f_attn_args_init", "b2f_attention_fp8",
-    "b2f_head_norm_rope", "b2f_fp8_to_bf16",
+    "b2f_head_norm_rope", "b2f_fp8_to_bf16", "b2f_swiglu_fp8",
     "b2f_registry_lookup", "b2f_registry_size", "b2f_registry_at",
 )
 
@@ -167,6 +168,10 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.b2f_fp8_to_bf16.argtypes = [vp, ctypes.c_longlong, vp, ctypes.c_longlong, ctypes.c_int,
                                     ctypes.c_int, ctypes.c_float, vp]
     lib.b2f_fp8_to_bf16.restype = ctypes.c_int
+    lib.b2f_swiglu_fp8.argtypes = [vp, ctypes.c_longlong, vp, ctypes.c_longlong, vp,
+                                   ctypes.c_longlong, ctypes.c_int, ctypes.c_int, ctypes.c_float,
+                                   ctypes.c_float, vp]
+    lib.b2f_swiglu_fp8.restype = ctypes.c_int
     lib.b2f_registry_lookup.argtypes = [ctypes.c_char_p]
     lib.b2f_registry_lookup.restype = ctypes.POINTER(Op)
     lib.b2f_registry_size.restype = ctypes.c_int

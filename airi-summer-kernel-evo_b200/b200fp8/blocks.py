@@ -1,0 +1,225 @@
+"""GPT-2-style and Qwen-style FP8 decoder blocks composed from the b200fp8 kernels.
+
+Every stage is one of this library's sm_100a kernels; the block keeps its intermediate
+tensors in preallocated device buffers so that a whole forward can be captured once into
+a CUDA graph (``capture``) and replayed without per-launch host cost (``replay``).
+
+GPT-2 block (tasks/model_gpt2_small_transformer_block_fp8/starter.py:114-140, reference
+math :393-488), 8 launches:
+  norm_quant(LN1) -> gemm(QKV + bias, e4m3) -> fp8_to_bf16(V) -> attention(causal)
+  -> gemm(out-proj + bias + residual x) -> norm_quant(LN2) -> gemm(FC + bias, GELU-tanh,
+  e4m3) -> gemm(proj + bias + residual r1)
+Qwen full-attention block (tasks/model_qwen35_4b_full_attention_block_fp8/starter.py:66-98,
+reference math :333-416):
+  norm_quant(RMSNorm 1+w) -> one fused gemm over [Wq | Wgate | Wk | Wv] with per-column
+  scales -> head_norm_rope(q), head_norm_rope(k) -> fp8_to_bf16(V) -> attention(causal,
+  GQA, sigmoid gate) -> gemm(o-proj + residual) [-> norm_quant -> gemm([Wgate|Wup])
+  -> swiglu -> gemm(down + residual)]
+Weights are passed as any object with the fields of the reference-style containers
+(e4m3 weight tensors, float per-tensor scales, f32 vectors); they are copied to the
+device once.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import ops
+
+_E4M3 = torch.float8_e4m3fn
+
+
+def _dev(t: Optional[torch.Tensor], device, dtype=None) -> Optional[torch.Tensor]:
+    if t is None:
+        return None
+    t = t.to(device=device)
+    if dtype is not None:
+        t = t.to(dtype)
+    return t.contiguous()
+
+
+class _Graphable:
+    """Capture/replay helper shared by the blocks."""
+
+    def _init_graph(self):
+        self._graph = None
+        self._g_in = None
+        self._g_out = None
+
+    def capture(self, hidden: torch.Tensor, hidden_scale: float = 1.0) -> torch.Tensor:
+        """Capture one forward on a side stream; later ``replay`` reruns it on the data
+        currently in ``self.graph_input``.  Returns the graph's output buffer."""
+        self._g_in = hidden.clone()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            self.forward(self._g_in, hidden_scale)  # warm caches outside the capture
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                self._g_out = self.forward(self._g_in, hidden_scale)
+        torch.cuda.current_stream().wait_stream(s)
+        self._graph = g
+        return self._g_out
+
+    @property
+    def graph_input(self) -> torch.Tensor:
+        return self._g_in
+
+    def replay(self) -> torch.Tensor:
+        self._graph.replay()
+        return self._g_out
+
+
+class GPT2Block(_Graphable):
+    launches_per_forward = 8
+
+    def __init__(self, w, *, batch: int, seq: int, residual_dtype=torch.float32,
+                 out_dtype=torch.float32, device="cuda"):
+        self.batch, self.seq = batch, seq
+        self.t = batch * seq
+        self.heads = w.heads
+        self.d = w.qkv_w.shape[1]
+        self.hd = self.d // self.heads
+        self.mlp = w.fc_w.shape[0]
+        self.eps = w.eps
+        self.ns, self.qs, self.cs, self.ms = w.norm_scale, w.qkv_scale, w.ctx_scale, w.mlp_scale
+        self.qkv_w, self.out_w = _dev(w.qkv_w, device), _dev(w.out_w, device)
+        self.fc_w, self.proj_w = _dev(w.fc_w, device), _dev(w.proj_w, device)
+        self.qkv_s, self.out_s, self.fc_s, self.proj_s = w.qkv_s, w.out_s, w.fc_s, w.proj_s
+        f32 = torch.float32
+        self.qkv_b, self.out_b = _dev(w.qkv_b, device, f32), _dev(w.out_b, device, f32)
+        self.fc_b, self.proj_b = _dev(w.fc_b, device, f32), _dev(w.proj_b, device, f32)
+        self.ln1_w, self.ln1_b = _dev(w.ln1_w, device, f32), _dev(w.ln1_b, device, f32)
+        self.ln2_w, self.ln2_b = _dev(w.ln2_w, device, f32), _dev(w.ln2_b, device, f32)
+        t, d = self.t, self.d
+        self.n1 = torch.empty((t, d), device=device, dtype=_E4M3)
+        self.qkv = torch.empty((t, 3 * d), device=device, dtype=_E4M3)
+        self.v16 = torch.empty((t, d), device=device, dtype=torch.bfloat16)
+        self.ctx = torch.empty((t, d), device=device, dtype=_E4M3)
+        self.r1 = torch.empty((t, d), device=device, dtype=residual_dtype)
+        self.n2 = torch.empty((t, d), device=device, dtype=_E4M3)
+        self.h = torch.empty((t, self.mlp), device=device, dtype=_E4M3)
+        self.out = torch.empty((t, d), device=device, dtype=out_dtype)
+        self._init_graph()
+
+    def flops(self) -> float:
+        t, d, m, s = self.t, self.d, self.mlp, self.seq
+        gemm = 2 * t * (3 * d * d + d * d + 2 * d * m)
+        attn = 2 * self.batch * self.heads * s * s * self.hd  # causal half of 4*S^2*D
+        return float(gemm + attn)
+
+    def forward(self, hidden: torch.Tensor, hidden_scale: float = 1.0) -> torch.Tensor:
+        d = self.d
+        ops.norm_quant(hidden, self.ln1_w, kind="layer", bias=self.ln1_b, eps=self.eps,
+                       x_scale=hidden_scale, q_out=self.n1, q_scale=self.ns)
+        ops.gemm_fp8(self.n1, self.qkv_w, scale_a=self.ns, scale_b=self.qkv_s, bias=self.qkv_b,
+                     out=self.qkv, out_scale=self.qs)
+        ops.fp8_to_bf16(self.qkv[:, 2 * d:], out=self.v16)
+        ops.attention_fp8(self.qkv[:, :d], self.qkv[:, d:2 * d], self.v16, batch=self.batch,
+                          heads=self.heads, kv_heads=self.heads, head_dim=self.hd, causal=True,
+                          q_scale=self.qs, k_scale=self.qs, v_scale=self.qs, ctx=self.ctx,
+                          ctx_scale=self.cs)
+        ops.gemm_fp8(self.ctx, self.out_w, scale_a=self.cs, scale_b=self.out_s, bias=self.out_b,
+                     residual=hidden, residual_scale=hidden_scale, out=self.r1)
+        ops.norm_quant(self.r1, self.ln2_w, kind="layer", bias=self.ln2_b, eps=self.eps,
+                       q_out=self.n2, q_scale=self.ns)
+        ops.gemm_fp8(self.n2, self.fc_w, scale_a=self.ns, scale_b=self.fc_s, bias=self.fc_b,
+                     act="gelu_tanh", out=self.h, out_scale=self.ms)
+        ops.gemm_fp8(self.h, self.proj_w, scale_a=self.ms, scale_b=self.proj_s, bias=self.proj_b,
+                     residual=self.r1, out=self.out)
+        return self.out
+
+
+class QwenBlock(_Graphable):
+    def __init__(self, w, *, batch: int, seq: int, residual_dtype=torch.float32,
+                 out_dtype=torch.float32, device="cuda"):
+        self.batch, self.seq = batch, seq
+        self.t = t = batch * seq
+        self.h, self.hk, self.dh = w.heads, w.kv_heads, w.head_dim
+        self.hidden = w.q_w.shape[1]
+        self.rot = w.rotary_dim
+        self.eps = w.eps
+        self.interleaved = w.interleaved
+        self.ns, self.qs, self.cs = w.norm_scale, w.qkv_scale, w.ctx_scale
+        self.mps, self.mas = w.mlp_proj_scale, w.mlp_act_scale
+        h, hk, dh = self.h, self.hk, self.dh
+        parts = [w.q_w] + ([] if w.interleaved else [w.gate_w]) + [w.k_w, w.v_w]
+        scales = [w.q_s] + ([] if w.interleaved else [w.gate_s]) + [w.k_s, w.v_s]
+        self.w_cat = torch.cat([p.to(device) for p in parts], dim=0).contiguous()
+        self.cs_cat = torch.cat([torch.full((p.shape[0],), s * self.ns, dtype=torch.float32)
+                                 for p, s in zip(parts, scales)]).to(device)
+        qg = 2 * h * dh if w.interleaved else h * dh
+        self.q_off, self.q_hstride = 0, (2 * dh if w.interleaved else dh)
+        self.g_off = dh if w.interleaved else h * dh
+        self.k_off = qg if w.interleaved else 2 * h * dh
+        self.v_off = self.k_off + hk * dh
+        self.n_cat = self.w_cat.shape[0]
+        self.o_w, self.o_s = _dev(w.o_w, device), w.o_s
+        f32 = torch.float32
+        self.in_norm = _dev(w.in_norm_w, device, f32)
+        self.q_norm, self.k_norm = _dev(w.q_norm_w, device, f32), _dev(w.k_norm_w, device, f32)
+        self.cos = _dev(w.cos[:seq], device, f32)
+        self.sin = _dev(w.sin[:seq], device, f32)
+        self.has_mlp = w.mlp_down_w is not None
+        self.n1 = torch.empty((t, self.hidden), device=device, dtype=_E4M3)
+        self.proj = torch.empty((t, self.n_cat), device=device, dtype=_E4M3)
+        self.q = torch.empty((t, h * dh), device=device, dtype=_E4M3)
+        self.k = torch.empty((t, hk * dh), device=device, dtype=_E4M3)
+        self.v16 = torch.empty((t, hk * dh), device=device, dtype=torch.bfloat16)
+        self.ctx = torch.empty((t, h * dh), device=device, dtype=_E4M3)
+        if self.has_mlp:
+            self.r1 = torch.empty((t, self.hidden), device=device, dtype=residual_dtype)
+            self.post_norm = _dev(w.post_norm_w, device, f32)
+            self.inter = w.mlp_gate_w.shape[0]
+            self.gu_w = torch.cat([w.mlp_gate_w.to(device), w.mlp_up_w.to(device)], 0).contiguous()
+            self.gu_cs = torch.cat([
+                torch.full((self.inter,), w.mlp_gate_s * self.ns, dtype=f32),
+                torch.full((self.inter,), w.mlp_up_s * self.ns, dtype=f32)]).to(device)
+            self.down_w, self.down_s = _dev(w.mlp_down_w, device), w.mlp_down_s
+            self.n2 = torch.empty((t, self.hidden), device=device, dtype=_E4M3)
+            self.gu = torch.empty((t, 2 * self.inter), device=device, dtype=_E4M3)
+            self.act = torch.empty((t, self.inter), device=device, dtype=_E4M3)
+        self.out = torch.empty((t, self.hidden), device=device, dtype=out_dtype)
+        self._init_graph()
+
+    def flops(self) -> float:
+        t, hd = self.t, self.hidden
+        gemm = 2 * t * hd * self.n_cat + 2 * t * self.h * self.dh * hd
+        if self.has_mlp:
+            gemm += 2 * t * hd * 2 * self.inter + 2 * t * self.inter * hd
+        attn = 2 * self.batch * self.h * self.seq * self.seq * self.dh
+        return float(gemm + attn)
+
+    def forward(self, hidden: torch.Tensor, hidden_scale: float = 1.0) -> torch.Tensor:
+        h, hk, dh = self.h, self.hk, self.dh
+        ops.norm_quant(hidden, self.in_norm, kind="rms", weight_offset=1.0, eps=self.eps,
+                       x_scale=hidden_scale, q_out=self.n1, q_scale=self.ns)
+        ops.gemm_fp8(self.n1, self.w_cat, col_scale=self.cs_cat, out=self.proj,
+                     out_scale=self.qs)
+        ops.head_norm_rope(self.proj[:, self.q_off:], heads=h, head_dim=dh, in_scale=self.qs,
+                           out_scale=self.qs, head_stride=self.q_hstride, weight=self.q_norm,
+                           weight_offset=1.0, eps=self.eps, cos=self.cos, sin=self.sin,
+                           rotary_dim=self.rot, seq=self.seq, out=self.q)
+        ops.head_norm_rope(self.proj[:, self.k_off:], heads=hk, head_dim=dh, in_scale=self.qs,
+                           out_scale=self.qs, weight=self.k_norm, weight_offset=1.0,
+                           eps=self.eps, cos=self.cos, sin=self.sin, rotary_dim=self.rot,
+                           seq=self.seq, out=self.k)
+        ops.fp8_to_bf16(self.proj[:, self.v_off:self.v_off + hk * dh], out=self.v16)
+        ops.attention_fp8(self.q, self.k, self.v16, batch=self.batch, heads=h, kv_heads=hk,
+                          head_dim=dh, causal=True, q_scale=self.qs, k_scale=self.qs,
+                          v_scale=self.qs, gate=self.proj[:, self.g_off:], gate_scale=self.qs,
+                          gate_head_stride=self.q_hstride, ctx=self.ctx, ctx_scale=self.cs)
+        r1 = self.r1 if self.has_mlp else self.out
+        ops.gemm_fp8(self.ctx, self.o_w, scale_a=self.cs, scale_b=self.o_s, residual=hidden,
+                     residual_scale=hidden_scale, out=r1)
+        if not self.has_mlp:
+            return self.out
+        ops.norm_quant(r1, self.post_norm, kind="rms", weight_offset=1.0, eps=self.eps,
+                       q_out=self.n2, q_scale=self.ns)
+        ops.gemm_fp8(self.n2, self.gu_w, col_scale=self.gu_cs, out=self.gu, out_scale=self.mps)
+        ops.swiglu_fp8(self.gu[:, :self.inter], self.gu[:, self.inter:], in_scale=self.mps,
+                       out_scale=self.mas, out=self.act)
+        ops.gemm_fp8(self.act, self.down_w, scale_a=self.mas, scale_b=self.down_s, residual=r1,
+                     out=self.out)
+        return self.out

@@ -51,6 +51,7 @@ def _fp8_rows(t: torch.Tensor, name: str) -> None:
 
 def gemm_fp8(a: torch.Tensor, b_nk: torch.Tensor, *, scale_a: float = 1.0,
              scale_b: float = 1.0, alpha_tensor: Optional[torch.Tensor] = None,
+             col_scale: Optional[torch.Tensor] = None,
              bias: Optional[torch.Tensor] = None, pre_mul: float = 1.0,
              pre_add: float = 0.0, act: Optional[str] = None, act_param: float = 0.0,
              post_mul: float = 1.0, residual: Optional[torch.Tensor] = None,
@@ -63,7 +64,7 @@ def gemm_fp8(a: torch.Tensor, b_nk: torch.Tensor, *, scale_a: float = 1.0,
     ``out_scale`` is the quantisation scale of an e4m3 output (stored = v / out_scale).
     With ``rowsum=True`` the output is f32 [M] holding sum over columns of v / out_scale.
     """
-    _check_cuda(a, b_nk, bias, residual, out, amax, alpha_tensor)
+    _check_cuda(a, b_nk, bias, residual, out, amax, alpha_tensor, col_scale)
     _fp8_rows(a, "a")
     _fp8_rows(b_nk, "b_nk")
     m, k = a.shape
@@ -83,6 +84,10 @@ def gemm_fp8(a: torch.Tensor, b_nk: torch.Tensor, *, scale_a: float = 1.0,
     args.b, args.ldb = b_nk.data_ptr(), b_nk.stride(0)
     args.alpha = float(scale_a) * float(scale_b)
     args.alpha_ptr = _ptr(alpha_tensor)
+    if col_scale is not None:
+        if col_scale.dtype != torch.float32 or not col_scale.is_contiguous() or col_scale.numel() != n:
+            raise TypeError("col_scale must be contiguous float32 [n]")
+    args.col_scale = _ptr(col_scale)
     if bias is not None:
         if bias.dtype != torch.float32 or not bias.is_contiguous():
             raise TypeError("bias must be contiguous float32")
@@ -238,4 +243,19 @@ def fp8_to_bf16(x: torch.Tensor, scale: float = 1.0,
         out = torch.empty((rows, cols), device=x.device, dtype=torch.bfloat16)
     check(_lib.lib().b2f_fp8_to_bf16(x.data_ptr(), x.stride(0), out.data_ptr(), out.stride(0),
                                      rows, cols, scale, _stream()))
+    return out
+
+
+def swiglu_fp8(gate: torch.Tensor, up: torch.Tensor, *, in_scale: float, out_scale: float,
+               out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """e4m3(silu(gate * s_in) * (up * s_in) / s_out) for e4m3 [rows, cols] views."""
+    _check_cuda(gate, up, out)
+    _fp8_rows(gate, "gate")
+    _fp8_rows(up, "up")
+    rows, cols = gate.shape
+    if out is None:
+        out = torch.empty((rows, cols), device=gate.device, dtype=torch.float8_e4m3fn)
+    check(_lib.lib().b2f_swiglu_fp8(gate.data_ptr(), gate.stride(0), up.data_ptr(), up.stride(0),
+                                    out.data_ptr(), out.stride(0), rows, cols, in_scale,
+                                    out_scale, _stream()))
     return out

@@ -31,6 +31,7 @@ EpilogueParams make_epilogue(const b2f_gemm_args* a) {
   EpilogueParams ep;
   ep.alpha = a->alpha;
   ep.alpha_ptr = a->alpha_ptr;
+  ep.col_scale = a->col_scale;
   ep.bias = a->bias;
   ep.pre_mul = a->pre_mul;
   ep.pre_add = a->pre_add;
@@ -204,6 +205,8 @@ int b2f_gemm_fp8(const b2f_gemm_args* a, b2f_stream_t stream) {
   if (((uintptr_t)a->out) % esz != 0) return fail(B2F_ERR_ARG, "gemm_fp8: misaligned out");
   if (a->residual != nullptr && a->residual_ld < a->n)
     return fail(B2F_ERR_ARG, "gemm_fp8: residual_ld < n");
+  if (a->col_scale != nullptr && ((uintptr_t)a->col_scale) % 16 != 0)
+    return fail(B2F_ERR_ARG, "gemm_fp8: col_scale must be 16-byte aligned");
   if (a->bias != nullptr && ((uintptr_t)a->bias) % 16 != 0)
     return fail(B2F_ERR_ARG, "gemm_fp8: bias must be 16-byte aligned");
   cudaStream_t s = (cudaStream_t)stream;

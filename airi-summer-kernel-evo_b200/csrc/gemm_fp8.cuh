@@ -39,6 +39,7 @@ enum : int { kModeStore = 0, kModeRowSum = 1 };
 struct EpilogueParams {
   float alpha;             // scale_a * scale_b
   const float* alpha_ptr;  // optional device scalar multiplied into alpha (may be null)
+  const float* col_scale;  // optional [N] f32 per-column scale (may be null)
   const float* bias;       // [N] f32, may be null
   float pre_mul, pre_add;  // v = (alpha*acc + bias)*pre_mul + pre_add
   int act;                 // activation applied after the affine step
@@ -123,6 +124,20 @@ __device__ __forceinline__ void epi_values(const EpilogueParams& ep, float alpha
   const bool row_ok = row < M;
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(acc[j]) * alpha;
+  if (ep.col_scale != nullptr) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      const int c = col0 + j;
+      if (c + 3 < N) {
+        float4 cs = *reinterpret_cast<const float4*>(ep.col_scale + c);
+        v[j] *= cs.x; v[j + 1] *= cs.y; v[j + 2] *= cs.z; v[j + 3] *= cs.w;
+      } else {
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (c + u < N) v[j + u] *= ep.col_scale[c + u];
+      }
+    }
+  }
   if (ep.bias != nullptr) {
 #pragma unroll
     for (int j = 0; j < 32; j += 4) {

@@ -103,10 +103,58 @@ __global__ void fp8_to_bf16_kernel(const uint8_t* in, long long in_ld, __nv_bflo
   *reinterpret_cast<uint4*>(out + (long long)r * out_ld + c) = o;
 }
 
+// out = e4m3( silu(gate * in_scale) * (up * in_scale) / out_scale ), 8 elements per thread.
+__global__ void swiglu_kernel(const uint8_t* gate, long long gate_ld, const uint8_t* up,
+                              long long up_ld, uint8_t* out, long long out_ld, int rows, int cols,
+                              float in_scale, float out_inv_scale) {
+  const int vec_per_row = cols / 8;
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)rows * vec_per_row) return;
+  const int r = int(i / vec_per_row);
+  const int c = int(i - (long long)r * vec_per_row) * 8;
+  const uint2 g = *reinterpret_cast<const uint2*>(gate + (long long)r * gate_ld + c);
+  const uint2 u = *reinterpret_cast<const uint2*>(up + (long long)r * up_ld + c);
+  const uint32_t gw[2] = {g.x, g.y}, uw[2] = {u.x, u.y};
+  uint32_t ow[2];
+#pragma unroll
+  for (int w = 0; w < 2; ++w) {
+    float res[4];
+#pragma unroll
+    for (int hlf = 0; hlf < 2; ++hlf) {
+      const float2 gg = e4m3x2_to_f32x2((gw[w] >> (16 * hlf)) & 0xFFFF);
+      const float2 uu = e4m3x2_to_f32x2((uw[w] >> (16 * hlf)) & 0xFFFF);
+      const float g0 = gg.x * in_scale, g1 = gg.y * in_scale;
+      res[2 * hlf] = g0 / (1.0f + expf(-g0)) * (uu.x * in_scale);
+      res[2 * hlf + 1] = g1 / (1.0f + expf(-g1)) * (uu.y * in_scale);
+    }
+    ow[w] = uint32_t(f32x2_to_e4m3x2(res[0] * out_inv_scale, res[1] * out_inv_scale)) |
+            (uint32_t(f32x2_to_e4m3x2(res[2] * out_inv_scale, res[3] * out_inv_scale)) << 16);
+  }
+  *reinterpret_cast<uint2*>(out + (long long)r * out_ld + c) = make_uint2(ow[0], ow[1]);
+}
+
 }  // namespace
 }  // namespace b2f
 
 extern "C" {
+
+int b2f_swiglu_fp8(const void* gate, long long gate_ld, const void* up, long long up_ld,
+                   void* out, long long out_ld, int rows, int cols, float in_scale,
+                   float out_scale, b2f_stream_t stream) {
+  using namespace b2f;
+  if (rows <= 0 || cols <= 0) return fail(B2F_ERR_ARG, "swiglu: empty shape");
+  if (gate == nullptr || up == nullptr || out == nullptr) return fail(B2F_ERR_ARG, "swiglu: null tensor");
+  if (cols % 8 || gate_ld % 8 || up_ld % 8 || out_ld % 8 || ((uintptr_t)gate & 7) ||
+      ((uintptr_t)up & 7) || ((uintptr_t)out & 7))
+    return fail(B2F_ERR_ARG, "swiglu: cols/ld multiples of 8, 8-byte aligned tensors required");
+  if (!(out_scale > 0.f)) return fail(B2F_ERR_ARG, "swiglu: out_scale must be > 0");
+  const long long n = (long long)rows * (cols / 8);
+  swiglu_kernel<<<(int)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+      reinterpret_cast<const uint8_t*>(gate), gate_ld, reinterpret_cast<const uint8_t*>(up), up_ld,
+      reinterpret_cast<uint8_t*>(out), out_ld, rows, cols, in_scale, 1.0f / out_scale);
+  B2F_CUDA_TRY(cudaGetLastError());
+  return B2F_OK;
+}
 
 int b2f_head_norm_rope(const b2f_rope_args* a, b2f_stream_t stream) {
   using namespace b2f;

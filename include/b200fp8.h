@@ -79,7 +79,7 @@ int b2f_debug_bounded_wait(unsigned long long wait_ns, b2f_stream_t stream);
 /* ------------------------------------------------------------------ GEMM
  * out = epilogue(alpha * (A . B^T))
  *   A: e4m3 [m, lda], K-major; B: e4m3 [n, ldb], K-major (the reference's `matrix_b_nk`).
- *   v = (alpha * acc [* *alpha_ptr] + bias[col]) * pre_mul + pre_add
+ *   v = (alpha * acc [* *alpha_ptr] [* col_scale[col]] + bias[col]) * pre_mul + pre_add
  *   v = act(v) * post_mul
  *   v += residual[row, col] * residual_scale           (optional)
  *   STORE : out[row, col] = v / out_scale  in out_dtype (e4m3 uses RN + saturation)
@@ -100,6 +100,7 @@ typedef struct b2f_gemm_args {
   long long ldb;
   float alpha;
   const float* alpha_ptr;
+  const float* col_scale; /* optional f32 [n]: per-column scale (fused multi-weight GEMMs) */
   const float* bias;
   float pre_mul, pre_add;
   int act;
@@ -249,6 +250,14 @@ int b2f_head_norm_rope(const b2f_rope_args* args, b2f_stream_t stream);
  * Produces the bf16 V operand of b2f_attention_fp8 (exact: bf16 holds every e4m3 value). */
 int b2f_fp8_to_bf16(const void* in, long long in_ld, void* out, long long out_ld, int rows,
                     int cols, float scale, b2f_stream_t stream);
+
+/* out = e4m3( silu(gate * in_scale) * (up * in_scale) / out_scale ); gate, up, out e4m3
+ * [rows, cols] with row pitches in elements.
+ * Replaces: swiglu_kernel (tasks/model_qwen35_4b_full_attention_block_fp8/starter.py:51-58;
+ *   reference math :404-412). */
+int b2f_swiglu_fp8(const void* gate, long long gate_ld, const void* up, long long up_ld,
+                   void* out, long long out_ld, int rows, int cols, float in_scale,
+                   float out_scale, b2f_stream_t stream);
 
 /* ------------------------------------------------------------------ op registry */
 typedef struct b2f_op {
