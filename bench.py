@@ -154,7 +154,9 @@ class GemmWorkload:
         b, self.sb = _fp8_inputs((self.n, self.k), g, xscale)
         self.bias_cpu = (torch.randn((self.n,), generator=g) * 0.02) if bias_relu else None
         self.a_cpu, self.b_cpu = a, b
-        self.flops = 2.0 * self.m * self.n * self.k
+        self.work = 2.0 * self.m * self.n * self.k
+        self.unit, self.bound = "TFLOP/s", "tensor"
+        self.kernel = "gemm_fp8_pair_kernel" if (self.m > 128) else "gemm_fp8_kernel<128>"
         self.algo_bytes = self.m * self.k + self.n * self.k + self.m * self.n * 2 + (
             4 * self.n if bias_relu else 0)
         # Rotate input sets so every step streams operands from HBM, not L2.
@@ -232,6 +234,210 @@ class GemmWorkload:
                           f"f32 dequantise + torch.matmul on CPU, {t:.2f} s"}
 
 
+class NormWorkload:
+    """residual-add + RMSNorm + per-tensor amax e4m3 quantisation,
+    bf16 x / residual [16384, 4096], gamma 1+N(0,0.02), eps 1e-6."""
+
+    name = "residual_rmsnorm_amax_quant"
+    unit = "GB/s"
+    bound = "hbm"
+    kernel = "norm_pass1_kernel<16> + norm_pass2_kernel<16>"
+
+    def __init__(self, rank: int, rows: int = 16384, cols: int = 4096):
+        g = torch.Generator("cpu").manual_seed(20260731 + rank)
+        self.rows, self.cols = rows, cols
+        self.x_cpu = torch.randn((rows, cols), generator=g).to(torch.bfloat16)
+        self.r_cpu = torch.randn((rows, cols), generator=g).to(torch.bfloat16)
+        self.g_cpu = (1 + 0.02 * torch.randn((cols,), generator=g)).to(torch.bfloat16)
+        self.x, self.r, self.gamma = self.x_cpu.cuda(), self.r_cpu.cuda(), self.g_cpu.cuda()
+        self.h = torch.empty_like(self.x)
+        self.q = torch.empty((rows, cols), device="cuda", dtype=torch.float8_e4m3fn)
+        self.amax = torch.zeros(1, device="cuda")
+        self.scale = torch.zeros(1, device="cuda")
+        # compulsory traffic: read x, r; write h (bf16) and q (e4m3)
+        self.work = float(rows * cols * (2 + 2 + 2 + 1))
+        self.algo_bytes = self.work
+
+    def config(self):
+        return {"workload": f"{self.name} [{self.rows} x {self.cols}] bf16 -> e4m3 + amax scale",
+                "rows": self.rows, "cols": self.cols, "eps": 1e-6,
+                "l2": "inputs 268 MB > 126 MB L2"}
+
+    def step(self):
+        from b200fp8 import ops
+        ops.norm_quant(self.x, self.gamma, residual=self.r, h_out=self.h, q_out=self.q,
+                       amax=self.amax, scale_out=self.scale)
+        return 2
+
+    def e2e_setup(self):
+        self.hx, self.hr = self.x_cpu.pin_memory(), self.r_cpu.pin_memory()
+        self.hq = torch.empty((self.rows, self.cols), dtype=torch.uint8).pin_memory()
+        self.hh = torch.empty((self.rows, self.cols), dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step(self):
+        self.x.copy_(self.hx, non_blocking=True)
+        self.r.copy_(self.hr, non_blocking=True)
+        self.step()
+        self.hq.copy_(self.q.view(torch.uint8), non_blocking=True)
+        self.hh.copy_(self.h, non_blocking=True)
+
+    def e2e_bytes(self):
+        n = self.rows * self.cols
+        return 4 * n, 3 * n
+
+    def cpu_sample(self, target_s: float):
+        from oracle import norm as onorm
+        threads = len(os.sched_getaffinity(0))
+        torch.set_num_threads(threads)
+        rows = 256
+        while True:
+            t0 = time.perf_counter()
+            onorm.residual_rmsnorm_amax_quant(self.x_cpu[:rows], self.r_cpu[:rows], self.g_cpu)
+            t = time.perf_counter() - t0
+            if t > target_s / 4 or rows >= self.rows:
+                break
+            rows = min(self.rows, rows * 4)
+        gbs = rows * self.cols * 7 / t / 1e9
+        return {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port",
+                "sample": f"{rows} of {self.rows} rows, oracle residual RMSNorm + amax quant on CPU, {t:.2f} s"}
+
+
+def _nq(shape, g, std=0.02):
+    w = torch.randn(shape, generator=g) * std
+    s = float(w.abs().max()) / 448.0
+    return (w / s).to(torch.float8_e4m3fn), s
+
+
+def _gpt2_weights(g, d=768, mlp=3072):
+    """BASELINE configs[3] weights: N(0, 0.02) e4m3 with per-tensor amax scales."""
+    from types import SimpleNamespace
+    w = SimpleNamespace(heads=12, eps=1e-5, norm_scale=1 / 64.0, qkv_scale=1 / 64.0,
+                        ctx_scale=1 / 64.0, mlp_scale=1 / 64.0)
+    w.qkv_w, w.qkv_s = _nq((3 * d, d), g)
+    w.out_w, w.out_s = _nq((d, d), g)
+    w.fc_w, w.fc_s = _nq((mlp, d), g)
+    w.proj_w, w.proj_s = _nq((d, mlp), g)
+    b = lambda n: torch.randn(n, generator=g) * 0.02  # noqa: E731
+    w.qkv_b, w.out_b, w.fc_b, w.proj_b = b(3 * d), b(d), b(mlp), b(d)
+    w.ln1_w, w.ln1_b, w.ln2_w, w.ln2_b = 1 + b(d), b(d), 1 + b(d), b(d)
+    return w
+
+
+def _qwen_weights(g, seq, hidden=2560, heads=32, kv_heads=8, hd=128, theta=1e6):
+    """BASELINE configs[4] weights: separate q / gate / k / v / o projections, RMSNorm
+    weights N(0, 0.02) used as (1 + w), full-dimension RoPE with theta 1e6."""
+    from types import SimpleNamespace
+    w = SimpleNamespace(heads=heads, kv_heads=kv_heads, head_dim=hd, rotary_dim=hd,
+                        interleaved=False, eps=1e-6, norm_scale=1 / 64.0, qkv_scale=1 / 64.0,
+                        ctx_scale=1 / 64.0, mlp_proj_scale=1 / 64.0, mlp_act_scale=1 / 32.0,
+                        post_norm_w=None, mlp_gate_w=None, mlp_up_w=None, mlp_down_w=None,
+                        mlp_gate_s=1.0, mlp_up_s=1.0, mlp_down_s=1.0)
+    w.q_w, w.q_s = _nq((heads * hd, hidden), g)
+    w.gate_w, w.gate_s = _nq((heads * hd, hidden), g)
+    w.k_w, w.k_s = _nq((kv_heads * hd, hidden), g)
+    w.v_w, w.v_s = _nq((kv_heads * hd, hidden), g)
+    w.o_w, w.o_s = _nq((hidden, heads * hd), g)
+    n = lambda k: torch.randn(k, generator=g) * 0.02  # noqa: E731
+    w.in_norm_w, w.q_norm_w, w.k_norm_w = n(hidden), n(hd), n(hd)
+    pos = torch.arange(seq, dtype=torch.float32)
+    inv = 1.0 / (theta ** (torch.arange(0, hd, 2, dtype=torch.float32) / hd))
+    f = pos[:, None] * inv[None, :]
+    emb = torch.cat((f, f), dim=-1)
+    w.cos, w.sin = emb.cos(), emb.sin()
+    return w
+
+
+class BlockWorkload:
+    """BASELINE configs[3] (GPT-2 block, B8 x S1024) or configs[4] (Qwen gated attention
+    block, B4 x S2048, 32q/8kv x 128, RoPE 1e6, separate gate projection), bf16 residual,
+    random-init e4m3 weights with per-tensor amax scales; the block runs as a CUDA graph."""
+
+    unit = "TFLOP/s"
+    bound = "tensor"
+
+    def __init__(self, kind: str, rank: int):
+        from b200fp8 import blocks
+        g = torch.Generator("cpu").manual_seed(20260801 + rank)
+        self.kind = kind
+        if kind == "gpt2":
+            self.batch, self.seq, self.hidden = 8, 1024, 768
+            self.w = _gpt2_weights(g)
+            cls = blocks.GPT2Block
+            self.name = "gpt2_block_fp8"
+            self.launches = 8
+        else:
+            self.batch, self.seq, self.hidden = 4, 2048, 2560
+            self.w = _qwen_weights(g, self.seq)
+            cls = blocks.QwenBlock
+            self.name = "qwen_gated_attention_block_fp8"
+            self.launches = 7
+        t = self.batch * self.seq
+        self.x_cpu = torch.randn((t, self.hidden), generator=g).to(torch.bfloat16)
+        self.blk = cls(self.w, batch=self.batch, seq=self.seq, residual_dtype=torch.bfloat16,
+                       out_dtype=torch.bfloat16)
+        self.x = self.x_cpu.cuda()
+        self.blk.capture(self.x)
+        self.blk.graph_input.copy_(self.x)
+        self.work = self.blk.flops()
+        self.kernel = "whole block (CUDA graph)"
+
+    def config(self):
+        c = {"workload": f"{self.name} B={self.batch} S={self.seq} hidden={self.hidden}",
+             "batch": self.batch, "seq": self.seq, "hidden": self.hidden,
+             "residual": "bf16", "graph": "one CUDA graph per forward",
+             "l2": "weights + activations per forward exceed L2 only for Qwen; GPT-2 weights "
+                   "(7 MB) stay L2-resident across steps as in serving"}
+        return c
+
+    def step(self):
+        self.blk.replay()
+        return self.launches
+
+    def e2e_setup(self):
+        self.hx = self.x_cpu.pin_memory()
+        self.ho = torch.empty_like(self.x_cpu).pin_memory()
+
+    def e2e_step(self):
+        self.blk.graph_input.copy_(self.hx, non_blocking=True)
+        out = self.blk.replay()
+        self.ho.copy_(out, non_blocking=True)
+
+    def e2e_bytes(self):
+        n = self.x_cpu.numel() * 2
+        return n, n
+
+    def cpu_sample(self, target_s: float):
+        from oracle import blocks as ob
+        threads = len(os.sched_getaffinity(0))
+        torch.set_num_threads(threads)
+        seq = self.seq
+        x = self.x_cpu[:seq].float()
+        t0 = time.perf_counter()
+        if self.kind == "gpt2":
+            ob.gpt2_block(x, self.w, batch=1, residual_dtype=torch.bfloat16,
+                          out_dtype=torch.bfloat16)
+        else:
+            ob.qwen_block(x, self.w, batch=1, residual_dtype=torch.bfloat16,
+                          out_dtype=torch.bfloat16)
+        t = time.perf_counter() - t0
+        frac = 1.0 / self.batch
+        return {"value": self.work * frac / t / 1e12, "unit": "TFLOP/s", "cores": threads,
+                "kind": "port",
+                "sample": f"1 of {self.batch} sequences through the CPU oracle block, {t:.2f} s"}
+
+
+def make_workload(name: str, n: int, rank: int):
+    if name == "gemm":
+        return GemmWorkload(n, rank)
+    if name == "gemm_bias_relu":
+        return GemmWorkload(8192, rank, bias_relu=True, m=128)
+    if name == "norm":
+        return NormWorkload(rank)
+    if name in ("gpt2", "qwen"):
+        return BlockWorkload(name, rank)
+    raise SystemExit(f"unknown workload {name}")
+
+
 def run_ours(args):
     world, rank, local = _dist()
     if world > 1:
@@ -242,17 +448,8 @@ def run_ours(args):
         torch.cuda.set_device(0)
     from b200fp8 import _lib, device_status  # noqa: F401  (fails loudly without the .so)
 
-    wl_name = args.workload
-    if wl_name in ("gemm", "gemm_bias_relu"):
-        if wl_name == "gemm":
-            wl = GemmWorkload(args.n, rank)
-        else:
-            wl = GemmWorkload(8192, rank, bias_relu=True, m=128)
-        metric = "TFLOP/s"
-        unit = "TFLOP/s"
-    else:
-        raise SystemExit(f"unknown workload {wl_name}")
-
+    wl = make_workload(args.workload, args.n, rank)
+    unit = wl.unit
     stream = torch.cuda.current_stream()
     for _ in range(args.warmup):
         wl.step()
@@ -289,10 +486,11 @@ def run_ours(args):
     per_launch_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
     per_launch_ms = _max_over_ranks(per_launch_ms, world)
     ms_per_step = total_ms / args.steps
-    value = wl.flops * world / (ms_per_step * 1e-3) / 1e12
+    scale = 1e12 if unit == "TFLOP/s" else 1e9
+    value = wl.work * world / (ms_per_step * 1e-3) / scale
     status = device_status()
 
-    # end-to-end through the public op with pinned host buffers
+    # end-to-end through the public API with pinned host buffers
     wl.e2e_setup()
     for _ in range(2):
         wl.e2e_step()
@@ -311,7 +509,7 @@ def run_ours(args):
 
     # cuBLASLt FP8 (torch._scaled_mm) on the same operands: a library reference point.
     cublas = None
-    if wl_name == "gemm":
+    if args.workload == "gemm":
         try:
             a, b = wl.sets[0]
             sa = torch.tensor(wl.sa, device="cuda")
@@ -328,44 +526,54 @@ def run_ours(args):
                 torch._scaled_mm(a, b.t(), scale_a=sa, scale_b=sb, out_dtype=torch.bfloat16)
             c1.record()
             torch.cuda.synchronize()
-            cublas = wl.flops / (c0.elapsed_time(c1) / reps * 1e-3) / 1e12
+            cublas = wl.work / (c0.elapsed_time(c1) / reps * 1e-3) / 1e12
         except Exception as exc:  # report, never fail the bench on the side measurement
             cublas = f"unavailable: {type(exc).__name__}"
 
     peaks = _peaks()
-    fp8_peak = 2.0 * peaks["bf16_tflops"]
-    achieved = wl.flops / (per_launch_ms * 1e-3) / 1e12
+    if wl.bound == "tensor":
+        peak = 2.0 * peaks["bf16_tflops"]
+        basis = (f"2 x {peaks['basis']} cuBLAS bf16 burst ({peaks['bf16_tflops']} TFLOP/s); "
+                 "e4m3 dense rate is 2x bf16")
+    else:
+        peak = peaks["hbm_gbs"]
+        basis = f"{peaks['basis']} HBM copy bandwidth"
+    achieved = wl.work / (per_launch_ms * 1e-3) / scale
+    parallel = {"gemm": "N-sharded columns", "gemm_bias_relu": "N-sharded columns",
+                "norm": "row-sharded", "gpt2": "independent replicas",
+                "qwen": "independent replicas"}[args.workload]
     out = {
-        "metric": f"{metric} ({wl.name}, whole job)", "value": round(value, 2), "unit": unit,
+        "metric": f"{unit} ({wl.name}, whole job)", "value": round(value, 2), "unit": unit,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms_per_step, 5), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 in, f32 accumulate, bf16 out",
-        "data": "synthetic (seeded N(0,1), per-tensor amax e4m3 scales)",
-        "config": dict(wl.config(), parallelism=f"N-sharded columns x{world} (no communication)"),
-        "roofline": {"bound": "tensor", "achieved": round(achieved, 1),
-                     "peak": round(fp8_peak, 1), "unit": "TFLOP/s",
-                     "frac": round(achieved / fp8_peak, 4),
-                     "peak_basis": f"2 x {peaks['basis']} cuBLAS bf16 burst "
-                                   f"({peaks['bf16_tflops']} TFLOP/s); e4m3 dense rate is 2x bf16",
-                     "traffic": None, "kernel": "gemm_fp8_kernel<256>",
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "e4m3 in, f32 accumulate, bf16 out",
+        "data": "synthetic (seeded N(0,1), per-tensor amax e4m3 scales; random-init weights)",
+        "config": dict(wl.config(), parallelism=f"{parallel} x{world} (no communication)"),
+        "roofline": {"bound": wl.bound, "achieved": round(achieved, 1), "peak": round(peak, 1),
+                     "unit": unit, "frac": round(achieved / peak, 4), "peak_basis": basis,
+                     "traffic": None, "kernel": getattr(wl, "kernel", "gemm_fp8"),
                      "per_launch_ms": round(per_launch_ms, 5),
-                     "algorithmic_bytes": wl.algo_bytes},
-        "e2e": {"value": round(wl.flops * world / (e2e_ms * 1e-3) / 1e12, 3), "unit": unit,
+                     "algorithmic_work_per_launch": wl.work},
+        "e2e": {"value": round(wl.work * world / (e2e_ms * 1e-3) / scale, 3), "unit": unit,
                 "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
-                "path": "b200fp8.ops.gemm_fp8 with pinned host A,B -> device, C -> host"},
+                "path": "public b200fp8 API with pinned host inputs -> device, result -> host"},
         "gpu_launches": launches,
         "clocks": clocks,
         "device_status": status,
-        "cublaslt_fp8_tflops_same_shape": (round(cublas, 1) if isinstance(cublas, float) else cublas),
     }
-    traffic_path = os.path.join(ROOT, "profiles", "gemm_fp8_traffic.json")
+    if cublas is not None:
+        out["cublaslt_fp8_tflops_same_shape"] = round(cublas, 1) if isinstance(cublas, float) else cublas
+    traffic_path = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(traffic_path):
         try:
             with open(traffic_path) as f:
                 tr = json.load(f)
-            if tr.get("n") == wl.n:
-                out["roofline"]["traffic"] = tr.get("traffic_bytes_per_launch")
+            entry = tr.get(args.workload)
+            if entry:
+                out["roofline"]["traffic"] = entry.get("traffic_bytes_per_launch")
+                out["roofline"]["traffic_source"] = entry.get("source")
         except Exception:
             pass
     if rank == 0 and world == 1:
