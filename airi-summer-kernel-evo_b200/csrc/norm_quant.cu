@@ -1,8 +1,8 @@
 // Residual-add + RMSNorm / LayerNorm + e4m3 quantisation (C ABI: b2f_norm_quant).
 //
-// One warp owns one row.  Each lane moves 16-byte vectors (8 elements) with coalesced
-// 512-byte warp accesses, keeps the whole row in registers, reduces with warp shuffles
-// and writes every output of the row in the same pass:
+// A group of up to 256 threads owns one row (4 vectors of 8 elements per thread, coalesced
+// 16-byte-per-lane sweeps), keeps the whole row in registers, reduces with warp shuffles
+// (plus shared memory across the warps of a row) and writes every output in one pass:
 //   h   = x * x_scale + residual                (updated residual stream, optional store)
 //   y   = RMSNorm(h) * (w + w_offset)           (w_offset = 1 for Qwen's (1 + w))
 //       | LayerNorm(h) * w + b
@@ -25,7 +25,7 @@ namespace b2f {
 
 namespace {
 
-constexpr int kMaxVecPerLane = 16;  // rows up to 32 * 16 * 8 = 4096 elements
+constexpr int kMaxCols = 8192;  // 256 threads x 4 vectors x 8 elements
 
 struct NormParams {
   const void* x;
@@ -105,41 +105,92 @@ __device__ __forceinline__ uint2 quant8(const float (&y)[8], float inv) {
   return r;
 }
 
-// Loads the row of h into registers (computing x*x_scale + residual), optionally stores
-// it, and returns the normalisation (mean, inv) of the row.
-template <int NV>
-__device__ __forceinline__ void row_stats(const NormParams& p, int row, int lane, int nvec,
-                                          float (&h)[NV][8], bool store_h, float& mean,
-                                          float& inv) {
-  const long long xo = (long long)row * p.x_ld;
-  const long long ro = (long long)row * p.res_ld;
-  const long long ho = (long long)row * p.h_ld;
-  float s1 = 0.f, s2 = 0.f;
+// ---------------------------------------------------------------------------------------
+// Row layout: a group of TPR threads (a multiple of 32) owns one row; thread t of the group
+// holds vectors vi = t + TPR * i (i < 4) of 8 elements, so each i is one coalesced
+// 16-byte-per-lane sweep.  All loads of a row are issued before any store (the stored
+// residual stream may alias nothing the kernel still has to read), and the dtype switch
+// sits outside the load loop so the loads issue back to back.
+constexpr int VPT = 4;  // vectors of 8 elements per thread
+
+template <int DT>
+__device__ __forceinline__ void load4(const void* __restrict__ base, long long row_off, int t,
+                                      int tpr, int nvec, float scale, float (&v)[VPT][8]) {
 #pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int vi = lane + 32 * i;
+  for (int i = 0; i < VPT; ++i) {
+    const int vi = t + tpr * i;
     if (vi < nvec) {
-      load8(p.x, p.x_dtype, xo + vi * 8, p.x_scale, h[i]);
-      if (p.residual != nullptr) {
-        float r[8];
-        load8(p.residual, p.res_dtype, ro + vi * 8, 1.0f, r);
+      load8(base, DT, row_off + (long long)vi * 8, scale, v[i]);
+    } else {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) h[i][j] += r[j];
-      }
-      // The stored residual stream is what downstream layers see; normalise that value.
-      if (p.h_out != nullptr && p.h_dtype == kBF16) round_bf16(h[i]);
-      if (store_h && p.h_out != nullptr) store8(p.h_out, p.h_dtype, ho + vi * 8, h[i]);
+      for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
+    }
+  }
+}
+
+__device__ __forceinline__ void load_any(const void* base, int dt, long long row_off, int t,
+                                         int tpr, int nvec, float scale, float (&v)[VPT][8]) {
+  switch (dt) {
+    case kBF16: load4<kBF16>(base, row_off, t, tpr, nvec, scale, v); break;
+    case kF32: load4<kF32>(base, row_off, t, tpr, nvec, scale, v); break;
+    default: load4<kE4M3>(base, row_off, t, tpr, nvec, scale, v); break;
+  }
+}
+
+// Sum over the TPR threads of a row group (every thread of the CTA must call it).
+__device__ __forceinline__ float group_sum(float v, float* red, int tpr) {
+  v = warp_sum(v);
+  const int wpr = tpr >> 5;
+  if (wpr == 1) return v;
+  const int warp = threadIdx.x >> 5;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[warp] = v;
+  __syncthreads();
+  const int g0 = (warp / wpr) * wpr;
+  float s = 0.f;
+  for (int w = 0; w < wpr; ++w) s += red[g0 + w];
+  return s;
+}
+
+// h = x * x_scale + residual (rounded to the stored residual dtype), optional store of h,
+// then the row statistics.
+__device__ __forceinline__ void row_stats(const NormParams& p, const void* x, int xdt, float xs,
+                                          long long xld, const void* res, bool store_h,
+                                          int row, bool row_ok, int t, int tpr, int nvec,
+                                          float* red, float (&h)[VPT][8], float& mean,
+                                          float& inv) {
+  const long long r = row_ok ? row : 0;
+  load_any(x, xdt, r * xld, t, tpr, nvec, xs, h);
+  if (res != nullptr) {
+    float rv[VPT][8];
+    load_any(res, p.res_dtype, r * p.res_ld, t, tpr, nvec, 1.0f, rv);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) s1 += h[i][j];
+    for (int i = 0; i < VPT; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) h[i][j] += rv[i][j];
+  }
+  if (p.h_out != nullptr && p.h_dtype == kBF16) {
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) round_bf16(h[i]);
+  }
+  if (store_h && row_ok && p.h_out != nullptr) {
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int vi = t + tpr * i;
+      if (vi < nvec) store8(p.h_out, p.h_dtype, r * p.h_ld + (long long)vi * 8, h[i]);
     }
   }
   const float n = float(p.cols);
+  float s1 = 0.f, s2 = 0.f;
   if (p.kind == 1) {
-    mean = warp_sum(s1) / n;
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int vi = lane + 32 * i;
-      if (vi < nvec) {
+    for (int i = 0; i < VPT; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s1 += h[i][j];
+    mean = group_sum(s1, red, tpr) / n;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      if (t + tpr * i < nvec) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const float d = h[i][j] - mean;
@@ -147,21 +198,14 @@ __device__ __forceinline__ void row_stats(const NormParams& p, int row, int lane
         }
       }
     }
-    s2 = warp_sum(s2);
-    inv = rsqrtf(s2 / n + p.eps);
   } else {
     mean = 0.f;
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int vi = lane + 32 * i;
-      if (vi < nvec) {
+    for (int i = 0; i < VPT; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) s2 += h[i][j] * h[i][j];
-      }
-    }
-    s2 = warp_sum(s2);
-    inv = rsqrtf(s2 / n + p.eps);
+      for (int j = 0; j < 8; ++j) s2 += h[i][j] * h[i][j];
   }
+  inv = rsqrtf(group_sum(s2, red, tpr) / n + p.eps);
 }
 
 __device__ __forceinline__ void norm8(const NormParams& p, int col, float mean, float inv,
@@ -184,80 +228,84 @@ __device__ __forceinline__ void norm8(const NormParams& p, int col, float mean, 
   }
 }
 
+__device__ __forceinline__ float block_max(float v, float* red) {
+  v = warp_max(v);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float m = 0.f;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, red[w]);
+  return m;
+}
+
 // Static scale (one pass), or pass 1 of the dynamic schedule (no q store; amax reduce).
-template <int NV>
-__global__ void __launch_bounds__(256) norm_pass1_kernel(const NormParams p) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x * 8 + warp;
+__global__ void __launch_bounds__(256) norm_pass1_kernel(const NormParams p, int tpr) {
+  __shared__ float red[8];
+  const int rpc = blockDim.x / tpr;
+  const int t = threadIdx.x % tpr;
+  const int row = blockIdx.x * rpc + threadIdx.x / tpr;
+  const bool row_ok = row < p.rows;
   const int nvec = p.cols / 8;
+  float h[VPT][8];
+  float mean, inv;
+  row_stats(p, p.x, p.x_dtype, p.x_scale, p.x_ld, p.residual, true, row, row_ok, t, tpr, nvec,
+            red, h, mean, inv);
+  const float qinv = 1.0f / p.q_scale;
   float amax = 0.f;
-  if (row < p.rows) {
-    float h[NV][8];
-    float mean, inv;
-    row_stats<NV>(p, row, lane, nvec, h, true, mean, inv);
-    const float qinv = 1.0f / p.q_scale;
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int vi = lane + 32 * i;
-      if (vi < nvec) {
-        float y[8];
-        norm8(p, vi * 8, mean, inv, h[i], y);
-        if (p.dynamic) {
+  for (int i = 0; i < VPT; ++i) {
+    const int vi = t + tpr * i;
+    if (row_ok && vi < nvec) {
+      float y[8];
+      norm8(p, vi * 8, mean, inv, h[i], y);
+      if (p.dynamic) {
+        round_bf16(y);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(y[j]));
+      } else {
+        // Quantise the f32 value (as the reference's `(y / scale).to(e4m3)`); the
+        // optional bf16 copy is rounded separately.
+        *reinterpret_cast<uint2*>(p.q_out + (long long)row * p.q_ld + vi * 8) = quant8(y, qinv);
+        if (p.y_out != nullptr) {
           round_bf16(y);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(y[j]));
-        } else {
-          // Quantise the f32 value (as the reference's `(y / scale).to(e4m3)`); the
-          // optional bf16 copy is rounded separately.
-          *reinterpret_cast<uint2*>(p.q_out + (long long)row * p.q_ld + vi * 8) = quant8(y, qinv);
-          if (p.y_out != nullptr) {
-            round_bf16(y);
-            store8(p.y_out, kBF16, (long long)row * p.y_ld + vi * 8, y);
-          }
+          store8(p.y_out, kBF16, (long long)row * p.y_ld + vi * 8, y);
         }
       }
     }
   }
   if (p.dynamic) {
-    __shared__ float red[8];
-    amax = warp_max(amax);
-    if (lane == 0) red[warp] = amax;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      float m = red[0];
-      for (int i = 1; i < 8; ++i) m = fmaxf(m, red[i]);
-      atomic_max_nonneg(p.amax, m);
-    }
+    const float m = block_max(amax, red);
+    if (threadIdx.x == 0) atomic_max_nonneg(p.amax, m);
   }
 }
 
-// Pass 2 of the dynamic schedule: rows in reverse order, h re-read (L2-warm), quantised
-// with s = amax / 448.
-template <int NV>
-__global__ void __launch_bounds__(256) norm_pass2_kernel(const NormParams p) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nblk = gridDim.x;
-  const int row = (nblk - 1 - blockIdx.x) * 8 + warp;
+// Pass 2 of the dynamic schedule: row blocks in reverse order (the most recently written
+// h rows are still in L2), h re-read, statistics recomputed, quantised with amax / 448.
+__global__ void __launch_bounds__(256) norm_pass2_kernel(const NormParams p, int tpr) {
+  __shared__ float red[8];
+  const int rpc = blockDim.x / tpr;
+  const int t = threadIdx.x % tpr;
+  const int row = (gridDim.x - 1 - blockIdx.x) * rpc + threadIdx.x / tpr;
+  const bool row_ok = row < p.rows;
   const float amax = *p.amax;
   const float s = amax > 0.f ? amax / 448.0f : 1.0f;
   if (blockIdx.x == 0 && threadIdx.x == 0) *p.scale_out = s;
-  if (row >= p.rows) return;
   const int nvec = p.cols / 8;
-  NormParams q = p;
-  if (p.h_out != nullptr) {
-    // Re-read the stored residual stream instead of x + residual.
-    q.x = p.h_out; q.x_dtype = p.h_dtype; q.x_scale = 1.0f; q.x_ld = p.h_ld;
-    q.residual = nullptr;
-  }
-  q.h_out = nullptr;
-  float h[NV][8];
+  float h[VPT][8];
   float mean, inv;
-  row_stats<NV>(q, row, lane, nvec, h, false, mean, inv);
+  NormParams q = p;
+  q.h_out = nullptr;
+  if (p.h_out != nullptr)
+    row_stats(q, p.h_out, p.h_dtype, 1.0f, p.h_ld, nullptr, false, row, row_ok, t, tpr, nvec,
+              red, h, mean, inv);
+  else
+    row_stats(q, p.x, p.x_dtype, p.x_scale, p.x_ld, p.residual, false, row, row_ok, t, tpr,
+              nvec, red, h, mean, inv);
   const float qinv = 1.0f / s;
 #pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int vi = lane + 32 * i;
-    if (vi < nvec) {
+  for (int i = 0; i < VPT; ++i) {
+    const int vi = t + tpr * i;
+    if (row_ok && vi < nvec) {
       float y[8];
       norm8(p, vi * 8, mean, inv, h[i], y);
       round_bf16(y);
@@ -267,16 +315,19 @@ __global__ void __launch_bounds__(256) norm_pass2_kernel(const NormParams p) {
   }
 }
 
-template <int NV>
 int launch_norm(const NormParams& p, cudaStream_t s) {
-  const int grid = (p.rows + 7) / 8;
+  const int nvec = p.cols / 8;
+  int tpr = ((nvec + VPT - 1) / VPT + 31) / 32 * 32;  // threads per row
+  const int rpc = 256 / tpr;                            // rows per CTA
+  const int threads = rpc * tpr;
+  const int grid = (p.rows + rpc - 1) / rpc;
   if (p.dynamic) {
     B2F_CUDA_TRY(cudaMemsetAsync(p.amax, 0, sizeof(float), s));
-    norm_pass1_kernel<NV><<<grid, 256, 0, s>>>(p);
+    norm_pass1_kernel<<<grid, threads, 0, s>>>(p, tpr);
     B2F_CUDA_TRY(cudaGetLastError());
-    norm_pass2_kernel<NV><<<grid, 256, 0, s>>>(p);
+    norm_pass2_kernel<<<grid, threads, 0, s>>>(p, tpr);
   } else {
-    norm_pass1_kernel<NV><<<grid, 256, 0, s>>>(p);
+    norm_pass1_kernel<<<grid, threads, 0, s>>>(p, tpr);
   }
   B2F_CUDA_TRY(cudaGetLastError());
   return B2F_OK;
@@ -307,8 +358,8 @@ int b2f_norm_quant(const b2f_norm_args* a, b2f_stream_t stream) {
   if (a == nullptr) return fail(B2F_ERR_ARG, "norm_quant: null args");
   if (a->rows <= 0 || a->cols <= 0) return fail(B2F_ERR_ARG, "norm_quant: empty shape");
   if (a->cols % 8 != 0) return fail(B2F_ERR_ARG, "norm_quant: cols must be a multiple of 8");
-  if (a->cols > 32 * kMaxVecPerLane * 8)
-    return fail(B2F_ERR_UNSUPPORTED, "norm_quant: cols > 4096 not supported");
+  if (a->cols > kMaxCols)
+    return fail(B2F_ERR_UNSUPPORTED, "norm_quant: cols > 8192 not supported");
   if (a->x == nullptr || a->weight == nullptr || a->q_out == nullptr)
     return fail(B2F_ERR_ARG, "norm_quant: null tensor");
   if (a->kind != B2F_NORM_RMS && a->kind != B2F_NORM_LAYER)
@@ -342,11 +393,7 @@ int b2f_norm_quant(const b2f_norm_args* a, b2f_stream_t stream) {
   p.amax = a->amax; p.scale_out = a->scale_out;
   p.rows = a->rows; p.cols = a->cols;
   cudaStream_t s = (cudaStream_t)stream;
-  const int nvec = a->cols / 8;
-  if (nvec <= 32 * 4) return launch_norm<4>(p, s);
-  if (nvec <= 32 * 8) return launch_norm<8>(p, s);
-  if (nvec <= 32 * 12) return launch_norm<12>(p, s);
-  return launch_norm<16>(p, s);
+  return launch_norm(p, s);
 }
 
 }  // extern "C"

@@ -41,10 +41,21 @@ __global__ void __launch_bounds__(256) head_norm_rope_kernel(const RopeParams p)
   const int t = warp_global / p.heads;
   const int h = warp_global - t * p.heads;
   const uint8_t* src = p.in + (long long)t * p.in_ld + (long long)h * p.in_hstride + lane * E;
+  // one load per lane of its E contiguous bytes
+  uint32_t raw[(E + 3) / 4];
+  if constexpr (E == 2) {
+    raw[0] = *reinterpret_cast<const uint16_t*>(src);
+  } else if constexpr (E == 4) {
+    raw[0] = *reinterpret_cast<const uint32_t*>(src);
+  } else {
+    const uint2 q = *reinterpret_cast<const uint2*>(src);
+    raw[0] = q.x;
+    raw[1] = q.y;
+  }
   float x[E];
 #pragma unroll
   for (int e = 0; e < E; e += 2) {
-    const float2 v = e4m3x2_to_f32x2(*reinterpret_cast<const uint16_t*>(src + e));
+    const float2 v = e4m3x2_to_f32x2((raw[e / 4] >> (8 * (e % 4))) & 0xFFFF);
     x[e] = v.x * p.in_scale;
     x[e + 1] = v.y * p.in_scale;
   }
@@ -79,10 +90,18 @@ __global__ void __launch_bounds__(256) head_norm_rope_kernel(const RopeParams p)
     for (int e = 0; e < E; ++e) x[e] = y[e];
   }
   uint8_t* dst = p.out + (long long)t * p.out_ld + (long long)h * D + lane * E;
+  uint32_t packed[(E + 3) / 4] = {};
 #pragma unroll
   for (int e = 0; e < E; e += 2)
-    *reinterpret_cast<uint16_t*>(dst + e) =
-        f32x2_to_e4m3x2(x[e] * p.out_inv_scale, x[e + 1] * p.out_inv_scale);
+    packed[e / 4] |= uint32_t(f32x2_to_e4m3x2(x[e] * p.out_inv_scale, x[e + 1] * p.out_inv_scale))
+                     << (8 * (e % 4));
+  if constexpr (E == 2) {
+    *reinterpret_cast<uint16_t*>(dst) = static_cast<uint16_t>(packed[0]);
+  } else if constexpr (E == 4) {
+    *reinterpret_cast<uint32_t*>(dst) = packed[0];
+  } else {
+    *reinterpret_cast<uint2*>(dst) = make_uint2(packed[0], packed[1]);
+  }
 }
 
 __global__ void fp8_to_bf16_kernel(const uint8_t* in, long long in_ld, __nv_bfloat16* out,
@@ -171,9 +190,10 @@ int b2f_head_norm_rope(const b2f_rope_args* a, b2f_stream_t stream) {
     if (a->rotary_dim <= 0 || a->rotary_dim > d || a->rotary_dim % (2 * e) != 0)
       return fail(B2F_ERR_ARG, "head_norm_rope: rotary_dim must be a multiple of 2*head_dim/32");
   }
-  if (((a->in_ld | a->in_head_stride | a->out_ld) & 1) || ((uintptr_t)a->in & 1) ||
-      ((uintptr_t)a->out & 1))
-    return fail(B2F_ERR_ARG, "head_norm_rope: 2-byte alignment required");
+  const long long al = d / 32;  // bytes per lane: rows and heads must keep lane loads aligned
+  if (((a->in_ld | a->in_head_stride | a->out_ld) % al) || ((uintptr_t)a->in % al) ||
+      ((uintptr_t)a->out % al))
+    return fail(B2F_ERR_ARG, "head_norm_rope: pointers and pitches must be multiples of head_dim/32");
   if (!(a->out_scale > 0.f)) return fail(B2F_ERR_ARG, "head_norm_rope: out_scale must be > 0");
   RopeParams p;
   p.in = reinterpret_cast<const uint8_t*>(a->in);

@@ -140,7 +140,7 @@ int b2f_gemm_pair_capacity(void);
  *   starter.py:167-171, used at :347-348 and :402-403), the GPT-2 LayerNorm steps
  *   (tasks/model_gpt2_small_transformer_block_fp8/starter.py:407-416, 461-470) and
  *   layer_norm (tasks/level1_40_layer_norm_fp8/starter.py).
- * Requirements: cols % 8 == 0, cols <= 4096, 16-byte aligned rows.
+ * Requirements: cols % 8 == 0, cols <= 8192, 16-byte aligned rows.
  */
 enum b2f_norm_kind { B2F_NORM_RMS = 0, B2F_NORM_LAYER = 1 };
 
