@@ -13,16 +13,20 @@ thread_local int g_pair_capacity = 0;  // co-resident CTA pairs seen by the last
 
 // Output tensor map for the epilogue's TMA stores: the output viewed as bytes
 // [m, n * esize] with 32-row x 128-byte boxes in the 128B swizzle layout.
-int encode_out_map(const b2f_gemm_args* a, const EpilogueParams& ep, CUtensorMap* map) {
+// Each epilogue warp drains `half_cols` columns of a tile; its TMA store box is the
+// largest of 64 / 128 bytes that fits inside that column range.
+int encode_out_map(const b2f_gemm_args* a, EpilogueParams& ep, int half_cols, CUtensorMap* map) {
   std::memset(map, 0, sizeof(*map));
-  if (!ep.out_vec || ep.mode != kModeStore) return B2F_OK;
   const int esz = a->out_dtype == B2F_DTYPE_F32 ? 4 : (a->out_dtype == B2F_DTYPE_BF16 ? 2 : 1);
+  ep.chunk_bytes = half_cols * esz >= 128 ? 128 : 64;
+  if (!ep.out_vec || ep.mode != kModeStore) return B2F_OK;
   const unsigned long long dims[2] = {(unsigned long long)a->n * esz, (unsigned long long)a->m};
   const unsigned long long strides[1] = {(unsigned long long)a->out_ld * esz};
-  const unsigned int box[2] = {128, 32};
+  const unsigned int box[2] = {(unsigned int)ep.chunk_bytes, 32};
   std::string err;
   if (!encode_tmap(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a->out, dims, strides, box,
-                   CU_TENSOR_MAP_SWIZZLE_128B, &err))
+                   ep.chunk_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                   &err))
     return fail(B2F_ERR_ARG, "gemm_fp8: output tensor map: " + err);
   return B2F_OK;
 }
@@ -58,7 +62,7 @@ EpilogueParams make_epilogue(const b2f_gemm_args* a) {
 }
 
 template <int BN>
-int launch_gemm(const b2f_gemm_args* a, const EpilogueParams& ep, cudaStream_t stream) {
+int launch_gemm(const b2f_gemm_args* a, EpilogueParams ep, cudaStream_t stream) {
   using Cfg = GemmCfg<BN>;
   CUtensorMap ta, tb;
   std::string err;
@@ -94,13 +98,13 @@ int launch_gemm(const b2f_gemm_args* a, const EpilogueParams& ep, cudaStream_t s
     attr_dev = dev;
   }
   CUtensorMap to;
-  if (int rc = encode_out_map(a, ep, &to)) return rc;
+  if (int rc = encode_out_map(a, ep, BN / 2, &to)) return rc;
   kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, to, shape, ep);
   B2F_CUDA_TRY(cudaGetLastError());
   return B2F_OK;
 }
 
-int launch_gemm_pair(const b2f_gemm_args* a, const EpilogueParams& ep, cudaStream_t stream) {
+int launch_gemm_pair(const b2f_gemm_args* a, EpilogueParams ep, cudaStream_t stream) {
   using Cfg = Gemm2Cfg;
   CUtensorMap ta, tb;
   std::string err;
@@ -147,7 +151,7 @@ int launch_gemm_pair(const b2f_gemm_args* a, const EpilogueParams& ep, cudaStrea
   g_pair_capacity = cached_pairs;
   const int pairs = num_tiles < cached_pairs ? num_tiles : cached_pairs;
   CUtensorMap to;
-  if (int rc = encode_out_map(a, ep, &to)) return rc;
+  if (int rc = encode_out_map(a, ep, Cfg::BN / 2, &to)) return rc;
   gemm_fp8_pair_kernel<<<2 * pairs, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, to, shape,
                                                                              ep);
   B2F_CUDA_TRY(cudaGetLastError());

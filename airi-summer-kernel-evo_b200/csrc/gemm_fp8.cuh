@@ -7,14 +7,15 @@
 // (tasks/level1_01_square_matrix_multiplication_fp8/starter.py:125-138,
 //  tasks/level2_76_gemm_add_relu_fp8/starter.py:148-169).
 //
-// Roles (192 threads, one CTA per SM, grid = min(#tiles, #SMs)):
+// Roles (320 threads, one CTA per SM, grid = min(#tiles, #SMs)):
 //   warp 0   TMA producer: streams 128-byte K blocks of A (128 rows) and B (BN rows) into
 //            a STAGES-deep ring of 128B-swizzled shared-memory slots.
 //   warp 1   allocates TMEM (2 accumulators x BN f32 columns), then one thread issues
 //            tcgen05.mma.kind::f8f6f4 (M=128, N=BN, K=32) four times per K block and
 //            releases each slot with tcgen05.commit.
-//   warps 2-5 epilogue: tcgen05.ld 32 columns at a time from the accumulator, apply the
-//            fused epilogue in registers and store.  Double-buffered accumulators let the
+//   warps 2-9 epilogue: two warps per TMEM lane quadrant, each draining half the tile's
+//            columns with tcgen05.ld; the fused epilogue runs in registers and leaves
+//            through shared memory with TMA stores.  Double-buffered accumulators let the
 //            epilogue of tile i overlap the main loop of tile i+1.
 #pragma once
 #include "common.cuh"
@@ -57,18 +58,27 @@ struct EpilogueParams {
   int mode;                // kModeStore / kModeRowSum
   int out_vec;             // out base and row pitch 16-byte aligned: vector stores
   int res_vec;             // residual base and row pitch 16-byte aligned: vector loads
+  int chunk_bytes;         // TMA store box width: 128 (SW128) or 64 (SW64) bytes
 };
 
 struct GemmShape {
   int M, N, K;
 };
 
+// Hardware tanh (MUFU, max relative error ~2^-11); every GELU output is requantised to
+// e4m3 (relative step 2^-3), so the approximation is far below the output resolution.
+__device__ __forceinline__ float tanh_hw(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ float gelu_tanh(float x) {
   // 0.5 x (1 + tanh( sqrt(2/pi) (x + 0.044715 x^3) )), as torch's approximate="tanh".
   const float k0 = 0.7978845608028654f;
   const float k1 = 0.044715f;
-  float u = k0 * (x + k1 * x * x * x);
-  return 0.5f * x * (1.0f + tanhf(u));
+  const float u = k0 * fmaf(k1 * x, x * x, x);
+  return 0.5f * x * (1.0f + tanh_hw(u));
 }
 
 // Activation selected at compile time: a runtime switch inside the element loop gets
@@ -100,7 +110,7 @@ struct GemmCfg {
   static constexpr int TMEM_COLS = 2 * BN;  // two accumulators
   static constexpr int SMEM_BYTES =
       STAGES * STAGE_BYTES + 4 * 8192 /*epilogue staging*/ + 1024 /*align*/ + 256 /*barriers*/;
-  static constexpr int THREADS = 192;
+  static constexpr int THREADS = 320;  // producer, MMA, 8 epilogue warps
 };
 
 // Tile order: groups of GROUP_M row-blocks sweep all column blocks, so the CTAs that run
@@ -120,37 +130,19 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb
 // residual; tracks |v| (amax) and the row sum.  Returns the f32 values before the store.
 __device__ __forceinline__ void epi_values(const EpilogueParams& ep, float alpha, int row,
                                            int col0, int M, int N, const uint32_t (&acc)[32],
-                                           float (&v)[32], float& rowsum, float& amax_local) {
+                                           float (&v)[32], float& rowsum, float& amax_local,
+                                           float lane_bias, float lane_cscale) {
   const bool row_ok = row < M;
+  // lane j of the warp holds bias / column scale of column col0 + j: broadcast by shuffle
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(acc[j]) * alpha;
   if (ep.col_scale != nullptr) {
 #pragma unroll
-    for (int j = 0; j < 32; j += 4) {
-      const int c = col0 + j;
-      if (c + 3 < N) {
-        float4 cs = *reinterpret_cast<const float4*>(ep.col_scale + c);
-        v[j] *= cs.x; v[j + 1] *= cs.y; v[j + 2] *= cs.z; v[j + 3] *= cs.w;
-      } else {
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-          if (c + u < N) v[j + u] *= ep.col_scale[c + u];
-      }
-    }
+    for (int j = 0; j < 32; ++j) v[j] *= __shfl_sync(0xffffffffu, lane_cscale, j);
   }
   if (ep.bias != nullptr) {
 #pragma unroll
-    for (int j = 0; j < 32; j += 4) {
-      const int c = col0 + j;
-      if (c + 3 < N) {
-        float4 b = *reinterpret_cast<const float4*>(ep.bias + c);
-        v[j] += b.x; v[j + 1] += b.y; v[j + 2] += b.z; v[j + 3] += b.w;
-      } else {
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-          if (c + u < N) v[j + u] += ep.bias[c + u];
-      }
-    }
+    for (int j = 0; j < 32; ++j) v[j] += __shfl_sync(0xffffffffu, lane_bias, j);
   }
   switch (ep.act) {  // uniform branch, once per 32 columns
     case kActRelu: act_affine32<kActRelu>(v, ep.pre_mul, ep.pre_add, ep.act_param, ep.post_mul); break;
@@ -255,81 +247,91 @@ __device__ __forceinline__ int out_esize(int dt) { return dt == kOutF32 ? 4 : (d
 // staging tile in the 128B-swizzle layout and leaves with TMA bulk-tensor stores (full
 // 128-byte lines, clipped at the M/N edges by the TMA unit).  `stage` points at this
 // warp's 2 x 4 KB staging area (1024-byte aligned).
+// Per-lane epilogue vectors for the 32 columns starting at col0 (one coalesced load each).
+__device__ __forceinline__ void epi_lane_vectors(const EpilogueParams& ep, int col0, int N,
+                                                 float& lane_bias, float& lane_cscale) {
+  const int c = col0 + (threadIdx.x & 31);
+  lane_bias = (ep.bias != nullptr && c < N) ? __ldg(ep.bias + c) : 0.f;
+  lane_cscale = (ep.col_scale != nullptr && c < N) ? __ldg(ep.col_scale + c) : 1.f;
+}
+
+// Drains one 128 x BN accumulator (this warp: 32 TMEM lanes = 32 rows) through the fused
+// epilogue.  TMEM loads are software-pipelined (the load of columns u+1 is in flight while
+// columns u are processed).  Output goes through a per-warp, double-buffered 32 x 128-byte
+// shared-memory staging tile in the 128B-swizzle layout and leaves with TMA bulk-tensor
+// stores (full 128-byte lines, clipped at the M/N edges by the TMA unit).  `stage` points
+// at this warp's 4 KB staging area (1024-byte aligned).
 template <int BN>
 __device__ __forceinline__ void epilogue_tile(const EpilogueParams& ep, const CUtensorMap* tmap_out,
                                               float alpha, uint32_t t_row, int row, int row0,
                                               int col_base, int M, int N, uint8_t* stage,
                                               int& buf, float& rowsum, float& amax_local) {
   const int lane = threadIdx.x & 31;
-  if (ep.mode == kModeRowSum) {
-#pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
-      uint32_t r[32];
-      float v[32];
-      tmem_ld32(t_row + c * 32, r);
-      const int col0 = col_base + c * 32;
-      if (col0 < N) epi_values(ep, alpha, row, col0, M, N, r, v, rowsum, amax_local);
-    }
-    return;
-  }
-  if (!ep.out_vec) {
-#pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
-      uint32_t r[32];
-      float v[32];
-      tmem_ld32(t_row + c * 32, r);
-      const int col0 = col_base + c * 32;
-      if (col0 < N) {
-        epi_values(ep, alpha, row, col0, M, N, r, v, rowsum, amax_local);
-        if (row < M) epi_store_direct(ep, row, col0, N, v);
-      }
-    }
-    return;
-  }
+  const bool tma = ep.out_vec && ep.mode == kModeStore;
   const int esz = out_esize(ep.out_dtype);
-  const int cw = 128 / esz;     // columns per 128-byte staging row
-  const int subs = cw / 32;     // tcgen05.ld x32 per staging chunk (f32 1, bf16 2, e4m3 4)
+  const int cb = ep.chunk_bytes;                 // staging row / TMA box width in bytes
+  const int subs = tma ? (cb / esz) / 32 : 1;    // 32-column units per staging row
+  const int g = 2 * esz;                         // 16-byte granules per unit
+  int units = BN / 32;
+  const int n_left = N - col_base;
+  if (n_left < BN) units = (n_left + 31) / 32;   // columns past N are skipped (uniform)
+  uint32_t ra[32], rb[32];
+  tmem_ld32_async(t_row, ra);
 #pragma unroll 1
-  for (int c0 = 0; c0 < BN; c0 += cw) {
-    if (col_base + c0 >= N) break;
-    uint8_t* sbuf = stage + buf * 4096;
-    // The store issued two chunks ago from this buffer must have finished reading it.
-    if (lane == 0) bulk_wait_read<1>();
-    __syncwarp();
-#pragma unroll 1
-    for (int sub = 0; sub < subs; ++sub) {
-      uint32_t r[32];
-      float v[32];
-      uint32_t w[32];
-      tmem_ld32(t_row + c0 + sub * 32, r);
-      epi_values(ep, alpha, row, col_base + c0 + sub * 32, M, N, r, v, rowsum, amax_local);
-      epi_pack(ep, v, w);
-      // this sub-chunk covers 16-byte granules [sub*g, sub*g + g) of the 128-byte row
-      const int g = 8 / subs;
-      uint8_t* rowp = sbuf + lane * 128;
+  for (int u = 0; u < units; u += 2) {
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        if (u < g) {
-          const int gi = sub * g + u;
-          uint4 q = make_uint4(w[4 * u], w[4 * u + 1], w[4 * u + 2], w[4 * u + 3]);
-          *reinterpret_cast<uint4*>(rowp + ((gi ^ (lane & 7)) << 4)) = q;
+    for (int half = 0; half < 2; ++half) {
+      const int uu = u + half;
+      if (uu >= units) break;
+      uint32_t (&cur)[32] = half == 0 ? ra : rb;
+      uint32_t (&nxt)[32] = half == 0 ? rb : ra;
+      const int col0 = col_base + uu * 32;
+      float lb, lc;
+      epi_lane_vectors(ep, col0, N, lb, lc);
+      tmem_ld_wait_regs(cur);
+      if (uu + 1 < units) tmem_ld32_async(t_row + (uu + 1) * 32, nxt);
+      float v[32];
+      epi_values(ep, alpha, row, col0, M, N, cur, v, rowsum, amax_local, lb, lc);
+      if (ep.mode == kModeRowSum) continue;
+      if (!tma) {
+        if (row < M) epi_store_direct(ep, row, col0, N, v);
+        continue;
+      }
+      const int sub = uu % subs;
+      uint8_t* sbuf = stage;
+      if (sub == 0) {
+        // The previous chunk's TMA store must have finished reading the staging buffer.
+        if (lane == 0) bulk_wait_read<0>();
+        __syncwarp();
+      }
+      uint32_t w[32];
+      epi_pack(ep, v, w);
+      // swizzled staging row: 128B pattern (granule ^ row%8) or 64B (granule ^ (row/2)%4)
+      uint8_t* rowp = sbuf + lane * cb;
+      const int sw = (cb == 128) ? (lane & 7) : ((lane >> 1) & 3);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        if (q < g) {
+          const int gi = sub * g + q;
+          *reinterpret_cast<uint4*>(rowp + ((gi ^ sw) << 4)) =
+              make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
         }
       }
+      if (sub == subs - 1 || uu == units - 1) {
+        fence_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(tmap_out, sbuf, (col_base + (uu - sub) * 32) * esz, row0);
+          bulk_commit();
+        }
+        buf ^= 1;
+      }
     }
-    fence_async_shared();
-    __syncwarp();
-#if !defined(B2F_EXP) || B2F_EXP != 4
-    if (lane == 0) {
-      tma_store_2d(tmap_out, sbuf, (col_base + c0) * esz, row0);
-      bulk_commit();
-    }
-#endif
-    buf ^= 1;
   }
 }
 
 template <int BN>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     const __grid_constant__ CUtensorMap tmap_b,
                     const __grid_constant__ CUtensorMap tmap_out, const GemmShape shape,
@@ -342,7 +344,7 @@ __global__ void __launch_bounds__(192, 1)
                                              ~uintptr_t(1023));
   uint8_t* smem_a = smem;
   uint8_t* smem_b = smem + STAGES * Cfg::A_BYTES;
-  uint8_t* smem_stage = smem + STAGES * Cfg::STAGE_BYTES;  // 4 warps x 2 x 4 KB
+  uint8_t* smem_stage = smem + STAGES * Cfg::STAGE_BYTES;  // 8 warps x 4 KB
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem_stage + 4 * 8192);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;   // [2]
@@ -366,7 +368,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 4);
+      mbar_init(&tempty_bar[a], 8);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -468,7 +470,9 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     // -------------------------------------------------------------- epilogue
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
-    uint8_t* stage = smem_stage + (warp - 2) * 8192;
+    const int ew = warp - 2;                 // epilogue warp 0..7
+    const int chalf = ew >> 2;               // which half of the tile's columns
+    uint8_t* stage = smem_stage + ew * 4096;
     int buf = 0;
     float alpha = ep.alpha;
     if (ep.alpha_ptr != nullptr) alpha *= *ep.alpha_ptr;
@@ -488,9 +492,9 @@ __global__ void __launch_bounds__(192, 1)
       const int row0 = mb * Cfg::BM + q * 32;
       const int row = row0 + lane;
       float rowsum = 0.0f;
-      const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
-      epilogue_tile<BN>(ep, &tmap_out, alpha, t_row, row, row0, nb * BN, M, N, stage, buf,
-                        rowsum, amax_local);
+      const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + acc * BN + chalf * (BN / 2);
+      epilogue_tile<BN / 2>(ep, &tmap_out, alpha, t_row, row, row0, nb * BN + chalf * (BN / 2),
+                            M, N, stage, buf, rowsum, amax_local);
       tc_fence_before();
       __syncwarp();
       if (warp == 2 && lane == 0) B2F_STAMP(it, 4);
@@ -532,10 +536,10 @@ struct Gemm2Cfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 4 * 8192 + 1024 + 256;
-  static constexpr int THREADS = 192;
+  static constexpr int THREADS = 320;  // producer, MMA, 8 epilogue warps
 };
 
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
     gemm_fp8_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                          const __grid_constant__ CUtensorMap tmap_b,
                          const __grid_constant__ CUtensorMap tmap_out, const GemmShape shape,
@@ -548,7 +552,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
                                              ~uintptr_t(1023));
   uint8_t* smem_a = smem;
   uint8_t* smem_b = smem + STAGES * Cfg::A_BYTES;
-  uint8_t* smem_stage = smem + STAGES * Cfg::STAGE_BYTES;  // 4 warps x 2 x 4 KB
+  uint8_t* smem_stage = smem + STAGES * Cfg::STAGE_BYTES;  // 8 warps x 4 KB
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem_stage + 4 * 8192);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;  // [2]
@@ -575,7 +579,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 8);
+      mbar_init(&tempty_bar[a], 16);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -669,7 +673,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
   } else {
     // -------------------------------------------------------------- epilogue (both CTAs)
     const int q = warp & 3;
-    uint8_t* stage = smem_stage + (warp - 2) * 8192;
+    const int ew = warp - 2;                 // epilogue warp 0..7
+    const int chalf = ew >> 2;               // which half of the tile's columns
+    uint8_t* stage = smem_stage + ew * 4096;
     int buf = 0;
     float alpha = ep.alpha;
     if (ep.alpha_ptr != nullptr) alpha *= *ep.alpha_ptr;
@@ -688,9 +694,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       const int row0 = mb * 2 * Cfg::BM + rank * Cfg::BM + q * 32;
       const int row = row0 + lane;
       float rowsum = 0.0f;
-      const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + acc * BN;
-      epilogue_tile<BN>(ep, &tmap_out, alpha, t_row, row, row0, nb * BN, M, N, stage, buf,
-                        rowsum, amax_local);
+      const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + acc * BN + chalf * (BN / 2);
+      epilogue_tile<BN / 2>(ep, &tmap_out, alpha, t_row, row, row0, nb * BN + chalf * (BN / 2),
+                            M, N, stage, buf, rowsum, amax_local);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(map_to_rank(&tempty_bar[acc], 0));

@@ -104,8 +104,9 @@ def test_gemm_rowsum_level2_14():
     assert err < 1e-3 * (1 + ref.abs().max().item()), err
 
 
+@pytest.mark.parametrize("tile_n", [0, 128, 256, 512])
 @pytest.mark.parametrize("res_dtype", [torch.bfloat16, torch.float32])
-def test_gemm_residual_requant_e4m3(res_dtype):
+def test_gemm_residual_requant_e4m3(res_dtype, tile_n):
     m, n, k = 512, 768, 768
     g = gen(20260801)
     a, sa = fp8_amax((m, k), g)
@@ -118,7 +119,7 @@ def test_gemm_residual_requant_e4m3(res_dtype):
     amax = torch.zeros(1, device="cuda")
     out = _ops().gemm_fp8(a.cuda(), b.cuda(), scale_a=sa, scale_b=sb, bias=bias.cuda(),
                           residual=res.cuda(), out_dtype=torch.float8_e4m3fn,
-                          out_scale=out_scale, amax=amax)
+                          out_scale=out_scale, amax=amax, tile_n=tile_n)
     torch.cuda.synchronize()
     d = e4m3_ulp_diff(out.cpu(), ref_q)
     assert int(d.max()) <= 1
