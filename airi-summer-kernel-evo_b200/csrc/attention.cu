@@ -391,9 +391,430 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// ---------------------------------------------------------------------------------------
+// Two query tiles per CTA (head_dim 64 / 128).  Query tiles A and B of the same (sequence,
+// head) share every K/V tile; softmax warpgroup A (warps 2-5) and B (warps 6-9) alternate
+// with the tensor core: while A exponentiates S_A(j) the MMA warp runs S_B(j) and
+// P_B(j-1).V, and vice versa.  With causal masking the pair is (i, n-1-i), so every CTA
+// walks n+1 key tiles in total (balanced grid); without masking it is (2c, 2c+1).
+// TMEM: S_A | S_B | O_A | O_B.  P_A, P_B live in shared memory (bf16, 128B swizzle).
+#ifdef B2F_TRACE
+// Debug-only timeline of attention2: [cta][key step][slot] globaltimer stamps.
+__device__ unsigned long long g_atrace[8][16][8];
+#define B2F_ASTAMP(j, slot)                                                         \
+  do {                                                                              \
+    const int _cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z); \
+    if (_cta < 8 && (j) < 16) g_atrace[_cta][(j)][(slot)] = globaltimer();           \
+  } while (0)
+#else
+#define B2F_ASTAMP(j, slot) do {} while (0)
+#endif
+
+__device__ __forceinline__ float ex2_hw(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 template <int D>
+struct Attn2Cfg {
+  static constexpr int BQ = 128;
+  static constexpr int BKV = 128;
+  static constexpr int ST = 2;
+  static constexpr int ROWB = (D >= 128) ? 128 : D;
+  static constexpr int KB = (D >= 128) ? D / 128 : 1;
+  static constexpr uint32_t LAYOUT8 = (ROWB == 128) ? 2u : 4u;
+  static constexpr uint32_t SBO8 = 8 * ROWB;
+  static constexpr int Q_BYTES = BQ * D;  // per query tile
+  static constexpr int K_BYTES = BKV * D;
+  static constexpr int V_BYTES = BKV * D * 2;
+  static constexpr int P_BYTES = BQ * BKV * 2;  // per query tile
+  static constexpr int STAGE_BYTES = K_BYTES + V_BYTES;
+  static constexpr int SMEM_BYTES = 2 * Q_BYTES + ST * STAGE_BYTES + 2 * P_BYTES + 1024 + 512;
+  static constexpr int S_COL = 0;             // S_X at X * BKV
+  static constexpr int O_COL = 2 * BKV;       // O_X at O_COL + X * D
+  static constexpr int TMEM_COLS = 512;
+  static_assert(D > 128 || 2 * BKV + 2 * D <= 512, "TMEM budget");
+};
+
+template <int D>
+__global__ void __launch_bounds__(320, 1)
+    attention2_kernel(const __grid_constant__ CUtensorMap tm_q,
+                      const __grid_constant__ CUtensorMap tm_k,
+                      const __grid_constant__ CUtensorMap tm_v, const AttnParams p) {
+  using C = Attn2Cfg<D>;
+  constexpr int BQ = C::BQ, BKV = C::BKV, ST = C::ST;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* sq = smem;                            // [2][Q_BYTES]
+  uint8_t* skv = sq + 2 * C::Q_BYTES;            // [ST][K | V]
+  uint8_t* sp = skv + ST * C::STAGE_BYTES;       // [2][P_BYTES]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sp + 2 * C::P_BYTES);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = kv_full + ST;
+  uint64_t* s_full = kv_empty + ST;  // [2] per query tile
+  uint64_t* s_free = s_full + 2;
+  uint64_t* p_full = s_free + 2;
+  uint64_t* pv_done = p_full + 2;
+  uint64_t* drain = pv_done + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_qt = (p.seq + BQ - 1) / BQ;
+  int qt[2];
+  bool act[2];
+  if (p.causal) {
+    qt[0] = blockIdx.x;
+    qt[1] = n_qt - 1 - blockIdx.x;
+  } else {
+    qt[0] = 2 * blockIdx.x;
+    qt[1] = min(2 * (int)blockIdx.x + 1, n_qt - 1);
+  }
+  act[1] = true;
+  act[0] = qt[0] < qt[1];
+  int nkv[2];
+#pragma unroll
+  for (int x = 0; x < 2; ++x) {
+    const int end = p.causal ? min(p.seq, qt[x] * BQ + BQ) : p.seq;
+    nkv[x] = act[x] ? (end + BKV - 1) / BKV : 0;
+  }
+  const int h = blockIdx.y;
+  const int b = blockIdx.z;
+  const int hk = h / (p.hq / p.hkv);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&pv_done[i], 1);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------------------------- producer
+      const uint64_t pol = policy_evict_last();
+      mbar_arrive_expect_tx(q_full, (act[0] ? 2 : 1) * C::Q_BYTES);
+      for (int x = 0; x < 2; ++x) {
+        if (!act[x]) continue;
+        for (int kb = 0; kb < C::KB; ++kb)
+          tma_load_3d(sq + x * C::Q_BYTES + kb * BQ * C::ROWB, &tm_q, q_full, h * D + kb * 128,
+                      qt[x] * BQ, b, pol);
+      }
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      for (int j = 0; j < nkv[1]; ++j) {
+        if (!mbar_wait(&kv_empty[stage], phase ^ 1, kDevTimeoutProducer, abort_flag)) break;
+        uint8_t* sk = skv + stage * C::STAGE_BYTES;
+        uint8_t* sv = sk + C::K_BYTES;
+        mbar_arrive_expect_tx(&kv_full[stage], C::STAGE_BYTES);
+        for (int kb = 0; kb < C::KB; ++kb)
+          tma_load_3d(sk + kb * BKV * C::ROWB, &tm_k, &kv_full[stage], hk * D + kb * 128,
+                      j * BKV, b, pol);
+        for (int vb = 0; vb < D / 64; ++vb)
+          tma_load_3d(sv + vb * BKV * 128, &tm_v, &kv_full[stage], hk * D + vb * 64, j * BKV, b,
+                      pol);
+        ++issued;
+        if (++stage == ST) { stage = 0; phase ^= 1; }
+      }
+      const int pending = issued < ST ? issued : ST;
+      for (int i = 0; i < pending; ++i) {
+        if (--stage < 0) { stage = ST - 1; phase ^= 1; }
+        const uint64_t t0 = globaltimer();
+        while (!mbar_test(&kv_full[stage], phase))
+          if (globaltimer() - t0 > B2F_WAIT_NS) { record_error(kDevTimeoutDrain); break; }
+      }
+      {
+        const uint64_t t0 = globaltimer();
+        while (!mbar_test(q_full, 0))
+          if (globaltimer() - t0 > B2F_WAIT_NS) { record_error(kDevTimeoutDrain); break; }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------------------------------------------------------- MMA issuer
+      constexpr uint32_t idesc_s = make_idesc_f8(BQ, BKV);
+      constexpr uint32_t idesc_pv = make_idesc_bf16(BQ, D, 1);
+      bool ok = mbar_wait(q_full, 0, kDevTimeoutMma, abort_flag);
+      auto issue_s = [&](int x, int j) -> bool {
+        const int st = j % ST;
+        if (!mbar_wait(&kv_full[st], (j / ST) & 1, kDevTimeoutMma, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t q_addr = smem_u32(sq + x * C::Q_BYTES);
+        const uint32_t k_addr = smem_u32(skv + st * C::STAGE_BYTES);
+#pragma unroll
+        for (int kb = 0; kb < C::KB; ++kb) {
+#pragma unroll
+          for (int k = 0; k < C::ROWB / 32; ++k) {
+            const uint64_t ad =
+                make_sdesc(q_addr + kb * BQ * C::ROWB + k * 32, C::LAYOUT8, 16, C::SBO8);
+            const uint64_t bd =
+                make_sdesc(k_addr + kb * BKV * C::ROWB + k * 32, C::LAYOUT8, 16, C::SBO8);
+            mma_f8(tmem + C::S_COL + x * BKV, ad, bd, idesc_s, (kb | k) != 0);
+          }
+        }
+        mma_commit(&s_full[x]);
+        return true;
+      };
+      auto issue_pv = [&](int x, int j) -> bool {
+        if (!mbar_wait(&p_full[x], j & 1, kDevTimeoutMma, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t p_addr = smem_u32(sp + x * C::P_BYTES);
+        const uint32_t v_addr = smem_u32(skv + (j % ST) * C::STAGE_BYTES + C::K_BYTES);
+#pragma unroll
+        for (int kb = 0; kb < BKV / 64; ++kb) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t ad = make_sdesc(p_addr + kb * BQ * 128 + k * 32, 2, 16, 1024);
+            const uint64_t bd = make_sdesc(v_addr + (kb * 4 + k) * 2048, 2, BKV * 128, 1024);
+            mma_bf16(tmem + C::O_COL + x * D, ad, bd, idesc_pv, (j | kb | k) != 0);
+          }
+        }
+        mma_commit(&pv_done[x]);
+        return true;
+      };
+      if (ok && act[0]) ok = issue_s(0, 0);
+      if (ok) ok = issue_s(1, 0);
+      for (int j = 0; j < nkv[1] && ok; ++j) {
+        if (j < nkv[0]) {
+          if (!(ok = issue_pv(0, j))) break;
+          if (j + 1 < nkv[0]) {
+            if (!(ok = mbar_wait(&s_free[0], j & 1, kDevTimeoutMma, abort_flag))) break;
+            if (!(ok = issue_s(0, j + 1))) break;
+          }
+        }
+        if (!(ok = issue_pv(1, j))) break;
+        mma_commit(&kv_empty[j % ST]);  // both P.V of this key tile issued before it
+        if (j + 1 < nkv[1]) {
+          if (!(ok = mbar_wait(&s_free[1], j & 1, kDevTimeoutMma, abort_flag))) break;
+          if (!(ok = issue_s(1, j + 1))) break;
+        }
+      }
+      mma_commit(drain);
+      const uint64_t t0 = globaltimer();
+      while (!mbar_test(drain, 0))
+        if (globaltimer() - t0 > B2F_WAIT_NS) { record_error(kDevTimeoutDrain); break; }
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax + epilogue
+    const int x = (warp - 2) >> 2;   // query tile handled by this warpgroup
+    const int qd = warp & 3;         // TMEM lane quadrant
+    const int r = qd * 32 + lane;
+    const int q0 = qt[x] * BQ;
+    const int qi = q0 + r;
+    const uint32_t t_lane = tmem + (uint32_t(qd * 32) << 16);
+    const uint32_t s_col = C::S_COL + x * BKV;
+    const uint32_t o_col = C::O_COL + x * D;
+    uint8_t* px = sp + x * C::P_BYTES;
+    const float c = p.qk_scale_log2;
+    float m_used = -INFINITY;
+    float l = 0.f;
+    bool ok = act[x];
+    for (int j = 0; j < nkv[x] && ok; ++j) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[x], j & 1, kDevTimeoutEpilogue, abort_flag));
+      if (!ok) break;
+      if (lane == 0 && (warp == 2 || warp == 6)) B2F_ASTAMP(j, x * 4 + 0);
+      tc_fence_after();
+      const int k0 = j * BKV;
+      // keys k0 + kk with kk > klim are masked (past the sequence end or, causal, past qi)
+      const int klim = min(p.seq - 1, p.causal ? qi : p.seq - 1) - k0;
+      const bool need_mask = klim < BKV - 1;
+      // pass 1 over S (TMEM -> registers, 32 columns at a time, next load in flight while
+      // the current chunk reduces): row max in log2 units, 8 independent partial maxima
+      float mp[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) mp[e] = -INFINITY;
+      {
+        uint32_t ra[32], rb[32];
+        tmem_ld32_async(t_lane + s_col, ra);
+#pragma unroll
+        for (int cc = 0; cc < BKV; cc += 32) {
+          uint32_t (&cur)[32] = ((cc / 32) & 1) ? rb : ra;
+          uint32_t (&nxt)[32] = ((cc / 32) & 1) ? ra : rb;
+          tmem_ld_wait_regs(cur);
+          if (cc + 32 < BKV) tmem_ld32_async(t_lane + s_col + cc + 32, nxt);
+#pragma unroll
+          for (int u = 0; u < 32; ++u) {
+            float v = __uint_as_float(cur[u]);
+            if (need_mask && cc + u > klim) v = -INFINITY;
+            mp[u & 7] = fmaxf(mp[u & 7], v);
+          }
+        }
+      }
+      float mt = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
+                       fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7]))) * c;
+      float corr = 1.0f;
+      bool rescale = false;
+      if (mt > m_used + 8.0f) {
+        if (m_used != -INFINITY) {
+          corr = ex2_hw(m_used - mt);
+          rescale = true;
+        }
+        m_used = mt;
+      }
+      const float mref = (m_used == -INFINITY) ? 0.0f : m_used;
+      if (lane == 0 && (warp == 2 || warp == 6)) B2F_ASTAMP(j, x * 4 + 1);
+      if (j > 0) {
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait(&pv_done[x], (j - 1) & 1, kDevTimeoutEpilogue, abort_flag));
+        if (!ok) break;
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+          for (int cc = 0; cc < D; cc += 16) {
+            uint32_t o[16];
+            tmem_ld16(t_lane + o_col + cc, o);
+#pragma unroll
+            for (int u = 0; u < 16; ++u) o[u] = __float_as_uint(__uint_as_float(o[u]) * corr);
+            tmem_st16(t_lane + o_col + cc, o);
+          }
+          tmem_st_wait();
+        }
+      }
+      if (lane == 0 && (warp == 2 || warp == 6)) B2F_ASTAMP(j, x * 4 + 2);
+      // pass 2: P = 2^(S*c - m) rounded to bf16, streamed into shared memory
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};
+      {
+        uint32_t ra[32], rb[32];
+        tmem_ld32_async(t_lane + s_col, ra);
+#pragma unroll
+        for (int cc = 0; cc < BKV; cc += 32) {
+          uint32_t (&cur)[32] = ((cc / 32) & 1) ? rb : ra;
+          uint32_t (&nxt)[32] = ((cc / 32) & 1) ? ra : rb;
+          tmem_ld_wait_regs(cur);
+          if (cc + 32 < BKV) tmem_ld32_async(t_lane + s_col + cc + 32, nxt);
+#pragma unroll
+          for (int gq = 0; gq < 4; ++gq) {
+            uint32_t w4[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int u = gq * 8 + 2 * e;
+              float v0 = fmaf(__uint_as_float(cur[u]), c, -mref);
+              float v1 = fmaf(__uint_as_float(cur[u + 1]), c, -mref);
+              if (need_mask) {
+                if (cc + u > klim) v0 = -INFINITY;
+                if (cc + u + 1 > klim) v1 = -INFINITY;
+              }
+              const float e0 = ex2_hw(v0), e1 = ex2_hw(v1);
+              const __nv_bfloat162 bb = __floats2bfloat162_rn(e0, e1);
+              // row sum from the f32 weights: the P.V MMA sees them rounded to bf16
+              // (relative 2^-9 per weight, averaging out over the row)
+              ls[e] += e0 + e1;
+              w4[e] = *reinterpret_cast<const uint32_t*>(&bb);
+            }
+            const int g = (cc >> 3) + gq;  // 16-byte granule index along the key row
+            const int kb = g >> 3, gi = g & 7;
+            *reinterpret_cast<uint4*>(px + kb * BQ * 128 + r * 128 + ((gi ^ (r & 7)) << 4)) =
+                make_uint4(w4[0], w4[1], w4[2], w4[3]);
+          }
+        }
+      }
+      const float lt = (ls[0] + ls[1]) + (ls[2] + ls[3]);
+      l = l * corr + lt;
+      fence_async_shared();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&s_free[x]);
+        mbar_arrive(&p_full[x]);
+      }
+      if (lane == 0 && (warp == 2 || warp == 6)) B2F_ASTAMP(j, x * 4 + 3);
+    }
+    // ---------------------------------------------------------------- epilogue
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[x], (nkv[x] - 1) & 1,
+                                                  kDevTimeoutEpilogue, abort_flag));
+    if (ok) {
+      tc_fence_after();
+      const long long row = (long long)b * p.seq + qi;
+      const bool valid = qi < p.seq;
+      const float inv_l = (l > 0.f) ? p.v_scale / l : 0.f;
+#pragma unroll 1
+      for (int cc = 0; cc < D; cc += 32) {
+        uint32_t o[32];
+        tmem_ld32(t_lane + o_col + cc, o);
+        if (!valid) continue;
+        float v[32];
+#pragma unroll
+        for (int u = 0; u < 32; ++u) v[u] = __uint_as_float(o[u]) * inv_l;
+        if (p.gate != nullptr) {
+          const long long go = row * p.gate_ld + (long long)h * p.gate_hstride + cc;
+          if (p.gate_dtype == kE4M3) {
+            const uint8_t* gp = reinterpret_cast<const uint8_t*>(p.gate) + go;
+#pragma unroll
+            for (int u = 0; u < 32; u += 16) {
+              const uint4 qv = *reinterpret_cast<const uint4*>(gp + u);
+              const uint32_t w[4] = {qv.x, qv.y, qv.z, qv.w};
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                const float2 a = e4m3x2_to_f32x2(w[t] & 0xFFFF);
+                const float2 bb = e4m3x2_to_f32x2(w[t] >> 16);
+                const float gv[4] = {a.x, a.y, bb.x, bb.y};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float gg = gv[e] * p.gate_scale;
+                  v[u + 4 * t + e] *= 1.0f / (1.0f + expf(-gg));
+                }
+              }
+            }
+          } else {
+            const __nv_bfloat16* gp = reinterpret_cast<const __nv_bfloat16*>(p.gate) + go;
+#pragma unroll
+            for (int u = 0; u < 32; ++u) {
+              const float gg = __bfloat162float(gp[u]) * p.gate_scale;
+              v[u] *= 1.0f / (1.0f + expf(-gg));
+            }
+          }
+        }
+        uint32_t w[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t)
+          w[t] = uint32_t(f32x2_to_e4m3x2(v[4 * t] * p.ctx_inv_scale,
+                                          v[4 * t + 1] * p.ctx_inv_scale)) |
+                 (uint32_t(f32x2_to_e4m3x2(v[4 * t + 2] * p.ctx_inv_scale,
+                                           v[4 * t + 3] * p.ctx_inv_scale))
+                  << 16);
+        uint8_t* dst = p.ctx + row * p.ctx_ld + (long long)h * D + cc;
+        *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(dst + 16) = make_uint4(w[4], w[5], w[6], w[7]);
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+template <int D, bool PAIR>
 int launch_attention(const b2f_attn_args* a, cudaStream_t stream) {
   using C = AttnCfg<D>;
+  constexpr int BKV = PAIR ? Attn2Cfg<D>::BKV : C::BKV;
+  constexpr int SMEM = PAIR ? Attn2Cfg<D>::SMEM_BYTES : C::SMEM_BYTES;
   CUtensorMap tq, tk, tv;
   std::string err;
   const CUtensorMapSwizzle sw8 =
@@ -412,7 +833,7 @@ int launch_attention(const b2f_attn_args* a, cudaStream_t stream) {
                                         (unsigned long long)a->batch};
     const unsigned long long strides[2] = {(unsigned long long)a->k_ld,
                                            (unsigned long long)a->k_ld * a->seq};
-    const unsigned int box[3] = {(unsigned int)C::ROWB, (unsigned int)C::BKV, 1};
+    const unsigned int box[3] = {(unsigned int)C::ROWB, (unsigned int)BKV, 1};
     if (!encode_tmap(&tk, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, a->k, dims, strides, box, sw8, &err))
       return fail(B2F_ERR_ARG, "attention: K tensor map: " + err);
   }
@@ -421,7 +842,7 @@ int launch_attention(const b2f_attn_args* a, cudaStream_t stream) {
                                         (unsigned long long)a->batch};
     const unsigned long long strides[2] = {(unsigned long long)a->v_ld * 2,
                                            (unsigned long long)a->v_ld * 2 * a->seq};
-    const unsigned int box[3] = {64, (unsigned int)C::BKV, 1};
+    const unsigned int box[3] = {64, (unsigned int)BKV, 1};
     if (!encode_tmap(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a->v, dims, strides, box,
                      CU_TENSOR_MAP_SWIZZLE_128B, &err))
       return fail(B2F_ERR_ARG, "attention: V tensor map: " + err);
@@ -436,17 +857,28 @@ int launch_attention(const b2f_attn_args* a, cudaStream_t stream) {
   p.ctx = reinterpret_cast<uint8_t*>(a->ctx); p.ctx_ld = a->ctx_ld;
   p.ctx_inv_scale = 1.0f / a->ctx_scale;
   p.v_scale = a->v_scale;
-  static thread_local int attr_dev[3] = {-1, -1, -1};
+  static thread_local int attr_dev[2][3] = {{-1, -1, -1}, {-1, -1, -1}};
   const int slot = D == 64 ? 0 : (D == 128 ? 1 : 2);
   int dev = 0;
   B2F_CUDA_TRY(cudaGetDevice(&dev));
-  if (attr_dev[slot] != dev) {
-    B2F_CUDA_TRY(cudaFuncSetAttribute(attention_kernel<D>,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
-    attr_dev[slot] = dev;
+  const int n_qt = (a->seq + C::BQ - 1) / C::BQ;
+  if constexpr (PAIR) {
+    if (attr_dev[1][slot] != dev) {
+      B2F_CUDA_TRY(cudaFuncSetAttribute(attention2_kernel<D>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+      attr_dev[1][slot] = dev;
+    }
+    dim3 grid((n_qt + 1) / 2, a->hq, a->batch);
+    attention2_kernel<D><<<grid, 320, SMEM, stream>>>(tq, tk, tv, p);
+  } else {
+    if (attr_dev[0][slot] != dev) {
+      B2F_CUDA_TRY(cudaFuncSetAttribute(attention_kernel<D>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+      attr_dev[0][slot] = dev;
+    }
+    dim3 grid(n_qt, a->hq, a->batch);
+    attention_kernel<D><<<grid, 192, SMEM, stream>>>(tq, tk, tv, p);
   }
-  dim3 grid((a->seq + C::BQ - 1) / C::BQ, a->hq, a->batch);
-  attention_kernel<D><<<grid, 192, C::SMEM_BYTES, stream>>>(tq, tk, tv, p);
   B2F_CUDA_TRY(cudaGetLastError());
   return B2F_OK;
 }
@@ -455,6 +887,18 @@ bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 }  // namespace
 }  // namespace b2f
+
+#ifdef B2F_TRACE
+extern "C" int b2f_atrace_read(void* host, unsigned long long bytes, int reset) {
+  if (bytes > sizeof(b2f::g_atrace)) bytes = sizeof(b2f::g_atrace);
+  if (cudaMemcpyFromSymbol(host, b2f::g_atrace, bytes) != cudaSuccess) return -1;
+  if (reset) {
+    static unsigned long long zeros[8 * 16 * 8] = {};
+    cudaMemcpyToSymbol(b2f::g_atrace, zeros, sizeof(zeros));
+  }
+  return 0;
+}
+#endif
 
 extern "C" {
 
@@ -495,9 +939,9 @@ int b2f_attention_fp8(const b2f_attn_args* a, b2f_stream_t stream) {
   }
   if (!(a->ctx_scale > 0.f)) return fail(B2F_ERR_ARG, "attention: ctx_scale must be > 0");
   cudaStream_t s = (cudaStream_t)stream;
-  if (d == 64) return launch_attention<64>(a, s);
-  if (d == 128) return launch_attention<128>(a, s);
-  return launch_attention<256>(a, s);
+  if (d == 64) return launch_attention<64, true>(a, s);
+  if (d == 128) return launch_attention<128, true>(a, s);
+  return launch_attention<256, false>(a, s);
 }
 
 }  // extern "C"
