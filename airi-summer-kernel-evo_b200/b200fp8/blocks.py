@@ -75,9 +75,14 @@ class GPT2Block(_Graphable):
     launches_per_forward = 8
 
     def __init__(self, w, *, batch: int, seq: int, residual_dtype=torch.float32,
-                 out_dtype=torch.float32, device="cuda"):
+                 out_dtype=torch.float32, device="cuda", causal: bool = True,
+                 rope_cos: Optional[torch.Tensor] = None,
+                 rope_sin: Optional[torch.Tensor] = None):
+        """``rope_cos/rope_sin`` [seq, head_dim] and ``causal=False`` give the Qwen vision
+        block (tasks/model_qwen35_4b_vision_block_fp8): RoPE on q, k, non-causal."""
         self.batch, self.seq = batch, seq
         self.t = batch * seq
+        self.causal = causal
         self.heads = w.heads
         self.d = w.qkv_w.shape[1]
         self.hd = self.d // self.heads
@@ -101,12 +106,19 @@ class GPT2Block(_Graphable):
         self.n2 = torch.empty((t, d), device=device, dtype=_E4M3)
         self.h = torch.empty((t, self.mlp), device=device, dtype=_E4M3)
         self.out = torch.empty((t, d), device=device, dtype=out_dtype)
+        self.rope = rope_cos is not None
+        if self.rope:
+            self.cos = _dev(rope_cos[:seq], device, f32)
+            self.sin = _dev(rope_sin[:seq], device, f32)
+            self.q_rot = torch.empty((t, d), device=device, dtype=_E4M3)
+            self.k_rot = torch.empty((t, d), device=device, dtype=_E4M3)
+            self.launches_per_forward = 10
         self._init_graph()
 
     def flops(self) -> float:
         t, d, m, s = self.t, self.d, self.mlp, self.seq
         gemm = 2 * t * (3 * d * d + d * d + 2 * d * m)
-        attn = 2 * self.batch * self.heads * s * s * self.hd  # causal half of 4*S^2*D
+        attn = (2 if self.causal else 4) * self.batch * self.heads * s * s * self.hd
         return float(gemm + attn)
 
     def forward(self, hidden: torch.Tensor, hidden_scale: float = 1.0) -> torch.Tensor:
@@ -116,8 +128,16 @@ class GPT2Block(_Graphable):
         ops.gemm_fp8(self.n1, self.qkv_w, scale_a=self.ns, scale_b=self.qkv_s, bias=self.qkv_b,
                      out=self.qkv, out_scale=self.qs)
         ops.fp8_to_bf16(self.qkv[:, 2 * d:], out=self.v16)
-        ops.attention_fp8(self.qkv[:, :d], self.qkv[:, d:2 * d], self.v16, batch=self.batch,
-                          heads=self.heads, kv_heads=self.heads, head_dim=self.hd, causal=True,
+        q, k = self.qkv[:, :d], self.qkv[:, d:2 * d]
+        if self.rope:
+            for src, dst in ((q, self.q_rot), (k, self.k_rot)):
+                ops.head_norm_rope(src, heads=self.heads, head_dim=self.hd, in_scale=self.qs,
+                                   out_scale=self.qs, cos=self.cos, sin=self.sin,
+                                   rotary_dim=self.hd, seq=self.seq, out=dst)
+            q, k = self.q_rot, self.k_rot
+        ops.attention_fp8(q, k, self.v16, batch=self.batch,
+                          heads=self.heads, kv_heads=self.heads, head_dim=self.hd,
+                          causal=self.causal,
                           q_scale=self.qs, k_scale=self.qs, v_scale=self.qs, ctx=self.ctx,
                           ctx_scale=self.cs)
         ops.gemm_fp8(self.ctx, self.out_w, scale_a=self.cs, scale_b=self.out_s, bias=self.out_b,

@@ -71,15 +71,27 @@ class GPT2Weights:
 
 def gpt2_block(x: torch.Tensor, w: GPT2Weights, *, batch: int,
                residual_dtype: torch.dtype = torch.float32,
-               out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
-    """x: f32 values of the hidden input [T, d] (already dequantised).  Returns f32."""
+               out_dtype: torch.dtype = torch.float32, causal: bool = True,
+               rope_cos: Optional[torch.Tensor] = None,
+               rope_sin: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """x: f32 values of the hidden input [T, d] (already dequantised).  Returns f32.
+
+    With ``rope_cos/rope_sin`` [T, head_dim] and ``causal=False`` this is the Qwen vision
+    block (tasks/model_qwen35_4b_vision_block_fp8/starter.py:303-369): rotate-half RoPE on
+    q and k after the QKV requantisation, q/k requantised again, non-causal attention."""
     t, d = x.shape
     hd = d // w.heads
     n1 = F.layer_norm(x, (d,), w.ln1_w.float(), w.ln1_b.float(), w.eps)
     n1_q = _q(n1, w.norm_scale)
     qkv = scaled_mm(n1_q, w.qkv_w, w.norm_scale, w.qkv_s) + w.qkv_b.float()
     qkv_d = _dq(_q(qkv, w.qkv_scale), w.qkv_scale).view(t, 3, w.heads, hd)
-    ctx = oatt.attention(qkv_d[:, 0], qkv_d[:, 1], qkv_d[:, 2], batch=batch, causal=True)
+    q, k, v = qkv_d[:, 0], qkv_d[:, 1], qkv_d[:, 2]
+    if rope_cos is not None:
+        q = _dq(_q(oatt.head_rmsnorm_rope(q, None, rope_cos, rope_sin, hd), w.qkv_scale),
+                w.qkv_scale)
+        k = _dq(_q(oatt.head_rmsnorm_rope(k, None, rope_cos, rope_sin, hd), w.qkv_scale),
+                w.qkv_scale)
+    ctx = oatt.attention(q, k, v, batch=batch, causal=causal)
     ctx_q = _q(ctx.reshape(t, d), w.ctx_scale)
     r1 = _round(x + scaled_mm(ctx_q, w.out_w, w.ctx_scale, w.out_s) + w.out_b.float(),
                 residual_dtype)
