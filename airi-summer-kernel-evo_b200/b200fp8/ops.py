@@ -42,6 +42,24 @@ def _check_cuda(*tensors: Optional[torch.Tensor]) -> None:
             raise ValueError("b200fp8 ops take CUDA tensors only (no CPU fallback)")
 
 
+_WORKSPACES = {}
+
+
+def gemm_workspace(m: int, n: int, device) -> torch.Tensor:
+    """Split-K workspace for an m x n GEMM output on ``device``: zero-filled once (its tile
+    counters must start at zero; every call leaves them zero), cached per device and grown
+    on demand.  One workspace per device means split-K GEMMs on one device must not
+    overlap in time (the library issues them on the caller's single stream)."""
+    need = int(_lib.lib().b2f_gemm_workspace_bytes(m, n))
+    dev = torch.device(device)
+    key = dev.index if dev.index is not None else torch.cuda.current_device()
+    ws = _WORKSPACES.get(key)
+    if ws is None or ws.numel() < need:
+        ws = torch.zeros((max(need, 1 << 20),), dtype=torch.uint8, device=dev)
+        _WORKSPACES[key] = ws
+    return ws
+
+
 def _fp8_rows(t: torch.Tensor, name: str) -> None:
     if t.dtype not in (torch.float8_e4m3fn, torch.uint8):
         raise TypeError(f"{name} must be float8_e4m3fn (or its uint8 storage)")
@@ -58,11 +76,14 @@ def gemm_fp8(a: torch.Tensor, b_nk: torch.Tensor, *, scale_a: float = 1.0,
              residual_scale: float = 1.0, out: Optional[torch.Tensor] = None,
              out_dtype: torch.dtype = torch.bfloat16, out_scale: float = 1.0,
              amax: Optional[torch.Tensor] = None, rowsum: bool = False,
-             tile_n: int = 0) -> torch.Tensor:
+             tile_n: int = 0, splits: Optional[int] = None,
+             workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
     """out = epilogue(scale_a*scale_b * A . B_nk^T)  (see b2f_gemm_fp8).
 
     ``out_scale`` is the quantisation scale of an e4m3 output (stored = v / out_scale).
     With ``rowsum=True`` the output is f32 [M] holding sum over columns of v / out_scale.
+    ``splits`` > 1 selects split-K with that many K slices (using ``workspace`` or the cached
+    one of :func:`gemm_workspace`); None / 1 = off.
     """
     _check_cuda(a, b_nk, bias, residual, out, amax, alpha_tensor, col_scale)
     _fp8_rows(a, "a")
@@ -110,6 +131,10 @@ def gemm_fp8(a: torch.Tensor, b_nk: torch.Tensor, *, scale_a: float = 1.0,
     args.amax = _ptr(amax)
     args.mode = _lib.GEMM_ROWSUM if rowsum else _lib.GEMM_STORE
     args.tile_n = tile_n
+    args.splits = 0 if splits is None else int(splits)
+    if splits is not None and splits > 1:
+        ws = workspace if workspace is not None else gemm_workspace(m, n, a.device)
+        args.workspace, args.workspace_bytes = ws.data_ptr(), ws.numel() * ws.element_size()
     check(_lib.lib().b2f_gemm_fp8(ctypes.byref(args), _stream()))
     return out
 

@@ -9,7 +9,15 @@ namespace b2f {
 
 namespace {
 
-thread_local int g_pair_capacity = 0;  // co-resident CTA pairs seen by the last pair launch
+thread_local int g_pair_capacity = 0;
+}  // namespace
+constexpr int kMaxSplits = 8;  // split-K slices per tile (workspace holds one f32 tile each)
+// Split-K workspace layout: a fixed region of per-tile arrival counters first (every call
+// leaves its counters at zero, and no call ever writes partial sums there, so calls of any
+// shape can share one workspace), then kMaxSplits f32 partial-tile slices.
+constexpr long long kCounterBytes = 16384;
+constexpr int kMaxSplitTiles = kCounterBytes / 4;
+namespace {  // co-resident CTA pairs seen by the last pair launch
 
 // Output tensor map for the epilogue's TMA stores: the output viewed as bytes
 // [m, n * esize] with 32-row x 128-byte boxes in the 128B swizzle layout.
@@ -52,6 +60,10 @@ EpilogueParams make_epilogue(const b2f_gemm_args* a) {
   ep.out_inv_scale = 1.0f / a->out_scale;
   ep.amax = a->amax;
   ep.mode = a->mode;
+  ep.ws = nullptr;
+  ep.ws_ld = 0;
+  ep.ws_slice = 0;
+  ep.counters = nullptr;
   const int esz = a->out_dtype == B2F_DTYPE_F32 ? 4 : (a->out_dtype == B2F_DTYPE_BF16 ? 2 : 1);
   const int rsz =
       a->residual_dtype == B2F_DTYPE_F32 ? 4 : (a->residual_dtype == B2F_DTYPE_BF16 ? 2 : 1);
@@ -82,12 +94,38 @@ int launch_gemm(const b2f_gemm_args* a, EpilogueParams ep, cudaStream_t stream) 
                      CU_TENSOR_MAP_SWIZZLE_128B, &err))
       return fail(B2F_ERR_ARG, "gemm_fp8: B tensor map: " + err);
   }
-  GemmShape shape{a->m, a->n, a->k};
-
   const int num_tiles = ((a->m + Cfg::BM - 1) / Cfg::BM) * ((a->n + BN - 1) / BN);
+  const int num_kb = (a->k + Cfg::BK - 1) / Cfg::BK;
   const int sms = sm_count();
   if (sms <= 0) return fail(B2F_ERR_CUDA, "gemm_fp8: cannot query SM count");
-  const int grid = num_tiles < sms ? num_tiles : sms;
+  int splits = a->splits;
+  if (splits == 0) {
+    // Automatic choice: no split.  Measured on B200 for M=128, N=K=8192, the last-slice
+    // reduction (row-per-thread L2 reads of every slice) costs more than the extra
+    // parallelism gains (118 us split 4-way vs 28 us unsplit), so split-K runs only when
+    // the caller asks for it.
+    splits = 1;
+  }
+  if (splits < 1 || splits > num_kb || splits > kMaxSplits)
+    return fail(B2F_ERR_ARG, "gemm_fp8: splits must be in [1, min(8, K/128)]");
+  if (splits > 1 && num_tiles > kMaxSplitTiles)
+    return fail(B2F_ERR_UNSUPPORTED, "gemm_fp8: split-K supports at most 4096 output tiles");
+  if (splits > 1) {
+    if (a->workspace == nullptr ||
+        a->workspace_bytes < b2f_gemm_workspace_bytes(a->m, a->n) ||
+        (((uintptr_t)a->workspace) & 15))
+      return fail(B2F_ERR_ARG, "gemm_fp8: split-K needs a 16-byte aligned workspace of "
+                               "b2f_gemm_workspace_bytes(m, n) bytes");
+    const long long ws_ld = (long long)((a->n + 255) / 256) * 256;
+    const long long ws_rows = (long long)((a->m + 127) / 128) * 128;
+    ep.counters = reinterpret_cast<unsigned int*>(a->workspace);
+    ep.ws = reinterpret_cast<float*>(reinterpret_cast<char*>(a->workspace) + kCounterBytes);
+    ep.ws_ld = ws_ld;
+    ep.ws_slice = ws_rows * ws_ld;
+  }
+  GemmShape shape{a->m, a->n, a->k, splits};
+  const int units = num_tiles * splits;
+  const int grid = units < sms ? units : sms;
   auto kern = gemm_fp8_kernel<BN>;
   static thread_local int attr_dev = -1;
   int dev = 0;
@@ -124,7 +162,7 @@ int launch_gemm_pair(const b2f_gemm_args* a, EpilogueParams ep, cudaStream_t str
                      CU_TENSOR_MAP_SWIZZLE_128B, &err))
       return fail(B2F_ERR_ARG, "gemm_fp8: B tensor map: " + err);
   }
-  GemmShape shape{a->m, a->n, a->k};
+  GemmShape shape{a->m, a->n, a->k, 1};
   const int num_tiles = ((a->m + 255) / 256) * ((a->n + Cfg::BN - 1) / Cfg::BN);
   static thread_local int cached_dev = -1, cached_pairs = 0;
   int dev = 0;
@@ -184,6 +222,13 @@ void b2f_gemm_args_init(b2f_gemm_args* a) {
 
 int b2f_gemm_pair_capacity(void) { return b2f::g_pair_capacity; }
 
+long long b2f_gemm_workspace_bytes(int m, int n) {
+  if (m <= 0 || n <= 0) return 0;
+  const long long ld = (long long)((n + 255) / 256) * 256;   // column tiles of 256
+  const long long rows = (long long)((m + 127) / 128) * 128;  // row tiles of 128
+  return b2f::kCounterBytes + b2f::kMaxSplits * rows * ld * 4;
+}
+
 int b2f_gemm_fp8(const b2f_gemm_args* a, b2f_stream_t stream) {
   using namespace b2f;
   if (a == nullptr) return fail(B2F_ERR_ARG, "gemm_fp8: null args");
@@ -221,10 +266,14 @@ int b2f_gemm_fp8(const b2f_gemm_args* a, b2f_stream_t stream) {
     const long long tiles256 = (long long)((a->m + 127) / 128) * ((a->n + 255) / 256);
     const long long pair_tiles = (long long)((a->m + 255) / 256) * ((a->n + 255) / 256);
     if (a->m > 128 && pair_tiles >= sms / 2) tn = 512;  // CTA-pair 256x256 tiles
+    else if (a->workspace != nullptr && a->splits > 1 && tiles256 * 2 <= sms) tn = 256;
     else tn = (tiles256 < sms) ? 128 : 256;
   }
   const EpilogueParams ep = make_epilogue(a);
-  if (tn == 512) return launch_gemm_pair(a, ep, s);
+  if (tn == 512) {
+    if (a->splits > 1) return fail(B2F_ERR_UNSUPPORTED, "gemm_fp8: split-K uses tile_n 128 or 256");
+    return launch_gemm_pair(a, ep, s);
+  }
   if (tn == 256) return launch_gemm<256>(a, ep, s);
   if (tn == 128) return launch_gemm<128>(a, ep, s);
   return fail(B2F_ERR_ARG, "gemm_fp8: tile_n must be 0, 128, 256 or 512 (CTA pair)");

@@ -59,10 +59,15 @@ struct EpilogueParams {
   int out_vec;             // out base and row pitch 16-byte aligned: vector stores
   int res_vec;             // residual base and row pitch 16-byte aligned: vector loads
   int chunk_bytes;         // TMA store box width: 128 (SW128) or 64 (SW64) bytes
+  float* ws;               // split-K: f32 partial tiles [splits][rows_pad][ws_ld]
+  long long ws_ld;
+  long long ws_slice;      // elements per split slice (rows_pad * ws_ld)
+  unsigned int* counters;  // split-K: arrivals per output tile, zero between calls
 };
 
 struct GemmShape {
   int M, N, K;
+  int splits;  // K slices per output tile (split-K, 1-CTA kernel only); 1 = off
 };
 
 // Hardware tanh (MUFU, max relative error ~2^-11); every GELU output is requantised to
@@ -247,6 +252,60 @@ __device__ __forceinline__ int out_esize(int dt) { return dt == kOutF32 ? 4 : (d
 // staging tile in the 128B-swizzle layout and leaves with TMA bulk-tensor stores (full
 // 128-byte lines, clipped at the M/N edges by the TMA unit).  `stage` points at this
 // warp's 2 x 4 KB staging area (1024-byte aligned).
+// Split-K drain of this warp's 32 rows x HALF columns: the f32 partial tile of K slice
+// `sk` goes to its own workspace slice (plain 16-byte stores; no atomics, so the final sum
+// below has a fixed order and results are bitwise reproducible).
+template <int HALF>
+__device__ __forceinline__ void splitk_store(const EpilogueParams& ep, uint32_t t_row, int row,
+                                             int col_base, int sk) {
+  float* w = ep.ws + (long long)sk * ep.ws_slice + (long long)row * ep.ws_ld + col_base;
+#pragma unroll 1
+  for (int c = 0; c < HALF; c += 32) {
+    uint32_t r[32];
+    tmem_ld32(t_row + c, r);
+#pragma unroll
+    for (int j = 0; j < 32; j += 4)
+      __stcg(reinterpret_cast<float4*>(w + c + j),
+             make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                         __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3])));
+  }
+}
+
+// The last K slice of a tile to finish: sum the slices in order 0..splits-1 (L2 reads),
+// apply the fused epilogue and store.
+template <int HALF>
+__device__ __forceinline__ void splitk_finish(const EpilogueParams& ep, float alpha, int row,
+                                              int col_base, int M, int N, int splits,
+                                              float& rowsum, float& amax_local) {
+  const float* w = ep.ws + (long long)row * ep.ws_ld + col_base;
+#pragma unroll 1
+  for (int c = 0; c < HALF; c += 32) {
+    float sum[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) sum[j] = 0.f;
+#pragma unroll 1
+    for (int s = 0; s < splits; ++s) {
+      const float* ws = w + (long long)s * ep.ws_slice + c;
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(ws + j));
+        sum[j] += v.x; sum[j + 1] += v.y; sum[j + 2] += v.z; sum[j + 3] += v.w;
+      }
+    }
+    const int col0 = col_base + c;
+    if (col0 >= N) continue;
+    uint32_t r[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(sum[j]);
+    const int cc = col0 + (threadIdx.x & 31);
+    const float lb = (ep.bias != nullptr && cc < N) ? __ldg(ep.bias + cc) : 0.f;
+    const float lc = (ep.col_scale != nullptr && cc < N) ? __ldg(ep.col_scale + cc) : 1.f;
+    float v[32];
+    epi_values(ep, alpha, row, col0, M, N, r, v, rowsum, amax_local, lb, lc);
+    if (ep.mode == kModeStore && row < M) epi_store_direct(ep, row, col0, N, v);
+  }
+}
+
 // Per-lane epilogue vectors for the 32 columns starting at col0 (one coalesced load each).
 __device__ __forceinline__ void epi_lane_vectors(const EpilogueParams& ep, int col0, int N,
                                                  float& lane_bias, float& lane_cscale) {
@@ -360,6 +419,11 @@ __global__ void __launch_bounds__(320, 1)
   const int num_n = (N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
   const int num_kb = (K + Cfg::BK - 1) / Cfg::BK;
+  const int splits = shape.splits;
+  const int num_units = num_tiles * splits;  // unit u: tile u / splits, K slice u % splits
+  uint64_t* split_done = drain_bar + 8;       // 8 epilogue warps finished their partials
+  uint64_t* split_flag_bar = split_done + 1;  // "is this the tile's last slice" published
+  volatile int* split_last = abort_flag + 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -370,6 +434,8 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(&tfull_bar[a], 1);
       mbar_init(&tempty_bar[a], 8);
     }
+    mbar_init(split_done, 8);
+    mbar_init(split_flag_bar, 1);
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
     fence_mbarrier_init();
@@ -397,15 +463,17 @@ __global__ void __launch_bounds__(320, 1)
       uint32_t phase = 0;
       long long issued = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+        const int t = u / splits, sk = u - t * splits;
         int mb, nb;
         tile_coords(t, num_m, num_n, mb, nb);
-        for (int kb = 0; kb < num_kb; ++kb) {
+        const int kb0 = (sk * num_kb) / splits, kb1 = ((sk + 1) * num_kb) / splits;
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, kDevTimeoutProducer, abort_flag)) {
             ok = false;
             break;
           }
-          if (kb == 0) B2F_STAMP((t - (int)blockIdx.x) / (int)gridDim.x, 0);
+          if (kb == kb0) B2F_STAMP((u - (int)blockIdx.x) / (int)gridDim.x, 0);
           mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
           tma_load_2d(smem_a + stage * Cfg::A_BYTES, &tmap_a, &full_bar[stage], kb * Cfg::BK,
                       mb * Cfg::BM, pol_a);
@@ -433,14 +501,16 @@ __global__ void __launch_bounds__(320, 1)
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++it) {
+        const int sk = u % splits;
+        const int kb0 = (sk * num_kb) / splits, kb1 = ((sk + 1) * num_kb) / splits;
         const int acc = it & 1;
         const uint32_t acc_phase = (it >> 1) & 1;
         if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, kDevTimeoutMma, abort_flag)) break;
         B2F_STAMP(it, 1);
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, kDevTimeoutMma, abort_flag)) {
             ok = false;
             break;
@@ -452,7 +522,7 @@ __global__ void __launch_bounds__(320, 1)
           for (int k = 0; k < Cfg::BK / 32; ++k) {
             const uint64_t ad = make_sdesc_sw128(a_addr + k * 32, 1024);
             const uint64_t bd = make_sdesc_sw128(b_addr + k * 32, 1024);
-            mma_f8(d_tmem, ad, bd, idesc, (kb | k) != 0);
+            mma_f8(d_tmem, ad, bd, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
           }
           mma_commit(&empty_bar[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -478,7 +548,8 @@ __global__ void __launch_bounds__(320, 1)
     if (ep.alpha_ptr != nullptr) alpha *= *ep.alpha_ptr;
     float amax_local = 0.0f;
     int it = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++it) {
+      const int t = u / splits;
       int mb, nb;
       tile_coords(t, num_m, num_n, mb, nb);
       const int acc = it & 1;
@@ -491,15 +562,52 @@ __global__ void __launch_bounds__(320, 1)
       tc_fence_after();
       const int row0 = mb * Cfg::BM + q * 32;
       const int row = row0 + lane;
+      const int col_base = nb * BN + chalf * (BN / 2);
       float rowsum = 0.0f;
       const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + acc * BN + chalf * (BN / 2);
-      epilogue_tile<BN / 2>(ep, &tmap_out, alpha, t_row, row, row0, nb * BN + chalf * (BN / 2),
-                            M, N, stage, buf, rowsum, amax_local);
-      tc_fence_before();
-      __syncwarp();
-      if (warp == 2 && lane == 0) B2F_STAMP(it, 4);
-      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
-      if (ep.mode == kModeRowSum && row < M)
+      if (splits == 1) {
+        epilogue_tile<BN / 2>(ep, &tmap_out, alpha, t_row, row, row0, col_base, M, N, stage,
+                              buf, rowsum, amax_local);
+        tc_fence_before();
+        __syncwarp();
+        if (warp == 2 && lane == 0) B2F_STAMP(it, 4);
+        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      } else {
+        splitk_store<BN / 2>(ep, t_row, row, col_base, u - t * splits);
+        tc_fence_before();
+        __threadfence();  // this thread's partials are visible before the tile counter moves
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&tempty_bar[acc]);
+          mbar_arrive(split_done);
+        }
+        const uint32_t sp = it & 1;
+        if (ew == 0) {
+          bool okw = mbar_wait(split_done, sp, kDevTimeoutEpilogue, abort_flag);
+          if (lane == 0) {
+            int last = 0;
+            if (okw) {
+              __threadfence();
+              last = atomicAdd(&ep.counters[t], 1u) == (unsigned)(splits - 1);
+              if (last) {
+                __threadfence();
+                ep.counters[t] = 0u;  // reset for the next call (every slice has arrived)
+              }
+            }
+            *split_last = last;
+            mbar_arrive(split_flag_bar);
+          }
+          __syncwarp();
+        }
+        if (!__all_sync(0xffffffffu,
+                        mbar_wait(split_flag_bar, sp, kDevTimeoutEpilogue, abort_flag)))
+          break;
+        if (*split_last) {
+          __threadfence();
+          splitk_finish<BN / 2>(ep, alpha, row, col_base, M, N, splits, rowsum, amax_local);
+        }
+      }
+      if (ep.mode == kModeRowSum && row < M && (splits == 1 || *split_last))
         atomicAdd(reinterpret_cast<float*>(ep.out) + row, rowsum * ep.out_inv_scale);
     }
     if (lane == 0) bulk_wait_all();  // output stores complete before the CTA exits

@@ -116,13 +116,26 @@ typedef struct b2f_gemm_args {
   float out_scale;
   float* amax;
   int mode;
-  int tile_n; /* 0 = automatic, else 128 or 256 */
+  int tile_n; /* 0 = automatic, else 128, 256 or 512 (CTA-pair 256 x 256 tiles) */
+  /* Split-K (few output tiles, long K): `splits` K slices per tile, at most 8 (0 =
+   * automatic, which only splits when a workspace is given).  The workspace holds a fixed
+   * 16 KB region of per-tile arrival counters, then one f32 partial tile per slice; the
+   * counters must be zero before the first use (zero-fill the buffer once) and every call
+   * leaves them zero, so one workspace serves calls of any shape (at most 4096 tiles).
+   * Slices are summed in a fixed order, so results are bitwise reproducible.
+   * Size: b2f_gemm_workspace_bytes(m, n). */
+  int splits;
+  void* workspace;
+  long long workspace_bytes;
 } b2f_gemm_args;
 
 /* Fill `args` with neutral defaults (alpha 1, pre_mul 1, post_mul 1, out_scale 1, bf16 out). */
 void b2f_gemm_args_init(b2f_gemm_args* args);
 
 int b2f_gemm_fp8(const b2f_gemm_args* args, b2f_stream_t stream);
+
+/* Bytes of split-K workspace that b2f_gemm_fp8 needs for an m x n output. */
+long long b2f_gemm_workspace_bytes(int m, int n);
 
 /* Co-resident CTA pairs the last CTA-pair GEMM launch on this thread used (0 = none yet). */
 int b2f_gemm_pair_capacity(void);
