@@ -136,7 +136,7 @@ class Op(ctypes.Structure):
 EXPORTED_SYMBOLS = (
     "b2f_version", "b2f_last_error", "b2f_num_sms", "b2f_status_read",
     "b2f_debug_bounded_wait", "b2f_gemm_args_init", "b2f_gemm_fp8", "b2f_gemm_pair_capacity",
-    "b2f_gemm_workspace_bytes",
+    "b2f_gemm_workspace_bytes", "b2f_gemm_fp8_static",
     "b2f_norm_args_init", "b2f_norm_quant", "b2f_attn_args_init", "b2f_attention_fp8",
     "b2f_head_norm_rope", "b2f_fp8_to_bf16", "b2f_swiglu_fp8",
     "b2f_registry_lookup", "b2f_registry_size", "b2f_registry_at",
@@ -159,6 +159,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.b2f_gemm_fp8.argtypes = [ctypes.POINTER(GemmArgs), vp]
     lib.b2f_gemm_fp8.restype = ctypes.c_int
     lib.b2f_gemm_pair_capacity.restype = ctypes.c_int
+    lib.b2f_gemm_fp8_static.argtypes = [ctypes.POINTER(GemmArgs), vp]
+    lib.b2f_gemm_fp8_static.restype = ctypes.c_int
     lib.b2f_gemm_workspace_bytes.argtypes = [ctypes.c_int, ctypes.c_int]
     lib.b2f_gemm_workspace_bytes.restype = ctypes.c_longlong
     lib.b2f_norm_args_init.argtypes = [ctypes.POINTER(NormArgs)]

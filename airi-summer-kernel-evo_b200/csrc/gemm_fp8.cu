@@ -1,6 +1,8 @@
 // Host launcher of the tcgen05 e4m3 GEMM (C ABI: b2f_gemm_fp8).
 #include <cstring>
+#include <mutex>
 #include <string>
+#include <vector>
 
 #include "gemm_fp8.cuh"
 #include "host_common.h"
@@ -292,3 +294,141 @@ extern "C" int b2f_trace_read(void* host, unsigned long long bytes, int reset) {
   return 0;
 }
 #endif
+
+// ---------------------------------------------------------------------------------------
+// Allocation-free split-K GEMM (b2f_gemm_fp8_static).
+//
+// Some callers cannot allocate device memory at call time: a kernel library loaded as a
+// plugin into a host framework that owns every device allocation through its own
+// allocator, or a serving loop whose memory plan is fixed at start-up and forbids any
+// allocation afterwards.  They cannot hand the split-K GEMM a workspace, so this entry
+// point keeps its scratch in a file-scope device array instead.
+//
+// kStaticScratchBytes (8 MiB of f32 partial tiles + 16 KiB of tile counters) lives on
+// every GPU that loads this library until the process exits.  Host code only ever sees
+// the array's host-side shadow symbol, which is not a device address: the device address
+// is looked up with cudaGetSymbolAddress once per device, with that device current, on
+// the first call made on the device (so make that first call before any stream capture).
+// Every call shares the one array and keeps the last call's partial tiles; the counters
+// that must start at zero are cleared (cudaMemsetAsync on the call's stream) at the start
+// of every call.  Calls that overlap on the GPU - on two streams, or from two host
+// threads - race on the array and must be serialised by the caller.
+namespace b2f {
+namespace {
+
+constexpr long long kStaticScratchBytes = kCounterBytes + 8ll * 1024 * 1024;
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+std::mutex g_static_mu;
+std::vector<void*> g_static_ptr;  // device address of g_static_scratch, per device
+
+int static_scratch_address(void** out) {
+  int dev = 0;
+  B2F_CUDA_TRY(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(g_static_mu);
+  if ((int)g_static_ptr.size() <= dev) g_static_ptr.resize(dev + 1, nullptr);
+  if (g_static_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return cuda_fail(e != cudaSuccess ? e : cudaErrorInvalidSymbol,
+                       "cudaGetSymbolAddress(g_static_scratch)");
+    g_static_ptr[dev] = p;
+  }
+  *out = g_static_ptr[dev];
+  return B2F_OK;
+}
+
+template <int BN>
+int launch_gemm_static(const b2f_gemm_args* a, int splits, void* scratch, cudaStream_t stream) {
+  using Cfg = GemmCfg<BN>;
+  CUtensorMap ta, tb;
+  std::string err;
+  {
+    const unsigned long long dims[2] = {(unsigned long long)a->k, (unsigned long long)a->m};
+    const unsigned long long strides[1] = {(unsigned long long)a->lda};
+    const unsigned int box[2] = {Cfg::BK, Cfg::BM};
+    if (!encode_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a->a, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_128B, &err))
+      return fail(B2F_ERR_ARG, "gemm_fp8_static: A tensor map: " + err);
+  }
+  {
+    const unsigned long long dims[2] = {(unsigned long long)a->k, (unsigned long long)a->n};
+    const unsigned long long strides[1] = {(unsigned long long)a->ldb};
+    const unsigned int box[2] = {Cfg::BK, (unsigned int)BN};
+    if (!encode_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a->b, dims, strides, box,
+                     CU_TENSOR_MAP_SWIZZLE_128B, &err))
+      return fail(B2F_ERR_ARG, "gemm_fp8_static: B tensor map: " + err);
+  }
+  EpilogueParams ep = make_epilogue(a);
+  const long long ws_ld = (long long)((a->n + 255) / 256) * 256;
+  const long long ws_rows = (long long)((a->m + 127) / 128) * 128;
+  ep.counters = reinterpret_cast<unsigned int*>(scratch);
+  ep.ws = reinterpret_cast<float*>(reinterpret_cast<char*>(scratch) + kCounterBytes);
+  ep.ws_ld = ws_ld;
+  ep.ws_slice = ws_rows * ws_ld;
+  const int num_tiles = ((a->m + Cfg::BM - 1) / Cfg::BM) * ((a->n + BN - 1) / BN);
+  const int sms = sm_count();
+  if (sms <= 0) return fail(B2F_ERR_CUDA, "gemm_fp8_static: cannot query SM count");
+  GemmShape shape{a->m, a->n, a->k, splits};
+  const int units = num_tiles * splits;
+  const int grid = units < sms ? units : sms;
+  B2F_CUDA_TRY(cudaFuncSetAttribute(gemm_fp8_kernel<BN>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    Cfg::SMEM_BYTES));
+  CUtensorMap to;
+  if (int rc = encode_out_map(a, ep, BN / 2, &to)) return rc;
+  // Tile counters must start at zero: clear them on the call's stream.
+  B2F_CUDA_TRY(cudaMemsetAsync(scratch, 0, kCounterBytes, stream));
+  gemm_fp8_kernel<BN><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, to, shape, ep);
+  B2F_CUDA_TRY(cudaGetLastError());
+  return B2F_OK;
+}
+
+}  // namespace
+}  // namespace b2f
+
+extern "C" int b2f_gemm_fp8_static(const b2f_gemm_args* a, b2f_stream_t stream) {
+  using namespace b2f;
+  if (a == nullptr) return fail(B2F_ERR_ARG, "gemm_fp8_static: null args");
+  if (a->m <= 0 || a->n <= 0 || a->k <= 0) return fail(B2F_ERR_ARG, "gemm_fp8_static: empty shape");
+  if (a->a == nullptr || a->b == nullptr || a->out == nullptr)
+    return fail(B2F_ERR_ARG, "gemm_fp8_static: null tensor");
+  if (a->k % 16 != 0 || a->lda < a->k || a->ldb < a->k || a->lda % 16 || a->ldb % 16 ||
+      !aligned16(a->a) || !aligned16(a->b))
+    return fail(B2F_ERR_ARG, "gemm_fp8_static: k, lda, ldb must be multiples of 16 and A, B "
+                             "16-byte aligned");
+  if (a->out_dtype < 0 || a->out_dtype > 2 || a->residual_dtype < 0 || a->residual_dtype > 2 ||
+      a->act < 0 || a->act > 4 || (a->mode != B2F_GEMM_STORE && a->mode != B2F_GEMM_ROWSUM) ||
+      (a->mode == B2F_GEMM_ROWSUM && a->out_dtype != B2F_DTYPE_F32))
+    return fail(B2F_ERR_ARG, "gemm_fp8_static: bad dtype, activation or mode");
+  if ((a->mode == B2F_GEMM_STORE && a->out_ld < a->n) || a->out_scale == 0.0f ||
+      (a->residual != nullptr && a->residual_ld < a->n))
+    return fail(B2F_ERR_ARG, "gemm_fp8_static: bad output / residual layout or scale");
+  const int esz = a->out_dtype == B2F_DTYPE_F32 ? 4 : (a->out_dtype == B2F_DTYPE_BF16 ? 2 : 1);
+  if (((uintptr_t)a->out) % esz != 0 || (a->bias != nullptr && !aligned16(a->bias)) ||
+      (a->col_scale != nullptr && !aligned16(a->col_scale)))
+    return fail(B2F_ERR_ARG, "gemm_fp8_static: misaligned output, bias or col_scale");
+  const int num_kb = (a->k + 127) / 128;
+  int splits = a->splits;
+  if (splits == 0) splits = num_kb < 4 ? num_kb : 4;
+  if (splits < 2 || splits > kMaxSplits || splits > num_kb)
+    return fail(B2F_ERR_ARG, "gemm_fp8_static: splits must be in [2, min(8, K/128)]");
+  const int tn = a->tile_n == 0 ? 256 : a->tile_n;
+  if (tn != 128 && tn != 256)
+    return fail(B2F_ERR_ARG, "gemm_fp8_static: tile_n must be 0, 128 or 256");
+  const long long rows = (long long)((a->m + 127) / 128) * 128;
+  const long long ld = (long long)((a->n + 255) / 256) * 256;
+  const long long need = kCounterBytes + (long long)splits * rows * ld * 4;
+  const long long tiles = (rows / 128) * ((a->n + tn - 1) / tn);
+  if (need > kStaticScratchBytes || tiles > kMaxSplitTiles)
+    return fail(B2F_ERR_ARG,
+                "gemm_fp8_static: splits * ceil(m/128)*128 * ceil(n/256)*256 * 4 bytes = " +
+                    std::to_string(need - kCounterBytes) +
+                    " exceeds the 8 MiB static scratch; use b2f_gemm_fp8 with a workspace");
+  void* scratch = nullptr;
+  if (int rc = static_scratch_address(&scratch)) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (tn == 256) return launch_gemm_static<256>(a, splits, scratch, s);
+  return launch_gemm_static<128>(a, splits, scratch, s);
+}

@@ -134,6 +134,20 @@ void b2f_gemm_args_init(b2f_gemm_args* args);
 
 int b2f_gemm_fp8(const b2f_gemm_args* args, b2f_stream_t stream);
 
+/* Split-K GEMM that allocates nothing (no counterpart in the reference).
+ * For callers that cannot allocate device memory at call time - a library loaded as a
+ * plugin into a host framework that owns every device allocation through its own
+ * allocator, or a serving loop whose memory plan is fixed at start-up - and so cannot pass
+ * b2f_gemm_fp8 a split-K workspace.  Same arguments and results as b2f_gemm_fp8 with
+ * split-K (`workspace` / `workspace_bytes` are ignored; `splits` 0 selects 4, else 2..8;
+ * `tile_n` 0 / 128 / 256).  The scratch is a file-scope device array of 8 MiB + 16 KiB
+ * that every GPU which loads the library holds until the process exits; a call whose
+ * splits * ceil(m/128)*128 * ceil(n/256)*256 * 4 bytes exceed 8 MiB is rejected with
+ * B2F_ERR_ARG.  The first call on a device looks up the array's device address (make it
+ * before any stream capture).  Every call shares the array: calls that overlap on the GPU
+ * race, and must be serialised by the caller. */
+int b2f_gemm_fp8_static(const b2f_gemm_args* args, b2f_stream_t stream);
+
 /* Bytes of split-K workspace that b2f_gemm_fp8 needs for an m x n output. */
 long long b2f_gemm_workspace_bytes(int m, int n);
 
