@@ -35,6 +35,8 @@ GEMM_ROWSUM = 1
 
 NORM_RMS = 0
 NORM_LAYER = 1
+SCALE_STATIC, SCALE_DYNAMIC, SCALE_DYNAMIC_STATS, SCALE_DYNAMIC_APPLY = 0, 1, 2, 3
+NORM_SCHEDULE_AUTO, NORM_SCHEDULE_ROWGROUP = 0, 1
 
 
 class B2FError(RuntimeError):
@@ -88,6 +90,7 @@ class NormArgs(ctypes.Structure):
         ("q_out", ctypes.c_void_p), ("q_ld", ctypes.c_longlong),
         ("q_scale", ctypes.c_float), ("dynamic_scale", ctypes.c_int),
         ("amax", ctypes.c_void_p), ("scale_out", ctypes.c_void_p),
+        ("schedule", ctypes.c_int),
     ]
 
 
@@ -137,7 +140,7 @@ EXPORTED_SYMBOLS = (
     "b2f_version", "b2f_last_error", "b2f_num_sms", "b2f_status_read",
     "b2f_debug_bounded_wait", "b2f_gemm_args_init", "b2f_gemm_fp8", "b2f_gemm_pair_capacity",
     "b2f_gemm_workspace_bytes", "b2f_gemm_fp8_static",
-    "b2f_norm_args_init", "b2f_norm_quant", "b2f_attn_args_init", "b2f_attention_fp8",
+    "b2f_norm_args_init", "b2f_norm_quant", "b2f_norm_plan", "b2f_attn_args_init", "b2f_attention_fp8",
     "b2f_head_norm_rope", "b2f_fp8_to_bf16", "b2f_swiglu_fp8",
     "b2f_registry_lookup", "b2f_registry_size", "b2f_registry_at",
 )
@@ -167,6 +170,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.b2f_norm_args_init.restype = None
     lib.b2f_norm_quant.argtypes = [ctypes.POINTER(NormArgs), vp]
     lib.b2f_norm_quant.restype = ctypes.c_int
+    lib.b2f_norm_plan.argtypes = [ctypes.POINTER(NormArgs)]
+    lib.b2f_norm_plan.restype = ctypes.c_int
     lib.b2f_attn_args_init.argtypes = [ctypes.POINTER(AttnArgs)]
     lib.b2f_attn_args_init.restype = None
     lib.b2f_attention_fp8.argtypes = [ctypes.POINTER(AttnArgs), vp]

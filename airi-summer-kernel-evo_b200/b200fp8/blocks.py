@@ -152,9 +152,14 @@ class GPT2Block(_Graphable):
 
 
 class QwenBlock(_Graphable):
+    """``add_residual=False`` leaves the residual add out of the o-projection: the block then
+    returns only this rank's partial of a heads-parallel o-projection (the other ranks'
+    partials and the residual are summed by the caller's all-reduce)."""
+
     def __init__(self, w, *, batch: int, seq: int, residual_dtype=torch.float32,
-                 out_dtype=torch.float32, device="cuda"):
+                 out_dtype=torch.float32, device="cuda", add_residual: bool = True):
         self.batch, self.seq = batch, seq
+        self.add_residual = add_residual
         self.t = t = batch * seq
         self.h, self.hk, self.dh = w.heads, w.kv_heads, w.head_dim
         self.hidden = w.q_w.shape[1]
@@ -182,6 +187,9 @@ class QwenBlock(_Graphable):
         self.cos = _dev(w.cos[:seq], device, f32)
         self.sin = _dev(w.sin[:seq], device, f32)
         self.has_mlp = w.mlp_down_w is not None
+        if self.has_mlp and not add_residual:
+            raise ValueError("add_residual=False needs a block without the MLP (the MLP "
+                             "reads the full residual stream r1)")
         self.n1 = torch.empty((t, self.hidden), device=device, dtype=_E4M3)
         self.proj = torch.empty((t, self.n_cat), device=device, dtype=_E4M3)
         self.q = torch.empty((t, h * dh), device=device, dtype=_E4M3)
@@ -231,7 +239,8 @@ class QwenBlock(_Graphable):
                           v_scale=self.qs, gate=self.proj[:, self.g_off:], gate_scale=self.qs,
                           gate_head_stride=self.q_hstride, ctx=self.ctx, ctx_scale=self.cs)
         r1 = self.r1 if self.has_mlp else self.out
-        ops.gemm_fp8(self.ctx, self.o_w, scale_a=self.cs, scale_b=self.o_s, residual=hidden,
+        ops.gemm_fp8(self.ctx, self.o_w, scale_a=self.cs, scale_b=self.o_s,
+                     residual=hidden if self.add_residual else None,
                      residual_scale=hidden_scale, out=r1)
         if not self.has_mlp:
             return self.out

@@ -146,11 +146,17 @@ def norm_quant(x: torch.Tensor, weight: torch.Tensor, *, kind: str = "rms",
                h_out: Optional[torch.Tensor] = None, y_out: Optional[torch.Tensor] = None,
                q_out: Optional[torch.Tensor] = None, q_scale: Optional[float] = None,
                amax: Optional[torch.Tensor] = None,
-               scale_out: Optional[torch.Tensor] = None):
+               scale_out: Optional[torch.Tensor] = None, phase: Optional[str] = None,
+               schedule: str = "auto", query_schedule: bool = False):
     """Residual-add + RMSNorm/LayerNorm + e4m3 quantisation (see b2f_norm_quant).
 
     ``q_scale=None`` selects the dynamic per-tensor scale amax(|y|)/448, returned in
-    ``scale_out`` (f32 [1]).  Returns ``(q_out, scale_out)``.
+    ``scale_out`` (f32 [1]).  With a dynamic scale, ``phase="stats"`` runs pass 1 only
+    (h_out written, amax of these rows left in ``amax``) and ``phase="apply"`` runs pass 2
+    only from the given ``amax`` (so row shards can share one scale after a MAX
+    all-reduce).  ``schedule="rowgroup"`` forces the unstaged kernels.
+    Returns ``(q_out, scale_out)``; with ``query_schedule`` launches nothing and returns
+    the schedule the call would use ("stream" or "rowgroup").
     """
     _check_cuda(x, weight, bias, residual, h_out, y_out, q_out, amax, scale_out)
     if x.dim() != 2 or x.stride(1) != 1:
@@ -187,8 +193,21 @@ def norm_quant(x: torch.Tensor, weight: torch.Tensor, *, kind: str = "rms",
         args.y_out, args.y_ld = y_out.data_ptr(), y_out.stride(0)
     args.q_out, args.q_ld = q_out.data_ptr(), q_out.stride(0)
     args.q_scale = 1.0 if dynamic else float(q_scale)
-    args.dynamic_scale = 1 if dynamic else 0
+    if not dynamic:
+        if phase is not None:
+            raise ValueError("phase applies to the dynamic scale only")
+        args.dynamic_scale = _lib.SCALE_STATIC
+    else:
+        args.dynamic_scale = {None: _lib.SCALE_DYNAMIC, "stats": _lib.SCALE_DYNAMIC_STATS,
+                              "apply": _lib.SCALE_DYNAMIC_APPLY}[phase]
     args.amax, args.scale_out = _ptr(amax), _ptr(scale_out)
+    args.schedule = {"auto": _lib.NORM_SCHEDULE_AUTO,
+                     "rowgroup": _lib.NORM_SCHEDULE_ROWGROUP}[schedule]
+    if query_schedule:
+        rc = _lib.lib().b2f_norm_plan(ctypes.byref(args))
+        if rc < 0:
+            check(-rc)
+        return "stream" if rc == 0 else "rowgroup"
     check(_lib.lib().b2f_norm_quant(ctypes.byref(args), _stream()))
     return q_out, scale_out
 

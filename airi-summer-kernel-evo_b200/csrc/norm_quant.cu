@@ -16,7 +16,11 @@
 // Reference math: residual RMSNorm cute_kernels/fused_residual_rmsnorm_fp8/submission.py:139-145,
 // Qwen RMSNorm tasks/model_qwen35_4b_full_attention_block_fp8/starter.py:167-171,
 // GPT-2 LayerNorm tasks/model_gpt2_small_transformer_block_fp8/starter.py:407-416,461-470.
+#include <algorithm>
+#include <map>
+#include <mutex>
 #include <string>
+#include <tuple>
 
 #include "common.cuh"
 #include "host_common.h"
@@ -53,6 +57,7 @@ struct NormParams {
   float* amax;       // dynamic: amax accumulator (zeroed by the launcher)
   float* scale_out;  // dynamic: s = amax/448 written by pass 2
   int rows, cols;
+  int schedule;  // B2F_NORM_SCHEDULE_*
 };
 
 __device__ __forceinline__ void load8(const void* base, int dtype, long long off, float scale,
@@ -91,9 +96,14 @@ __device__ __forceinline__ void store8(void* base, int dtype, long long off, con
   }
 }
 
+// Round to bf16 (RN) in place, two values per conversion.
 __device__ __forceinline__ void round_bf16(float (&v)[8]) {
 #pragma unroll
-  for (int j = 0; j < 8; ++j) v[j] = __bfloat162float(__float2bfloat16_rn(v[j]));
+  for (int j = 0; j < 8; j += 2) {
+    const float2 f = unpack_bf16x2(pack_bf16x2(v[j], v[j + 1]));
+    v[j] = f.x;
+    v[j + 1] = f.y;
+  }
 }
 
 __device__ __forceinline__ uint2 quant8(const float (&y)[8], float inv) {
@@ -315,25 +325,471 @@ __global__ void __launch_bounds__(256) norm_pass2_kernel(const NormParams p, int
   }
 }
 
+
+// ---------------------------------------------------------------------------------------
+// Streaming schedule (the default whenever rows are 16-byte multiples): a persistent CTA of
+// TPR threads owns one row at a time and keeps STAGES rows in flight in a shared-memory
+// ring, each row fetched by one or two untiled bulk copies (cp.async.bulk, completion on
+// the slot's mbarrier) issued by thread 0 as soon as the slot is free.  Per-row arithmetic
+// and the thread->vector mapping are those of the row-group kernels above (registers hold
+// the row between the statistics and the outputs).  Gamma (and the LayerNorm bias) are
+// staged once per CTA in shared memory.
+//   PASS2 == false: static scale (one pass) or pass 1 of the dynamic schedule.
+//   PASS2 == true : pass 2 of the dynamic schedule, rows walked in reverse order.
+constexpr int kStreamMaxStages = 8;
+
+struct StreamCfg {
+  const void* src0;  // x (pass 1) or h (pass 2)
+  int dt0;
+  float scale0;
+  long long ld0;
+  const void* src1;  // residual or nullptr
+  int dt1;
+  long long ld1;
+  uint32_t bytes0, bytes1;  // row bytes of each source (16-byte multiples)
+  uint32_t slot_bytes;      // bytes0 + bytes1
+  uint32_t wbytes;          // staged gamma bytes, 16-byte rounded
+  uint32_t bbytes;          // staged bias bytes (0 without a LayerNorm bias)
+  int stages;
+  int tpr;
+  bool round_h;  // round h to bf16 before the statistics (pass 1 writing a bf16 h)
+};
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+template <int DT>
+__device__ __forceinline__ void smem_load4(const uint8_t* row, int t, int tpr, int nvec,
+                                           float scale, float (&v)[VPT][8]) {
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int vi = t + tpr * i;
+    if (vi < nvec) {
+      load8(row, DT, (long long)vi * 8, scale, v[i]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
+    }
+  }
+}
+
+__device__ __forceinline__ void smem_load_any(const uint8_t* row, int dt, int t, int tpr,
+                                              int nvec, float scale, float (&v)[VPT][8]) {
+  switch (dt) {
+    case kBF16: smem_load4<kBF16>(row, t, tpr, nvec, scale, v); break;
+    case kF32: smem_load4<kF32>(row, t, tpr, nvec, scale, v); break;
+    default: smem_load4<kE4M3>(row, t, tpr, nvec, scale, v); break;
+  }
+}
+
+// Compile-time specialisation of the streaming kernel.  kDyn selects the runtime value
+// (the generic instance); kNone (residual only) means no residual.  FULL: every thread owns
+// exactly VPT vectors (cols == 8 * VPT * TPR), so no per-vector bounds checks.
+constexpr int kDyn = -1;
+constexpr int kNone = -2;
+
+__device__ __forceinline__ void st16_hint(void* ptr, uint4 v, uint64_t pol) {
+  asm volatile("st.global.L2::cache_hint.v4.b32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(ptr),
+               "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "l"(pol)
+               : "memory");
+}
+
+template <int DT>
+__device__ __forceinline__ void ld8(const uint8_t* base, int rt, long long off, float (&v)[8]) {
+  load8(base, DT == kDyn ? rt : DT, off, 1.0f, v);
+}
+
+template <bool PASS2, int KIND, int DT0, int DT1, int WDT, bool FULL>
+__global__ void __launch_bounds__(256, 3) norm_stream_kernel(const NormParams p, const StreamCfg c) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t full[kStreamMaxStages];
+  __shared__ float red[8];
+  const int tpr = c.tpr;
+  const int t = threadIdx.x;
+  const int nvec = p.cols / 8;
+  const int G = gridDim.x;
+  const int kind = KIND == kDyn ? p.kind : KIND;
+  const int dt0 = DT0 == kDyn ? c.dt0 : DT0;
+  const bool has_res = DT1 == kNone ? false : (DT1 == kDyn ? c.src1 != nullptr : true);
+  const int dt1 = DT1 >= 0 ? DT1 : c.dt1;
+  const int wdt = WDT == kDyn ? p.w_dtype : WDT;
+  uint8_t* sw = smem;
+  uint8_t* sb = smem + c.wbytes;
+  uint8_t* ring = smem + c.wbytes + c.bbytes;
+  const int nrows = blockIdx.x < p.rows ? (p.rows - 1 - blockIdx.x) / G + 1 : 0;
+  auto row_of = [&](int k) -> long long {
+    const int r = blockIdx.x + k * G;
+    return PASS2 ? p.rows - 1 - r : r;
+  };
+  const uint64_t pol = policy_evict_first();
+  const uint64_t pol_keep = policy_evict_last();
+  const int e0 = dt0 == kF32 ? 4 : (dt0 == kBF16 ? 2 : 1);
+  const int e1 = dt1 == kF32 ? 4 : 2;
+  auto issue = [&](int k) {
+    const int slot = k % c.stages;
+    const long long r = row_of(k);
+    uint8_t* dst = ring + (size_t)slot * c.slot_bytes;
+    mbar_arrive_expect_tx(&full[slot], c.slot_bytes);
+    bulk_load(dst, static_cast<const uint8_t*>(c.src0) + r * c.ld0 * e0, c.bytes0, &full[slot],
+              pol);
+    if (has_res)
+      bulk_load(dst + c.bytes0, static_cast<const uint8_t*>(c.src1) + r * c.ld1 * e1, c.bytes1,
+                &full[slot], pol);
+  };
+  if (t == 0) {
+    for (int i = 0; i < c.stages; ++i) mbar_init(&full[i], 1);
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+  int issued = 0;
+  if (t == 0)
+    for (; issued < c.stages && issued < nrows; ++issued) issue(issued);
+  const bool has_b = kind == 1 && p.bias != nullptr;
+  {
+    const int n16 = p.cols * (wdt == kF32 ? 4 : 2) / 16;
+    for (int i = t; i < n16; i += blockDim.x) {
+      reinterpret_cast<uint4*>(sw)[i] = reinterpret_cast<const uint4*>(p.weight)[i];
+      if (has_b) reinterpret_cast<uint4*>(sb)[i] = reinterpret_cast<const uint4*>(p.bias)[i];
+    }
+  }
+  // (the first row-wait's barrier below publishes the staged gamma / bias)
+
+  float s = p.q_scale;
+  if (PASS2) {
+    const float amax = *p.amax;
+    s = amax > 0.f ? amax / 448.0f : 1.0f;
+    if (blockIdx.x == 0 && t == 0) *p.scale_out = s;
+  }
+  const float qinv = 1.0f / s;
+  const bool dyn1 = !PASS2 && p.dynamic;
+  const bool store_h = !PASS2 && p.h_out != nullptr;
+  const bool scale0 = c.scale0 != 1.0f;
+  const float n = float(p.cols);
+  const float w_off = p.w_offset;
+  float amax = 0.f;
+  int k = 0;
+  bool aborted = false;
+  for (; k < nrows; ++k) {
+    const int slot = k % c.stages;
+    const bool ok = mbar_wait(&full[slot], (k / c.stages) & 1, kDevTimeoutProducer, nullptr);
+    if (__syncthreads_or(!ok)) {
+      aborted = true;
+      break;
+    }
+    const uint8_t* src = ring + (size_t)slot * c.slot_bytes;
+    float h[VPT][8];
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int vi = t + tpr * i;
+      if (FULL || vi < nvec) {
+        ld8<DT0>(src, dt0, (long long)vi * 8, h[i]);
+        if (scale0) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) h[i][j] *= c.scale0;
+        }
+        if (has_res) {
+          float r[8];
+          ld8<DT1 >= 0 ? DT1 : kDyn>(src + c.bytes0, dt1, (long long)vi * 8, r);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) h[i][j] += r[j];
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) h[i][j] = 0.f;
+      }
+    }
+    __syncthreads();  // every thread has its row in registers: the slot can be refilled
+    if (t == 0 && issued < nrows) {
+      fence_proxy_async_smem();
+      issue(issued);
+    }
+    if (issued < nrows) ++issued;
+    const long long row = row_of(k);
+    if (c.round_h) {
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) round_bf16(h[i]);
+    }
+    if (store_h) {
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int vi = t + tpr * i;
+        if (FULL || vi < nvec) {
+          const long long off = row * p.h_ld + (long long)vi * 8;
+          if (dyn1 && p.h_dtype == kBF16) {
+            // Pass 2 re-reads h (newest rows first): ask L2 to keep it.
+            uint4 q;
+            q.x = pack_bf16x2(h[i][0], h[i][1]); q.y = pack_bf16x2(h[i][2], h[i][3]);
+            q.z = pack_bf16x2(h[i][4], h[i][5]); q.w = pack_bf16x2(h[i][6], h[i][7]);
+            st16_hint(reinterpret_cast<__nv_bfloat16*>(p.h_out) + off, q, pol_keep);
+          } else {
+            store8(p.h_out, p.h_dtype, off, h[i]);
+          }
+        }
+      }
+    }
+    float mean = 0.f, s1 = 0.f, s2 = 0.f;
+    if (kind == 1) {
+#pragma unroll
+      for (int i = 0; i < VPT; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s1 += h[i][j];
+      mean = group_sum(s1, red, tpr) / n;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        if (FULL || t + tpr * i < nvec) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float d = h[i][j] - mean;
+            s2 += d * d;
+          }
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < VPT; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s2 += h[i][j] * h[i][j];
+    }
+    const float inv = rsqrtf(group_sum(s2, red, tpr) / n + p.eps);
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int vi = t + tpr * i;
+      if (FULL || vi < nvec) {
+        float w[8], y[8];
+        ld8<WDT>(sw, wdt, (long long)vi * 8, w);
+        if (kind == 1) {
+          float b[8];
+          if (has_b) {
+            ld8<WDT>(sb, wdt, (long long)vi * 8, b);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) b[j] = 0.f;
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) y[j] = (h[i][j] - mean) * inv * w[j] + b[j];
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) y[j] = h[i][j] * inv * (w[j] + w_off);
+        }
+        if (dyn1) {
+          round_bf16(y);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(y[j]));
+        } else if (PASS2) {
+          round_bf16(y);
+          if (p.y_out != nullptr) store8(p.y_out, kBF16, row * p.y_ld + (long long)vi * 8, y);
+          *reinterpret_cast<uint2*>(p.q_out + row * p.q_ld + vi * 8) = quant8(y, qinv);
+        } else {
+          *reinterpret_cast<uint2*>(p.q_out + row * p.q_ld + vi * 8) = quant8(y, qinv);
+          if (p.y_out != nullptr) {
+            round_bf16(y);
+            store8(p.y_out, kBF16, row * p.y_ld + (long long)vi * 8, y);
+          }
+        }
+      }
+    }
+  }
+  if (aborted) {
+    // Let the copies still in flight land before the CTA's shared memory is released.
+    if (t == 0)
+      for (int j = k; j < issued; ++j)
+        mbar_wait(&full[j % c.stages], (j / c.stages) & 1, kDevTimeoutDrain, nullptr);
+    return;
+  }
+  if (dyn1) {
+    const float m = block_max(amax, red);
+    if (t == 0) atomic_max_nonneg(p.amax, m);
+  }
+}
+
+using StreamFn = void (*)(const NormParams, const StreamCfg);
+
+// The specialised instances: (KIND, DT0, DT1, WDT) of the library's callers (BASELINE
+// config 3 passes 1 and 2, the GPT-2 / vision LayerNorms, the Qwen RMSNorms); anything
+// else runs the generic instance.
+template <bool PASS2, bool FULL>
+StreamFn pick_stream(int kind, int dt0, int dt1, int wdt) {
+#define B2F_STREAM(K, D0, D1, W)                                   \
+  if (kind == K && dt0 == D0 && dt1 == D1 && wdt == W)             \
+    return norm_stream_kernel<PASS2, K, D0, D1, W, FULL>;
+  B2F_STREAM(0, kBF16, kBF16, kBF16)
+  B2F_STREAM(0, kBF16, kNone, kBF16)
+  B2F_STREAM(0, kBF16, kNone, kF32)
+  B2F_STREAM(0, kF32, kNone, kF32)
+  B2F_STREAM(0, kE4M3, kNone, kF32)
+  B2F_STREAM(1, kBF16, kNone, kF32)
+  B2F_STREAM(1, kF32, kNone, kF32)
+  B2F_STREAM(1, kE4M3, kNone, kF32)
+  B2F_STREAM(1, kBF16, kBF16, kF32)
+#undef B2F_STREAM
+  return norm_stream_kernel<PASS2, kDyn, kDyn, kDyn, kDyn, false>;
+}
+
+// Host-side choice between the streaming schedule and the one-row-per-group kernels.
+struct StreamLaunch {
+  StreamCfg cfg;
+  StreamFn fn;
+  int grid;
+  size_t smem;
+};
+
+int stream_occupancy(const void* fn, int threads, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, const void*, int, size_t>, int> cache;
+  static std::map<std::pair<int, const void*>, bool> opted;
+  std::lock_guard<std::mutex> g(mu);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  auto key = std::make_tuple(dev, fn, threads, smem);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  // Opt the kernel in once to the device's whole per-block shared memory (a per-function
+  // attribute: lowering it for one launch size would break launches of larger ones).
+  if (!opted[{dev, fn}]) {
+    int optin = 0;
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - 1024) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      return 0;
+    }
+    opted[{dev, fn}] = true;
+  }
+  int blocks = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, fn, threads, smem) != cudaSuccess) {
+    cudaGetLastError();
+    blocks = 0;
+  }
+  cache[key] = blocks;
+  return blocks;
+}
+
+bool plan_stream(const NormParams& p, bool pass2, StreamLaunch& L) {
+  StreamCfg& c = L.cfg;
+  const int nvec = p.cols / 8;
+  c.tpr = ((nvec + VPT - 1) / VPT + 31) / 32 * 32;
+  auto esz = [](int dt) { return dt == kF32 ? 4 : (dt == kBF16 ? 2 : 1); };
+  if (pass2 && p.h_out != nullptr) {
+    c.src0 = p.h_out; c.dt0 = p.h_dtype; c.scale0 = 1.0f; c.ld0 = p.h_ld;
+    c.src1 = nullptr; c.dt1 = kBF16; c.ld1 = 0;
+    c.round_h = false;
+  } else {
+    c.src0 = p.x; c.dt0 = p.x_dtype; c.scale0 = p.x_scale; c.ld0 = p.x_ld;
+    c.src1 = p.residual; c.dt1 = p.res_dtype; c.ld1 = p.res_ld;
+    c.round_h = !pass2 && p.h_out != nullptr && p.h_dtype == kBF16;
+  }
+  c.bytes0 = (uint32_t)(p.cols * esz(c.dt0));
+  c.bytes1 = c.src1 != nullptr ? (uint32_t)(p.cols * esz(c.dt1)) : 0u;
+  if (c.bytes0 % 16 || c.bytes1 % 16) return false;
+  if ((reinterpret_cast<uintptr_t>(c.src0) & 15) || (c.ld0 * esz(c.dt0)) % 16) return false;
+  if (c.src1 != nullptr &&
+      ((reinterpret_cast<uintptr_t>(c.src1) & 15) || (c.ld1 * esz(c.dt1)) % 16))
+    return false;
+  c.slot_bytes = c.bytes0 + c.bytes1;
+  c.wbytes = (uint32_t)((p.cols * (p.w_dtype == kF32 ? 4 : 2) + 15) / 16 * 16);
+  c.bbytes = (p.kind == 1 && p.bias != nullptr) ? c.wbytes : 0u;
+  // About 32 KiB of rows in flight per CTA (at least two), several CTAs per SM.
+  c.stages = (int)std::max<uint32_t>(
+      2u, std::min<uint32_t>((uint32_t)kStreamMaxStages, (32u * 1024u) / c.slot_bytes));
+  L.smem = (size_t)c.wbytes + c.bbytes + (size_t)c.stages * c.slot_bytes;
+  const bool full = c.tpr * VPT == nvec;
+  const int d1 = c.src1 != nullptr ? c.dt1 : kNone;
+  L.fn = pass2 ? (full ? pick_stream<true, true>(p.kind, c.dt0, d1, p.w_dtype)
+                       : pick_stream<true, false>(p.kind, c.dt0, d1, p.w_dtype))
+               : (full ? pick_stream<false, true>(p.kind, c.dt0, d1, p.w_dtype)
+                       : pick_stream<false, false>(p.kind, c.dt0, d1, p.w_dtype));
+  const int per_sm = stream_occupancy((const void*)L.fn, c.tpr, L.smem);
+  if (per_sm <= 0) return false;
+  L.grid = std::min(p.rows, sm_count() * per_sm);
+  return true;
+}
+
+int launch_stream(const NormParams& p, const StreamLaunch& L, cudaStream_t s) {
+  L.fn<<<L.grid, L.cfg.tpr, L.smem, s>>>(p, L.cfg);
+  B2F_CUDA_TRY(cudaGetLastError());
+  return B2F_OK;
+}
+
 int launch_norm(const NormParams& p, cudaStream_t s) {
   const int nvec = p.cols / 8;
   int tpr = ((nvec + VPT - 1) / VPT + 31) / 32 * 32;  // threads per row
   const int rpc = 256 / tpr;                            // rows per CTA
   const int threads = rpc * tpr;
   const int grid = (p.rows + rpc - 1) / rpc;
-  if (p.dynamic) {
-    B2F_CUDA_TRY(cudaMemsetAsync(p.amax, 0, sizeof(float), s));
-    norm_pass1_kernel<<<grid, threads, 0, s>>>(p, tpr);
-    B2F_CUDA_TRY(cudaGetLastError());
-    norm_pass2_kernel<<<grid, threads, 0, s>>>(p, tpr);
-  } else {
-    norm_pass1_kernel<<<grid, threads, 0, s>>>(p, tpr);
+  const bool run1 = p.dynamic != B2F_SCALE_DYNAMIC_APPLY;
+  const bool run2 = p.dynamic == B2F_SCALE_DYNAMIC || p.dynamic == B2F_SCALE_DYNAMIC_APPLY;
+  if (run1 && p.dynamic) B2F_CUDA_TRY(cudaMemsetAsync(p.amax, 0, sizeof(float), s));
+  StreamLaunch L;
+  if (run1) {
+    if (p.schedule == B2F_NORM_SCHEDULE_AUTO && plan_stream(p, false, L)) {
+      if (int rc = launch_stream(p, L, s)) return rc;
+    } else {
+      norm_pass1_kernel<<<grid, threads, 0, s>>>(p, tpr);
+      B2F_CUDA_TRY(cudaGetLastError());
+    }
   }
-  B2F_CUDA_TRY(cudaGetLastError());
+  if (run2) {
+    if (p.schedule == B2F_NORM_SCHEDULE_AUTO && plan_stream(p, true, L)) {
+      if (int rc = launch_stream(p, L, s)) return rc;
+    } else {
+      norm_pass2_kernel<<<grid, threads, 0, s>>>(p, tpr);
+      B2F_CUDA_TRY(cudaGetLastError());
+    }
+  }
   return B2F_OK;
 }
 
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Validates the C-ABI arguments and fills the kernel parameters.
+int build_params(const b2f_norm_args* a, NormParams& p) {
+  if (a == nullptr) return fail(B2F_ERR_ARG, "norm_quant: null args");
+  if (a->rows <= 0 || a->cols <= 0) return fail(B2F_ERR_ARG, "norm_quant: empty shape");
+  if (a->cols % 8 != 0) return fail(B2F_ERR_ARG, "norm_quant: cols must be a multiple of 8");
+  if (a->cols > kMaxCols)
+    return fail(B2F_ERR_UNSUPPORTED, "norm_quant: cols > 8192 not supported");
+  if (a->x == nullptr || a->weight == nullptr || a->q_out == nullptr)
+    return fail(B2F_ERR_ARG, "norm_quant: null tensor");
+  if (a->kind != B2F_NORM_RMS && a->kind != B2F_NORM_LAYER)
+    return fail(B2F_ERR_ARG, "norm_quant: bad kind");
+  if (a->x_dtype < 0 || a->x_dtype > 2 || a->residual_dtype < 0 || a->residual_dtype > 1 ||
+      a->weight_dtype < 0 || a->weight_dtype > 1 || a->h_dtype < 0 || a->h_dtype > 1)
+    return fail(B2F_ERR_ARG, "norm_quant: bad dtype");
+  if (a->dynamic_scale < B2F_SCALE_STATIC || a->dynamic_scale > B2F_SCALE_DYNAMIC_APPLY)
+    return fail(B2F_ERR_ARG, "norm_quant: bad dynamic_scale mode");
+  if (a->schedule != B2F_NORM_SCHEDULE_AUTO && a->schedule != B2F_NORM_SCHEDULE_ROWGROUP)
+    return fail(B2F_ERR_ARG, "norm_quant: bad schedule");
+  if (a->dynamic_scale == B2F_SCALE_DYNAMIC_STATS && a->amax == nullptr)
+    return fail(B2F_ERR_ARG, "norm_quant: the stats pass needs an amax buffer");
+  if ((a->dynamic_scale == B2F_SCALE_DYNAMIC || a->dynamic_scale == B2F_SCALE_DYNAMIC_APPLY) &&
+      (a->amax == nullptr || a->scale_out == nullptr))
+    return fail(B2F_ERR_ARG, "norm_quant: dynamic scale needs amax and scale_out buffers");
+  if (!a->dynamic_scale && !(a->q_scale > 0.0f))
+    return fail(B2F_ERR_ARG, "norm_quant: q_scale must be > 0");
+  const int xs = a->x_dtype == B2F_DTYPE_F32 ? 4 : (a->x_dtype == B2F_DTYPE_BF16 ? 2 : 1);
+  if (!al16(a->x) || (a->x_ld * xs) % 16 || a->x_ld < a->cols) return fail(B2F_ERR_ARG, "norm_quant: x layout");
+  if (a->residual && (!al16(a->residual) || a->residual_ld < a->cols || (a->residual_ld * 2) % 16))
+    return fail(B2F_ERR_ARG, "norm_quant: residual layout");
+  if (a->h_out && (!al16(a->h_out) || a->h_ld < a->cols || (a->h_ld * 2) % 16))
+    return fail(B2F_ERR_ARG, "norm_quant: h_out layout");
+  if (a->y_out && (!al16(a->y_out) || a->y_ld < a->cols || (a->y_ld * 2) % 16))
+    return fail(B2F_ERR_ARG, "norm_quant: y_out layout");
+  if ((((uintptr_t)a->q_out) & 7) || a->q_ld < a->cols || a->q_ld % 8) return fail(B2F_ERR_ARG, "norm_quant: q_out layout");
+  if (!al16(a->weight) || (a->bias && !al16(a->bias))) return fail(B2F_ERR_ARG, "norm_quant: weight alignment");
+  p.x = a->x; p.x_dtype = a->x_dtype; p.x_scale = a->x_scale; p.x_ld = a->x_ld;
+  p.residual = a->residual; p.res_dtype = a->residual_dtype; p.res_ld = a->residual_ld;
+  p.weight = a->weight; p.bias = a->bias; p.w_dtype = a->weight_dtype; p.w_offset = a->weight_offset;
+  p.kind = a->kind; p.eps = a->eps;
+  p.h_out = a->h_out; p.h_dtype = a->h_dtype; p.h_ld = a->h_ld;
+  p.y_out = a->y_out; p.y_ld = a->y_ld;
+  p.q_out = reinterpret_cast<uint8_t*>(a->q_out); p.q_ld = a->q_ld;
+  p.q_scale = a->q_scale; p.dynamic = a->dynamic_scale;
+  p.amax = a->amax; p.scale_out = a->scale_out;
+  p.rows = a->rows; p.cols = a->cols;
+  p.schedule = a->schedule;
+  return B2F_OK;
+}
 
 }  // namespace
 }  // namespace b2f
@@ -355,45 +811,20 @@ void b2f_norm_args_init(b2f_norm_args* a) {
 
 int b2f_norm_quant(const b2f_norm_args* a, b2f_stream_t stream) {
   using namespace b2f;
-  if (a == nullptr) return fail(B2F_ERR_ARG, "norm_quant: null args");
-  if (a->rows <= 0 || a->cols <= 0) return fail(B2F_ERR_ARG, "norm_quant: empty shape");
-  if (a->cols % 8 != 0) return fail(B2F_ERR_ARG, "norm_quant: cols must be a multiple of 8");
-  if (a->cols > kMaxCols)
-    return fail(B2F_ERR_UNSUPPORTED, "norm_quant: cols > 8192 not supported");
-  if (a->x == nullptr || a->weight == nullptr || a->q_out == nullptr)
-    return fail(B2F_ERR_ARG, "norm_quant: null tensor");
-  if (a->kind != B2F_NORM_RMS && a->kind != B2F_NORM_LAYER)
-    return fail(B2F_ERR_ARG, "norm_quant: bad kind");
-  if (a->x_dtype < 0 || a->x_dtype > 2 || a->residual_dtype < 0 || a->residual_dtype > 1 ||
-      a->weight_dtype < 0 || a->weight_dtype > 1 || a->h_dtype < 0 || a->h_dtype > 1)
-    return fail(B2F_ERR_ARG, "norm_quant: bad dtype");
-  if (a->dynamic_scale && (a->amax == nullptr || a->scale_out == nullptr))
-    return fail(B2F_ERR_ARG, "norm_quant: dynamic scale needs amax and scale_out buffers");
-  if (!a->dynamic_scale && !(a->q_scale > 0.0f))
-    return fail(B2F_ERR_ARG, "norm_quant: q_scale must be > 0");
-  const int xs = a->x_dtype == B2F_DTYPE_F32 ? 4 : (a->x_dtype == B2F_DTYPE_BF16 ? 2 : 1);
-  if (!al16(a->x) || (a->x_ld * xs) % 16 || a->x_ld < a->cols) return fail(B2F_ERR_ARG, "norm_quant: x layout");
-  if (a->residual && (!al16(a->residual) || a->residual_ld < a->cols || (a->residual_ld * 2) % 16))
-    return fail(B2F_ERR_ARG, "norm_quant: residual layout");
-  if (a->h_out && (!al16(a->h_out) || a->h_ld < a->cols || (a->h_ld * 2) % 16))
-    return fail(B2F_ERR_ARG, "norm_quant: h_out layout");
-  if (a->y_out && (!al16(a->y_out) || a->y_ld < a->cols || (a->y_ld * 2) % 16))
-    return fail(B2F_ERR_ARG, "norm_quant: y_out layout");
-  if ((((uintptr_t)a->q_out) & 7) || a->q_ld < a->cols || a->q_ld % 8) return fail(B2F_ERR_ARG, "norm_quant: q_out layout");
-  if (!al16(a->weight) || (a->bias && !al16(a->bias))) return fail(B2F_ERR_ARG, "norm_quant: weight alignment");
   NormParams p;
-  p.x = a->x; p.x_dtype = a->x_dtype; p.x_scale = a->x_scale; p.x_ld = a->x_ld;
-  p.residual = a->residual; p.res_dtype = a->residual_dtype; p.res_ld = a->residual_ld;
-  p.weight = a->weight; p.bias = a->bias; p.w_dtype = a->weight_dtype; p.w_offset = a->weight_offset;
-  p.kind = a->kind; p.eps = a->eps;
-  p.h_out = a->h_out; p.h_dtype = a->h_dtype; p.h_ld = a->h_ld;
-  p.y_out = a->y_out; p.y_ld = a->y_ld;
-  p.q_out = reinterpret_cast<uint8_t*>(a->q_out); p.q_ld = a->q_ld;
-  p.q_scale = a->q_scale; p.dynamic = a->dynamic_scale;
-  p.amax = a->amax; p.scale_out = a->scale_out;
-  p.rows = a->rows; p.cols = a->cols;
-  cudaStream_t s = (cudaStream_t)stream;
-  return launch_norm(p, s);
+  if (int rc = build_params(a, p)) return rc;
+  return launch_norm(p, (cudaStream_t)stream);
 }
+
+int b2f_norm_plan(const b2f_norm_args* a) {
+  using namespace b2f;
+  NormParams p;
+  if (int rc = build_params(a, p)) return -rc;
+  if (p.schedule != B2F_NORM_SCHEDULE_AUTO) return B2F_NORM_SCHEDULE_ROWGROUP;
+  StreamLaunch L;
+  const bool pass1 = p.dynamic != B2F_SCALE_DYNAMIC_APPLY;
+  return plan_stream(p, !pass1, L) ? B2F_NORM_SCHEDULE_AUTO : B2F_NORM_SCHEDULE_ROWGROUP;
+}
+
 
 }  // extern "C"

@@ -243,8 +243,15 @@ class NormWorkload:
     bound = "hbm"
     kernel = "norm_pass1_kernel<16> + norm_pass2_kernel<16>"
 
-    def __init__(self, rank: int, rows: int = 16384, cols: int = 4096):
+    scaling = "weak"
+
+    def __init__(self, rank: int, world: int = 1, rows: int = 16384, cols: int = 4096):
         g = torch.Generator("cpu").manual_seed(20260731 + rank)
+        self.world = world
+        self.sharded = None
+        if world > 1:
+            from b200fp8.sharding import RowShardedNorm
+            self.sharded = RowShardedNorm()
         self.rows, self.cols = rows, cols
         self.x_cpu = torch.randn((rows, cols), generator=g).to(torch.bfloat16)
         self.r_cpu = torch.randn((rows, cols), generator=g).to(torch.bfloat16)
@@ -263,10 +270,21 @@ class NormWorkload:
                 "rows": self.rows, "cols": self.cols, "eps": 1e-6,
                 "l2": "inputs 268 MB > 126 MB L2"}
 
+    def parallelism(self):
+        if self.world == 1:
+            return "single GPU"
+        return (f"row-sharded x{self.world}: each rank owns {self.rows} rows of a "
+                f"{self.rows * self.world}-row tensor; one f32 MAX all-reduce (NCCL) of the "
+                "amax between pass 1 and pass 2")
+
     def step(self):
         from b200fp8 import ops
-        ops.norm_quant(self.x, self.gamma, residual=self.r, h_out=self.h, q_out=self.q,
-                       amax=self.amax, scale_out=self.scale)
+        if self.sharded is not None:
+            self.sharded(self.x, self.gamma, residual=self.r, h_out=self.h, q_out=self.q,
+                         amax=self.amax, scale_out=self.scale)
+        else:
+            ops.norm_quant(self.x, self.gamma, residual=self.r, h_out=self.h, q_out=self.q,
+                           amax=self.amax, scale_out=self.scale)
         return 2
 
     def e2e_setup(self):
@@ -355,35 +373,60 @@ class BlockWorkload:
     unit = "TFLOP/s"
     bound = "tensor"
 
-    def __init__(self, kind: str, rank: int):
-        from b200fp8 import blocks
-        g = torch.Generator("cpu").manual_seed(20260801 + rank)
-        self.kind = kind
+    scaling = "strong"
+
+    def __init__(self, kind: str, rank: int, world: int = 1, tp=None):
+        from b200fp8 import blocks, sharding
+        # Weights are identical on every rank (fixed seed); inputs depend on the batch group.
+        g = torch.Generator("cpu").manual_seed(20260801)
+        self.kind, self.world = kind, world
         if kind == "gpt2":
             self.batch, self.seq, self.hidden = 8, 1024, 768
             self.w = _gpt2_weights(g)
-            cls = blocks.GPT2Block
+            self.dp, self.tp = sharding.plan_block_parallel(world, self.batch, 12, 12, tp=tp or 1)
             self.name = "gpt2_block_fp8"
             self.launches = 8
         else:
             self.batch, self.seq, self.hidden = 4, 2048, 2560
             self.w = _qwen_weights(g, self.seq)
-            cls = blocks.QwenBlock
+            self.dp, self.tp = sharding.plan_block_parallel(world, self.batch, 32, 8, tp=tp)
             self.name = "qwen_gated_attention_block_fp8"
             self.launches = 7
-        t = self.batch * self.seq
-        self.x_cpu = torch.randn((t, self.hidden), generator=g).to(torch.bfloat16)
-        self.blk = cls(self.w, batch=self.batch, seq=self.seq, residual_dtype=torch.bfloat16,
-                       out_dtype=torch.bfloat16)
+        if world > 1:
+            d, self.tp_rank, group = sharding.tp_groups(world, self.tp)
+        else:
+            d, self.tp_rank, group = 0, 0, None
+        self.local_batch = self.batch // self.dp
+        gx = torch.Generator("cpu").manual_seed(20260802 + d)
+        t = self.local_batch * self.seq
+        self.x_cpu = torch.randn((t, self.hidden), generator=gx).to(torch.bfloat16)
+        kw = dict(batch=self.local_batch, seq=self.seq, residual_dtype=torch.bfloat16,
+                  out_dtype=torch.bfloat16)
+        if kind == "gpt2":
+            self.blk = blocks.GPT2Block(self.w, **kw)
+        elif self.tp > 1:
+            self.blk = sharding.QwenBlockTP(self.w, group=group, tp_rank=self.tp_rank,
+                                            tp=self.tp, **kw)
+        else:
+            self.blk = blocks.QwenBlock(self.w, **kw)
         self.x = self.x_cpu.cuda()
         self.blk.capture(self.x)
         self.blk.graph_input.copy_(self.x)
         self.work = self.blk.flops()
         self.kernel = "whole block (CUDA graph)"
 
+    def parallelism(self):
+        if self.world == 1:
+            return "single GPU"
+        p = f"{self.dp} batch groups ({self.local_batch} sequences each, no communication)"
+        if self.tp > 1:
+            p += (f" x {self.tp}-way heads (column-parallel q/gate/k/v, row-parallel o-proj, "
+                  "one NCCL all-reduce of the bf16 [T x hidden] output)")
+        return p
+
     def config(self):
         c = {"workload": f"{self.name} B={self.batch} S={self.seq} hidden={self.hidden}",
-             "batch": self.batch, "seq": self.seq, "hidden": self.hidden,
+             "batch": self.batch, "dp": self.dp, "tp": self.tp, "seq": self.seq, "hidden": self.hidden,
              "residual": "bf16", "graph": "one CUDA graph per forward",
              "l2": "weights + activations per forward exceed L2 only for Qwen; GPT-2 weights "
                    "(7 MB) stay L2-resident across steps as in serving"}
@@ -426,15 +469,15 @@ class BlockWorkload:
                 "sample": f"1 of {self.batch} sequences through the CPU oracle block, {t:.2f} s"}
 
 
-def make_workload(name: str, n: int, rank: int):
+def make_workload(name: str, n: int, rank: int, world: int = 1, tp=None):
     if name == "gemm":
         return GemmWorkload(n, rank)
     if name == "gemm_bias_relu":
         return GemmWorkload(8192, rank, bias_relu=True, m=128)
     if name == "norm":
-        return NormWorkload(rank)
+        return NormWorkload(rank, world)
     if name in ("gpt2", "qwen"):
-        return BlockWorkload(name, rank)
+        return BlockWorkload(name, rank, world, tp)
     raise SystemExit(f"unknown workload {name}")
 
 
@@ -448,7 +491,7 @@ def run_ours(args):
         torch.cuda.set_device(0)
     from b200fp8 import _lib, device_status  # noqa: F401  (fails loudly without the .so)
 
-    wl = make_workload(args.workload, args.n, rank)
+    wl = make_workload(args.workload, args.n, rank, world, args.tp)
     unit = wl.unit
     stream = torch.cuda.current_stream()
     for _ in range(args.warmup):
@@ -539,17 +582,20 @@ def run_ours(args):
         peak = peaks["hbm_gbs"]
         basis = f"{peaks['basis']} HBM copy bandwidth"
     achieved = wl.work / (per_launch_ms * 1e-3) / scale
-    parallel = {"gemm": "N-sharded columns", "gemm_bias_relu": "N-sharded columns",
-                "norm": "row-sharded", "gpt2": "independent replicas",
-                "qwen": "independent replicas"}[args.workload]
+    if hasattr(wl, "parallelism"):
+        parallel = wl.parallelism()
+    else:
+        parallel = ("single GPU" if world == 1 else
+                    f"N-sharded columns x{world} (each rank its own column block, "
+                    "no communication)")
     out = {
         "metric": f"{unit} ({wl.name}, whole job)", "value": round(value, 2), "unit": unit,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms_per_step, 5), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None,
+        "scaling": getattr(wl, "scaling", "weak"), "vs_baseline": None,
         "dtype": "e4m3 in, f32 accumulate, bf16 out",
         "data": "synthetic (seeded N(0,1), per-tensor amax e4m3 scales; random-init weights)",
-        "config": dict(wl.config(), parallelism=f"{parallel} x{world} (no communication)"),
+        "config": dict(wl.config(), parallelism=parallel),
         "roofline": {"bound": wl.bound, "achieved": round(achieved, 1), "peak": round(peak, 1),
                      "unit": unit, "frac": round(achieved / peak, 4), "peak_basis": basis,
                      "traffic": None, "kernel": getattr(wl, "kernel", "gemm_fp8"),
@@ -648,6 +694,8 @@ def main():
     ap.add_argument("--ref-rows", type=int, default=0,
                     help="rows per reference step (0 = sized for a ~2 minute run)")
     ap.add_argument("--soak-seconds", type=float, default=1.0)
+    ap.add_argument("--tp", type=int, default=None,
+                    help="qwen: head-parallel group size (default: batch groups first)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -167,9 +167,27 @@ int b2f_gemm_pair_capacity(void);
  *   starter.py:167-171, used at :347-348 and :402-403), the GPT-2 LayerNorm steps
  *   (tasks/model_gpt2_small_transformer_block_fp8/starter.py:407-416, 461-470) and
  *   layer_norm (tasks/level1_40_layer_norm_fp8/starter.py).
+ * dynamic_scale selects the scale:
+ *   B2F_SCALE_STATIC        s = q_scale, one pass;
+ *   B2F_SCALE_DYNAMIC       both passes below on this device;
+ *   B2F_SCALE_DYNAMIC_STATS pass 1 only: writes h_out, leaves amax(|bf16(y)|) of these rows
+ *                           in *amax (zeroed first), stores no q;
+ *   B2F_SCALE_DYNAMIC_APPLY pass 2 only: reads *amax (e.g. after a MAX all-reduce of every
+ *                           row shard's amax), writes *scale_out and q (and y_out).
+ * The STATS / APPLY split lets row shards on several GPUs share one per-tensor scale.
+ * schedule: B2F_NORM_SCHEDULE_AUTO streams rows through shared memory with bulk copies
+ * (persistent CTAs) whenever every row is a 16-byte multiple, else falls back to
+ * B2F_NORM_SCHEDULE_ROWGROUP (one row per thread group, no staging); both give identical bits.
  * Requirements: cols % 8 == 0, cols <= 8192, 16-byte aligned rows.
  */
 enum b2f_norm_kind { B2F_NORM_RMS = 0, B2F_NORM_LAYER = 1 };
+enum b2f_scale_mode {
+  B2F_SCALE_STATIC = 0,
+  B2F_SCALE_DYNAMIC = 1,
+  B2F_SCALE_DYNAMIC_STATS = 2,
+  B2F_SCALE_DYNAMIC_APPLY = 3
+};
+enum b2f_norm_schedule { B2F_NORM_SCHEDULE_AUTO = 0, B2F_NORM_SCHEDULE_ROWGROUP = 1 };
 
 typedef struct b2f_norm_args {
   int rows, cols;
@@ -194,13 +212,19 @@ typedef struct b2f_norm_args {
   void* q_out;
   long long q_ld;
   float q_scale;
-  int dynamic_scale;
+  int dynamic_scale; /* b2f_scale_mode */
   float* amax;
   float* scale_out;
+  int schedule; /* b2f_norm_schedule */
 } b2f_norm_args;
 
 void b2f_norm_args_init(b2f_norm_args* args);
 int b2f_norm_quant(const b2f_norm_args* args, b2f_stream_t stream);
+
+/* Which kernels b2f_norm_quant would run for these arguments (first pass it runs):
+ * 0 = streaming schedule (shared-memory ring of rows), 1 = row-group kernels, or -code when
+ * the arguments are invalid.  Launches nothing; needs the current device. */
+int b2f_norm_plan(const b2f_norm_args* args);
 
 /* ------------------------------------------------------------------ attention
  * ctx[t, h*D:(h+1)*D] = e4m3( softmax(q_h k_g^T * sm_scale [causal]) v_g * sigmoid(gate) / ctx_scale )

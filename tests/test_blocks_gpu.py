@@ -85,3 +85,26 @@ def test_qwen_block_baseline_style_bf16():
     out = blk.forward(x.cuda())
     torch.cuda.synchronize()
     _check(out, ref, 0.08, 2.0 ** -8)
+
+
+@pytest.mark.parametrize("tp", [2, 4, 8])
+def test_qwen_heads_parallel_partials_sum_to_block(tp):
+    """The head slices of the tensor-parallel block, run on one GPU and summed in f32 (what
+    the all-reduce does across GPUs), match the unsharded block and the oracle."""
+    from b200fp8 import sharding
+    g = gen(20260803)
+    batch, seq = 2, 256
+    w = qwen_weights(hidden=2560, heads=32, kv_heads=8, head_dim=128, rotary_dim=128,
+                     theta=1e6, seq=seq, g=g, interleaved=False, reference=False)
+    x = torch.randn((batch * seq, 2560), generator=g).to(torch.bfloat16)
+    ref = ob.qwen_block(x.float(), w, batch=batch, residual_dtype=torch.bfloat16,
+                        out_dtype=torch.bfloat16)
+    total = torch.zeros((batch * seq, 2560), device="cuda")
+    xd = x.cuda()
+    for r in range(tp):
+        local = sharding.qwen_tp_weights(w, r, tp)
+        blk = _blocks().QwenBlock(local, batch=batch, seq=seq, residual_dtype=torch.bfloat16,
+                                  out_dtype=torch.bfloat16, add_residual=(r == 0))
+        total += blk.forward(xd).float()
+    torch.cuda.synchronize()
+    _check(total.to(torch.bfloat16), ref, 0.08, 2.0 ** -7)

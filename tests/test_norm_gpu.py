@@ -86,3 +86,129 @@ def test_f32_residual_stream():
     torch.cuda.synchronize()
     assert torch.allclose(h.cpu(), h_ref, rtol=0, atol=0)
     _assert_q(q, (y / (1 / 64.0)).to(torch.float8_e4m3fn))
+
+
+def _norm_case(rows, cols, x_dtype, res_dtype, kind, static, seed):
+    g = gen(seed)
+    x = randn((rows, cols), g)
+    if x_dtype == torch.float8_e4m3fn:
+        # rows padded to a 16-byte pitch (the ABI's e4m3 row rule); a view keeps `cols`
+        pitch = (cols + 15) // 16 * 16
+        xp = torch.zeros((rows, pitch))
+        xp[:, :cols] = x * 448 / float(x.abs().max())
+        x = xp.to(x_dtype)  # callers slice [:, :cols] on the device
+    else:
+        x = x.to(x_dtype)
+    r = None if res_dtype is None else randn((rows, cols), g).to(res_dtype)
+    w = (1 + randn((cols,), g, 0.02))
+    b = randn((cols,), g, 0.02) if kind == "layer" else None
+    return x, r, w, b
+
+
+@pytest.mark.parametrize("rows,cols,x_dtype,res_dtype,kind,static", [
+    (1000, 4096, torch.bfloat16, torch.bfloat16, "rms", False),
+    (333, 768, torch.bfloat16, torch.bfloat16, "layer", True),
+    (257, 2560, torch.float8_e4m3fn, None, "rms", True),
+    (130, 8192, torch.float32, torch.float32, "layer", False),
+    (77, 1024, torch.bfloat16, torch.float32, "rms", True),
+    (5, 8, torch.float8_e4m3fn, None, "rms", False),       # 8-byte rows: row-group fallback
+    (64, 16, torch.float8_e4m3fn, torch.bfloat16, "layer", True),
+    (2049, 512, torch.bfloat16, None, "layer", False),
+])
+def test_stream_and_rowgroup_schedules_agree(rows, cols, x_dtype, res_dtype, kind, static):
+    """The streaming schedule (warp-per-row, bulk copies into shared-memory rings) and the
+    row-group kernels compute the same formulas with different f32 summation orders: h is
+    identical, the scale equal to 1e-6, y within 1 bf16 ulp, q within 1 e4m3 step."""
+    ops = _ops()
+    x, r, w, b = _norm_case(rows, cols, x_dtype, res_dtype, kind, static, 7 + rows)
+    dev = lambda t: None if t is None else t.cuda()  # noqa: E731
+    xd = dev(x)[:, :cols]
+    expect = "rowgroup" if (x_dtype == torch.float8_e4m3fn and cols % 16) else "stream"
+    probe = ops.norm_quant(xd, w.cuda(), kind=kind, bias=dev(b), residual=dev(r),
+                           q_scale=(1 / 64.0) if static else None, query_schedule=True)
+    assert probe == expect
+    outs = []
+    for schedule in ("auto", "rowgroup"):
+        h = torch.empty((rows, cols), dtype=res_dtype or torch.bfloat16, device="cuda") \
+            if r is not None else None
+        y = torch.empty((rows, cols), dtype=torch.bfloat16, device="cuda")
+        q, s = ops.norm_quant(xd, w.cuda(), kind=kind, bias=dev(b), eps=1e-5,
+                              x_scale=0.5 if x_dtype == torch.float8_e4m3fn else 1.0,
+                              residual=dev(r), h_out=h, y_out=y,
+                              q_scale=(1 / 64.0) if static else None, schedule=schedule)
+        torch.cuda.synchronize()
+        outs.append((q.view(torch.uint8).cpu(), None if s is None else s.cpu(),
+                     None if h is None else h.cpu(), y.cpu()))
+    (qa, sa, ha, ya), (qb, sb, hb, yb) = outs
+    if ha is not None:
+        assert torch.equal(ha, hb)
+    if sa is not None:
+        assert abs(float(sa) - float(sb)) <= 1e-6 * abs(float(sb))
+    yd = (ya.float() - yb.float()).abs()
+    assert bool((yd <= yb.float().abs() * 2.0 ** -7 + 1e-30).all())
+    _assert_q(qa.view(torch.float8_e4m3fn), qb.view(torch.float8_e4m3fn).cpu())
+
+
+@pytest.mark.parametrize("shards", [2, 3])
+def test_stats_apply_phases_share_one_scale_across_row_shards(shards):
+    """Row shards run pass 1 (``phase="stats"``), their amax values are max-reduced (the
+    all-reduce of a row-sharded job), then each runs pass 2 (``phase="apply"``): the result
+    equals the single-device dynamic-scale run."""
+    ops = _ops()
+    rows, cols = 1500, 4096
+    x, r, w, _ = _norm_case(rows, cols, torch.bfloat16, torch.bfloat16, "rms", False, 99)
+    x, r, w = x.cuda(), r.cuda(), w.to(torch.bfloat16).cuda()
+    h_full = torch.empty_like(x)
+    q_full, s_full = ops.norm_quant(x, w, residual=r, h_out=h_full)
+    bounds = [rows * i // shards for i in range(shards + 1)]
+    amaxes, hs = [], []
+    for i in range(shards):
+        sl = slice(bounds[i], bounds[i + 1])
+        a = torch.zeros(1, device="cuda")
+        h = torch.empty_like(x[sl])
+        ops.norm_quant(x[sl], w, residual=r[sl], h_out=h, amax=a, phase="stats")
+        amaxes.append(a)
+        hs.append(h)
+    amax = torch.stack(amaxes).max().reshape(1)
+    qs, ss = [], []
+    for i in range(shards):
+        sl = slice(bounds[i], bounds[i + 1])
+        s = torch.empty(1, device="cuda")
+        q, _ = ops.norm_quant(x[sl], w, residual=r[sl], h_out=hs[i], amax=amax.clone(),
+                              scale_out=s, phase="apply")
+        qs.append(q)
+        ss.append(s)
+    torch.cuda.synchronize()
+    assert torch.equal(torch.cat(hs), h_full)
+    for s in ss:
+        assert torch.equal(s, s_full)
+    assert torch.equal(torch.cat(qs).view(torch.uint8), q_full.view(torch.uint8))
+
+
+@pytest.mark.parametrize("kind,static", [("rms", False), ("rms", True), ("layer", True)])
+def test_stream_schedule_against_oracle_large(kind, static):
+    """BASELINE config 3 size through the streaming schedule against the CPU oracle."""
+    ops = _ops()
+    rows, cols = 16384, 4096
+    g = gen(4242)
+    x = randn((rows, cols), g).to(torch.bfloat16)
+    r = randn((rows, cols), g).to(torch.bfloat16)
+    w = (1 + randn((cols,), g, 0.02)).to(torch.bfloat16)
+    b = randn((cols,), g, 0.02).to(torch.bfloat16) if kind == "layer" else None
+    h_ref, y_ref = onorm.residual_norm(x, w, kind=kind, bias=b, eps=1e-6, residual=r,
+                                       h_dtype=torch.bfloat16)
+    if static:
+        q_ref = (y_ref / (1 / 64.0)).to(torch.float8_e4m3fn)
+    else:
+        yb = y_ref.to(torch.bfloat16).float()
+        s_ref = float(yb.abs().max()) / 448.0
+        q_ref = (yb / s_ref).to(torch.float8_e4m3fn)
+    h = torch.empty((rows, cols), dtype=torch.bfloat16, device="cuda")
+    q, s = ops.norm_quant(x.cuda(), w.cuda(), kind=kind, bias=None if b is None else b.cuda(),
+                          eps=1e-6, residual=r.cuda(), h_out=h,
+                          q_scale=(1 / 64.0) if static else None)
+    torch.cuda.synchronize()
+    assert torch.equal(h.cpu(), h_ref.to(torch.bfloat16))
+    if not static:
+        assert abs(float(s.cpu()) - s_ref) <= 1e-6 * s_ref
+    _assert_q(q, q_ref)
