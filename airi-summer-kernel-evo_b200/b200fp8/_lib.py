@@ -94,6 +94,17 @@ class NormArgs(ctypes.Structure):
     ]
 
 
+class QuantArgs(ctypes.Structure):
+    _fields_ = [
+        ("rows", ctypes.c_int), ("cols", ctypes.c_int),
+        ("x", ctypes.c_void_p), ("x_dtype", ctypes.c_int), ("x_ld", ctypes.c_longlong),
+        ("q", ctypes.c_void_p), ("q_ld", ctypes.c_longlong),
+        ("dynamic", ctypes.c_int), ("scale", ctypes.c_float),
+        ("amax", ctypes.c_void_p), ("scale_out", ctypes.c_void_p),
+        ("scale_mul", ctypes.c_void_p), ("scale_prod_out", ctypes.c_void_p),
+    ]
+
+
 class AttnArgs(ctypes.Structure):
     """Mirror of ``b2f_attn_args`` (include/b200fp8.h)."""
 
@@ -142,6 +153,7 @@ EXPORTED_SYMBOLS = (
     "b2f_gemm_workspace_bytes", "b2f_gemm_fp8_static",
     "b2f_norm_args_init", "b2f_norm_quant", "b2f_norm_plan", "b2f_attn_args_init", "b2f_attention_fp8",
     "b2f_head_norm_rope", "b2f_fp8_to_bf16", "b2f_swiglu_fp8",
+    "b2f_quant_args_init", "b2f_quantize_fp8",
     "b2f_registry_lookup", "b2f_registry_size", "b2f_registry_at",
 )
 
@@ -170,6 +182,10 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.b2f_norm_args_init.restype = None
     lib.b2f_norm_quant.argtypes = [ctypes.POINTER(NormArgs), vp]
     lib.b2f_norm_quant.restype = ctypes.c_int
+    lib.b2f_quant_args_init.argtypes = [ctypes.POINTER(QuantArgs)]
+    lib.b2f_quant_args_init.restype = None
+    lib.b2f_quantize_fp8.argtypes = [ctypes.POINTER(QuantArgs), vp]
+    lib.b2f_quantize_fp8.restype = ctypes.c_int
     lib.b2f_norm_plan.argtypes = [ctypes.POINTER(NormArgs)]
     lib.b2f_norm_plan.restype = ctypes.c_int
     lib.b2f_attn_args_init.argtypes = [ctypes.POINTER(AttnArgs)]

@@ -277,6 +277,37 @@ def head_norm_rope(x: torch.Tensor, *, heads: int, head_dim: int, in_scale: floa
     return out
 
 
+def quantize_fp8(x: torch.Tensor, *, scale: Optional[float] = None,
+                 out: Optional[torch.Tensor] = None, amax: Optional[torch.Tensor] = None,
+                 scale_out: Optional[torch.Tensor] = None,
+                 scale_mul: Optional[torch.Tensor] = None,
+                 scale_prod_out: Optional[torch.Tensor] = None):
+    """Per-tensor e4m3 quantisation of an f32 / bf16 [rows, cols] tensor (see
+    b2f_quantize_fp8).  ``scale=None`` selects s = amax(|x|) / 448, returned as an f32 [1]
+    device tensor.  Returns ``(q, s)``."""
+    _check_cuda(x, out, amax, scale_out, scale_mul, scale_prod_out)
+    if x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError("x must be row-major 2-D")
+    rows, cols = x.shape
+    if out is None:
+        out = torch.empty((rows, cols), device=x.device, dtype=torch.float8_e4m3fn)
+    a = _lib.QuantArgs()
+    _lib.lib().b2f_quant_args_init(ctypes.byref(a))
+    a.rows, a.cols = rows, cols
+    a.x, a.x_dtype, a.x_ld = x.data_ptr(), _DT[x.dtype], x.stride(0)
+    a.q, a.q_ld = out.data_ptr(), out.stride(0)
+    if scale is None:
+        amax = torch.empty(1, device=x.device) if amax is None else amax
+        scale_out = torch.empty(1, device=x.device) if scale_out is None else scale_out
+        a.dynamic = 1
+    else:
+        a.scale = float(scale)
+    a.amax, a.scale_out = _ptr(amax), _ptr(scale_out)
+    a.scale_mul, a.scale_prod_out = _ptr(scale_mul), _ptr(scale_prod_out)
+    check(_lib.lib().b2f_quantize_fp8(ctypes.byref(a), _stream()))
+    return out, (scale_out if scale is None else scale)
+
+
 def fp8_to_bf16(x: torch.Tensor, scale: float = 1.0,
                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """bf16 copy of an e4m3 [rows, cols] view (exact), times ``scale``."""

@@ -486,7 +486,9 @@ def run_ours(args):
     if world > 1:
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        import datetime
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                timeout=datetime.timedelta(seconds=120))
     else:
         torch.cuda.set_device(0)
     from b200fp8 import _lib, device_status  # noqa: F401  (fails loudly without the .so)
@@ -504,11 +506,18 @@ def run_ours(args):
         time.sleep(0.3)
     # Untimed soak (~1 s of the same steps) so the clocks the sampler sees, and the
     # timed region, are the sustained under-load state rather than an idle-clock burst.
-    t_soak = time.time()
-    while time.time() - t_soak < args.soak_seconds:
-        for _ in range(8):
-            wl.step()
-        torch.cuda.synchronize()
+    # Every rank runs the same number of soak steps (steps may hold collectives).
+    t_est = time.time()
+    for _ in range(2):
+        wl.step()
+    torch.cuda.synchronize()
+    per_step_s = max((time.time() - t_est) / 2, 1e-6)
+    n_soak = int(_max_over_ranks(float(min(20000, args.soak_seconds / per_step_s)), world))
+    for i in range(n_soak):
+        wl.step()
+        if i % 64 == 63:
+            torch.cuda.synchronize()
+    torch.cuda.synchronize()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(args.steps)]
     _barrier(world)

@@ -302,6 +302,33 @@ int b2f_head_norm_rope(const b2f_rope_args* args, b2f_stream_t stream);
 int b2f_fp8_to_bf16(const void* in, long long in_ld, void* out, long long out_ld, int rows,
                     int cols, float scale, b2f_stream_t stream);
 
+/* ------------------------------------------------------------------ quantise
+ * q = e4m3(x / s), x f32 or bf16 [rows, cols] (row pitch x_ld elements, 16-byte aligned
+ * rows), q e4m3 bytes (row pitch q_ld, 8-byte aligned rows); IEEE division, RN, saturating.
+ * dynamic != 0: s = amax(|x|) / 448 (1 for an all-zero x), reduced into *amax and written to
+ * *scale_out; else s = scale.  With scale_mul, *scale_prod_out = s * *scale_mul (the GEMM
+ * alpha of two dynamically scaled operands, for b2f_gemm_args.alpha_ptr).
+ * Replaces: the per-tensor FP8 quantisation the reference applies to its operands
+ *   (`(source / scale).to(torch.float8_e4m3fn)`, e.g.
+ *   tasks/level1_01_square_matrix_multiplication_fp8/starter.py:61-99). */
+typedef struct b2f_quant_args {
+  int rows, cols;
+  const void* x;
+  int x_dtype;
+  long long x_ld;
+  void* q;
+  long long q_ld;
+  int dynamic;
+  float scale;
+  float* amax;
+  float* scale_out;
+  const float* scale_mul;
+  float* scale_prod_out;
+} b2f_quant_args;
+
+void b2f_quant_args_init(b2f_quant_args* args);
+int b2f_quantize_fp8(const b2f_quant_args* args, b2f_stream_t stream);
+
 /* out = e4m3( silu(gate * in_scale) * (up * in_scale) / out_scale ); gate, up, out e4m3
  * [rows, cols] with row pitches in elements.
  * Replaces: swiglu_kernel (tasks/model_qwen35_4b_full_attention_block_fp8/starter.py:51-58;

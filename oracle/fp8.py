@@ -31,3 +31,14 @@ def quantize_amax(x: torch.Tensor):
     """(e4m3 tensor, scale) with the per-tensor amax scale."""
     s = amax_scale(x)
     return quantize(x, s), s
+
+
+def quantize_amax_f32(x: torch.Tensor):
+    """(e4m3 tensor, f32 scale) with s = amax(|x|) / 448 computed in f32 and q = e4m3(x / s)
+    by f32 division: the device quantiser's convention (b2f_quantize_fp8), equal to the torch
+    expression ``s = x.abs().max() / 448.0; (x / s).to(float8_e4m3fn)`` on an f32 tensor."""
+    xf = x.float()
+    s = xf.abs().max() / FP8_MAX
+    if float(s) == 0.0:
+        s = torch.ones((), dtype=torch.float32)
+    return (xf / s).to(torch.float8_e4m3fn), float(s)

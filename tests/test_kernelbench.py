@@ -28,25 +28,49 @@ def test_task_sources_define_contract(name):
     assert issubclass(n["ModelNew"], r["Model"])
 
 
-def _flat(out):
-    return list(out) if isinstance(out, (tuple, list)) else [out]
+def _set_seed(seed):
+    torch.manual_seed(seed)
+    torch.cuda.manual_seed(seed)
+
+
+def _kernelevo_trial(name, precision, seed=42, trial_seed=1234):
+    """One correctness trial the way KernelEvo runs it (eval.py:418-439, 590-606, 840-900):
+    seeded construction of both models, ``.to(device, dtype=precision)``, seeded inputs cast
+    to ``precision`` on the device, ``torch.allclose`` on the single output."""
+    ref, new = kernelbench.task_source(name)
+    r, n = _load(ref), _load(new)
+    dev = torch.device("cuda", 0)
+    init = r["get_init_inputs"]()
+    _set_seed(seed)
+    model = r["Model"](*init)
+    _set_seed(seed)
+    model_new = n["ModelNew"](*init)
+    model = model.to(device=dev, dtype=precision)
+    model_new = model_new.to(device=dev, dtype=precision)
+    _set_seed(trial_seed)
+    inputs = [x.to(dtype=precision).to(device=dev) if torch.is_tensor(x) else x
+              for x in r["get_inputs"]()]
+    with torch.no_grad():
+        expected = model(*inputs)
+        actual = model_new(*inputs)
+    torch.cuda.synchronize()
+    assert expected.shape == actual.shape
+    e32, a32 = expected.float(), actual.float()
+    assert bool(torch.isfinite(a32).all())
+    err = (e32 - a32).abs().max().item()
+    ok = torch.allclose(e32, a32, atol=r["output_atol"], rtol=r["output_rtol"])
+    return ok, err
 
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("name", sorted(kernelbench.TASKS))
 def test_model_new_matches_model(name):
-    ref, new = kernelbench.task_source(name)
-    r, n = _load(ref), _load(new)
-    init = r["get_init_inputs"]()
-    inputs = r["get_inputs"]()
-    expected = _flat(r["Model"](*init)(*inputs))
-    actual = _flat(n["ModelNew"](*init)(*inputs))
-    torch.cuda.synchronize()
-    assert len(expected) == len(actual)
-    for e, a in zip(expected, actual):
-        assert e.shape == a.shape and e.dtype == a.dtype
-        e32, a32 = e.float(), a.float()
-        assert bool(torch.isfinite(a32).all())
-        err = (e32 - a32).abs().max().item()
-        ok = torch.allclose(e32, a32, atol=r["output_atol"], rtol=r["output_rtol"])
-        assert ok, f"{name}: max abs error {err}"
+    ok, err = _kernelevo_trial(name, torch.float32)
+    assert ok, f"{name}: max abs error {err}"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", ["gemm_bias_relu_fp8", "gpt2_block_fp8"])
+def test_model_new_matches_model_bf16_precision(name):
+    ok, err = _kernelevo_trial(name, torch.bfloat16)
+    assert ok, f"{name}: max abs error {err}"
