@@ -23,6 +23,7 @@ B2F_ERR_NCCL = 5
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
 DTYPE_E4M3 = 2
+DTYPE_F16 = 3
 
 ACT_NONE = 0
 ACT_RELU = 1
@@ -118,6 +119,7 @@ class AttnArgs(ctypes.Structure):
         ("gate", ctypes.c_void_p), ("gate_dtype", ctypes.c_int), ("gate_ld", ctypes.c_longlong),
         ("gate_head_stride", ctypes.c_longlong), ("gate_scale", ctypes.c_float),
         ("ctx", ctypes.c_void_p), ("ctx_ld", ctypes.c_longlong), ("ctx_scale", ctypes.c_float),
+        ("v_dtype", ctypes.c_int),
     ]
 
 
@@ -152,7 +154,7 @@ EXPORTED_SYMBOLS = (
     "b2f_debug_bounded_wait", "b2f_gemm_args_init", "b2f_gemm_fp8", "b2f_gemm_pair_capacity",
     "b2f_gemm_workspace_bytes", "b2f_gemm_fp8_static",
     "b2f_norm_args_init", "b2f_norm_quant", "b2f_norm_plan", "b2f_attn_args_init", "b2f_attention_fp8",
-    "b2f_head_norm_rope", "b2f_fp8_to_bf16", "b2f_swiglu_fp8",
+    "b2f_head_norm_rope", "b2f_fp8_to_bf16", "b2f_fp8_to_f16", "b2f_swiglu_fp8",
     "b2f_quant_args_init", "b2f_quantize_fp8",
     "b2f_registry_lookup", "b2f_registry_size", "b2f_registry_at",
 )
@@ -197,6 +199,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.b2f_fp8_to_bf16.argtypes = [vp, ctypes.c_longlong, vp, ctypes.c_longlong, ctypes.c_int,
                                     ctypes.c_int, ctypes.c_float, vp]
     lib.b2f_fp8_to_bf16.restype = ctypes.c_int
+    lib.b2f_fp8_to_f16.argtypes = lib.b2f_fp8_to_bf16.argtypes
+    lib.b2f_fp8_to_f16.restype = ctypes.c_int
     lib.b2f_swiglu_fp8.argtypes = [vp, ctypes.c_longlong, vp, ctypes.c_longlong, vp,
                                    ctypes.c_longlong, ctypes.c_int, ctypes.c_int, ctypes.c_float,
                                    ctypes.c_float, vp]

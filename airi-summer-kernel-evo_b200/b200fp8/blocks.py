@@ -6,13 +6,13 @@ a CUDA graph (``capture``) and replayed without per-launch host cost (``replay``
 
 GPT-2 block (tasks/model_gpt2_small_transformer_block_fp8/starter.py:114-140, reference
 math :393-488), 8 launches:
-  norm_quant(LN1) -> gemm(QKV + bias, e4m3) -> fp8_to_bf16(V) -> attention(causal)
+  norm_quant(LN1) -> gemm(QKV + bias, e4m3) -> fp8_to_f16(V) -> attention(causal)
   -> gemm(out-proj + bias + residual x) -> norm_quant(LN2) -> gemm(FC + bias, GELU-tanh,
   e4m3) -> gemm(proj + bias + residual r1)
 Qwen full-attention block (tasks/model_qwen35_4b_full_attention_block_fp8/starter.py:66-98,
 reference math :333-416):
   norm_quant(RMSNorm 1+w) -> one fused gemm over [Wq | Wgate | Wk | Wv] with per-column
-  scales -> head_norm_rope(q), head_norm_rope(k) -> fp8_to_bf16(V) -> attention(causal,
+  scales -> head_norm_rope(q), head_norm_rope(k) -> fp8_to_f16(V) -> attention(causal,
   GQA, sigmoid gate) -> gemm(o-proj + residual) [-> norm_quant -> gemm([Wgate|Wup])
   -> swiglu -> gemm(down + residual)]
 Weights are passed as any object with the fields of the reference-style containers
@@ -37,6 +37,19 @@ def _dev(t: Optional[torch.Tensor], device, dtype=None) -> Optional[torch.Tensor
     if dtype is not None:
         t = t.to(dtype)
     return t.contiguous()
+
+
+def _v_dtype(head_dim: int) -> torch.dtype:
+    """V operand type: f16 (P in f16, exponentials in pairs) where the attention kernel
+    offers it (head_dim 64 / 128), bf16 otherwise.  Both hold e4m3 values exactly."""
+    return torch.float16 if head_dim in (64, 128) else torch.bfloat16
+
+
+def _v_convert(src: torch.Tensor, dst: torch.Tensor) -> None:
+    if dst.dtype == torch.float16:
+        ops.fp8_to_f16(src, out=dst)
+    else:
+        ops.fp8_to_bf16(src, out=dst)
 
 
 class _Graphable:
@@ -100,7 +113,7 @@ class GPT2Block(_Graphable):
         t, d = self.t, self.d
         self.n1 = torch.empty((t, d), device=device, dtype=_E4M3)
         self.qkv = torch.empty((t, 3 * d), device=device, dtype=_E4M3)
-        self.v16 = torch.empty((t, d), device=device, dtype=torch.bfloat16)
+        self.v16 = torch.empty((t, d), device=device, dtype=_v_dtype(self.hd))
         self.ctx = torch.empty((t, d), device=device, dtype=_E4M3)
         self.r1 = torch.empty((t, d), device=device, dtype=residual_dtype)
         self.n2 = torch.empty((t, d), device=device, dtype=_E4M3)
@@ -127,7 +140,7 @@ class GPT2Block(_Graphable):
                        x_scale=hidden_scale, q_out=self.n1, q_scale=self.ns)
         ops.gemm_fp8(self.n1, self.qkv_w, scale_a=self.ns, scale_b=self.qkv_s, bias=self.qkv_b,
                      out=self.qkv, out_scale=self.qs)
-        ops.fp8_to_bf16(self.qkv[:, 2 * d:], out=self.v16)
+        _v_convert(self.qkv[:, 2 * d:], self.v16)
         q, k = self.qkv[:, :d], self.qkv[:, d:2 * d]
         if self.rope:
             for src, dst in ((q, self.q_rot), (k, self.k_rot)):
@@ -194,7 +207,7 @@ class QwenBlock(_Graphable):
         self.proj = torch.empty((t, self.n_cat), device=device, dtype=_E4M3)
         self.q = torch.empty((t, h * dh), device=device, dtype=_E4M3)
         self.k = torch.empty((t, hk * dh), device=device, dtype=_E4M3)
-        self.v16 = torch.empty((t, hk * dh), device=device, dtype=torch.bfloat16)
+        self.v16 = torch.empty((t, hk * dh), device=device, dtype=_v_dtype(dh))
         self.ctx = torch.empty((t, h * dh), device=device, dtype=_E4M3)
         if self.has_mlp:
             self.r1 = torch.empty((t, self.hidden), device=device, dtype=residual_dtype)
@@ -233,7 +246,7 @@ class QwenBlock(_Graphable):
                            out_scale=self.qs, weight=self.k_norm, weight_offset=1.0,
                            eps=self.eps, cos=self.cos, sin=self.sin, rotary_dim=self.rot,
                            seq=self.seq, out=self.k)
-        ops.fp8_to_bf16(self.proj[:, self.v_off:self.v_off + hk * dh], out=self.v16)
+        _v_convert(self.proj[:, self.v_off:self.v_off + hk * dh], self.v16)
         ops.attention_fp8(self.q, self.k, self.v16, batch=self.batch, heads=h, kv_heads=hk,
                           head_dim=dh, causal=True, q_scale=self.qs, k_scale=self.qs,
                           v_scale=self.qs, gate=self.proj[:, self.g_off:], gate_scale=self.qs,

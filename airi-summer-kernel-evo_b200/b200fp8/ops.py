@@ -25,6 +25,7 @@ _DT = {
     torch.bfloat16: _lib.DTYPE_BF16,
     torch.float8_e4m3fn: _lib.DTYPE_E4M3,
     torch.uint8: _lib.DTYPE_E4M3,
+    torch.float16: _lib.DTYPE_F16,
 }
 
 
@@ -219,13 +220,15 @@ def attention_fp8(q: torch.Tensor, k: torch.Tensor, v_bf16: torch.Tensor, *, bat
                   gate_scale: float = 1.0, gate_head_stride: Optional[int] = None,
                   ctx: Optional[torch.Tensor] = None, ctx_scale: float = 1.0) -> torch.Tensor:
     """Fused attention (see b2f_attention_fp8).  q/k are e4m3 2-D [T, cols] views with head h
-    at column h*head_dim (row pitch = stride(0)); v_bf16 is bf16 [T, cols]; returns the e4m3
-    context [T, heads*head_dim]."""
+    at column h*head_dim (row pitch = stride(0)); v is bf16 or f16 [T, cols] (f16 selects
+    the f16-probability path, head_dim 64 / 128); returns the e4m3 context
+    [T, heads*head_dim]."""
     _check_cuda(q, k, v_bf16, gate, ctx)
     _fp8_rows(q, "q")
     _fp8_rows(k, "k")
-    if v_bf16.dtype != torch.bfloat16 or v_bf16.dim() != 2 or v_bf16.stride(1) != 1:
-        raise TypeError("v must be a row-major bf16 2-D tensor")
+    if (v_bf16.dtype not in (torch.bfloat16, torch.float16) or v_bf16.dim() != 2
+            or v_bf16.stride(1) != 1):
+        raise TypeError("v must be a row-major bf16 or f16 2-D tensor")
     t = q.shape[0]
     if t % batch:
         raise ValueError("token count must be batch * seq")
@@ -238,6 +241,7 @@ def attention_fp8(q: torch.Tensor, k: torch.Tensor, v_bf16: torch.Tensor, *, bat
     a.q, a.q_ld, a.q_scale = q.data_ptr(), q.stride(0), q_scale
     a.k, a.k_ld, a.k_scale = k.data_ptr(), k.stride(0), k_scale
     a.v, a.v_ld, a.v_scale = v_bf16.data_ptr(), v_bf16.stride(0), v_scale
+    a.v_dtype = _DT[v_bf16.dtype]
     a.sm_scale = sm_scale
     if gate is not None:
         if gate.dim() != 2 or gate.stride(1) != 1:
@@ -318,6 +322,19 @@ def fp8_to_bf16(x: torch.Tensor, scale: float = 1.0,
         out = torch.empty((rows, cols), device=x.device, dtype=torch.bfloat16)
     check(_lib.lib().b2f_fp8_to_bf16(x.data_ptr(), x.stride(0), out.data_ptr(), out.stride(0),
                                      rows, cols, scale, _stream()))
+    return out
+
+
+def fp8_to_f16(x: torch.Tensor, scale: float = 1.0,
+               out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """f16 copy of an e4m3 [rows, cols] view (exact), times ``scale``."""
+    _check_cuda(x, out)
+    _fp8_rows(x, "x")
+    rows, cols = x.shape
+    if out is None:
+        out = torch.empty((rows, cols), device=x.device, dtype=torch.float16)
+    check(_lib.lib().b2f_fp8_to_f16(x.data_ptr(), x.stride(0), out.data_ptr(), out.stride(0),
+                                    rows, cols, scale, _stream()))
     return out
 
 

@@ -37,6 +37,7 @@ struct AttnParams {
   long long ctx_ld;
   float ctx_inv_scale;
   float v_scale;        // V bf16 values are multiplied by v_scale in the epilogue
+  int pair_heads;       // two-tile kernel: the tiles are query heads 2y, 2y+1 (same KV head)
 };
 
 __device__ __forceinline__ uint64_t make_sdesc(uint32_t addr, uint32_t layout, uint32_t lbo,
@@ -400,7 +401,7 @@ __global__ void __launch_bounds__(192, 1)
 // TMEM: S_A | S_B | O_A | O_B.  P_A, P_B live in shared memory (bf16, 128B swizzle).
 #ifdef B2F_TRACE
 // Debug-only timeline of attention2: [cta][key step][slot] globaltimer stamps.
-__device__ unsigned long long g_atrace[8][16][8];
+__device__ unsigned long long g_atrace[8][16][16];
 #define B2F_ASTAMP(j, slot)                                                         \
   do {                                                                              \
     const int _cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z); \
@@ -420,7 +421,6 @@ template <int D>
 struct Attn2Cfg {
   static constexpr int BQ = 128;
   static constexpr int BKV = 128;
-  static constexpr int ST = 2;
   static constexpr int ROWB = (D >= 128) ? 128 : D;
   static constexpr int KB = (D >= 128) ? D / 128 : 1;
   static constexpr uint32_t LAYOUT8 = (ROWB == 128) ? 2u : 4u;
@@ -428,33 +428,38 @@ struct Attn2Cfg {
   static constexpr int Q_BYTES = BQ * D;  // per query tile
   static constexpr int K_BYTES = BKV * D;
   static constexpr int V_BYTES = BKV * D * 2;
-  static constexpr int P_BYTES = BQ * BKV * 2;  // per query tile
-  static constexpr int STAGE_BYTES = K_BYTES + V_BYTES;
-  static constexpr int SMEM_BYTES = 2 * Q_BYTES + ST * STAGE_BYTES + 2 * P_BYTES + 1024 + 512;
+  // Separate K and V rings: K(j) is released as soon as both S(j) MMAs are issued, so
+  // the K ring runs further ahead than the (larger) V ring.  P lives in tensor memory.
+  static constexpr int KST = (D >= 128) ? 4 : 6;
+  static constexpr int VST = (D >= 128) ? 3 : 4;
+  static constexpr int SMEM_BYTES = 2 * Q_BYTES + KST * K_BYTES + VST * V_BYTES + 1024 + 512;
   static constexpr int S_COL = 0;             // S_X at X * BKV
   static constexpr int O_COL = 2 * BKV;       // O_X at O_COL + X * D
   static constexpr int TMEM_COLS = 512;
   static_assert(D > 128 || 2 * BKV + 2 * D <= 512, "TMEM budget");
+  static_assert(D > 128 || SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 
-template <int D>
+template <int D, bool VF16>
 __global__ void __launch_bounds__(320, 1)
     attention2_kernel(const __grid_constant__ CUtensorMap tm_q,
                       const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v, const AttnParams p) {
   using C = Attn2Cfg<D>;
-  constexpr int BQ = C::BQ, BKV = C::BKV, ST = C::ST;
+  constexpr int BQ = C::BQ, BKV = C::BKV, KST = C::KST, VST = C::VST;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* sq = smem;                            // [2][Q_BYTES]
-  uint8_t* skv = sq + 2 * C::Q_BYTES;            // [ST][K | V]
-  uint8_t* sp = skv + ST * C::STAGE_BYTES;       // [2][P_BYTES]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sp + 2 * C::P_BYTES);
+  uint8_t* sk = sq + 2 * C::Q_BYTES;             // [KST][K_BYTES]
+  uint8_t* sv = sk + KST * C::K_BYTES;           // [VST][V_BYTES]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sv + VST * C::V_BYTES);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;
-  uint64_t* kv_empty = kv_full + ST;
-  uint64_t* s_full = kv_empty + ST;  // [2] per query tile
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = k_full + KST;
+  uint64_t* v_full = k_empty + KST;
+  uint64_t* v_empty = v_full + VST;
+  uint64_t* s_full = v_empty + VST;  // [2] per query tile
   uint64_t* s_free = s_full + 2;
   uint64_t* p_full = s_free + 2;
   uint64_t* pv_done = p_full + 2;
@@ -464,32 +469,46 @@ __global__ void __launch_bounds__(320, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_qt = (p.seq + BQ - 1) / BQ;
-  int qt[2];
+  int qt[2], hx[2];
   bool act[2];
-  if (p.causal) {
-    qt[0] = blockIdx.x;
-    qt[1] = n_qt - 1 - blockIdx.x;
+  if (p.pair_heads) {
+    // GQA: query heads 2y and 2y+1 read the same KV head; both tiles take the same query
+    // rows, so both stay active for every key tile and share each K / V load.  Longest
+    // causal rows first.
+    qt[0] = qt[1] = n_qt - 1 - blockIdx.x;
+    hx[0] = 2 * blockIdx.y;
+    hx[1] = hx[0] + 1;
+    act[0] = true;
   } else {
-    qt[0] = 2 * blockIdx.x;
-    qt[1] = min(2 * (int)blockIdx.x + 1, n_qt - 1);
+    if (p.causal) {
+      qt[0] = blockIdx.x;
+      qt[1] = n_qt - 1 - blockIdx.x;
+    } else {
+      qt[0] = 2 * blockIdx.x;
+      qt[1] = min(2 * (int)blockIdx.x + 1, n_qt - 1);
+    }
+    hx[0] = hx[1] = blockIdx.y;
+    act[0] = qt[0] < qt[1];
   }
   act[1] = true;
-  act[0] = qt[0] < qt[1];
   int nkv[2];
 #pragma unroll
   for (int x = 0; x < 2; ++x) {
     const int end = p.causal ? min(p.seq, qt[x] * BQ + BQ) : p.seq;
     nkv[x] = act[x] ? (end + BKV - 1) / BKV : 0;
   }
-  const int h = blockIdx.y;
   const int b = blockIdx.z;
-  const int hk = h / (p.hq / p.hkv);
+  const int hk = hx[0] / (p.hq / p.hkv);
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < ST; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+    for (int s = 0; s < KST; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < VST; ++s) {
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
@@ -511,41 +530,53 @@ __global__ void __launch_bounds__(320, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
+    // ---------------------------------------------------------------- producers
+    // lane 0: Q once, then the K ring; lane 1: the V ring (independent waits).
+    const uint64_t pol = policy_evict_last();
     if (lane == 0) {
-      // ---------------------------------------------------------------- producer
-      const uint64_t pol = policy_evict_last();
       mbar_arrive_expect_tx(q_full, (act[0] ? 2 : 1) * C::Q_BYTES);
       for (int x = 0; x < 2; ++x) {
         if (!act[x]) continue;
         for (int kb = 0; kb < C::KB; ++kb)
-          tma_load_3d(sq + x * C::Q_BYTES + kb * BQ * C::ROWB, &tm_q, q_full, h * D + kb * 128,
+          tma_load_3d(sq + x * C::Q_BYTES + kb * BQ * C::ROWB, &tm_q, q_full, hx[x] * D + kb * 128,
                       qt[x] * BQ, b, pol);
       }
+    }
+    if (lane < 2) {
+      const bool is_k = lane == 0;
+      const int NS = is_k ? KST : VST;
+      uint64_t* fullb = is_k ? k_full : v_full;
+      uint64_t* emptyb = is_k ? k_empty : v_empty;
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0;
       for (int j = 0; j < nkv[1]; ++j) {
-        if (!mbar_wait(&kv_empty[stage], phase ^ 1, kDevTimeoutProducer, abort_flag)) break;
-        uint8_t* sk = skv + stage * C::STAGE_BYTES;
-        uint8_t* sv = sk + C::K_BYTES;
-        mbar_arrive_expect_tx(&kv_full[stage], C::STAGE_BYTES);
-        for (int kb = 0; kb < C::KB; ++kb)
-          tma_load_3d(sk + kb * BKV * C::ROWB, &tm_k, &kv_full[stage], hk * D + kb * 128,
-                      j * BKV, b, pol);
-        for (int vb = 0; vb < D / 64; ++vb)
-          tma_load_3d(sv + vb * BKV * 128, &tm_v, &kv_full[stage], hk * D + vb * 64, j * BKV, b,
-                      pol);
+        if (!mbar_wait(&emptyb[stage], phase ^ 1, kDevTimeoutProducer, abort_flag)) break;
+        if (is_k) {
+          uint8_t* dst = sk + stage * C::K_BYTES;
+          mbar_arrive_expect_tx(&fullb[stage], C::K_BYTES);
+          for (int kb = 0; kb < C::KB; ++kb)
+            tma_load_3d(dst + kb * BKV * C::ROWB, &tm_k, &fullb[stage], hk * D + kb * 128,
+                        j * BKV, b, pol);
+        } else {
+          uint8_t* dst = sv + stage * C::V_BYTES;
+          mbar_arrive_expect_tx(&fullb[stage], C::V_BYTES);
+          for (int vb = 0; vb < D / 64; ++vb)
+            tma_load_3d(dst + vb * BKV * 128, &tm_v, &fullb[stage], hk * D + vb * 64, j * BKV,
+                        b, pol);
+        }
         ++issued;
-        if (++stage == ST) { stage = 0; phase ^= 1; }
+        if (++stage == NS) { stage = 0; phase ^= 1; }
       }
-      const int pending = issued < ST ? issued : ST;
+      // Let the copies still in flight land before the CTA exits.
+      const int pending = issued < NS ? issued : NS;
       for (int i = 0; i < pending; ++i) {
-        if (--stage < 0) { stage = ST - 1; phase ^= 1; }
+        if (--stage < 0) { stage = NS - 1; phase ^= 1; }
         const uint64_t t0 = globaltimer();
-        while (!mbar_test(&kv_full[stage], phase))
+        while (!mbar_test(&fullb[stage], phase))
           if (globaltimer() - t0 > B2F_WAIT_NS) { record_error(kDevTimeoutDrain); break; }
       }
-      {
+      if (is_k) {
         const uint64_t t0 = globaltimer();
         while (!mbar_test(q_full, 0))
           if (globaltimer() - t0 > B2F_WAIT_NS) { record_error(kDevTimeoutDrain); break; }
@@ -555,14 +586,14 @@ __global__ void __launch_bounds__(320, 1)
     if (lane == 0) {
       // ---------------------------------------------------------------- MMA issuer
       constexpr uint32_t idesc_s = make_idesc_f8(BQ, BKV);
-      constexpr uint32_t idesc_pv = make_idesc_bf16(BQ, D, 1);
+      constexpr uint32_t idesc_pv = VF16 ? make_idesc_f16(BQ, D, 1) : make_idesc_bf16(BQ, D, 1);
       bool ok = mbar_wait(q_full, 0, kDevTimeoutMma, abort_flag);
       auto issue_s = [&](int x, int j) -> bool {
-        const int st = j % ST;
-        if (!mbar_wait(&kv_full[st], (j / ST) & 1, kDevTimeoutMma, abort_flag)) return false;
+        const int st = j % KST;
+        if (!mbar_wait(&k_full[st], (j / KST) & 1, kDevTimeoutMma, abort_flag)) return false;
         tc_fence_after();
         const uint32_t q_addr = smem_u32(sq + x * C::Q_BYTES);
-        const uint32_t k_addr = smem_u32(skv + st * C::STAGE_BYTES);
+        const uint32_t k_addr = smem_u32(sk + st * C::K_BYTES);
 #pragma unroll
         for (int kb = 0; kb < C::KB; ++kb) {
 #pragma unroll
@@ -575,20 +606,28 @@ __global__ void __launch_bounds__(320, 1)
           }
         }
         mma_commit(&s_full[x]);
+        if (x == 1) mma_commit(&k_empty[st]);  // tile 1 is the last reader of K(j)
         return true;
       };
       auto issue_pv = [&](int x, int j) -> bool {
         if (!mbar_wait(&p_full[x], j & 1, kDevTimeoutMma, abort_flag)) return false;
+        if (x == 1) B2F_ASTAMP(j, 8);
+        const int vs = j % VST;
+        if (x == 0 || j >= nkv[0]) {  // first reader of V(j)
+          if (!mbar_wait(&v_full[vs], (j / VST) & 1, kDevTimeoutMma, abort_flag)) return false;
+        }
         tc_fence_after();
-        const uint32_t p_addr = smem_u32(sp + x * C::P_BYTES);
-        const uint32_t v_addr = smem_u32(skv + (j % ST) * C::STAGE_BYTES + C::K_BYTES);
+        // P(j) sits in tensor memory over the first BKV/2 columns of S_x (bf16 pairs).
+        const uint32_t p_tmem = tmem + C::S_COL + x * BKV;
+        const uint32_t v_addr = smem_u32(sv + vs * C::V_BYTES);
 #pragma unroll
         for (int kb = 0; kb < BKV / 64; ++kb) {
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            const uint64_t ad = make_sdesc(p_addr + kb * BQ * 128 + k * 32, 2, 16, 1024);
-            const uint64_t bd = make_sdesc(v_addr + (kb * 4 + k) * 2048, 2, BKV * 128, 1024);
-            mma_bf16(tmem + C::O_COL + x * D, ad, bd, idesc_pv, (j | kb | k) != 0);
+            const int ks = kb * 4 + k;  // 16 keys per MMA
+            const uint64_t bd = make_sdesc(v_addr + ks * 2048, 2, BKV * 128, 1024);
+            mma_bf16_ts(tmem + C::O_COL + x * D, p_tmem + ks * 8, bd, idesc_pv,
+                        (j | kb | k) != 0);
           }
         }
         mma_commit(&pv_done[x]);
@@ -605,10 +644,13 @@ __global__ void __launch_bounds__(320, 1)
           }
         }
         if (!(ok = issue_pv(1, j))) break;
-        mma_commit(&kv_empty[j % ST]);  // both P.V of this key tile issued before it
+        B2F_ASTAMP(j, 9);
+        mma_commit(&v_empty[j % VST]);  // both P.V of this key tile issued before it
         if (j + 1 < nkv[1]) {
           if (!(ok = mbar_wait(&s_free[1], j & 1, kDevTimeoutMma, abort_flag))) break;
+          B2F_ASTAMP(j, 10);
           if (!(ok = issue_s(1, j + 1))) break;
+          B2F_ASTAMP(j, 11);
         }
       }
       mma_commit(drain);
@@ -626,7 +668,6 @@ __global__ void __launch_bounds__(320, 1)
     const uint32_t t_lane = tmem + (uint32_t(qd * 32) << 16);
     const uint32_t s_col = C::S_COL + x * BKV;
     const uint32_t o_col = C::O_COL + x * D;
-    uint8_t* px = sp + x * C::P_BYTES;
     const float c = p.qk_scale_log2;
     float m_used = -INFINITY;
     float l = 0.f;
@@ -640,12 +681,12 @@ __global__ void __launch_bounds__(320, 1)
       // keys k0 + kk with kk > klim are masked (past the sequence end or, causal, past qi)
       const int klim = min(p.seq - 1, p.causal ? qi : p.seq - 1) - k0;
       const bool need_mask = klim < BKV - 1;
-      // pass 1 over S (TMEM -> registers, 32 columns at a time, next load in flight while
-      // the current chunk reduces): row max in log2 units, 8 independent partial maxima
-      float mp[8];
+      // Row max of S * c (f32): TMEM -> registers 32 columns at a time, next load in flight
+      // while the current chunk reduces, 8 independent partial maxima.
+      auto max_pass = [&]() -> float {
+        float mp[8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) mp[e] = -INFINITY;
-      {
+        for (int e = 0; e < 8; ++e) mp[e] = -INFINITY;
         uint32_t ra[32], rb[32];
         tmem_ld32_async(t_lane + s_col, ra);
 #pragma unroll
@@ -655,47 +696,57 @@ __global__ void __launch_bounds__(320, 1)
           tmem_ld_wait_regs(cur);
           if (cc + 32 < BKV) tmem_ld32_async(t_lane + s_col + cc + 32, nxt);
 #pragma unroll
-          for (int u = 0; u < 32; ++u) {
-            float v = __uint_as_float(cur[u]);
-            if (need_mask && cc + u > klim) v = -INFINITY;
-            mp[u & 7] = fmaxf(mp[u & 7], v);
+          for (int u = 0; u < 32; u += 2) {
+            float v0 = __uint_as_float(cur[u]), v1 = __uint_as_float(cur[u + 1]);
+            if (need_mask) {
+              if (cc + u > klim) v0 = -INFINITY;
+              if (cc + u + 1 > klim) v1 = -INFINITY;
+            }
+            mp[(u >> 1) & 7] = fmax3(mp[(u >> 1) & 7], v0, v1);
           }
         }
-      }
-      float mt = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
-                       fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7]))) * c;
-      float corr = 1.0f;
-      bool rescale = false;
-      if (mt > m_used + 8.0f) {
-        if (m_used != -INFINITY) {
-          corr = ex2_hw(m_used - mt);
-          rescale = true;
-        }
-        m_used = mt;
-      }
-      const float mref = (m_used == -INFINITY) ? 0.0f : m_used;
-      if (lane == 0 && (warp == 2 || warp == 6)) B2F_ASTAMP(j, x * 4 + 1);
-      if (j > 0) {
-        ok = __all_sync(0xffffffffu,
-                        mbar_wait(&pv_done[x], (j - 1) & 1, kDevTimeoutEpilogue, abort_flag));
-        if (!ok) break;
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, rescale)) {
+        return fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
+                     fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7]))) * c;
+      };
+      // O *= corr (warp-collective; lanes whose row keeps its reference pass corr = 1).
+      auto rescale_o = [&](float corr) {
 #pragma unroll 1
-          for (int cc = 0; cc < D; cc += 16) {
-            uint32_t o[16];
-            tmem_ld16(t_lane + o_col + cc, o);
+        for (int cc = 0; cc < D; cc += 16) {
+          uint32_t o[16];
+          tmem_ld16(t_lane + o_col + cc, o);
 #pragma unroll
-            for (int u = 0; u < 16; ++u) o[u] = __float_as_uint(__uint_as_float(o[u]) * corr);
-            tmem_st16(t_lane + o_col + cc, o);
-          }
-          tmem_st_wait();
+          for (int u = 0; u < 16; ++u) o[u] = __float_as_uint(__uint_as_float(o[u]) * corr);
+          tmem_st16(t_lane + o_col + cc, o);
         }
-      }
-      if (lane == 0 && (warp == 2 || warp == 6)) B2F_ASTAMP(j, x * 4 + 2);
-      // pass 2: P = 2^(S*c - m) rounded to bf16, streamed into shared memory
-      float ls[4] = {0.f, 0.f, 0.f, 0.f};
+        tmem_st_wait();
+      };
+      float corr = 1.0f, lt;
       {
+        const float mt = max_pass();
+        bool rescale = false;
+        if (mt > m_used + 8.0f) {
+          if (m_used != -INFINITY) {
+            corr = ex2_hw(m_used - mt);
+            rescale = true;
+          }
+          m_used = mt;
+        }
+        const float mref = (m_used == -INFINITY) ? 0.0f : m_used;
+        if (lane == 0 && (warp == 2 || warp == 6)) B2F_ASTAMP(j, x * 4 + 1);
+        if (j > 0) {
+          ok = __all_sync(0xffffffffu,
+                          mbar_wait(&pv_done[x], (j - 1) & 1, kDevTimeoutEpilogue, abort_flag));
+          if (!ok) break;
+          tc_fence_after();
+          if (__any_sync(0xffffffffu, rescale)) rescale_o(corr);
+        }
+        if (lane == 0 && (warp == 2 || warp == 6)) B2F_ASTAMP(j, x * 4 + 2);
+        // P = 2^(S*c - m), written back to tensor memory over the S columns already read
+        // (P column k/2 < S column k): the A operand of P.V.  With f16 V, x = S*c - m
+        // (<= 8 after the lazy update) is packed to f16x2 and exponentiated a pair at a
+        // time, the row sum accumulating in f16x2 over 4 pairs and then in f32; with bf16 V,
+        // each weight is exponentiated in f32 and P rounded to bf16.
+        float ls[4] = {0.f, 0.f, 0.f, 0.f};
         uint32_t ra[32], rb[32];
         tmem_ld32_async(t_lane + s_col, ra);
 #pragma unroll
@@ -704,12 +755,30 @@ __global__ void __launch_bounds__(320, 1)
           uint32_t (&nxt)[32] = ((cc / 32) & 1) ? ra : rb;
           tmem_ld_wait_regs(cur);
           if (cc + 32 < BKV) tmem_ld32_async(t_lane + s_col + cc + 32, nxt);
+          uint32_t pk[16];
+          if constexpr (VF16) {
+            uint32_t acc[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-          for (int gq = 0; gq < 4; ++gq) {
-            uint32_t w4[4];
+            for (int e = 0; e < 16; ++e) {
+              const int u = 2 * e;
+              float v0 = fmaf(__uint_as_float(cur[u]), c, -mref);
+              float v1 = fmaf(__uint_as_float(cur[u + 1]), c, -mref);
+              if (need_mask) {
+                if (cc + u > klim) v0 = -INFINITY;
+                if (cc + u + 1 > klim) v1 = -INFINITY;
+              }
+              pk[e] = ex2_f16x2(pack_f16x2(v0, v1));
+              acc[e & 3] = hadd2(acc[e & 3], pk[e]);
+            }
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int u = gq * 8 + 2 * e;
+            for (int a2 = 0; a2 < 4; ++a2) {
+              const float2 f = unpack_f16x2(acc[a2]);
+              ls[a2] += f.x + f.y;
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const int u = 2 * e;
               float v0 = fmaf(__uint_as_float(cur[u]), c, -mref);
               float v1 = fmaf(__uint_as_float(cur[u + 1]), c, -mref);
               if (need_mask) {
@@ -720,19 +789,16 @@ __global__ void __launch_bounds__(320, 1)
               const __nv_bfloat162 bb = __floats2bfloat162_rn(e0, e1);
               // row sum from the f32 weights: the P.V MMA sees them rounded to bf16
               // (relative 2^-9 per weight, averaging out over the row)
-              ls[e] += e0 + e1;
-              w4[e] = *reinterpret_cast<const uint32_t*>(&bb);
+              ls[e & 3] += e0 + e1;
+              pk[e] = *reinterpret_cast<const uint32_t*>(&bb);
             }
-            const int g = (cc >> 3) + gq;  // 16-byte granule index along the key row
-            const int kb = g >> 3, gi = g & 7;
-            *reinterpret_cast<uint4*>(px + kb * BQ * 128 + r * 128 + ((gi ^ (r & 7)) << 4)) =
-                make_uint4(w4[0], w4[1], w4[2], w4[3]);
           }
+          tmem_st16(t_lane + s_col + cc / 2, pk);
         }
+        tmem_st_wait();
+        lt = (ls[0] + ls[1]) + (ls[2] + ls[3]);
       }
-      const float lt = (ls[0] + ls[1]) + (ls[2] + ls[3]);
       l = l * corr + lt;
-      fence_async_shared();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -758,7 +824,7 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
         for (int u = 0; u < 32; ++u) v[u] = __uint_as_float(o[u]) * inv_l;
         if (p.gate != nullptr) {
-          const long long go = row * p.gate_ld + (long long)h * p.gate_hstride + cc;
+          const long long go = row * p.gate_ld + (long long)hx[x] * p.gate_hstride + cc;
           if (p.gate_dtype == kE4M3) {
             const uint8_t* gp = reinterpret_cast<const uint8_t*>(p.gate) + go;
 #pragma unroll
@@ -794,7 +860,7 @@ __global__ void __launch_bounds__(320, 1)
                  (uint32_t(f32x2_to_e4m3x2(v[4 * t + 2] * p.ctx_inv_scale,
                                            v[4 * t + 3] * p.ctx_inv_scale))
                   << 16);
-        uint8_t* dst = p.ctx + row * p.ctx_ld + (long long)h * D + cc;
+        uint8_t* dst = p.ctx + row * p.ctx_ld + (long long)hx[x] * D + cc;
         *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
         *reinterpret_cast<uint4*>(dst + 16) = make_uint4(w[4], w[5], w[6], w[7]);
       }
@@ -843,8 +909,9 @@ int launch_attention(const b2f_attn_args* a, cudaStream_t stream) {
     const unsigned long long strides[2] = {(unsigned long long)a->v_ld * 2,
                                            (unsigned long long)a->v_ld * 2 * a->seq};
     const unsigned int box[3] = {64, (unsigned int)BKV, 1};
-    if (!encode_tmap(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a->v, dims, strides, box,
-                     CU_TENSOR_MAP_SWIZZLE_128B, &err))
+    const CUtensorMapDataType vt = a->v_dtype == B2F_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                               : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    if (!encode_tmap(&tv, vt, 3, a->v, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B, &err))
       return fail(B2F_ERR_ARG, "attention: V tensor map: " + err);
   }
   AttnParams p;
@@ -857,6 +924,7 @@ int launch_attention(const b2f_attn_args* a, cudaStream_t stream) {
   p.ctx = reinterpret_cast<uint8_t*>(a->ctx); p.ctx_ld = a->ctx_ld;
   p.ctx_inv_scale = 1.0f / a->ctx_scale;
   p.v_scale = a->v_scale;
+  p.pair_heads = 0;
   static thread_local int attr_dev[2][3] = {{-1, -1, -1}, {-1, -1, -1}};
   const int slot = D == 64 ? 0 : (D == 128 ? 1 : 2);
   int dev = 0;
@@ -864,12 +932,18 @@ int launch_attention(const b2f_attn_args* a, cudaStream_t stream) {
   const int n_qt = (a->seq + C::BQ - 1) / C::BQ;
   if constexpr (PAIR) {
     if (attr_dev[1][slot] != dev) {
-      B2F_CUDA_TRY(cudaFuncSetAttribute(attention2_kernel<D>,
+      B2F_CUDA_TRY(cudaFuncSetAttribute(attention2_kernel<D, false>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+      B2F_CUDA_TRY(cudaFuncSetAttribute(attention2_kernel<D, true>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
       attr_dev[1][slot] = dev;
     }
-    dim3 grid((n_qt + 1) / 2, a->hq, a->batch);
-    attention2_kernel<D><<<grid, 320, SMEM, stream>>>(tq, tk, tv, p);
+    p.pair_heads = (a->hq / a->hkv) % 2 == 0;
+    dim3 grid(p.pair_heads ? n_qt : (n_qt + 1) / 2, p.pair_heads ? a->hq / 2 : a->hq, a->batch);
+    if (a->v_dtype == B2F_DTYPE_F16)
+      attention2_kernel<D, true><<<grid, 320, SMEM, stream>>>(tq, tk, tv, p);
+    else
+      attention2_kernel<D, false><<<grid, 320, SMEM, stream>>>(tq, tk, tv, p);
   } else {
     if (attr_dev[0][slot] != dev) {
       B2F_CUDA_TRY(cudaFuncSetAttribute(attention_kernel<D>,
@@ -893,7 +967,7 @@ extern "C" int b2f_atrace_read(void* host, unsigned long long bytes, int reset) 
   if (bytes > sizeof(b2f::g_atrace)) bytes = sizeof(b2f::g_atrace);
   if (cudaMemcpyFromSymbol(host, b2f::g_atrace, bytes) != cudaSuccess) return -1;
   if (reset) {
-    static unsigned long long zeros[8 * 16 * 8] = {};
+    static unsigned long long zeros[8 * 16 * 16] = {};
     cudaMemcpyToSymbol(b2f::g_atrace, zeros, sizeof(zeros));
   }
   return 0;
@@ -910,6 +984,7 @@ void b2f_attn_args_init(b2f_attn_args* a) {
   a->gate_dtype = B2F_DTYPE_E4M3;
   a->gate_scale = 1.0f;
   a->ctx_scale = 1.0f;
+  a->v_dtype = B2F_DTYPE_BF16;
 }
 
 int b2f_attention_fp8(const b2f_attn_args* a, b2f_stream_t stream) {
@@ -938,6 +1013,10 @@ int b2f_attention_fp8(const b2f_attn_args* a, b2f_stream_t stream) {
       return fail(B2F_ERR_ARG, "attention: gate must be 16-byte aligned");
   }
   if (!(a->ctx_scale > 0.f)) return fail(B2F_ERR_ARG, "attention: ctx_scale must be > 0");
+  if (a->v_dtype != B2F_DTYPE_BF16 && a->v_dtype != B2F_DTYPE_F16)
+    return fail(B2F_ERR_ARG, "attention: v must be bf16 or f16");
+  if (a->v_dtype == B2F_DTYPE_F16 && d == 256)
+    return fail(B2F_ERR_UNSUPPORTED, "attention: f16 V needs head_dim 64 or 128");
   cudaStream_t s = (cudaStream_t)stream;
   if (d == 64) return launch_attention<64, true>(a, s);
   if (d == 128) return launch_attention<128, true>(a, s);

@@ -1,4 +1,4 @@
-// Attention operand preparation (C ABI: b2f_head_norm_rope, b2f_fp8_to_bf16).
+// Attention operand preparation (C ABI: b2f_head_norm_rope, b2f_fp8_to_bf16, b2f_fp8_to_f16).
 //
 // b2f_head_norm_rope: one warp per (token, head) row of D e4m3 values:
 //   x = stored * in_scale; y = x * rsqrt(mean(x^2) + eps) * (w + w_offset)   (optional)
@@ -104,7 +104,8 @@ __global__ void __launch_bounds__(256) head_norm_rope_kernel(const RopeParams p)
   }
 }
 
-__global__ void fp8_to_bf16_kernel(const uint8_t* in, long long in_ld, __nv_bfloat16* out,
+template <bool F16>
+__global__ void fp8_to_bf16_kernel(const uint8_t* in, long long in_ld, uint16_t* out,
                                    long long out_ld, int rows, int cols, float scale) {
   const int vec_per_row = cols / 8;
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -115,10 +116,17 @@ __global__ void fp8_to_bf16_kernel(const uint8_t* in, long long in_ld, __nv_bflo
   const float2 a = e4m3x2_to_f32x2(q.x & 0xFFFF), b = e4m3x2_to_f32x2(q.x >> 16),
                cc = e4m3x2_to_f32x2(q.y & 0xFFFF), d = e4m3x2_to_f32x2(q.y >> 16);
   uint4 o;
-  o.x = pack_bf16x2(a.x * scale, a.y * scale);
-  o.y = pack_bf16x2(b.x * scale, b.y * scale);
-  o.z = pack_bf16x2(cc.x * scale, cc.y * scale);
-  o.w = pack_bf16x2(d.x * scale, d.y * scale);
+  if constexpr (F16) {
+    o.x = pack_f16x2(a.x * scale, a.y * scale);
+    o.y = pack_f16x2(b.x * scale, b.y * scale);
+    o.z = pack_f16x2(cc.x * scale, cc.y * scale);
+    o.w = pack_f16x2(d.x * scale, d.y * scale);
+  } else {
+    o.x = pack_bf16x2(a.x * scale, a.y * scale);
+    o.y = pack_bf16x2(b.x * scale, b.y * scale);
+    o.z = pack_bf16x2(cc.x * scale, cc.y * scale);
+    o.w = pack_bf16x2(d.x * scale, d.y * scale);
+  }
   *reinterpret_cast<uint4*>(out + (long long)r * out_ld + c) = o;
 }
 
@@ -214,20 +222,37 @@ int b2f_head_norm_rope(const b2f_rope_args* a, b2f_stream_t stream) {
   return B2F_OK;
 }
 
-int b2f_fp8_to_bf16(const void* in, long long in_ld, void* out, long long out_ld, int rows,
-                    int cols, float scale, b2f_stream_t stream) {
+static int fp8_convert(const void* in, long long in_ld, void* out, long long out_ld, int rows,
+                       int cols, float scale, bool f16, b2f_stream_t stream) {
   using namespace b2f;
-  if (rows <= 0 || cols <= 0) return fail(B2F_ERR_ARG, "fp8_to_bf16: empty shape");
-  if (in == nullptr || out == nullptr) return fail(B2F_ERR_ARG, "fp8_to_bf16: null tensor");
+  const char* name = f16 ? "fp8_to_f16" : "fp8_to_bf16";
+  if (rows <= 0 || cols <= 0) return fail(B2F_ERR_ARG, std::string(name) + ": empty shape");
+  if (in == nullptr || out == nullptr) return fail(B2F_ERR_ARG, std::string(name) + ": null tensor");
   if (cols % 8 || in_ld % 8 || out_ld % 8 || ((uintptr_t)in & 7) || ((uintptr_t)out & 15))
-    return fail(B2F_ERR_ARG, "fp8_to_bf16: cols/ld multiples of 8, aligned tensors required");
+    return fail(B2F_ERR_ARG,
+                std::string(name) + ": cols/ld multiples of 8, aligned tensors required");
   const long long n = (long long)rows * (cols / 8);
   const int grid = (int)((n + 255) / 256);
-  fp8_to_bf16_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(
-      reinterpret_cast<const uint8_t*>(in), in_ld, reinterpret_cast<__nv_bfloat16*>(out), out_ld,
-      rows, cols, scale);
+  if (f16)
+    fp8_to_bf16_kernel<true><<<grid, 256, 0, (cudaStream_t)stream>>>(
+        reinterpret_cast<const uint8_t*>(in), in_ld, reinterpret_cast<uint16_t*>(out), out_ld,
+        rows, cols, scale);
+  else
+    fp8_to_bf16_kernel<false><<<grid, 256, 0, (cudaStream_t)stream>>>(
+        reinterpret_cast<const uint8_t*>(in), in_ld, reinterpret_cast<uint16_t*>(out), out_ld,
+        rows, cols, scale);
   B2F_CUDA_TRY(cudaGetLastError());
   return B2F_OK;
+}
+
+int b2f_fp8_to_bf16(const void* in, long long in_ld, void* out, long long out_ld, int rows,
+                    int cols, float scale, b2f_stream_t stream) {
+  return fp8_convert(in, in_ld, out, out_ld, rows, cols, scale, false, stream);
+}
+
+int b2f_fp8_to_f16(const void* in, long long in_ld, void* out, long long out_ld, int rows,
+                   int cols, float scale, b2f_stream_t stream) {
+  return fp8_convert(in, in_ld, out, out_ld, rows, cols, scale, true, stream);
 }
 
 }  // extern "C"

@@ -38,7 +38,7 @@ enum b2f_status {
   B2F_ERR_NCCL = 5
 };
 
-enum b2f_dtype { B2F_DTYPE_F32 = 0, B2F_DTYPE_BF16 = 1, B2F_DTYPE_E4M3 = 2 };
+enum b2f_dtype { B2F_DTYPE_F32 = 0, B2F_DTYPE_BF16 = 1, B2F_DTYPE_E4M3 = 2, B2F_DTYPE_F16 = 3 };
 
 enum b2f_act {
   B2F_ACT_NONE = 0,
@@ -231,7 +231,9 @@ int b2f_norm_plan(const b2f_norm_args* args);
  *   tokens t = b * seq + s (attention stays inside each sequence); g = h / (hq / hkv) (GQA)
  *   q: e4m3 [T, q_ld], head h at column h*D, value = stored * q_scale
  *   k: e4m3 [T, k_ld], head g at column g*D, value = stored * k_scale
- *   v: bf16 [T, v_ld], head g at column g*D, value = stored * v_scale
+ *   v: bf16 or f16 (v_dtype) [T, v_ld], head g at column g*D, value = stored * v_scale;
+ *      with f16 V the probabilities P are f16 too (exponentials taken in pairs), with bf16 V
+ *      they are bf16
  *   gate (optional): e4m3 or bf16 [T, gate_ld], head h at column h*gate_head_stride,
  *         value = stored * gate_scale
  *   sm_scale <= 0 selects 1/sqrt(D).
@@ -263,6 +265,7 @@ typedef struct b2f_attn_args {
   void* ctx;
   long long ctx_ld;
   float ctx_scale;
+  int v_dtype; /* B2F_DTYPE_BF16 (default) or B2F_DTYPE_F16 (head_dim 64 / 128) */
 } b2f_attn_args;
 
 void b2f_attn_args_init(b2f_attn_args* args);
@@ -301,6 +304,10 @@ int b2f_head_norm_rope(const b2f_rope_args* args, b2f_stream_t stream);
  * Produces the bf16 V operand of b2f_attention_fp8 (exact: bf16 holds every e4m3 value). */
 int b2f_fp8_to_bf16(const void* in, long long in_ld, void* out, long long out_ld, int rows,
                     int cols, float scale, b2f_stream_t stream);
+
+/* out (f16) = in (e4m3 bytes) * scale; the f16 V operand (exact: f16 holds every e4m3 value). */
+int b2f_fp8_to_f16(const void* in, long long in_ld, void* out, long long out_ld, int rows,
+                   int cols, float scale, b2f_stream_t stream);
 
 /* ------------------------------------------------------------------ quantise
  * q = e4m3(x / s), x f32 or bf16 [rows, cols] (row pitch x_ld elements, 16-byte aligned

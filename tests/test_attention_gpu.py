@@ -1,10 +1,11 @@
 """Parity of the fused tcgen05 attention (b2f_attention_fp8) and its operand prep
-(b2f_head_norm_rope, b2f_fp8_to_bf16) with the CPU oracle.
+(b2f_head_norm_rope, b2f_fp8_to_bf16, b2f_fp8_to_f16) with the CPU oracle.
 
 Bar for the e4m3 context, in value space against the oracle's unquantised f32 context:
   |ctx - ref| <= half an e4m3 step at |ref|  (the requantisation itself)
                + 2^-7 * max|v|               (P is rounded to bf16 before the P.V MMA,
-                                              the reference keeps f32; f32 sum order)
+                                              (f16 with f16 V), the reference keeps f32;
+                                              f32 sum order)
 and at least 95% of the stored e4m3 codes equal the oracle's requantised codes.
 An e4m3 "ulp" count is not used: near-zero contexts change sign under tiny absolute
 errors, which spans many codes without being a meaningful error.
@@ -49,13 +50,19 @@ def _qkv(t, hq, hkv, d, g, scale=1 / 64.0):
     return q, k, v
 
 
-@pytest.mark.parametrize("batch,seq,hq,hkv,d,causal", [
+_CASES = [
     (1, 128, 1, 1, 64, True), (2, 256, 2, 2, 64, True), (1, 128, 12, 12, 64, True),
     (1, 384, 4, 2, 128, True), (2, 128, 16, 4, 256, True), (1, 128, 16, 16, 64, False),
     (1, 200, 2, 1, 128, True), (1, 256, 4, 1, 128, False), (1, 1024, 2, 2, 64, True),
-    (1, 512, 2, 1, 256, True),
-])
-def test_attention_matches_oracle(batch, seq, hq, hkv, d, causal):
+    (1, 512, 2, 1, 256, True), (2, 640, 8, 2, 128, True), (1, 384, 6, 3, 64, False),
+]
+
+
+@pytest.mark.parametrize("vtype", ["bf16", "f16"])
+@pytest.mark.parametrize("batch,seq,hq,hkv,d,causal", _CASES)
+def test_attention_matches_oracle(batch, seq, hq, hkv, d, causal, vtype):
+    if vtype == "f16" and d == 256:
+        pytest.skip("f16 V is offered for head_dim 64 / 128")
     g = gen(1000 + seq + hq + d)
     s = 1 / 64.0
     t = batch * seq
@@ -64,7 +71,8 @@ def test_attention_matches_oracle(batch, seq, hq, hkv, d, causal):
     ref = oatt.attention(q.float().view(t, hq, d) * s, k.float().view(t, hkv, d) * s, vf,
                          batch=batch, causal=causal).reshape(t, hq * d)
     ops = _ops()
-    ctx = ops.attention_fp8(q.cuda(), k.cuda(), ops.fp8_to_bf16(v.cuda()), batch=batch,
+    vd = ops.fp8_to_f16(v.cuda()) if vtype == "f16" else ops.fp8_to_bf16(v.cuda())
+    ctx = ops.attention_fp8(q.cuda(), k.cuda(), vd, batch=batch,
                             heads=hq, kv_heads=hkv, head_dim=d, causal=causal, q_scale=s,
                             k_scale=s, v_scale=s, ctx_scale=s)
     torch.cuda.synchronize()
@@ -111,6 +119,14 @@ def test_head_norm_rope(d, rot):
     diff = e4m3_ulp_diff(out.cpu(), ref_q)
     assert int(diff.max()) <= 1
     assert float((diff > 0).float().mean()) < 0.01
+
+
+def test_fp8_to_f16_exact():
+    g = gen(4)
+    x = (torch.randn((64, 256), generator=g) * 50).to(torch.float8_e4m3fn)
+    out = _ops().fp8_to_f16(x.cuda(), scale=1 / 64.0)
+    torch.cuda.synchronize()
+    assert torch.equal(out.cpu(), (x.float() / 64.0).to(torch.float16))
 
 
 def test_fp8_to_bf16_exact():
