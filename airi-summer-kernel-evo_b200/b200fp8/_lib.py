@@ -91,7 +91,7 @@ class NormArgs(ctypes.Structure):
         ("q_out", ctypes.c_void_p), ("q_ld", ctypes.c_longlong),
         ("q_scale", ctypes.c_float), ("dynamic_scale", ctypes.c_int),
         ("amax", ctypes.c_void_p), ("scale_out", ctypes.c_void_p),
-        ("schedule", ctypes.c_int),
+        ("schedule", ctypes.c_int), ("row_stats", ctypes.c_void_p),
     ]
 
 

@@ -44,6 +44,19 @@ def _check_cuda(*tensors: Optional[torch.Tensor]) -> None:
 
 
 _WORKSPACES = {}
+_STATS = {}
+
+
+def _stats_scratch(rows: int, device) -> torch.Tensor:
+    """Per-device f32 scratch for the norm's (mean, rstd) hand-off between its passes (the
+    two passes of one call run back to back on the caller's stream)."""
+    dev = torch.device(device)
+    key = dev.index if dev.index is not None else torch.cuda.current_device()
+    buf = _STATS.get(key)
+    if buf is None or buf.numel() < 2 * rows:
+        buf = torch.empty((max(2 * rows, 1 << 16),), dtype=torch.float32, device=dev)
+        _STATS[key] = buf
+    return buf
 
 
 def gemm_workspace(m: int, n: int, device) -> torch.Tensor:
@@ -148,14 +161,17 @@ def norm_quant(x: torch.Tensor, weight: torch.Tensor, *, kind: str = "rms",
                q_out: Optional[torch.Tensor] = None, q_scale: Optional[float] = None,
                amax: Optional[torch.Tensor] = None,
                scale_out: Optional[torch.Tensor] = None, phase: Optional[str] = None,
-               schedule: str = "auto", query_schedule: bool = False):
+               schedule: str = "auto", query_schedule: bool = False,
+               row_stats: Optional[torch.Tensor] = None):
     """Residual-add + RMSNorm/LayerNorm + e4m3 quantisation (see b2f_norm_quant).
 
     ``q_scale=None`` selects the dynamic per-tensor scale amax(|y|)/448, returned in
     ``scale_out`` (f32 [1]).  With a dynamic scale, ``phase="stats"`` runs pass 1 only
     (h_out written, amax of these rows left in ``amax``) and ``phase="apply"`` runs pass 2
     only from the given ``amax`` (so row shards can share one scale after a MAX
-    all-reduce).  ``schedule="rowgroup"`` forces the unstaged kernels.
+    all-reduce).  ``schedule="rowgroup"`` forces the unstaged kernels.  ``row_stats``
+    (f32 [rows, 2]) carries each row's (mean, rstd) from pass 1 to pass 2; a full dynamic
+    call without it uses a per-device scratch buffer.
     Returns ``(q_out, scale_out)``; with ``query_schedule`` launches nothing and returns
     the schedule the call would use ("stream" or "rowgroup").
     """
@@ -202,6 +218,13 @@ def norm_quant(x: torch.Tensor, weight: torch.Tensor, *, kind: str = "rms",
         args.dynamic_scale = {None: _lib.SCALE_DYNAMIC, "stats": _lib.SCALE_DYNAMIC_STATS,
                               "apply": _lib.SCALE_DYNAMIC_APPLY}[phase]
     args.amax, args.scale_out = _ptr(amax), _ptr(scale_out)
+    if row_stats is None and dynamic and phase is None:
+        row_stats = _stats_scratch(rows, x.device)
+    if row_stats is not None:
+        _check_cuda(row_stats)
+        if row_stats.dtype != torch.float32 or row_stats.numel() < 2 * rows:
+            raise ValueError("row_stats must be f32 with room for [rows, 2]")
+        args.row_stats = row_stats.data_ptr()
     args.schedule = {"auto": _lib.NORM_SCHEDULE_AUTO,
                      "rowgroup": _lib.NORM_SCHEDULE_ROWGROUP}[schedule]
     if query_schedule:

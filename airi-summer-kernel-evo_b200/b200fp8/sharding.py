@@ -81,6 +81,7 @@ class RowShardedNorm:
 
     def __init__(self, group=None):
         self.group = group
+        self._stats = None  # per-row (mean, rstd) handed from the stats to the apply phase
 
     def __call__(self, x, weight, *, residual=None, h_out=None, q_out=None, kind="rms",
                  bias=None, weight_offset=0.0, eps=1e-6, amax=None, scale_out=None):
@@ -90,8 +91,11 @@ class RowShardedNorm:
         dev = x.device
         amax = torch.zeros(1, device=dev) if amax is None else amax
         scale_out = torch.empty(1, device=dev) if scale_out is None else scale_out
+        if self._stats is None or self._stats.numel() < 2 * x.shape[0]:
+            self._stats = torch.empty((2 * x.shape[0],), dtype=torch.float32, device=dev)
         common = dict(kind=kind, bias=bias, weight_offset=weight_offset, eps=eps,
-                      residual=residual, h_out=h_out, q_out=q_out, amax=amax)
+                      residual=residual, h_out=h_out, q_out=q_out, amax=amax,
+                      row_stats=self._stats)
         q_out, _ = ops.norm_quant(x, weight, phase="stats", **common)
         if dist.is_initialized() and dist.get_world_size(self.group) > 1:
             dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=self.group)

@@ -57,7 +57,8 @@ struct NormParams {
   float* amax;       // dynamic: amax accumulator (zeroed by the launcher)
   float* scale_out;  // dynamic: s = amax/448 written by pass 2
   int rows, cols;
-  int schedule;  // B2F_NORM_SCHEDULE_*
+  int schedule;       // B2F_NORM_SCHEDULE_*
+  float* row_stats;   // optional [rows] x (mean, rstd) handed from pass 1 to pass 2
 };
 
 __device__ __forceinline__ void load8(const void* base, int dtype, long long off, float scale,
@@ -528,30 +529,40 @@ __global__ void __launch_bounds__(256, 3) norm_stream_kernel(const NormParams p,
         }
       }
     }
-    float mean = 0.f, s1 = 0.f, s2 = 0.f;
-    if (kind == 1) {
+    float mean = 0.f, inv;
+    if (PASS2 && p.row_stats != nullptr) {
+      // (mean, rstd) left by pass 1: bit-identical to recomputing them from h
+      const float2 st = reinterpret_cast<const float2*>(p.row_stats)[row];
+      mean = st.x;
+      inv = st.y;
+    } else {
+      float s1 = 0.f, s2 = 0.f;
+      if (kind == 1) {
 #pragma unroll
-      for (int i = 0; i < VPT; ++i)
+        for (int i = 0; i < VPT; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) s1 += h[i][j];
-      mean = group_sum(s1, red, tpr) / n;
+          for (int j = 0; j < 8; ++j) s1 += h[i][j];
+        mean = group_sum(s1, red, tpr) / n;
 #pragma unroll
-      for (int i = 0; i < VPT; ++i) {
-        if (FULL || t + tpr * i < nvec) {
+        for (int i = 0; i < VPT; ++i) {
+          if (FULL || t + tpr * i < nvec) {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float d = h[i][j] - mean;
-            s2 += d * d;
+            for (int j = 0; j < 8; ++j) {
+              const float d = h[i][j] - mean;
+              s2 += d * d;
+            }
           }
         }
+      } else {
+#pragma unroll
+        for (int i = 0; i < VPT; ++i)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) s2 += h[i][j] * h[i][j];
       }
-    } else {
-#pragma unroll
-      for (int i = 0; i < VPT; ++i)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) s2 += h[i][j] * h[i][j];
+      inv = rsqrtf(group_sum(s2, red, tpr) / n + p.eps);
+      if (!PASS2 && dyn1 && p.row_stats != nullptr && t == 0)
+        reinterpret_cast<float2*>(p.row_stats)[row] = make_float2(mean, inv);
     }
-    const float inv = rsqrtf(group_sum(s2, red, tpr) / n + p.eps);
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const int vi = t + tpr * i;
@@ -788,6 +799,9 @@ int build_params(const b2f_norm_args* a, NormParams& p) {
   p.amax = a->amax; p.scale_out = a->scale_out;
   p.rows = a->rows; p.cols = a->cols;
   p.schedule = a->schedule;
+  p.row_stats = a->row_stats;
+  if (a->row_stats != nullptr && (reinterpret_cast<uintptr_t>(a->row_stats) & 7))
+    return fail(B2F_ERR_ARG, "norm_quant: row_stats must be 8-byte aligned");
   return B2F_OK;
 }
 

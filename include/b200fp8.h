@@ -216,6 +216,9 @@ typedef struct b2f_norm_args {
   float* amax;
   float* scale_out;
   int schedule; /* b2f_norm_schedule */
+  float* row_stats; /* optional f32 [rows][2] scratch (8-byte aligned): with a dynamic scale,
+                       pass 1 leaves each row's (mean, rstd) there and pass 2 reads them
+                       instead of recomputing (same bits); null: pass 2 recomputes */
 } b2f_norm_args;
 
 void b2f_norm_args_init(b2f_norm_args* args);
