@@ -306,6 +306,20 @@ __device__ __forceinline__ void splitk_finish(const EpilogueParams& ep, float al
   }
 }
 
+// Pulls this lane's residual row segment [col_base, col_base + HALF) into L2 while the
+// accumulator is still being computed, so the epilogue's residual loads hit L2.
+template <int HALF>
+__device__ __forceinline__ void epi_prefetch_residual(const EpilogueParams& ep, int row,
+                                                      int col_base, int M, int N) {
+  if (ep.residual == nullptr || row >= M || col_base >= N) return;
+  const int esz = ep.res_dtype == kOutF32 ? 4 : (ep.res_dtype == kOutBF16 ? 2 : 1);
+  const int cols = min(HALF, N - col_base);
+  const uint8_t* p = reinterpret_cast<const uint8_t*>(ep.residual) +
+                     ((long long)row * ep.res_ld + col_base) * esz;
+  for (int off = 0; off < cols * esz; off += 32)
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p + off));
+}
+
 // Per-lane epilogue vectors for the 32 columns starting at col0 (one coalesced load each).
 __device__ __forceinline__ void epi_lane_vectors(const EpilogueParams& ep, int col0, int N,
                                                  float& lane_bias, float& lane_cscale) {
@@ -324,7 +338,9 @@ template <int BN>
 __device__ __forceinline__ void epilogue_tile(const EpilogueParams& ep, const CUtensorMap* tmap_out,
                                               float alpha, uint32_t t_row, int row, int row0,
                                               int col_base, int M, int N, uint8_t* stage,
-                                              int& buf, float& rowsum, float& amax_local) {
+                                              int& buf, float& rowsum, float& amax_local,
+                                              const float (&lbv)[BN / 32],
+                                              const float (&lcv)[BN / 32]) {
   const int lane = threadIdx.x & 31;
   const bool tma = ep.out_vec && ep.mode == kModeStore;
   const int esz = out_esize(ep.out_dtype);
@@ -345,8 +361,11 @@ __device__ __forceinline__ void epilogue_tile(const EpilogueParams& ep, const CU
       uint32_t (&cur)[32] = half == 0 ? ra : rb;
       uint32_t (&nxt)[32] = half == 0 ? rb : ra;
       const int col0 = col_base + uu * 32;
-      float lb, lc;
-      epi_lane_vectors(ep, col0, N, lb, lc);
+      // this chunk's bias / column scale (loaded before the accumulator was ready)
+      float lb = lbv[0], lc = lcv[0];
+#pragma unroll
+      for (int x = 1; x < BN / 32; ++x)
+        if (uu == x) { lb = lbv[x]; lc = lcv[x]; }
       tmem_ld_wait_regs(cur);
       if (uu + 1 < units) tmem_ld32_async(t_row + (uu + 1) * 32, nxt);
       float v[32];
@@ -554,6 +573,13 @@ __global__ void __launch_bounds__(320, 1)
       tile_coords(t, num_m, num_n, mb, nb);
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
+      float lbv[BN / 64], lcv[BN / 64];
+      if (splits == 1) {
+        const int cb0 = nb * BN + chalf * (BN / 2);
+        epi_prefetch_residual<BN / 2>(ep, mb * Cfg::BM + q * 32 + lane, cb0, M, N);
+#pragma unroll
+        for (int x = 0; x < BN / 64; ++x) epi_lane_vectors(ep, cb0 + x * 32, N, lbv[x], lcv[x]);
+      }
       // tcgen05.ld is warp-collective: the whole warp leaves together or not at all.
       if (!__all_sync(0xffffffffu,
                       mbar_wait(&tfull_bar[acc], acc_phase, kDevTimeoutEpilogue, abort_flag)))
@@ -567,7 +593,7 @@ __global__ void __launch_bounds__(320, 1)
       const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + acc * BN + chalf * (BN / 2);
       if (splits == 1) {
         epilogue_tile<BN / 2>(ep, &tmap_out, alpha, t_row, row, row0, col_base, M, N, stage,
-                              buf, rowsum, amax_local);
+                              buf, rowsum, amax_local, lbv, lcv);
         tc_fence_before();
         __syncwarp();
         if (warp == 2 && lane == 0) B2F_STAMP(it, 4);
@@ -794,6 +820,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
       tile_coords(t, num_m, num_n, mb, nb);
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
+      float lbv[BN / 64], lcv[BN / 64];
+      {
+        const int cb0 = nb * BN + chalf * (BN / 2);
+        epi_prefetch_residual<BN / 2>(ep, mb * 2 * Cfg::BM + rank * Cfg::BM + q * 32 + lane, cb0,
+                                      M, N);
+#pragma unroll
+        for (int x = 0; x < BN / 64; ++x) epi_lane_vectors(ep, cb0 + x * 32, N, lbv[x], lcv[x]);
+      }
       // tcgen05.ld is warp-collective: the whole warp leaves together or not at all.
       if (!__all_sync(0xffffffffu,
                       mbar_wait(&tfull_bar[acc], acc_phase, kDevTimeoutEpilogue, abort_flag)))
@@ -804,7 +838,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
       float rowsum = 0.0f;
       const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + acc * BN + chalf * (BN / 2);
       epilogue_tile<BN / 2>(ep, &tmap_out, alpha, t_row, row, row0, nb * BN + chalf * (BN / 2),
-                            M, N, stage, buf, rowsum, amax_local);
+                            M, N, stage, buf, rowsum, amax_local, lbv, lcv);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(map_to_rank(&tempty_bar[acc], 0));
