@@ -138,6 +138,10 @@ int launch_gemm(const b2f_gemm_args* a, EpilogueParams ep, cudaStream_t stream) 
     attr_dev = dev;
   }
   CUtensorMap to;
+  // A warp's half tile must fill the 64-byte store box; narrower halves (e4m3 with
+  // 64-column tiles) store directly.
+  if ((BN / 2) * (a->out_dtype == B2F_DTYPE_F32 ? 4 : (a->out_dtype == B2F_DTYPE_BF16 ? 2 : 1)) < 64)
+    ep.out_vec = 0;
   if (int rc = encode_out_map(a, ep, BN / 2, &to)) return rc;
   kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, to, shape, ep);
   B2F_CUDA_TRY(cudaGetLastError());
@@ -278,7 +282,11 @@ int b2f_gemm_fp8(const b2f_gemm_args* a, b2f_stream_t stream) {
   }
   if (tn == 256) return launch_gemm<256>(a, ep, s);
   if (tn == 128) return launch_gemm<128>(a, ep, s);
-  return fail(B2F_ERR_ARG, "gemm_fp8: tile_n must be 0, 128, 256 or 512 (CTA pair)");
+  if (tn == 64) {
+    if (a->splits > 1) return fail(B2F_ERR_UNSUPPORTED, "gemm_fp8: split-K uses tile_n 128 or 256");
+    return launch_gemm<64>(a, ep, s);
+  }
+  return fail(B2F_ERR_ARG, "gemm_fp8: tile_n must be 0, 64, 128, 256 or 512 (CTA pair)");
 }
 
 }  // extern "C"

@@ -108,7 +108,7 @@ template <int BN>
 struct GemmCfg {
   static constexpr int BM = 128;
   static constexpr int BK = 128;  // bytes of K per stage = one 128B swizzle row
-  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static constexpr int STAGES = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
   static constexpr int A_BYTES = BM * BK;
   static constexpr int B_BYTES = BN * BK;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;

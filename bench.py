@@ -155,7 +155,10 @@ class GemmWorkload:
         self.bias_cpu = (torch.randn((self.n,), generator=g) * 0.02) if bias_relu else None
         self.a_cpu, self.b_cpu = a, b
         self.work = 2.0 * self.m * self.n * self.k
-        self.unit, self.bound = "TFLOP/s", "tensor"
+        # M=128 (config 0) streams the 64 MB weight once: bandwidth-bound, so its roofline
+        # is HBM bytes; the square configs are tensor-bound.
+        self.unit = "TFLOP/s"
+        self.bound = "tensor" if self.m > 128 else "hbm"
         self.kernel = "gemm_fp8_pair_kernel" if (self.m > 128) else "gemm_fp8_kernel<128>"
         self.algo_bytes = self.m * self.k + self.n * self.k + self.m * self.n * 2 + (
             4 * self.n if bias_relu else 0)
@@ -241,7 +244,7 @@ class NormWorkload:
     name = "residual_rmsnorm_amax_quant"
     unit = "GB/s"
     bound = "hbm"
-    kernel = "norm_pass1_kernel<16> + norm_pass2_kernel<16>"
+    kernel = "norm_stream_kernel pass 1 + pass 2"
 
     scaling = "weak"
 
@@ -590,7 +593,13 @@ def run_ours(args):
     else:
         peak = peaks["hbm_gbs"]
         basis = f"{peaks['basis']} HBM copy bandwidth"
-    achieved = wl.work / (per_launch_ms * 1e-3) / scale
+    if wl.bound == "hbm" and unit != "GB/s":
+        # bandwidth roofline of a workload whose metric is FLOP-based: algorithmic bytes
+        achieved = wl.algo_bytes / (per_launch_ms * 1e-3) / 1e9
+        roof_unit, roof_work = "GB/s", wl.algo_bytes
+    else:
+        achieved = wl.work / (per_launch_ms * 1e-3) / scale
+        roof_unit, roof_work = unit, wl.work
     if hasattr(wl, "parallelism"):
         parallel = wl.parallelism()
     else:
@@ -606,10 +615,10 @@ def run_ours(args):
         "data": "synthetic (seeded N(0,1), per-tensor amax e4m3 scales; random-init weights)",
         "config": dict(wl.config(), parallelism=parallel),
         "roofline": {"bound": wl.bound, "achieved": round(achieved, 1), "peak": round(peak, 1),
-                     "unit": unit, "frac": round(achieved / peak, 4), "peak_basis": basis,
+                     "unit": roof_unit, "frac": round(achieved / peak, 4), "peak_basis": basis,
                      "traffic": None, "kernel": getattr(wl, "kernel", "gemm_fp8"),
                      "per_launch_ms": round(per_launch_ms, 5),
-                     "algorithmic_work_per_launch": wl.work},
+                     "algorithmic_work_per_launch": roof_work},
         "e2e": {"value": round(wl.work * world / (e2e_ms * 1e-3) / scale, 3), "unit": unit,
                 "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
