@@ -123,6 +123,50 @@ class AttnArgs(ctypes.Structure):
     ]
 
 
+class Gpt2BlockArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", ctypes.c_int), ("seq", ctypes.c_int), ("d_model", ctypes.c_int),
+        ("heads", ctypes.c_int), ("mlp", ctypes.c_int),
+        ("hidden", ctypes.c_void_p), ("hidden_dtype", ctypes.c_int),
+        ("hidden_ld", ctypes.c_longlong), ("hidden_scale", ctypes.c_float),
+        ("qkv_w", ctypes.c_void_p), ("qkv_s", ctypes.c_float), ("qkv_b", ctypes.c_void_p),
+        ("out_w", ctypes.c_void_p), ("out_s", ctypes.c_float), ("out_b", ctypes.c_void_p),
+        ("fc_w", ctypes.c_void_p), ("fc_s", ctypes.c_float), ("fc_b", ctypes.c_void_p),
+        ("proj_w", ctypes.c_void_p), ("proj_s", ctypes.c_float), ("proj_b", ctypes.c_void_p),
+        ("ln1_w", ctypes.c_void_p), ("ln1_b", ctypes.c_void_p), ("ln2_w", ctypes.c_void_p),
+        ("ln2_b", ctypes.c_void_p), ("eps", ctypes.c_float),
+        ("norm_scale", ctypes.c_float), ("qkv_scale", ctypes.c_float),
+        ("ctx_scale", ctypes.c_float), ("mlp_scale", ctypes.c_float),
+        ("causal", ctypes.c_int), ("rope_cos", ctypes.c_void_p), ("rope_sin", ctypes.c_void_p),
+        ("residual_dtype", ctypes.c_int), ("out", ctypes.c_void_p), ("out_dtype", ctypes.c_int),
+        ("out_ld", ctypes.c_longlong), ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_longlong),
+    ]
+
+
+class QwenBlockArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", ctypes.c_int), ("seq", ctypes.c_int), ("hidden", ctypes.c_int),
+        ("heads", ctypes.c_int), ("kv_heads", ctypes.c_int), ("head_dim", ctypes.c_int),
+        ("rotary_dim", ctypes.c_int), ("interleaved", ctypes.c_int),
+        ("hidden_in", ctypes.c_void_p), ("hidden_dtype", ctypes.c_int),
+        ("hidden_ld", ctypes.c_longlong), ("hidden_scale", ctypes.c_float),
+        ("qgkv_w", ctypes.c_void_p), ("qgkv_col_scale", ctypes.c_void_p),
+        ("o_w", ctypes.c_void_p), ("o_s", ctypes.c_float),
+        ("in_norm_w", ctypes.c_void_p), ("q_norm_w", ctypes.c_void_p),
+        ("k_norm_w", ctypes.c_void_p), ("rope_cos", ctypes.c_void_p),
+        ("rope_sin", ctypes.c_void_p), ("eps", ctypes.c_float), ("norm_scale", ctypes.c_float),
+        ("qkv_scale", ctypes.c_float), ("ctx_scale", ctypes.c_float),
+        ("add_residual", ctypes.c_int), ("post_norm_w", ctypes.c_void_p),
+        ("mlp_gu_w", ctypes.c_void_p), ("mlp_gu_col_scale", ctypes.c_void_p),
+        ("inter", ctypes.c_int), ("mlp_down_w", ctypes.c_void_p),
+        ("mlp_down_s", ctypes.c_float), ("mlp_proj_scale", ctypes.c_float),
+        ("mlp_act_scale", ctypes.c_float), ("residual_dtype", ctypes.c_int),
+        ("out", ctypes.c_void_p), ("out_dtype", ctypes.c_int), ("out_ld", ctypes.c_longlong),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_longlong),
+    ]
+
+
 class RopeArgs(ctypes.Structure):
     """Mirror of ``b2f_rope_args`` (include/b200fp8.h)."""
 
@@ -156,6 +200,8 @@ EXPORTED_SYMBOLS = (
     "b2f_norm_args_init", "b2f_norm_quant", "b2f_norm_plan", "b2f_attn_args_init", "b2f_attention_fp8",
     "b2f_head_norm_rope", "b2f_fp8_to_bf16", "b2f_fp8_to_f16", "b2f_swiglu_fp8",
     "b2f_quant_args_init", "b2f_quantize_fp8",
+    "b2f_gpt2_block_args_init", "b2f_gpt2_block_workspace_bytes", "b2f_gpt2_block",
+    "b2f_qwen_block_args_init", "b2f_qwen_block_workspace_bytes", "b2f_qwen_block",
     "b2f_registry_lookup", "b2f_registry_size", "b2f_registry_at",
 )
 
@@ -188,6 +234,13 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.b2f_quant_args_init.restype = None
     lib.b2f_quantize_fp8.argtypes = [ctypes.POINTER(QuantArgs), vp]
     lib.b2f_quantize_fp8.restype = ctypes.c_int
+    for nm, st in (("gpt2", Gpt2BlockArgs), ("qwen", QwenBlockArgs)):
+        getattr(lib, f"b2f_{nm}_block_args_init").argtypes = [ctypes.POINTER(st)]
+        getattr(lib, f"b2f_{nm}_block_args_init").restype = None
+        getattr(lib, f"b2f_{nm}_block_workspace_bytes").argtypes = [ctypes.POINTER(st)]
+        getattr(lib, f"b2f_{nm}_block_workspace_bytes").restype = ctypes.c_longlong
+        getattr(lib, f"b2f_{nm}_block").argtypes = [ctypes.POINTER(st), vp]
+        getattr(lib, f"b2f_{nm}_block").restype = ctypes.c_int
     lib.b2f_norm_plan.argtypes = [ctypes.POINTER(NormArgs)]
     lib.b2f_norm_plan.restype = ctypes.c_int
     lib.b2f_attn_args_init.argtypes = [ctypes.POINTER(AttnArgs)]

@@ -118,6 +118,8 @@ const b2f_op g_ops[] = {
     {"swiglu_fp8", B2F_ABI_VERSION, (void*)&b2f_swiglu_fp8, "(gate, gate_ld, up, up_ld, out, out_ld, rows, cols, in_scale, out_scale)"},
     {"fp8_to_bf16", B2F_ABI_VERSION, (void*)&b2f_fp8_to_bf16, "(in, in_ld, out, out_ld, rows, cols, scale)"},
     {"fp8_to_f16", B2F_ABI_VERSION, (void*)&b2f_fp8_to_f16, "(in, in_ld, out, out_ld, rows, cols, scale)"},
+    {"gpt2_block", B2F_ABI_VERSION, (void*)&b2f_gpt2_block, "b2f_gpt2_block_args"},
+    {"qwen_block", B2F_ABI_VERSION, (void*)&b2f_qwen_block, "b2f_qwen_block_args"},
     {"quantize_fp8", B2F_ABI_VERSION, (void*)&b2f_quantize_fp8, "b2f_quant_args"},
 };
 }

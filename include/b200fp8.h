@@ -361,6 +361,106 @@ const b2f_op* b2f_registry_lookup(const char* name);
 int b2f_registry_size(void);
 const b2f_op* b2f_registry_at(int index);
 
+
+/* ------------------------------------------------------------------ decoder blocks
+ * Whole-block entry points: the kernels above in each reference evaluator's dataflow order
+ * on one stream; intermediates live in a caller workspace of
+ * b2f_*_block_workspace_bytes(args) bytes (256-byte aligned).  Tokens t = b * seq + s.
+ * Weights are e4m3 [out, in] with per-tensor scales; biases / norm weights f32.
+ *
+ * GPT-2 block (also the Qwen vision block with rope_cos / rope_sin and causal = 0):
+ *   n1 = e4m3(LN1(hidden) / norm_scale); qkv = e4m3((n1 . Wqkv^T + b) / qkv_scale);
+ *   [q, k: RoPE -> e4m3]; ctx = e4m3(attention / ctx_scale);
+ *   r1 = hidden + ctx . Wout^T + b  (residual_dtype); n2 = e4m3(LN2(r1) / norm_scale);
+ *   h = e4m3(gelu_tanh(n2 . Wfc^T + b) / mlp_scale); out = r1 + h . Wproj^T + b.
+ * Replaces: gpt2_transformer_block (tasks/model_gpt2_small_transformer_block_fp8/starter.py:
+ *   114-140, reference math :393-488) and the vision block
+ *   (tasks/model_qwen35_4b_vision_block_fp8/starter.py:303-369). */
+typedef struct b2f_gpt2_block_args {
+  int batch, seq, d_model, heads, mlp;
+  const void* hidden;
+  int hidden_dtype; /* f32, bf16 or e4m3 */
+  long long hidden_ld;
+  float hidden_scale;
+  const void* qkv_w;
+  float qkv_s;
+  const float* qkv_b;
+  const void* out_w;
+  float out_s;
+  const float* out_b;
+  const void* fc_w;
+  float fc_s;
+  const float* fc_b;
+  const void* proj_w;
+  float proj_s;
+  const float* proj_b;
+  const float *ln1_w, *ln1_b, *ln2_w, *ln2_b;
+  float eps;
+  float norm_scale, qkv_scale, ctx_scale, mlp_scale;
+  int causal;
+  const float* rope_cos; /* optional f32 [seq, head_dim] */
+  const float* rope_sin;
+  int residual_dtype; /* r1: f32 or bf16 */
+  void* out;
+  int out_dtype; /* f32 or bf16 */
+  long long out_ld;
+  void* workspace;
+  long long workspace_bytes;
+} b2f_gpt2_block_args;
+
+void b2f_gpt2_block_args_init(b2f_gpt2_block_args* args);
+long long b2f_gpt2_block_workspace_bytes(const b2f_gpt2_block_args* args);
+int b2f_gpt2_block(const b2f_gpt2_block_args* args, b2f_stream_t stream);
+
+/* Qwen gated full-attention block (optional SwiGLU MLP):
+ *   n1 = e4m3(RMSNorm_(1+w)(hidden) / norm_scale);
+ *   proj = e4m3(n1 . Wqgkv^T * qgkv_col_scale[col] / qkv_scale)   (one GEMM over the packed
+ *     weights; qgkv_col_scale[j] = norm_scale * scale of the weight that row j belongs to);
+ *   q, k: per-head RMSNorm (1+w) + rotate-half RoPE on rotary_dim dims -> e4m3;
+ *   ctx = e4m3(causal GQA attention * sigmoid(gate) / ctx_scale);
+ *   r1 = [hidden] + ctx . Wo^T * (ctx_scale * o_s)   (add_residual = 0 leaves the residual
+ *     out: the partial of a heads-parallel o-projection);
+ *   MLP: n2 = e4m3(RMSNorm_(1+w)(r1)); gu = e4m3(n2 . [Wgate|Wup]^T * mlp_gu_col_scale /
+ *     mlp_proj_scale); act = e4m3(silu(gate) * up / mlp_act_scale); out = r1 + act . Wdown^T.
+ * Packed row order: interleaved = 1: [q_h | gate_h] per head, then k, then v (the reference's
+ *   q_gate weight); interleaved = 0: [q | gate | k | v].
+ * Replaces: qwen35_full_attention_block (tasks/model_qwen35_4b_full_attention_block_fp8/
+ *   starter.py:66-98, reference math :333-416). */
+typedef struct b2f_qwen_block_args {
+  int batch, seq, hidden, heads, kv_heads, head_dim, rotary_dim;
+  int interleaved;
+  const void* hidden_in;
+  int hidden_dtype; /* f32, bf16 or e4m3 */
+  long long hidden_ld;
+  float hidden_scale;
+  const void* qgkv_w;
+  const float* qgkv_col_scale;
+  const void* o_w;
+  float o_s;
+  const float *in_norm_w, *q_norm_w, *k_norm_w;
+  const float* rope_cos; /* f32 [seq, rotary_dim] */
+  const float* rope_sin;
+  float eps, norm_scale, qkv_scale, ctx_scale;
+  int add_residual;
+  const float* post_norm_w; /* MLP (mlp_gu_w null: attention block only) */
+  const void* mlp_gu_w;     /* [2 * inter, hidden]: gate rows then up rows */
+  const float* mlp_gu_col_scale;
+  int inter;
+  const void* mlp_down_w;
+  float mlp_down_s;
+  float mlp_proj_scale, mlp_act_scale;
+  int residual_dtype;
+  void* out;
+  int out_dtype;
+  long long out_ld;
+  void* workspace;
+  long long workspace_bytes;
+} b2f_qwen_block_args;
+
+void b2f_qwen_block_args_init(b2f_qwen_block_args* args);
+long long b2f_qwen_block_workspace_bytes(const b2f_qwen_block_args* args);
+int b2f_qwen_block(const b2f_qwen_block_args* args, b2f_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
