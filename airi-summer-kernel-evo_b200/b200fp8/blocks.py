@@ -21,11 +21,12 @@ device once.
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Optional
 
 import torch
 
-from . import ops
+from . import _lib, ops
 
 _E4M3 = torch.float8_e4m3fn
 
@@ -50,6 +51,21 @@ def _v_convert(src: torch.Tensor, dst: torch.Tensor) -> None:
         ops.fp8_to_f16(src, out=dst)
     else:
         ops.fp8_to_bf16(src, out=dst)
+
+
+_DTC = {torch.float32: 0, torch.bfloat16: 1, torch.float8_e4m3fn: 2, torch.float16: 3}
+
+
+def _p(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _block_workspace(owner, nbytes: int, device) -> torch.Tensor:
+    ws = getattr(owner, "_abi_ws", None)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty((max(nbytes, 256),), dtype=torch.uint8, device=device)
+        owner._abi_ws = ws
+    return ws
 
 
 class _Graphable:
@@ -163,6 +179,33 @@ class GPT2Block(_Graphable):
                      residual=self.r1, out=self.out)
         return self.out
 
+    def forward_abi(self, hidden: torch.Tensor, hidden_scale: float = 1.0) -> torch.Tensor:
+        """The same forward through the native entry point b2f_gpt2_block (one C call;
+        intermediates in a block-owned workspace); writes and returns ``self.out``."""
+        a = _lib.Gpt2BlockArgs()
+        L = _lib.lib()
+        L.b2f_gpt2_block_args_init(ctypes.byref(a))
+        a.batch, a.seq, a.d_model, a.heads, a.mlp = self.batch, self.seq, self.d, self.heads, self.mlp
+        a.hidden, a.hidden_dtype, a.hidden_ld = hidden.data_ptr(), _DTC[hidden.dtype], hidden.stride(0)
+        a.hidden_scale = hidden_scale
+        a.qkv_w, a.qkv_s, a.qkv_b = _p(self.qkv_w), self.qkv_s, _p(self.qkv_b)
+        a.out_w, a.out_s, a.out_b = _p(self.out_w), self.out_s, _p(self.out_b)
+        a.fc_w, a.fc_s, a.fc_b = _p(self.fc_w), self.fc_s, _p(self.fc_b)
+        a.proj_w, a.proj_s, a.proj_b = _p(self.proj_w), self.proj_s, _p(self.proj_b)
+        a.ln1_w, a.ln1_b, a.ln2_w, a.ln2_b = _p(self.ln1_w), _p(self.ln1_b), _p(self.ln2_w), _p(self.ln2_b)
+        a.eps = self.eps
+        a.norm_scale, a.qkv_scale, a.ctx_scale, a.mlp_scale = self.ns, self.qs, self.cs, self.ms
+        a.causal = 1 if self.causal else 0
+        if self.rope:
+            a.rope_cos, a.rope_sin = _p(self.cos), _p(self.sin)
+        a.residual_dtype = _DTC[self.r1.dtype]
+        a.out, a.out_dtype, a.out_ld = self.out.data_ptr(), _DTC[self.out.dtype], self.out.stride(0)
+        ws = _block_workspace(self, int(L.b2f_gpt2_block_workspace_bytes(ctypes.byref(a))),
+                              self.out.device)
+        a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+        ops.check(L.b2f_gpt2_block(ctypes.byref(a), ops._stream()))
+        return self.out
+
 
 class QwenBlock(_Graphable):
     """``add_residual=False`` leaves the residual add out of the o-projection: the block then
@@ -264,4 +307,33 @@ class QwenBlock(_Graphable):
                        out_scale=self.mas, out=self.act)
         ops.gemm_fp8(self.act, self.down_w, scale_a=self.mas, scale_b=self.down_s, residual=r1,
                      out=self.out)
+        return self.out
+
+    def forward_abi(self, hidden: torch.Tensor, hidden_scale: float = 1.0) -> torch.Tensor:
+        """The same forward through the native entry point b2f_qwen_block; writes and
+        returns ``self.out``."""
+        a = _lib.QwenBlockArgs()
+        L = _lib.lib()
+        L.b2f_qwen_block_args_init(ctypes.byref(a))
+        a.batch, a.seq, a.hidden = self.batch, self.seq, self.hidden
+        a.heads, a.kv_heads, a.head_dim, a.rotary_dim = self.h, self.hk, self.dh, self.rot
+        a.interleaved = 1 if self.interleaved else 0
+        a.hidden_in, a.hidden_dtype, a.hidden_ld = hidden.data_ptr(), _DTC[hidden.dtype], hidden.stride(0)
+        a.hidden_scale = hidden_scale
+        a.qgkv_w, a.qgkv_col_scale = _p(self.w_cat), _p(self.cs_cat)
+        a.o_w, a.o_s = _p(self.o_w), self.o_s
+        a.in_norm_w, a.q_norm_w, a.k_norm_w = _p(self.in_norm), _p(self.q_norm), _p(self.k_norm)
+        a.rope_cos, a.rope_sin = _p(self.cos), _p(self.sin)
+        a.eps, a.norm_scale, a.qkv_scale, a.ctx_scale = self.eps, self.ns, self.qs, self.cs
+        a.add_residual = 1 if self.add_residual else 0
+        if self.has_mlp:
+            a.post_norm_w, a.mlp_gu_w, a.mlp_gu_col_scale = _p(self.post_norm), _p(self.gu_w), _p(self.gu_cs)
+            a.inter, a.mlp_down_w, a.mlp_down_s = self.inter, _p(self.down_w), self.down_s
+            a.mlp_proj_scale, a.mlp_act_scale = self.mps, self.mas
+            a.residual_dtype = _DTC[self.r1.dtype]
+        a.out, a.out_dtype, a.out_ld = self.out.data_ptr(), _DTC[self.out.dtype], self.out.stride(0)
+        ws = _block_workspace(self, int(L.b2f_qwen_block_workspace_bytes(ctypes.byref(a))),
+                              self.out.device)
+        a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+        ops.check(L.b2f_qwen_block(ctypes.byref(a), ops._stream()))
         return self.out

@@ -12,6 +12,7 @@ import torch
 
 from block_inputs import gpt2_weights, qwen_weights, reference_hidden
 from helpers import gen
+from oracle import attention as oatt
 from oracle import blocks as ob
 
 pytestmark = pytest.mark.gpu
@@ -108,3 +109,54 @@ def test_qwen_heads_parallel_partials_sum_to_block(tp):
         total += blk.forward(xd).float()
     torch.cuda.synchronize()
     _check(total.to(torch.bfloat16), ref, 0.08, 2.0 ** -7)
+
+
+def _f32_scales(w, names):
+    # the C ABI takes f32 scales; round them so both paths form the same GEMM alpha
+    for n in names:
+        setattr(w, n, float(torch.tensor(getattr(w, n), dtype=torch.float32)))
+
+
+@pytest.mark.parametrize("vision", [False, True])
+def test_gpt2_block_native_entry_matches_python_block(vision):
+    """b2f_gpt2_block (one C call) reproduces the Python-composed block bit for bit."""
+    g = gen(20260805)
+    w = gpt2_weights(g=g, reference=False, d=1024 if vision else 768, heads=16 if vision else 12,
+                     mlp=4096 if vision else 3072)
+    _f32_scales(w, ("qkv_s", "out_s", "fc_s", "proj_s"))
+    batch, seq, d = 2, 256, w.qkv_w.shape[1]
+    kw = {}
+    if vision:
+        cos, sin = oatt.rope_tables(seq, d // 16, 1e4)
+        kw = dict(causal=False, rope_cos=cos, rope_sin=sin)
+    x = torch.randn((batch * seq, d), generator=g).to(torch.bfloat16).cuda()
+    blk = _blocks().GPT2Block(w, batch=batch, seq=seq, residual_dtype=torch.bfloat16,
+                              out_dtype=torch.bfloat16, **kw)
+    a = blk.forward(x).clone()
+    b = blk.forward_abi(x).clone()
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("mlp", [False, True])
+def test_qwen_block_native_entry_matches_python_block(mlp):
+    """b2f_qwen_block reproduces the Python-composed block bit for bit (BASELINE geometry
+    without the MLP, the reference task's geometry with it)."""
+    g = gen(20260806)
+    if mlp:
+        w = qwen_weights(hidden=2560, heads=16, kv_heads=4, head_dim=256, rotary_dim=64,
+                         theta=1e7, seq=128, g=g, interleaved=True, mlp=9216)
+        batch, seq = 1, 128
+        _f32_scales(w, ("o_s", "mlp_down_s"))
+    else:
+        batch, seq = 2, 256
+        w = qwen_weights(hidden=2560, heads=32, kv_heads=8, head_dim=128, rotary_dim=128,
+                         theta=1e6, seq=seq, g=g, interleaved=False, reference=False)
+        _f32_scales(w, ("o_s",))
+    x = torch.randn((batch * seq, 2560), generator=g).to(torch.bfloat16).cuda()
+    blk = _blocks().QwenBlock(w, batch=batch, seq=seq, residual_dtype=torch.bfloat16,
+                              out_dtype=torch.bfloat16)
+    a = blk.forward(x).clone()
+    b = blk.forward_abi(x).clone()
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
