@@ -360,30 +360,6 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-template <int DT>
-__device__ __forceinline__ void smem_load4(const uint8_t* row, int t, int tpr, int nvec,
-                                           float scale, float (&v)[VPT][8]) {
-#pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    const int vi = t + tpr * i;
-    if (vi < nvec) {
-      load8(row, DT, (long long)vi * 8, scale, v[i]);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
-    }
-  }
-}
-
-__device__ __forceinline__ void smem_load_any(const uint8_t* row, int dt, int t, int tpr,
-                                              int nvec, float scale, float (&v)[VPT][8]) {
-  switch (dt) {
-    case kBF16: smem_load4<kBF16>(row, t, tpr, nvec, scale, v); break;
-    case kF32: smem_load4<kF32>(row, t, tpr, nvec, scale, v); break;
-    default: smem_load4<kE4M3>(row, t, tpr, nvec, scale, v); break;
-  }
-}
-
 // Compile-time specialisation of the streaming kernel.  kDyn selects the runtime value
 // (the generic instance); kNone (residual only) means no residual.  FULL: every thread owns
 // exactly VPT vectors (cols == 8 * VPT * TPR), so no per-vector bounds checks.
