@@ -32,75 +32,108 @@ struct RopeParams {
   int rows, heads;
 };
 
+// One warp per token: the token's cos / sin row and the norm weights are loaded once (as
+// vectors) and reused for every head; the heads stream through HB at a time (their loads
+// issued together).  Lane l holds elements [l*E, l*E + E) of a head; the rotate-half
+// partner of element i sits in lane l +- (rotary/2)/E.
 template <int D>
 __global__ void __launch_bounds__(256) head_norm_rope_kernel(const RopeParams p) {
   constexpr int E = D / 32;  // elements per lane
-  const int warp_global = blockIdx.x * 8 + (threadIdx.x >> 5);
+  constexpr int W = (E + 3) / 4;  // 32-bit words per lane
+  constexpr int HB = 4;      // heads in flight per warp
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  if (warp_global >= p.rows * p.heads) return;
-  const int t = warp_global / p.heads;
-  const int h = warp_global - t * p.heads;
-  const uint8_t* src = p.in + (long long)t * p.in_ld + (long long)h * p.in_hstride + lane * E;
-  // one load per lane of its E contiguous bytes
-  uint32_t raw[(E + 3) / 4];
-  if constexpr (E == 2) {
-    raw[0] = *reinterpret_cast<const uint16_t*>(src);
-  } else if constexpr (E == 4) {
-    raw[0] = *reinterpret_cast<const uint32_t*>(src);
-  } else {
-    const uint2 q = *reinterpret_cast<const uint2*>(src);
-    raw[0] = q.x;
-    raw[1] = q.y;
-  }
-  float x[E];
+  if (t >= p.rows) return;
+  const int i0 = lane * E;
+  float w[E], cs[E], sn[E];
 #pragma unroll
-  for (int e = 0; e < E; e += 2) {
-    const float2 v = e4m3x2_to_f32x2((raw[e / 4] >> (8 * (e % 4))) & 0xFFFF);
-    x[e] = v.x * p.in_scale;
-    x[e + 1] = v.y * p.in_scale;
-  }
+  for (int e = 0; e < E; ++e) { w[e] = 1.0f; cs[e] = 1.0f; sn[e] = 0.0f; }
   if (p.weight != nullptr) {
-    float ss = 0.f;
 #pragma unroll
-    for (int e = 0; e < E; ++e) ss += x[e] * x[e];
-    ss = warp_sum(ss);
-    const float inv = rsqrtf(ss / float(D) + p.eps);
-#pragma unroll
-    for (int e = 0; e < E; ++e) x[e] = x[e] * inv * (p.weight[lane * E + e] + p.w_offset);
+    for (int e = 0; e < E; e += 2) {
+      const float2 v = *reinterpret_cast<const float2*>(p.weight + i0 + e);
+      w[e] = v.x + p.w_offset;
+      w[e + 1] = v.y + p.w_offset;
+    }
   }
-  if (p.cos != nullptr) {
-    const int pos = t % p.seq;
-    const int half = p.rotary / 2;
-    const int off = half / E;  // lane distance between rotation partners
-    float y[E];
+  const bool rope = p.cos != nullptr;
+  const int half = p.rotary / 2;
+  const int off = rope ? half / E : 0;  // lane distance between rotation partners
+  if (rope && i0 < p.rotary) {
+    const long long base = (long long)(t % p.seq) * p.rotary + i0;
 #pragma unroll
-    for (int e = 0; e < E; ++e) {
-      const int i = lane * E + e;
-      const int src_lane = (i < half) ? lane + off : lane - off;
-      const float partner = __shfl_sync(0xffffffffu, x[e], src_lane & 31);
-      if (i < p.rotary) {
-        const float rh = (i < half) ? -partner : partner;
-        y[e] = x[e] * p.cos[(long long)pos * p.rotary + i] +
-               rh * p.sin[(long long)pos * p.rotary + i];
-      } else {
-        y[e] = x[e];
+    for (int e = 0; e < E; e += 2) {
+      const float2 c = *reinterpret_cast<const float2*>(p.cos + base + e);
+      const float2 sv = *reinterpret_cast<const float2*>(p.sin + base + e);
+      cs[e] = c.x; cs[e + 1] = c.y;
+      sn[e] = (i0 + e < half) ? -sv.x : sv.x;  // rotate_half sign folded into sin
+      sn[e + 1] = (i0 + e + 1 < half) ? -sv.y : sv.y;
+    }
+  }
+  const int src_lane = (i0 < half) ? lane + off : lane - off;
+  const uint8_t* row_in = p.in + (long long)t * p.in_ld + i0;
+  uint8_t* row_out = p.out + (long long)t * p.out_ld + i0;
+  for (int h0 = 0; h0 < p.heads; h0 += HB) {
+    uint32_t raw[HB][W];
+#pragma unroll
+    for (int hb = 0; hb < HB; ++hb) {
+      if (h0 + hb < p.heads) {
+        const uint8_t* src = row_in + (long long)(h0 + hb) * p.in_hstride;
+        if constexpr (E == 2) {
+          raw[hb][0] = *reinterpret_cast<const uint16_t*>(src);
+        } else if constexpr (E == 4) {
+          raw[hb][0] = *reinterpret_cast<const uint32_t*>(src);
+        } else {
+          const uint2 q = *reinterpret_cast<const uint2*>(src);
+          raw[hb][0] = q.x;
+          raw[hb][1] = q.y;
+        }
       }
     }
 #pragma unroll
-    for (int e = 0; e < E; ++e) x[e] = y[e];
-  }
-  uint8_t* dst = p.out + (long long)t * p.out_ld + (long long)h * D + lane * E;
-  uint32_t packed[(E + 3) / 4] = {};
+    for (int hb = 0; hb < HB; ++hb) {
+      if (h0 + hb >= p.heads) break;  // warp-uniform
+      float x[E];
 #pragma unroll
-  for (int e = 0; e < E; e += 2)
-    packed[e / 4] |= uint32_t(f32x2_to_e4m3x2(x[e] * p.out_inv_scale, x[e + 1] * p.out_inv_scale))
-                     << (8 * (e % 4));
-  if constexpr (E == 2) {
-    *reinterpret_cast<uint16_t*>(dst) = static_cast<uint16_t>(packed[0]);
-  } else if constexpr (E == 4) {
-    *reinterpret_cast<uint32_t*>(dst) = packed[0];
-  } else {
-    *reinterpret_cast<uint2*>(dst) = make_uint2(packed[0], packed[1]);
+      for (int e = 0; e < E; e += 2) {
+        const float2 v = e4m3x2_to_f32x2((raw[hb][e / 4] >> (8 * (e % 4))) & 0xFFFF);
+        x[e] = v.x * p.in_scale;
+        x[e + 1] = v.y * p.in_scale;
+      }
+      if (p.weight != nullptr) {
+        float ss = 0.f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) ss += x[e] * x[e];
+        ss = warp_sum(ss);
+        const float inv = rsqrtf(ss / float(D) + p.eps);
+#pragma unroll
+        for (int e = 0; e < E; ++e) x[e] = x[e] * inv * w[e];
+      }
+      if (rope) {
+        float y[E];
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const float partner = __shfl_sync(0xffffffffu, x[e], src_lane & 31);
+          y[e] = (i0 + e < p.rotary) ? x[e] * cs[e] + partner * sn[e] : x[e];
+        }
+#pragma unroll
+        for (int e = 0; e < E; ++e) x[e] = y[e];
+      }
+      uint32_t packed[W] = {};
+#pragma unroll
+      for (int e = 0; e < E; e += 2)
+        packed[e / 4] |= uint32_t(f32x2_to_e4m3x2(x[e] * p.out_inv_scale,
+                                                  x[e + 1] * p.out_inv_scale))
+                         << (8 * (e % 4));
+      uint8_t* dst = row_out + (long long)(h0 + hb) * D;
+      if constexpr (E == 2) {
+        *reinterpret_cast<uint16_t*>(dst) = static_cast<uint16_t>(packed[0]);
+      } else if constexpr (E == 4) {
+        *reinterpret_cast<uint32_t*>(dst) = packed[0];
+      } else {
+        *reinterpret_cast<uint2*>(dst) = make_uint2(packed[0], packed[1]);
+      }
+    }
   }
 }
 
@@ -212,8 +245,11 @@ int b2f_head_norm_rope(const b2f_rope_args* a, b2f_stream_t stream) {
   p.out = reinterpret_cast<uint8_t*>(a->out); p.out_ld = a->out_ld;
   p.out_inv_scale = 1.0f / a->out_scale;
   p.rows = a->rows; p.heads = a->heads;
-  const long long warps = (long long)a->rows * a->heads;
-  const int grid = (int)((warps + 7) / 8);
+  if ((a->weight != nullptr && (reinterpret_cast<uintptr_t>(a->weight) & 7)) ||
+      (a->cos != nullptr && ((reinterpret_cast<uintptr_t>(a->cos) & 7) ||
+                             (reinterpret_cast<uintptr_t>(a->sin) & 7) || (a->rotary_dim % 2))))
+    return fail(B2F_ERR_ARG, "head_norm_rope: weight / cos / sin must be 8-byte aligned");
+  const int grid = (a->rows + 7) / 8;  // one warp per token
   cudaStream_t s = (cudaStream_t)stream;
   if (d == 64) head_norm_rope_kernel<64><<<grid, 256, 0, s>>>(p);
   else if (d == 128) head_norm_rope_kernel<128><<<grid, 256, 0, s>>>(p);
