@@ -108,3 +108,47 @@ def test_heads_parallel_qwen_and_row_sharded_norm_gloo(interleaved):
         assert (h, hk) == (2, 1)
         assert err < 1e-4, err
         assert ok_norm
+
+
+def _fault_worker(rank, world, port, q):
+    import datetime
+    import time
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=5))
+    try:
+        if rank == 1:
+            # this rank fails on the host before the row-sharded norm's MAX all-reduce
+            q.put((rank, "raised"))
+            raise RuntimeError("injected host-side failure")
+        amax = torch.tensor([1.0])
+        t0 = time.time()
+        try:
+            dist.all_reduce(amax, op=dist.ReduceOp.MAX)
+            q.put((rank, "completed"))
+        except Exception as exc:  # the collective must fail, not hang
+            q.put((rank, f"error after {time.time() - t0:.1f}s: {type(exc).__name__}"))
+    except RuntimeError:
+        pass
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def test_failed_rank_surfaces_as_collective_error_gloo():
+    """A rank that dies before the amax all-reduce makes the surviving rank's collective
+    fail within the process-group timeout (host-side failure detection; no GPU involved)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_fault_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+    assert results[1] == "raised"
+    assert results[0].startswith("error after"), results[0]
+    assert float(results[0].split()[2].rstrip("s:")) < 60
