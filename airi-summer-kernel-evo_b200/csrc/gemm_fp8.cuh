@@ -121,7 +121,10 @@ struct GemmCfg {
 // Tile order: groups of GROUP_M row-blocks sweep all column blocks, so the CTAs that run
 // concurrently share A rows and B columns in L2.
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
-  constexpr int GROUP_M = 8;
+#ifndef B2F_GROUP_M
+#define B2F_GROUP_M 16
+#endif
+  constexpr int GROUP_M = B2F_GROUP_M;
   const int per_group = GROUP_M * num_n;
   const int g = t / per_group;
   const int first_m = g * GROUP_M;
