@@ -32,6 +32,10 @@ __device__ unsigned long long g_trace[160][8][8];
 #else
 #define B2F_STAMP(tile, slot) do {} while (0)
 #endif
+#ifdef B2F_TRACE
+static __device__ __forceinline__ int& epi_it_ref() { static __shared__ int v; return v; }
+#define g_epi_it (epi_it_ref())
+#endif
 
 enum : int { kOutF32 = 0, kOutBF16 = 1, kOutE4M3 = 2 };
 enum : int { kActNone = 0, kActRelu = 1, kActGeluTanh = 2, kActLeakyRelu = 3, kActSilu = 4 };
@@ -370,9 +374,15 @@ __device__ __forceinline__ void epilogue_tile(const EpilogueParams& ep, const CU
       for (int x = 1; x < BN / 32; ++x)
         if (uu == x) { lb = lbv[x]; lc = lcv[x]; }
       tmem_ld_wait_regs(cur);
+#ifdef B2F_TRACE
+      if (uu == 0 && (threadIdx.x >> 5) == 2 && (threadIdx.x & 31) == 0) B2F_STAMP(g_epi_it, 5);
+#endif
       if (uu + 1 < units) tmem_ld32_async(t_row + (uu + 1) * 32, nxt);
       float v[32];
       epi_values(ep, alpha, row, col0, M, N, cur, v, rowsum, amax_local, lb, lc);
+#ifdef B2F_TRACE
+      if (uu == 0 && (threadIdx.x >> 5) == 2 && (threadIdx.x & 31) == 0) B2F_STAMP(g_epi_it, 6);
+#endif
       if (ep.mode == kModeRowSum) continue;
       if (!tma) {
         if (row < M) epi_store_direct(ep, row, col0, N, v);
@@ -398,6 +408,9 @@ __device__ __forceinline__ void epilogue_tile(const EpilogueParams& ep, const CU
               make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
         }
       }
+#ifdef B2F_TRACE
+      if (uu == 0 && (threadIdx.x >> 5) == 2 && (threadIdx.x & 31) == 0) B2F_STAMP(g_epi_it, 7);
+#endif
       if (sub == subs - 1 || uu == units - 1) {
         fence_async_shared();
         __syncwarp();
@@ -595,6 +608,9 @@ __global__ void __launch_bounds__(320, 1)
       float rowsum = 0.0f;
       const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + acc * BN + chalf * (BN / 2);
       if (splits == 1) {
+#ifdef B2F_TRACE
+        if (warp == 2 && lane == 0) g_epi_it = it;
+#endif
         epilogue_tile<BN / 2>(ep, &tmap_out, alpha, t_row, row, row0, col_base, M, N, stage,
                               buf, rowsum, amax_local, lbv, lcv);
         tc_fence_before();
