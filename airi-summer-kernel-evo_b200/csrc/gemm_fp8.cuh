@@ -357,27 +357,24 @@ __device__ __forceinline__ void epilogue_tile(const EpilogueParams& ep, const CU
   int units = BN / 32;
   const int n_left = N - col_base;
   if (n_left < BN) units = (n_left + 31) / 32;   // columns past N are skipped (uniform)
-  uint32_t ra[32], rb[32];
-  tmem_ld32_async(t_row, ra);
+  // One 32-column TMEM load in flight at a time: a second buffer (prefetching the next
+  // chunk) pushed the 168-register budget into spills, which cost more than the exposed
+  // load latency (measured on the K = 768 GEMMs of the GPT-2 block).
+  uint32_t cur[32];
 #pragma unroll 1
-  for (int u = 0; u < units; u += 2) {
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const int uu = u + half;
-      if (uu >= units) break;
-      uint32_t (&cur)[32] = half == 0 ? ra : rb;
-      uint32_t (&nxt)[32] = half == 0 ? rb : ra;
+  for (int uu = 0; uu < units; ++uu) {
+    {
       const int col0 = col_base + uu * 32;
       // this chunk's bias / column scale (loaded before the accumulator was ready)
       float lb = lbv[0], lc = lcv[0];
 #pragma unroll
       for (int x = 1; x < BN / 32; ++x)
         if (uu == x) { lb = lbv[x]; lc = lcv[x]; }
+      tmem_ld32_async(t_row + uu * 32, cur);
       tmem_ld_wait_regs(cur);
 #ifdef B2F_TRACE
       if (uu == 0 && (threadIdx.x >> 5) == 2 && (threadIdx.x & 31) == 0) B2F_STAMP(g_epi_it, 5);
 #endif
-      if (uu + 1 < units) tmem_ld32_async(t_row + (uu + 1) * 32, nxt);
       float v[32];
       epi_values(ep, alpha, row, col0, M, N, cur, v, rowsum, amax_local, lb, lc);
 #ifdef B2F_TRACE
