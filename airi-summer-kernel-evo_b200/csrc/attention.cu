@@ -38,7 +38,14 @@ struct AttnParams {
   float ctx_inv_scale;
   float v_scale;        // V bf16 values are multiplied by v_scale in the epilogue
   int pair_heads;       // two-tile kernel: the tiles are query heads 2y, 2y+1 (same KV head)
+  int gate_tma;         // two-tile kernel: e4m3 gate tiles arrive in shared memory by TMA
 };
+
+// sigmoid(g) from the hardware exponential and an approximate reciprocal: the product with
+// the context is requantised to e4m3 (3 mantissa bits), far coarser than their error.
+__device__ __forceinline__ float sigmoid_fast(float g) {
+  return __fdividef(1.0f, 1.0f + __expf(-g));
+}
 
 __device__ __forceinline__ uint64_t make_sdesc(uint32_t addr, uint32_t layout, uint32_t lbo,
                                                uint32_t sbo) {
@@ -355,7 +362,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                   const float gg = gv[e] * p.gate_scale;
-                  v[u + 4 * t + e] *= 1.0f / (1.0f + expf(-gg));
+                  v[u + 4 * t + e] *= sigmoid_fast(gg);
                 }
               }
             }
@@ -364,7 +371,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
             for (int u = 0; u < 32; ++u) {
               const float gg = __bfloat162float(gp[u]) * p.gate_scale;
-              v[u] *= 1.0f / (1.0f + expf(-gg));
+              v[u] *= sigmoid_fast(gg);
             }
           }
         }
@@ -432,7 +439,10 @@ struct Attn2Cfg {
   // the K ring runs further ahead than the (larger) V ring.  P lives in tensor memory.
   static constexpr int KST = (D >= 128) ? 4 : 6;
   static constexpr int VST = (D >= 128) ? 3 : 4;
-  static constexpr int SMEM_BYTES = 2 * Q_BYTES + KST * K_BYTES + VST * V_BYTES + 1024 + 512;
+  // e4m3 gate tiles (one per query tile, same shape as Q) for the gated epilogue.
+  static constexpr int G_BYTES = Q_BYTES;
+  static constexpr int SMEM_BYTES =
+      2 * Q_BYTES + KST * K_BYTES + VST * V_BYTES + 2 * G_BYTES + 1024 + 512;
   static constexpr int S_COL = 0;             // S_X at X * BKV
   static constexpr int O_COL = 2 * BKV;       // O_X at O_COL + X * D
   static constexpr int TMEM_COLS = 512;
@@ -444,7 +454,8 @@ template <int D, bool VF16>
 __global__ void __launch_bounds__(320, 1)
     attention2_kernel(const __grid_constant__ CUtensorMap tm_q,
                       const __grid_constant__ CUtensorMap tm_k,
-                      const __grid_constant__ CUtensorMap tm_v, const AttnParams p) {
+                      const __grid_constant__ CUtensorMap tm_v,
+                      const __grid_constant__ CUtensorMap tm_g, const AttnParams p) {
   using C = Attn2Cfg<D>;
   constexpr int BQ = C::BQ, BKV = C::BKV, KST = C::KST, VST = C::VST;
   extern __shared__ uint8_t smem_raw[];
@@ -453,7 +464,8 @@ __global__ void __launch_bounds__(320, 1)
   uint8_t* sq = smem;                            // [2][Q_BYTES]
   uint8_t* sk = sq + 2 * C::Q_BYTES;             // [KST][K_BYTES]
   uint8_t* sv = sk + KST * C::K_BYTES;           // [VST][V_BYTES]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sv + VST * C::V_BYTES);
+  uint8_t* sg = sv + VST * C::V_BYTES;           // [2][G_BYTES]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sg + 2 * C::G_BYTES);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
   uint64_t* k_empty = k_full + KST;
@@ -464,10 +476,12 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* p_full = s_free + 2;
   uint64_t* pv_done = p_full + 2;
   uint64_t* drain = pv_done + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* g_full = drain + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g_full + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) B2F_ASTAMP(15, 12);
   const int n_qt = (p.seq + BQ - 1) / BQ;
   int qt[2], hx[2];
   bool act[2];
@@ -517,16 +531,19 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(&pv_done[i], 1);
     }
     mbar_init(drain, 1);
+    mbar_init(g_full, 1);
     *abort_flag = 0;
     fence_mbarrier_init();
     tma_prefetch_desc(&tm_q);
     tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_v);
+    if (p.gate_tma) tma_prefetch_desc(&tm_g);
   }
   if (warp == 1) tmem_alloc(tmem_slot, C::TMEM_COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if (threadIdx.x == 0) B2F_ASTAMP(15, 13);
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
@@ -550,6 +567,10 @@ __global__ void __launch_bounds__(320, 1)
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0;
+      bool g_issued = false;
+      // The gate tiles follow the second K tile: off the first S's critical path, long
+      // before the epilogue reads them.
+      const int g_after = min(1, nkv[1] - 1);
       for (int j = 0; j < nkv[1]; ++j) {
         if (!mbar_wait(&emptyb[stage], phase ^ 1, kDevTimeoutProducer, abort_flag)) break;
         if (is_k) {
@@ -567,6 +588,17 @@ __global__ void __launch_bounds__(320, 1)
         }
         ++issued;
         if (++stage == NS) { stage = 0; phase ^= 1; }
+        if (is_k && p.gate_tma && j == g_after) {
+          mbar_arrive_expect_tx(g_full, (act[0] ? 2 : 1) * C::G_BYTES);
+          for (int x = 0; x < 2; ++x) {
+            if (!act[x]) continue;
+            for (int kb = 0; kb < C::KB; ++kb)
+              tma_load_3d(sg + x * C::G_BYTES + kb * BQ * C::ROWB, &tm_g, g_full,
+                          int(hx[x] * p.gate_hstride) + kb * 128, qt[x] * BQ, b,
+                          policy_evict_first());
+          }
+          g_issued = true;
+        }
       }
       // Let the copies still in flight land before the CTA exits.
       const int pending = issued < NS ? issued : NS;
@@ -579,6 +611,8 @@ __global__ void __launch_bounds__(320, 1)
       if (is_k) {
         const uint64_t t0 = globaltimer();
         while (!mbar_test(q_full, 0))
+          if (globaltimer() - t0 > B2F_WAIT_NS) { record_error(kDevTimeoutDrain); break; }
+        while (g_issued && !mbar_test(g_full, 0))
           if (globaltimer() - t0 > B2F_WAIT_NS) { record_error(kDevTimeoutDrain); break; }
       }
     }
@@ -681,33 +715,25 @@ __global__ void __launch_bounds__(320, 1)
       // keys k0 + kk with kk > klim are masked (past the sequence end or, causal, past qi)
       const int klim = min(p.seq - 1, p.causal ? qi : p.seq - 1) - k0;
       const bool need_mask = klim < BKV - 1;
-      // Row max of S * c (f32): TMEM -> registers 32 columns at a time, next load in flight
-      // while the current chunk reduces, 8 independent partial maxima.
-      auto max_pass = [&]() -> float {
-        float mp[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) mp[e] = -INFINITY;
-        uint32_t ra[32], rb[32];
-        tmem_ld32_async(t_lane + s_col, ra);
-#pragma unroll
-        for (int cc = 0; cc < BKV; cc += 32) {
-          uint32_t (&cur)[32] = ((cc / 32) & 1) ? rb : ra;
-          uint32_t (&nxt)[32] = ((cc / 32) & 1) ? ra : rb;
-          tmem_ld_wait_regs(cur);
-          if (cc + 32 < BKV) tmem_ld32_async(t_lane + s_col + cc + 32, nxt);
-#pragma unroll
-          for (int u = 0; u < 32; u += 2) {
-            float v0 = __uint_as_float(cur[u]), v1 = __uint_as_float(cur[u + 1]);
-            if (need_mask) {
-              if (cc + u > klim) v0 = -INFINITY;
-              if (cc + u + 1 > klim) v1 = -INFINITY;
-            }
-            mp[(u >> 1) & 7] = fmax3(mp[(u >> 1) & 7], v0, v1);
-          }
-        }
-        return fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
-                     fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7]))) * c;
+      // The whole S row (128 f32 columns) in registers: four loads in flight, one wait;
+      // S is read from tensor memory once per key tile.
+      uint32_t s0[32], s1[32], s2[32], s3[32];
+      tmem_ld32_async(t_lane + s_col, s0);
+      tmem_ld32_async(t_lane + s_col + 32, s1);
+      tmem_ld32_async(t_lane + s_col + 64, s2);
+      tmem_ld32_async(t_lane + s_col + 96, s3);
+      tmem_ld_wait_regs(s0);
+      reg_fence32(s1);
+      reg_fence32(s2);
+      reg_fence32(s3);
+      auto sv = [&](int u) -> uint32_t& {
+        return u < 32 ? s0[u] : u < 64 ? s1[u - 32] : u < 96 ? s2[u - 64] : s3[u - 96];
       };
+      if (need_mask) {
+#pragma unroll
+        for (int u = 0; u < BKV; ++u)
+          if (u > klim) sv(u) = __float_as_uint(-INFINITY);
+      }
       // O *= corr (warp-collective; lanes whose row keeps its reference pass corr = 1).
       auto rescale_o = [&](float corr) {
 #pragma unroll 1
@@ -721,9 +747,17 @@ __global__ void __launch_bounds__(320, 1)
         tmem_st_wait();
       };
       float corr = 1.0f, lt;
+      bool rescale = false;
       {
-        const float mt = max_pass();
-        bool rescale = false;
+        // Row max of S * c: 4 independent partial maxima over 3-input max.
+        float mp[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) mp[e] = -INFINITY;
+#pragma unroll
+        for (int u = 0; u < BKV; u += 2)
+          mp[(u >> 1) & 3] = fmax3(mp[(u >> 1) & 3], __uint_as_float(sv(u)),
+                                   __uint_as_float(sv(u + 1)));
+        const float mt = fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])) * c;
         if (mt > m_used + 8.0f) {
           if (m_used != -INFINITY) {
             corr = ex2_hw(m_used - mt);
@@ -733,40 +767,24 @@ __global__ void __launch_bounds__(320, 1)
         }
         const float mref = (m_used == -INFINITY) ? 0.0f : m_used;
         if (lane == 0 && (warp == 2 || warp == 6)) B2F_ASTAMP(j, x * 4 + 1);
-        if (j > 0) {
-          ok = __all_sync(0xffffffffu,
-                          mbar_wait(&pv_done[x], (j - 1) & 1, kDevTimeoutEpilogue, abort_flag));
-          if (!ok) break;
-          tc_fence_after();
-          if (__any_sync(0xffffffffu, rescale)) rescale_o(corr);
-        }
-        if (lane == 0 && (warp == 2 || warp == 6)) B2F_ASTAMP(j, x * 4 + 2);
-        // P = 2^(S*c - m), written back to tensor memory over the S columns already read
-        // (P column k/2 < S column k): the A operand of P.V.  With f16 V, x = S*c - m
-        // (<= 8 after the lazy update) is packed to f16x2 and exponentiated a pair at a
-        // time, the row sum accumulating in f16x2 over 4 pairs and then in f32; with bf16 V,
-        // each weight is exponentiated in f32 and P rounded to bf16.
+        // P = 2^(S*c - m), written back to tensor memory over the S columns (P column k/2
+        // < S column k; the row is already in registers): the A operand of P.V.  P(j-1)
+        // is no longer read there: S(j) was written after P(j-1).V in the tensor pipe's
+        // order.  With f16 V, x = S*c - m (<= 8 after the lazy update) is packed to f16x2
+        // and exponentiated a pair at a time, the row sum accumulating in f16x2 over 4
+        // pairs and then in f32; with bf16 V, each weight is exponentiated in f32 and P
+        // rounded to bf16.  Masked keys hold -inf, whose weight is 0.
         float ls[4] = {0.f, 0.f, 0.f, 0.f};
-        uint32_t ra[32], rb[32];
-        tmem_ld32_async(t_lane + s_col, ra);
 #pragma unroll
         for (int cc = 0; cc < BKV; cc += 32) {
-          uint32_t (&cur)[32] = ((cc / 32) & 1) ? rb : ra;
-          uint32_t (&nxt)[32] = ((cc / 32) & 1) ? ra : rb;
-          tmem_ld_wait_regs(cur);
-          if (cc + 32 < BKV) tmem_ld32_async(t_lane + s_col + cc + 32, nxt);
           uint32_t pk[16];
           if constexpr (VF16) {
             uint32_t acc[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
-              const int u = 2 * e;
-              float v0 = fmaf(__uint_as_float(cur[u]), c, -mref);
-              float v1 = fmaf(__uint_as_float(cur[u + 1]), c, -mref);
-              if (need_mask) {
-                if (cc + u > klim) v0 = -INFINITY;
-                if (cc + u + 1 > klim) v1 = -INFINITY;
-              }
+              const int u = cc + 2 * e;
+              const float v0 = fmaf(__uint_as_float(sv(u)), c, -mref);
+              const float v1 = fmaf(__uint_as_float(sv(u + 1)), c, -mref);
               pk[e] = ex2_f16x2(pack_f16x2(v0, v1));
               acc[e & 3] = hadd2(acc[e & 3], pk[e]);
             }
@@ -778,13 +796,9 @@ __global__ void __launch_bounds__(320, 1)
           } else {
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
-              const int u = 2 * e;
-              float v0 = fmaf(__uint_as_float(cur[u]), c, -mref);
-              float v1 = fmaf(__uint_as_float(cur[u + 1]), c, -mref);
-              if (need_mask) {
-                if (cc + u > klim) v0 = -INFINITY;
-                if (cc + u + 1 > klim) v1 = -INFINITY;
-              }
+              const int u = cc + 2 * e;
+              const float v0 = fmaf(__uint_as_float(sv(u)), c, -mref);
+              const float v1 = fmaf(__uint_as_float(sv(u + 1)), c, -mref);
               const float e0 = ex2_hw(v0), e1 = ex2_hw(v1);
               const __nv_bfloat162 bb = __floats2bfloat162_rn(e0, e1);
               // row sum from the f32 weights: the P.V MMA sees them rounded to bf16
@@ -795,8 +809,17 @@ __global__ void __launch_bounds__(320, 1)
           }
           tmem_st16(t_lane + s_col + cc / 2, pk);
         }
-        tmem_st_wait();
         lt = (ls[0] + ls[1]) + (ls[2] + ls[3]);
+      }
+      if (lane == 0 && (warp == 2 || warp == 6)) B2F_ASTAMP(j, x * 4 + 2);
+      tmem_st_wait();
+      // O *= corr once P(j-1).V has landed (before P(j).V is released below).
+      if (j > 0) {
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait(&pv_done[x], (j - 1) & 1, kDevTimeoutEpilogue, abort_flag));
+        if (!ok) break;
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, rescale)) rescale_o(corr);
       }
       l = l * corr + lt;
       tc_fence_before();
@@ -810,59 +833,91 @@ __global__ void __launch_bounds__(320, 1)
     // ---------------------------------------------------------------- epilogue
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[x], (nkv[x] - 1) & 1,
                                                   kDevTimeoutEpilogue, abort_flag));
+    if (lane == 0 && warp == 4) B2F_ASTAMP(15, 14);
     if (ok) {
       tc_fence_after();
       const long long row = (long long)b * p.seq + qi;
       const bool valid = qi < p.seq;
       const float inv_l = (l > 0.f) ? p.v_scale / l : 0.f;
-#pragma unroll 1
-      for (int cc = 0; cc < D; cc += 32) {
-        uint32_t o[32];
-        tmem_ld32(t_lane + o_col + cc, o);
-        if (!valid) continue;
-        float v[32];
+      const bool gate_smem = p.gate_tma != 0;
+      if (gate_smem)
+        ok = __all_sync(0xffffffffu, mbar_wait(g_full, 0, kDevTimeoutEpilogue, abort_flag));
+      // 32 columns at a time, the next chunk's tensor-memory load in flight meanwhile.
+      uint32_t oa[32], ob[32];
+      if (ok) tmem_ld32_async(t_lane + o_col, oa);
 #pragma unroll
-        for (int u = 0; u < 32; ++u) v[u] = __uint_as_float(o[u]) * inv_l;
-        if (p.gate != nullptr) {
-          const long long go = row * p.gate_ld + (long long)hx[x] * p.gate_hstride + cc;
-          if (p.gate_dtype == kE4M3) {
-            const uint8_t* gp = reinterpret_cast<const uint8_t*>(p.gate) + go;
-#pragma unroll
-            for (int u = 0; u < 32; u += 16) {
-              const uint4 qv = *reinterpret_cast<const uint4*>(gp + u);
-              const uint32_t w[4] = {qv.x, qv.y, qv.z, qv.w};
-#pragma unroll
-              for (int t = 0; t < 4; ++t) {
-                const float2 a = e4m3x2_to_f32x2(w[t] & 0xFFFF);
-                const float2 bb = e4m3x2_to_f32x2(w[t] >> 16);
-                const float gv[4] = {a.x, a.y, bb.x, bb.y};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  const float gg = gv[e] * p.gate_scale;
-                  v[u + 4 * t + e] *= 1.0f / (1.0f + expf(-gg));
+      for (int cc = 0; cc < D && ok; cc += 32) {
+        uint32_t (&o)[32] = ((cc / 32) & 1) ? ob : oa;
+        uint32_t (&on)[32] = ((cc / 32) & 1) ? oa : ob;
+        tmem_ld_wait_regs(o);
+        if (cc + 32 < D) tmem_ld32_async(t_lane + o_col + cc + 32, on);
+        // (rows past the sequence end store nothing; the warp reconverges before the next
+        // chunk's warp-collective tensor-memory load)
+        if (valid) {
+          float v[32];
+  #pragma unroll
+          for (int u = 0; u < 32; ++u) v[u] = __uint_as_float(o[u]) * inv_l;
+          if (p.gate != nullptr) {
+            if (gate_smem) {
+              // Row r of this tile's gate, as the TMA wrote it (16-byte chunks swizzled by
+              // the row: 128B pattern for 128-byte rows, 64B pattern for 64-byte rows).
+              const uint8_t* gt = sg + x * C::G_BYTES + (cc / C::ROWB) * (BQ * C::ROWB);
+  #pragma unroll
+              for (int h16 = 0; h16 < 2; ++h16) {
+                const uint32_t off = uint32_t(r * C::ROWB + (cc % C::ROWB) + h16 * 16);
+                const uint32_t sw = off ^ (((off >> 7) & (C::ROWB == 128 ? 7u : 3u)) << 4);
+                const uint4 qv = *reinterpret_cast<const uint4*>(gt + sw);
+                const uint32_t w4[4] = {qv.x, qv.y, qv.z, qv.w};
+  #pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                  const float2 a = e4m3x2_to_f32x2(w4[t] & 0xFFFF);
+                  const float2 bb = e4m3x2_to_f32x2(w4[t] >> 16);
+                  const int u = h16 * 16 + 4 * t;
+                  v[u] *= sigmoid_fast(a.x * p.gate_scale);
+                  v[u + 1] *= sigmoid_fast(a.y * p.gate_scale);
+                  v[u + 2] *= sigmoid_fast(bb.x * p.gate_scale);
+                  v[u + 3] *= sigmoid_fast(bb.y * p.gate_scale);
                 }
               }
-            }
-          } else {
-            const __nv_bfloat16* gp = reinterpret_cast<const __nv_bfloat16*>(p.gate) + go;
-#pragma unroll
-            for (int u = 0; u < 32; ++u) {
-              const float gg = __bfloat162float(gp[u]) * p.gate_scale;
-              v[u] *= 1.0f / (1.0f + expf(-gg));
+            } else {
+              const long long go = row * p.gate_ld + (long long)hx[x] * p.gate_hstride + cc;
+              if (p.gate_dtype == kE4M3) {
+                const uint8_t* gp = reinterpret_cast<const uint8_t*>(p.gate) + go;
+  #pragma unroll
+                for (int u = 0; u < 32; u += 16) {
+                  const uint4 qv = *reinterpret_cast<const uint4*>(gp + u);
+                  const uint32_t w4[4] = {qv.x, qv.y, qv.z, qv.w};
+  #pragma unroll
+                  for (int t = 0; t < 4; ++t) {
+                    const float2 a = e4m3x2_to_f32x2(w4[t] & 0xFFFF);
+                    const float2 bb = e4m3x2_to_f32x2(w4[t] >> 16);
+                    v[u + 4 * t] *= sigmoid_fast(a.x * p.gate_scale);
+                    v[u + 4 * t + 1] *= sigmoid_fast(a.y * p.gate_scale);
+                    v[u + 4 * t + 2] *= sigmoid_fast(bb.x * p.gate_scale);
+                    v[u + 4 * t + 3] *= sigmoid_fast(bb.y * p.gate_scale);
+                  }
+                }
+              } else {
+                const __nv_bfloat16* gp = reinterpret_cast<const __nv_bfloat16*>(p.gate) + go;
+  #pragma unroll
+                for (int u = 0; u < 32; ++u)
+                  v[u] *= sigmoid_fast(__bfloat162float(gp[u]) * p.gate_scale);
+              }
             }
           }
+          uint32_t w[8];
+  #pragma unroll
+          for (int t = 0; t < 8; ++t)
+            w[t] = uint32_t(f32x2_to_e4m3x2(v[4 * t] * p.ctx_inv_scale,
+                                            v[4 * t + 1] * p.ctx_inv_scale)) |
+                   (uint32_t(f32x2_to_e4m3x2(v[4 * t + 2] * p.ctx_inv_scale,
+                                             v[4 * t + 3] * p.ctx_inv_scale))
+                    << 16);
+          uint8_t* dst = p.ctx + row * p.ctx_ld + (long long)hx[x] * D + cc;
+          *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+          *reinterpret_cast<uint4*>(dst + 16) = make_uint4(w[4], w[5], w[6], w[7]);
         }
-        uint32_t w[8];
-#pragma unroll
-        for (int t = 0; t < 8; ++t)
-          w[t] = uint32_t(f32x2_to_e4m3x2(v[4 * t] * p.ctx_inv_scale,
-                                          v[4 * t + 1] * p.ctx_inv_scale)) |
-                 (uint32_t(f32x2_to_e4m3x2(v[4 * t + 2] * p.ctx_inv_scale,
-                                           v[4 * t + 3] * p.ctx_inv_scale))
-                  << 16);
-        uint8_t* dst = p.ctx + row * p.ctx_ld + (long long)hx[x] * D + cc;
-        *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
-        *reinterpret_cast<uint4*>(dst + 16) = make_uint4(w[4], w[5], w[6], w[7]);
+        __syncwarp();
       }
     }
   }
@@ -874,6 +929,7 @@ __global__ void __launch_bounds__(320, 1)
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
+  if (threadIdx.x == 0) B2F_ASTAMP(15, 15);
 }
 
 template <int D, bool PAIR>
@@ -925,6 +981,22 @@ int launch_attention(const b2f_attn_args* a, cudaStream_t stream) {
   p.ctx_inv_scale = 1.0f / a->ctx_scale;
   p.v_scale = a->v_scale;
   p.pair_heads = 0;
+  p.gate_tma = 0;
+  CUtensorMap tg = tq;  // (unused unless gate_tma)
+  if (PAIR && a->gate != nullptr && a->gate_dtype == B2F_DTYPE_E4M3) {
+    // e4m3 gate tiles [BQ rows x D] by TMA, the same box and swizzle as Q; the column
+    // extent ends with the last head's D columns.
+    const unsigned long long dims[3] = {
+        (unsigned long long)((a->hq - 1) * a->gate_head_stride + D), (unsigned long long)a->seq,
+        (unsigned long long)a->batch};
+    const unsigned long long strides[2] = {(unsigned long long)a->gate_ld,
+                                           (unsigned long long)a->gate_ld * a->seq};
+    const unsigned int box[3] = {(unsigned int)C::ROWB, (unsigned int)C::BQ, 1};
+    if (!encode_tmap(&tg, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, a->gate, dims, strides, box, sw8,
+                     &err))
+      return fail(B2F_ERR_ARG, "attention: gate tensor map: " + err);
+    p.gate_tma = 1;
+  }
   static thread_local int attr_dev[2][3] = {{-1, -1, -1}, {-1, -1, -1}};
   const int slot = D == 64 ? 0 : (D == 128 ? 1 : 2);
   int dev = 0;
@@ -941,9 +1013,9 @@ int launch_attention(const b2f_attn_args* a, cudaStream_t stream) {
     p.pair_heads = (a->hq / a->hkv) % 2 == 0;
     dim3 grid(p.pair_heads ? n_qt : (n_qt + 1) / 2, p.pair_heads ? a->hq / 2 : a->hq, a->batch);
     if (a->v_dtype == B2F_DTYPE_F16)
-      attention2_kernel<D, true><<<grid, 320, SMEM, stream>>>(tq, tk, tv, p);
+      attention2_kernel<D, true><<<grid, 320, SMEM, stream>>>(tq, tk, tv, tg, p);
     else
-      attention2_kernel<D, false><<<grid, 320, SMEM, stream>>>(tq, tk, tv, p);
+      attention2_kernel<D, false><<<grid, 320, SMEM, stream>>>(tq, tk, tv, tg, p);
   } else {
     if (attr_dev[0][slot] != dev) {
       B2F_CUDA_TRY(cudaFuncSetAttribute(attention_kernel<D>,

@@ -33,8 +33,8 @@ struct Carve {
   }
 };
 
-// V operand type of the attention kernel: f16 for head_dim 64 / 128, bf16 otherwise.
-int v_dtype(int head_dim) { return (head_dim == 64 || head_dim == 128) ? B2F_DTYPE_F16 : B2F_DTYPE_BF16; }
+// V operand of the blocks: bf16 (the f16 form measured slower on B200).
+int v_dtype(int /*head_dim*/) { return B2F_DTYPE_BF16; }
 
 int v_convert(const void* in, long long in_ld, void* out, long long rows, int cols, int dt,
               b2f_stream_t s) {
