@@ -855,20 +855,20 @@ __global__ void __launch_bounds__(320, 1)
         // chunk's warp-collective tensor-memory load)
         if (valid) {
           float v[32];
-  #pragma unroll
+#pragma unroll
           for (int u = 0; u < 32; ++u) v[u] = __uint_as_float(o[u]) * inv_l;
           if (p.gate != nullptr) {
             if (gate_smem) {
               // Row r of this tile's gate, as the TMA wrote it (16-byte chunks swizzled by
               // the row: 128B pattern for 128-byte rows, 64B pattern for 64-byte rows).
               const uint8_t* gt = sg + x * C::G_BYTES + (cc / C::ROWB) * (BQ * C::ROWB);
-  #pragma unroll
+#pragma unroll
               for (int h16 = 0; h16 < 2; ++h16) {
                 const uint32_t off = uint32_t(r * C::ROWB + (cc % C::ROWB) + h16 * 16);
                 const uint32_t sw = off ^ (((off >> 7) & (C::ROWB == 128 ? 7u : 3u)) << 4);
                 const uint4 qv = *reinterpret_cast<const uint4*>(gt + sw);
                 const uint32_t w4[4] = {qv.x, qv.y, qv.z, qv.w};
-  #pragma unroll
+#pragma unroll
                 for (int t = 0; t < 4; ++t) {
                   const float2 a = e4m3x2_to_f32x2(w4[t] & 0xFFFF);
                   const float2 bb = e4m3x2_to_f32x2(w4[t] >> 16);
@@ -883,11 +883,11 @@ __global__ void __launch_bounds__(320, 1)
               const long long go = row * p.gate_ld + (long long)hx[x] * p.gate_hstride + cc;
               if (p.gate_dtype == kE4M3) {
                 const uint8_t* gp = reinterpret_cast<const uint8_t*>(p.gate) + go;
-  #pragma unroll
+#pragma unroll
                 for (int u = 0; u < 32; u += 16) {
                   const uint4 qv = *reinterpret_cast<const uint4*>(gp + u);
                   const uint32_t w4[4] = {qv.x, qv.y, qv.z, qv.w};
-  #pragma unroll
+#pragma unroll
                   for (int t = 0; t < 4; ++t) {
                     const float2 a = e4m3x2_to_f32x2(w4[t] & 0xFFFF);
                     const float2 bb = e4m3x2_to_f32x2(w4[t] >> 16);
@@ -899,14 +899,14 @@ __global__ void __launch_bounds__(320, 1)
                 }
               } else {
                 const __nv_bfloat16* gp = reinterpret_cast<const __nv_bfloat16*>(p.gate) + go;
-  #pragma unroll
+#pragma unroll
                 for (int u = 0; u < 32; ++u)
                   v[u] *= sigmoid_fast(__bfloat162float(gp[u]) * p.gate_scale);
               }
             }
           }
           uint32_t w[8];
-  #pragma unroll
+#pragma unroll
           for (int t = 0; t < 8; ++t)
             w[t] = uint32_t(f32x2_to_e4m3x2(v[4 * t] * p.ctx_inv_scale,
                                             v[4 * t + 1] * p.ctx_inv_scale)) |
