@@ -173,7 +173,7 @@ def norm_quant(x: torch.Tensor, weight: torch.Tensor, *, kind: str = "rms",
     (f32 [rows, 2]) carries each row's (mean, rstd) from pass 1 to pass 2; a full dynamic
     call without it uses a per-device scratch buffer.
     Returns ``(q_out, scale_out)``; with ``query_schedule`` launches nothing and returns
-    the schedule the call would use ("stream" or "rowgroup").
+    the schedule the call would use ("stream", "rowgroup" or "warp").
     """
     _check_cuda(x, weight, bias, residual, h_out, y_out, q_out, amax, scale_out)
     if x.dim() != 2 or x.stride(1) != 1:
@@ -231,7 +231,7 @@ def norm_quant(x: torch.Tensor, weight: torch.Tensor, *, kind: str = "rms",
         rc = _lib.lib().b2f_norm_plan(ctypes.byref(args))
         if rc < 0:
             check(-rc)
-        return "stream" if rc == 0 else "rowgroup"
+        return {0: "stream", 1: "rowgroup", 2: "warp"}[rc]
     check(_lib.lib().b2f_norm_quant(ctypes.byref(args), _stream()))
     return q_out, scale_out
 

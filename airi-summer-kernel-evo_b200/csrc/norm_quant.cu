@@ -613,6 +613,177 @@ StreamFn pick_stream(int kind, int dt0, int dt1, int wdt) {
   return norm_stream_kernel<PASS2, kDyn, kDyn, kDyn, kDyn, false>;
 }
 
+// ---------------------------------------------------------------------------------------
+// Short rows (the blocks' LayerNorms / input RMSNorms: <= 32 * 8 * kWarpMaxNV columns, bf16
+// x and weights, static scale, no residual / h / y outputs): one warp per row, persistent
+// warps striding over the rows, the next row's raw bf16 vectors loaded into registers while
+// the current row is normalised.  Gamma (and the LayerNorm bias) are staged once per CTA
+// in shared memory.  Lane l owns vectors l + 32 i, the order of the row-group kernels with
+// 32 threads per row.
+constexpr int kWarpMaxNV = 12;
+
+template <int NV>
+__global__ void __launch_bounds__(256) norm_warp_kernel(const NormParams p) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int lane = threadIdx.x & 31;
+  const int nvec = p.cols / 8;
+  uint4* sw = reinterpret_cast<uint4*>(smem);
+  uint4* sb = sw + nvec;
+  const bool ln = p.kind == 1;
+  const bool has_b = ln && p.bias != nullptr;
+  for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
+    sw[i] = reinterpret_cast<const uint4*>(p.weight)[i];
+    if (has_b) sb[i] = reinterpret_cast<const uint4*>(p.bias)[i];
+  }
+  __syncthreads();
+  const int wpc = blockDim.x >> 5;
+  const int nw = gridDim.x * wpc;
+  int row = blockIdx.x * wpc + (threadIdx.x >> 5);
+  const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(p.x);
+  uint4 cur[NV], nxt[NV];
+  auto load_row = [&](int r, uint4 (&d)[NV]) {
+    const uint4* src = reinterpret_cast<const uint4*>(xb + (long long)r * p.x_ld);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int vi = lane + 32 * i;
+      d[i] = vi < nvec ? __ldcs(src + vi) : make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+  auto unpack = [&](const uint4& q, float (&v)[8]) {
+    const float2 a = unpack_bf16x2(q.x), b = unpack_bf16x2(q.y), c = unpack_bf16x2(q.z),
+                 d = unpack_bf16x2(q.w);
+    v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y; v[4] = c.x; v[5] = c.y; v[6] = d.x;
+    v[7] = d.y;
+    if (p.x_scale != 1.0f) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] *= p.x_scale;
+    }
+  };
+  if (row < p.rows) load_row(row, cur);
+  const float n = float(p.cols);
+  const float qinv = 1.0f / p.q_scale;
+  for (; row < p.rows; row += nw) {
+    if (row + nw < p.rows) load_row(row + nw, nxt);
+    float mean = 0.f, s2 = 0.f;
+    if (ln) {
+      float s1 = 0.f;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        float v[8];
+        unpack(cur[i], v);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s1 += v[j];
+      }
+      mean = warp_sum(s1) / n;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        if (lane + 32 * i < nvec) {
+          float v[8];
+          unpack(cur[i], v);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float d = v[j] - mean;
+            s2 += d * d;
+          }
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        float v[8];
+        unpack(cur[i], v);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s2 += v[j] * v[j];
+      }
+    }
+    const float inv = rsqrtf(warp_sum(s2) / n + p.eps);
+    uint8_t* qrow = p.q_out + (long long)row * p.q_ld;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int vi = lane + 32 * i;
+      if (vi < nvec) {
+        float h[8], w[8], y[8];
+        unpack(cur[i], h);
+        {
+          const uint4 wq = sw[vi];
+          const float2 a = unpack_bf16x2(wq.x), b = unpack_bf16x2(wq.y),
+                       c = unpack_bf16x2(wq.z), d = unpack_bf16x2(wq.w);
+          w[0] = a.x; w[1] = a.y; w[2] = b.x; w[3] = b.y; w[4] = c.x; w[5] = c.y; w[6] = d.x;
+          w[7] = d.y;
+        }
+        if (ln) {
+          float bb[8];
+          if (has_b) {
+            const uint4 bq = sb[vi];
+            const float2 a = unpack_bf16x2(bq.x), b = unpack_bf16x2(bq.y),
+                         c = unpack_bf16x2(bq.z), d = unpack_bf16x2(bq.w);
+            bb[0] = a.x; bb[1] = a.y; bb[2] = b.x; bb[3] = b.y; bb[4] = c.x; bb[5] = c.y;
+            bb[6] = d.x; bb[7] = d.y;
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) bb[j] = 0.f;
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) y[j] = (h[j] - mean) * inv * w[j] + bb[j];
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) y[j] = h[j] * inv * (w[j] + p.w_offset);
+        }
+        __stcs(reinterpret_cast<uint2*>(qrow + vi * 8), quant8(y, qinv));
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < NV; ++i) cur[i] = nxt[i];
+  }
+}
+
+using WarpFn = void (*)(const NormParams);
+
+WarpFn pick_warp(int nv) {
+  switch (nv) {
+    case 1: return norm_warp_kernel<1>;
+    case 2: return norm_warp_kernel<2>;
+    case 3: return norm_warp_kernel<3>;
+    case 4: return norm_warp_kernel<4>;
+    case 5: return norm_warp_kernel<5>;
+    case 6: return norm_warp_kernel<6>;
+    case 7: return norm_warp_kernel<7>;
+    case 8: return norm_warp_kernel<8>;
+    case 9: return norm_warp_kernel<9>;
+    case 10: return norm_warp_kernel<10>;
+    case 11: return norm_warp_kernel<11>;
+    default: return norm_warp_kernel<12>;
+  }
+}
+
+// The warp-per-row schedule applies to: static scale, bf16 x and weights, no residual /
+// h / y outputs, 16-byte aligned rows and 8-byte aligned q rows.
+bool plan_warp(const NormParams& p) {
+  const int nvec = p.cols / 8;
+  if (p.dynamic != B2F_SCALE_STATIC || p.residual != nullptr || p.h_out != nullptr ||
+      p.y_out != nullptr)
+    return false;
+  if (p.x_dtype != kBF16 || p.w_dtype != kBF16 || nvec > 32 * kWarpMaxNV) return false;
+  if ((reinterpret_cast<uintptr_t>(p.x) & 15) || (p.x_ld * 2) % 16) return false;
+  if ((reinterpret_cast<uintptr_t>(p.weight) & 15) ||
+      (p.bias != nullptr && (reinterpret_cast<uintptr_t>(p.bias) & 15)))
+    return false;
+  if ((reinterpret_cast<uintptr_t>(p.q_out) & 7) || p.q_ld % 8) return false;
+  return true;
+}
+
+int launch_warp(const NormParams& p, cudaStream_t s) {
+  const int nvec = p.cols / 8;
+  const WarpFn fn = pick_warp((nvec + 31) / 32);
+  const size_t smem = (size_t)2 * nvec * 16;
+  int per_sm = 0;
+  B2F_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 256, smem));
+  const int grid = std::max(1, std::min((p.rows + 7) / 8, sm_count() * std::max(per_sm, 1)));
+  fn<<<grid, 256, smem, s>>>(p);
+  B2F_CUDA_TRY(cudaGetLastError());
+  return B2F_OK;
+}
+
 // Host-side choice between the streaming schedule and the one-row-per-group kernels.
 struct StreamLaunch {
   StreamCfg cfg;
@@ -708,6 +879,7 @@ int launch_norm(const NormParams& p, cudaStream_t s) {
   const bool run2 = p.dynamic == B2F_SCALE_DYNAMIC || p.dynamic == B2F_SCALE_DYNAMIC_APPLY;
   if (run1 && p.dynamic) B2F_CUDA_TRY(cudaMemsetAsync(p.amax, 0, sizeof(float), s));
   StreamLaunch L;
+  if (p.schedule == B2F_NORM_SCHEDULE_AUTO && plan_warp(p)) return launch_warp(p, s);
   if (run1) {
     if (p.schedule == B2F_NORM_SCHEDULE_AUTO && plan_stream(p, false, L)) {
       if (int rc = launch_stream(p, L, s)) return rc;
@@ -811,6 +983,7 @@ int b2f_norm_plan(const b2f_norm_args* a) {
   NormParams p;
   if (int rc = build_params(a, p)) return -rc;
   if (p.schedule != B2F_NORM_SCHEDULE_AUTO) return B2F_NORM_SCHEDULE_ROWGROUP;
+  if (plan_warp(p)) return 2;  // warp-per-row schedule
   StreamLaunch L;
   const bool pass1 = p.dynamic != B2F_SCALE_DYNAMIC_APPLY;
   return plan_stream(p, !pass1, L) ? B2F_NORM_SCHEDULE_AUTO : B2F_NORM_SCHEDULE_ROWGROUP;

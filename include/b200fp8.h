@@ -225,8 +225,9 @@ void b2f_norm_args_init(b2f_norm_args* args);
 int b2f_norm_quant(const b2f_norm_args* args, b2f_stream_t stream);
 
 /* Which kernels b2f_norm_quant would run for these arguments (first pass it runs):
- * 0 = streaming schedule (shared-memory ring of rows), 1 = row-group kernels, or -code when
- * the arguments are invalid.  Launches nothing; needs the current device. */
+ * 0 = streaming schedule (shared-memory ring of rows), 1 = row-group kernels, 2 = one warp per
+ * row (short bf16 rows, static scale, no residual), or -code when the arguments are
+ * invalid.  Launches nothing; needs the current device. */
 int b2f_norm_plan(const b2f_norm_args* args);
 
 /* ------------------------------------------------------------------ attention
