@@ -615,27 +615,43 @@ StreamFn pick_stream(int kind, int dt0, int dt1, int wdt) {
 
 // ---------------------------------------------------------------------------------------
 // Short rows (the blocks' LayerNorms / input RMSNorms: <= 32 * 8 * kWarpMaxNV columns, bf16
-// x and weights, static scale, no residual / h / y outputs): one warp per row, persistent
+// x, bf16 or f32 weights, static scale, no residual / h / y outputs): one warp per row, persistent
 // warps striding over the rows, the next row's raw bf16 vectors loaded into registers while
 // the current row is normalised.  Gamma (and the LayerNorm bias) are staged once per CTA
 // in shared memory.  Lane l owns vectors l + 32 i, the order of the row-group kernels with
 // 32 threads per row.
 constexpr int kWarpMaxNV = 12;
 
-template <int NV>
+template <int NV, bool WF32>
 __global__ void __launch_bounds__(256) norm_warp_kernel(const NormParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
   const int lane = threadIdx.x & 31;
   const int nvec = p.cols / 8;
+  constexpr int WV = WF32 ? 2 : 1;  // 16-byte words per 8 weights
   uint4* sw = reinterpret_cast<uint4*>(smem);
-  uint4* sb = sw + nvec;
+  uint4* sb = sw + nvec * WV;
   const bool ln = p.kind == 1;
   const bool has_b = ln && p.bias != nullptr;
-  for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
+  for (int i = threadIdx.x; i < nvec * WV; i += blockDim.x) {
     sw[i] = reinterpret_cast<const uint4*>(p.weight)[i];
     if (has_b) sb[i] = reinterpret_cast<const uint4*>(p.bias)[i];
   }
   __syncthreads();
+  // 8 weights of vector vi from shared memory as f32
+  auto wload = [&](const uint4* base, int vi, float (&o)[8]) {
+    if constexpr (WF32) {
+      const float4 a = reinterpret_cast<const float4*>(base)[2 * vi];
+      const float4 b = reinterpret_cast<const float4*>(base)[2 * vi + 1];
+      o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w; o[4] = b.x; o[5] = b.y; o[6] = b.z;
+      o[7] = b.w;
+    } else {
+      const uint4 q = base[vi];
+      const float2 a = unpack_bf16x2(q.x), b = unpack_bf16x2(q.y), c = unpack_bf16x2(q.z),
+                   d = unpack_bf16x2(q.w);
+      o[0] = a.x; o[1] = a.y; o[2] = b.x; o[3] = b.y; o[4] = c.x; o[5] = c.y; o[6] = d.x;
+      o[7] = d.y;
+    }
+  };
   const int wpc = blockDim.x >> 5;
   const int nw = gridDim.x * wpc;
   int row = blockIdx.x * wpc + (threadIdx.x >> 5);
@@ -704,21 +720,11 @@ __global__ void __launch_bounds__(256) norm_warp_kernel(const NormParams p) {
       if (vi < nvec) {
         float h[8], w[8], y[8];
         unpack(cur[i], h);
-        {
-          const uint4 wq = sw[vi];
-          const float2 a = unpack_bf16x2(wq.x), b = unpack_bf16x2(wq.y),
-                       c = unpack_bf16x2(wq.z), d = unpack_bf16x2(wq.w);
-          w[0] = a.x; w[1] = a.y; w[2] = b.x; w[3] = b.y; w[4] = c.x; w[5] = c.y; w[6] = d.x;
-          w[7] = d.y;
-        }
+        wload(sw, vi, w);
         if (ln) {
           float bb[8];
           if (has_b) {
-            const uint4 bq = sb[vi];
-            const float2 a = unpack_bf16x2(bq.x), b = unpack_bf16x2(bq.y),
-                         c = unpack_bf16x2(bq.z), d = unpack_bf16x2(bq.w);
-            bb[0] = a.x; bb[1] = a.y; bb[2] = b.x; bb[3] = b.y; bb[4] = c.x; bb[5] = c.y;
-            bb[6] = d.x; bb[7] = d.y;
+            wload(sb, vi, bb);
           } else {
 #pragma unroll
             for (int j = 0; j < 8; ++j) bb[j] = 0.f;
@@ -739,31 +745,34 @@ __global__ void __launch_bounds__(256) norm_warp_kernel(const NormParams p) {
 
 using WarpFn = void (*)(const NormParams);
 
+template <bool WF32>
 WarpFn pick_warp(int nv) {
   switch (nv) {
-    case 1: return norm_warp_kernel<1>;
-    case 2: return norm_warp_kernel<2>;
-    case 3: return norm_warp_kernel<3>;
-    case 4: return norm_warp_kernel<4>;
-    case 5: return norm_warp_kernel<5>;
-    case 6: return norm_warp_kernel<6>;
-    case 7: return norm_warp_kernel<7>;
-    case 8: return norm_warp_kernel<8>;
-    case 9: return norm_warp_kernel<9>;
-    case 10: return norm_warp_kernel<10>;
-    case 11: return norm_warp_kernel<11>;
-    default: return norm_warp_kernel<12>;
+    case 1: return norm_warp_kernel<1, WF32>;
+    case 2: return norm_warp_kernel<2, WF32>;
+    case 3: return norm_warp_kernel<3, WF32>;
+    case 4: return norm_warp_kernel<4, WF32>;
+    case 5: return norm_warp_kernel<5, WF32>;
+    case 6: return norm_warp_kernel<6, WF32>;
+    case 7: return norm_warp_kernel<7, WF32>;
+    case 8: return norm_warp_kernel<8, WF32>;
+    case 9: return norm_warp_kernel<9, WF32>;
+    case 10: return norm_warp_kernel<10, WF32>;
+    case 11: return norm_warp_kernel<11, WF32>;
+    default: return norm_warp_kernel<12, WF32>;
   }
 }
 
-// The warp-per-row schedule applies to: static scale, bf16 x and weights, no residual /
-// h / y outputs, 16-byte aligned rows and 8-byte aligned q rows.
+// The warp-per-row schedule applies to: static scale, bf16 x, bf16 or f32 weights, no
+// residual / h / y outputs, 16-byte aligned rows and 8-byte aligned q rows.
 bool plan_warp(const NormParams& p) {
   const int nvec = p.cols / 8;
   if (p.dynamic != B2F_SCALE_STATIC || p.residual != nullptr || p.h_out != nullptr ||
       p.y_out != nullptr)
     return false;
-  if (p.x_dtype != kBF16 || p.w_dtype != kBF16 || nvec > 32 * kWarpMaxNV) return false;
+  if (p.x_dtype != kBF16 || (p.w_dtype != kBF16 && p.w_dtype != kF32) ||
+      nvec > 32 * kWarpMaxNV)
+    return false;
   if ((reinterpret_cast<uintptr_t>(p.x) & 15) || (p.x_ld * 2) % 16) return false;
   if ((reinterpret_cast<uintptr_t>(p.weight) & 15) ||
       (p.bias != nullptr && (reinterpret_cast<uintptr_t>(p.bias) & 15)))
@@ -774,8 +783,9 @@ bool plan_warp(const NormParams& p) {
 
 int launch_warp(const NormParams& p, cudaStream_t s) {
   const int nvec = p.cols / 8;
-  const WarpFn fn = pick_warp((nvec + 31) / 32);
-  const size_t smem = (size_t)2 * nvec * 16;
+  const bool wf32 = p.w_dtype == kF32;
+  const WarpFn fn = wf32 ? pick_warp<true>((nvec + 31) / 32) : pick_warp<false>((nvec + 31) / 32);
+  const size_t smem = (size_t)2 * nvec * 16 * (wf32 ? 2 : 1);
   int per_sm = 0;
   B2F_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 256, smem));
   const int grid = std::max(1, std::min((p.rows + 7) / 8, sm_count() * std::max(per_sm, 1)));

@@ -149,6 +149,7 @@ def test_stream_and_rowgroup_schedules_agree(rows, cols, x_dtype, res_dtype, kin
     _assert_q(qa.view(torch.float8_e4m3fn), qb.view(torch.float8_e4m3fn).cpu())
 
 
+@pytest.mark.parametrize("wdt", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("rows,cols,kind,bias,x_scale", [
     (8192, 768, "layer", True, 1.0),    # GPT-2 LayerNorm: same lane order as row groups
     (333, 768, "layer", False, 0.5),
@@ -157,7 +158,7 @@ def test_stream_and_rowgroup_schedules_agree(rows, cols, x_dtype, res_dtype, kin
     (7, 3072, "rms", False, 2.0),       # widest row of the warp schedule
     (3, 8, "layer", True, 1.0),
 ])
-def test_warp_schedule_matches_rowgroup(rows, cols, kind, bias, x_scale):
+def test_warp_schedule_matches_rowgroup(rows, cols, kind, bias, x_scale, wdt):
     """Short bf16 rows with a static scale and no residual run one warp per row.  Same
     formulas as the row-group kernels; with 32 threads per row (cols <= 1024) the f32
     summation order is the same too, so the bytes are identical; wider rows are within one
@@ -165,8 +166,8 @@ def test_warp_schedule_matches_rowgroup(rows, cols, kind, bias, x_scale):
     ops = _ops()
     g = torch.Generator().manual_seed(rows + cols)
     x = randn((rows, cols), g).to(torch.bfloat16).cuda()
-    w = (1 + randn((cols,), g, 0.02)).to(torch.bfloat16).cuda()
-    b = randn((cols,), g, 0.02).to(torch.bfloat16).cuda() if bias else None
+    w = (1 + randn((cols,), g, 0.02)).to(wdt).cuda()
+    b = randn((cols,), g, 0.02).to(wdt).cuda() if bias else None
     off = 1.0 if kind == "rms" else 0.0
     kw = dict(kind=kind, bias=b, weight_offset=off, eps=1e-5, x_scale=x_scale, q_scale=1 / 64.0)
     assert ops.norm_quant(x, w, query_schedule=True, **kw) == "warp"
