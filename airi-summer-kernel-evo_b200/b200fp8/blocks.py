@@ -40,6 +40,12 @@ def _dev(t: Optional[torch.Tensor], device, dtype=None) -> Optional[torch.Tensor
     return t.contiguous()
 
 
+def _gemm(*args, **kwargs):
+    """The blocks' GEMMs run with one K slice: the native block entry points carry no
+    split-K workspace, and the two forms of a block stay bit-identical."""
+    return ops.gemm_fp8(*args, splits=1, **kwargs)
+
+
 def _v_dtype(head_dim: int) -> torch.dtype:
     """V operand type of the blocks: bf16 (P in bf16).  It holds e4m3 values exactly; the
     f16 form the attention kernel also accepts (head_dim 64 / 128) measured slower on B200
@@ -155,8 +161,8 @@ class GPT2Block(_Graphable):
         d = self.d
         ops.norm_quant(hidden, self.ln1_w, kind="layer", bias=self.ln1_b, eps=self.eps,
                        x_scale=hidden_scale, q_out=self.n1, q_scale=self.ns)
-        ops.gemm_fp8(self.n1, self.qkv_w, scale_a=self.ns, scale_b=self.qkv_s, bias=self.qkv_b,
-                     out=self.qkv, out_scale=self.qs)
+        _gemm(self.n1, self.qkv_w, scale_a=self.ns, scale_b=self.qkv_s, bias=self.qkv_b,
+              out=self.qkv, out_scale=self.qs)
         _v_convert(self.qkv[:, 2 * d:], self.v16)
         q, k = self.qkv[:, :d], self.qkv[:, d:2 * d]
         if self.rope:
@@ -170,14 +176,14 @@ class GPT2Block(_Graphable):
                           causal=self.causal,
                           q_scale=self.qs, k_scale=self.qs, v_scale=self.qs, ctx=self.ctx,
                           ctx_scale=self.cs)
-        ops.gemm_fp8(self.ctx, self.out_w, scale_a=self.cs, scale_b=self.out_s, bias=self.out_b,
-                     residual=hidden, residual_scale=hidden_scale, out=self.r1)
+        _gemm(self.ctx, self.out_w, scale_a=self.cs, scale_b=self.out_s, bias=self.out_b,
+              residual=hidden, residual_scale=hidden_scale, out=self.r1)
         ops.norm_quant(self.r1, self.ln2_w, kind="layer", bias=self.ln2_b, eps=self.eps,
                        q_out=self.n2, q_scale=self.ns)
-        ops.gemm_fp8(self.n2, self.fc_w, scale_a=self.ns, scale_b=self.fc_s, bias=self.fc_b,
-                     act="gelu_tanh", out=self.h, out_scale=self.ms)
-        ops.gemm_fp8(self.h, self.proj_w, scale_a=self.ms, scale_b=self.proj_s, bias=self.proj_b,
-                     residual=self.r1, out=self.out)
+        _gemm(self.n2, self.fc_w, scale_a=self.ns, scale_b=self.fc_s, bias=self.fc_b,
+              act="gelu_tanh", out=self.h, out_scale=self.ms)
+        _gemm(self.h, self.proj_w, scale_a=self.ms, scale_b=self.proj_s, bias=self.proj_b,
+              residual=self.r1, out=self.out)
         return self.out
 
     def forward_abi(self, hidden: torch.Tensor, hidden_scale: float = 1.0) -> torch.Tensor:
@@ -280,8 +286,8 @@ class QwenBlock(_Graphable):
         h, hk, dh = self.h, self.hk, self.dh
         ops.norm_quant(hidden, self.in_norm, kind="rms", weight_offset=1.0, eps=self.eps,
                        x_scale=hidden_scale, q_out=self.n1, q_scale=self.ns)
-        ops.gemm_fp8(self.n1, self.w_cat, col_scale=self.cs_cat, out=self.proj,
-                     out_scale=self.qs)
+        _gemm(self.n1, self.w_cat, col_scale=self.cs_cat, out=self.proj,
+              out_scale=self.qs)
         ops.head_norm_rope(self.proj[:, self.q_off:], heads=h, head_dim=dh, in_scale=self.qs,
                            out_scale=self.qs, head_stride=self.q_hstride, weight=self.q_norm,
                            weight_offset=1.0, eps=self.eps, cos=self.cos, sin=self.sin,
@@ -296,18 +302,18 @@ class QwenBlock(_Graphable):
                           v_scale=self.qs, gate=self.proj[:, self.g_off:], gate_scale=self.qs,
                           gate_head_stride=self.q_hstride, ctx=self.ctx, ctx_scale=self.cs)
         r1 = self.r1 if self.has_mlp else self.out
-        ops.gemm_fp8(self.ctx, self.o_w, scale_a=self.cs, scale_b=self.o_s,
-                     residual=hidden if self.add_residual else None,
-                     residual_scale=hidden_scale, out=r1)
+        _gemm(self.ctx, self.o_w, scale_a=self.cs, scale_b=self.o_s,
+              residual=hidden if self.add_residual else None,
+              residual_scale=hidden_scale, out=r1)
         if not self.has_mlp:
             return self.out
         ops.norm_quant(r1, self.post_norm, kind="rms", weight_offset=1.0, eps=self.eps,
                        q_out=self.n2, q_scale=self.ns)
-        ops.gemm_fp8(self.n2, self.gu_w, col_scale=self.gu_cs, out=self.gu, out_scale=self.mps)
+        _gemm(self.n2, self.gu_w, col_scale=self.gu_cs, out=self.gu, out_scale=self.mps)
         ops.swiglu_fp8(self.gu[:, :self.inter], self.gu[:, self.inter:], in_scale=self.mps,
                        out_scale=self.mas, out=self.act)
-        ops.gemm_fp8(self.act, self.down_w, scale_a=self.mas, scale_b=self.down_s, residual=r1,
-                     out=self.out)
+        _gemm(self.act, self.down_w, scale_a=self.mas, scale_b=self.down_s, residual=r1,
+              out=self.out)
         return self.out
 
     def forward_abi(self, hidden: torch.Tensor, hidden_scale: float = 1.0) -> torch.Tensor:

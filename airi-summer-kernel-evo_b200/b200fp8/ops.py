@@ -7,6 +7,7 @@ FP8 data; a per-tensor scale ``s`` means ``value = stored * s``.
 from __future__ import annotations
 
 import ctypes
+import functools
 from typing import Optional
 
 import torch
@@ -57,6 +58,20 @@ def _stats_scratch(rows: int, device) -> torch.Tensor:
         buf = torch.empty((max(2 * rows, 1 << 16),), dtype=torch.float32, device=dev)
         _STATS[key] = buf
     return buf
+
+
+@functools.lru_cache(maxsize=None)
+def _sm_count(index: int) -> int:
+    return torch.cuda.get_device_properties(index).multi_processor_count
+
+
+def _auto_split(m: int, n: int, k: int, device) -> bool:
+    """Shapes for which the library splits K in two when ``splits`` is None (few 128 x 128
+    tiles, long K: the rule of b2f_gemm_fp8's automatic choice); they get the cached
+    workspace."""
+    dev = torch.device(device)
+    tiles = ((m + 127) // 128) * ((n + 127) // 128)
+    return m <= 128 and k >= 32 * 128 and tiles * 2 <= _sm_count(dev.index or 0)
 
 
 def gemm_workspace(m: int, n: int, device) -> torch.Tensor:
@@ -146,7 +161,7 @@ def gemm_fp8(a: torch.Tensor, b_nk: torch.Tensor, *, scale_a: float = 1.0,
     args.mode = _lib.GEMM_ROWSUM if rowsum else _lib.GEMM_STORE
     args.tile_n = tile_n
     args.splits = 0 if splits is None else int(splits)
-    if splits is not None and splits > 1:
+    if (splits is not None and splits > 1) or (splits is None and _auto_split(m, n, k, a.device)):
         ws = workspace if workspace is not None else gemm_workspace(m, n, a.device)
         args.workspace, args.workspace_bytes = ws.data_ptr(), ws.numel() * ws.element_size()
     check(_lib.lib().b2f_gemm_fp8(ctypes.byref(args), _stream()))

@@ -259,57 +259,32 @@ __device__ __forceinline__ int out_esize(int dt) { return dt == kOutF32 ? 4 : (d
 // staging tile in the 128B-swizzle layout and leaves with TMA bulk-tensor stores (full
 // 128-byte lines, clipped at the M/N edges by the TMA unit).  `stage` points at this
 // warp's 2 x 4 KB staging area (1024-byte aligned).
+// Split-K workspace layout: each 32-row x 32-column block of a slice is 1024 contiguous
+// floats ordered [column / 4][row % 32][column % 4], so a warp (32 rows) moving one float4
+// column group touches 512 contiguous bytes.  Offset of the block holding (row0, col0),
+// row0 and col0 multiples of 32, within a slice:
+__device__ __forceinline__ long long splitk_block(const EpilogueParams& ep, int row0, int col0) {
+  return (long long)row0 * ep.ws_ld + (long long)col0 * 32;
+}
+
 // Split-K drain of this warp's 32 rows x HALF columns: the f32 partial tile of K slice
 // `sk` goes to its own workspace slice (plain 16-byte stores; no atomics, so the final sum
-// below has a fixed order and results are bitwise reproducible).
+// has a fixed order and results are bitwise reproducible).
 template <int HALF>
-__device__ __forceinline__ void splitk_store(const EpilogueParams& ep, uint32_t t_row, int row,
+__device__ __forceinline__ void splitk_store(const EpilogueParams& ep, uint32_t t_row, int row0,
                                              int col_base, int sk) {
-  float* w = ep.ws + (long long)sk * ep.ws_slice + (long long)row * ep.ws_ld + col_base;
+  const int lane = threadIdx.x & 31;
+  float* w = ep.ws + (long long)sk * ep.ws_slice;
 #pragma unroll 1
   for (int c = 0; c < HALF; c += 32) {
     uint32_t r[32];
     tmem_ld32(t_row + c, r);
+    float* blk = w + splitk_block(ep, row0, col_base + c) + lane * 4;
 #pragma unroll
     for (int j = 0; j < 32; j += 4)
-      __stcg(reinterpret_cast<float4*>(w + c + j),
+      __stcg(reinterpret_cast<float4*>(blk + j * 32),
              make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
                          __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3])));
-  }
-}
-
-// The last K slice of a tile to finish: sum the slices in order 0..splits-1 (L2 reads),
-// apply the fused epilogue and store.
-template <int HALF>
-__device__ __forceinline__ void splitk_finish(const EpilogueParams& ep, float alpha, int row,
-                                              int col_base, int M, int N, int splits,
-                                              float& rowsum, float& amax_local) {
-  const float* w = ep.ws + (long long)row * ep.ws_ld + col_base;
-#pragma unroll 1
-  for (int c = 0; c < HALF; c += 32) {
-    float sum[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) sum[j] = 0.f;
-#pragma unroll 1
-    for (int s = 0; s < splits; ++s) {
-      const float* ws = w + (long long)s * ep.ws_slice + c;
-#pragma unroll
-      for (int j = 0; j < 32; j += 4) {
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(ws + j));
-        sum[j] += v.x; sum[j + 1] += v.y; sum[j + 2] += v.z; sum[j + 3] += v.w;
-      }
-    }
-    const int col0 = col_base + c;
-    if (col0 >= N) continue;
-    uint32_t r[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(sum[j]);
-    const int cc = col0 + (threadIdx.x & 31);
-    const float lb = (ep.bias != nullptr && cc < N) ? __ldg(ep.bias + cc) : 0.f;
-    const float lc = (ep.col_scale != nullptr && cc < N) ? __ldg(ep.col_scale + cc) : 1.f;
-    float v[32];
-    epi_values(ep, alpha, row, col0, M, N, r, v, rowsum, amax_local, lb, lc);
-    if (ep.mode == kModeStore && row < M) epi_store_direct(ep, row, col0, N, v);
   }
 }
 
@@ -341,13 +316,16 @@ __device__ __forceinline__ void epi_lane_vectors(const EpilogueParams& ep, int c
 // shared-memory staging tile in the 128B-swizzle layout and leaves with TMA bulk-tensor
 // stores (full 128-byte lines, clipped at the M/N edges by the TMA unit).  `stage` points
 // at this warp's 4 KB staging area (1024-byte aligned).
-template <int BN>
+//
+// SPLIT: the last K slice of a split-K tile to finish; the accumulator chunks come from the
+// workspace, the slices summed in order 0..splits-1, instead of from tensor memory.
+template <int BN, bool SPLIT = false>
 __device__ __forceinline__ void epilogue_tile(const EpilogueParams& ep, const CUtensorMap* tmap_out,
                                               float alpha, uint32_t t_row, int row, int row0,
                                               int col_base, int M, int N, uint8_t* stage,
                                               int& buf, float& rowsum, float& amax_local,
                                               const float (&lbv)[BN / 32],
-                                              const float (&lcv)[BN / 32]) {
+                                              const float (&lcv)[BN / 32], int splits = 1) {
   const int lane = threadIdx.x & 31;
   const bool tma = ep.out_vec && ep.mode == kModeStore;
   const int esz = out_esize(ep.out_dtype);
@@ -370,8 +348,26 @@ __device__ __forceinline__ void epilogue_tile(const EpilogueParams& ep, const CU
 #pragma unroll
       for (int x = 1; x < BN / 32; ++x)
         if (uu == x) { lb = lbv[x]; lc = lcv[x]; }
-      tmem_ld32_async(t_row + uu * 32, cur);
-      tmem_ld_wait_regs(cur);
+      if constexpr (SPLIT) {
+        float sum[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) sum[j] = 0.f;
+        const float* blk = ep.ws + splitk_block(ep, row0, col0) + lane * 4;
+#pragma unroll 1
+        for (int sk = 0; sk < splits; ++sk) {
+          const float* bs = blk + (long long)sk * ep.ws_slice;
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(bs + j * 32));
+            sum[j] += v.x; sum[j + 1] += v.y; sum[j + 2] += v.z; sum[j + 3] += v.w;
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) cur[j] = __float_as_uint(sum[j]);
+      } else {
+        tmem_ld32_async(t_row + uu * 32, cur);
+        tmem_ld_wait_regs(cur);
+      }
 #ifdef B2F_TRACE
       if (uu == 0 && (threadIdx.x >> 5) == 2 && (threadIdx.x & 31) == 0) B2F_STAMP(g_epi_it, 5);
 #endif
@@ -587,7 +583,7 @@ __global__ void __launch_bounds__(320, 1)
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       float lbv[BN / 64], lcv[BN / 64];
-      if (splits == 1) {
+      {
         const int cb0 = nb * BN + chalf * (BN / 2);
         epi_prefetch_residual<BN / 2>(ep, mb * Cfg::BM + q * 32 + lane, cb0, M, N);
 #pragma unroll
@@ -615,10 +611,11 @@ __global__ void __launch_bounds__(320, 1)
         if (warp == 2 && lane == 0) B2F_STAMP(it, 4);
         if (lane == 0) mbar_arrive(&tempty_bar[acc]);
       } else {
-        splitk_store<BN / 2>(ep, t_row, row, col_base, u - t * splits);
+        splitk_store<BN / 2>(ep, t_row, row0, col_base, u - t * splits);
         tc_fence_before();
         __threadfence();  // this thread's partials are visible before the tile counter moves
         __syncwarp();
+        if (warp == 2 && lane == 0) B2F_STAMP(it, 5);
         if (lane == 0) {
           mbar_arrive(&tempty_bar[acc]);
           mbar_arrive(split_done);
@@ -644,9 +641,12 @@ __global__ void __launch_bounds__(320, 1)
         if (!__all_sync(0xffffffffu,
                         mbar_wait(split_flag_bar, sp, kDevTimeoutEpilogue, abort_flag)))
           break;
+        if (warp == 2 && lane == 0) B2F_STAMP(it, 6);
         if (*split_last) {
           __threadfence();
-          splitk_finish<BN / 2>(ep, alpha, row, col_base, M, N, splits, rowsum, amax_local);
+          epilogue_tile<BN / 2, true>(ep, &tmap_out, alpha, t_row, row, row0, col_base, M, N,
+                                      stage, buf, rowsum, amax_local, lbv, lcv, splits);
+          if (warp == 2 && lane == 0) B2F_STAMP(it, 7);
         }
       }
       if (ep.mode == kModeRowSum && row < M && (splits == 1 || *split_last))

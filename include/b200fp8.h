@@ -118,7 +118,8 @@ typedef struct b2f_gemm_args {
   int mode;
   int tile_n; /* 0 = automatic, else 128, 256 or 512 (CTA-pair 256 x 256 tiles) */
   /* Split-K (few output tiles, long K): `splits` K slices per tile, at most 8 (0 =
-   * automatic, which only splits when a workspace is given).  The workspace holds a fixed
+   * automatic: two slices when a large-enough workspace is given, the 128 x 128 tiles fill
+   * at most half of the SMs and K >= 4096; otherwise none).  The workspace holds a fixed
    * 16 KB region of per-tile arrival counters, then one f32 partial tile per slice; the
    * counters must be zero before the first use (zero-fill the buffer once) and every call
    * leaves them zero, so one workspace serves calls of any shape (at most 4096 tiles).
