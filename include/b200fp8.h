@@ -140,7 +140,7 @@ int b2f_gemm_fp8(const b2f_gemm_args* args, b2f_stream_t stream);
  * plugin into a host framework that owns every device allocation through its own
  * allocator, or a serving loop whose memory plan is fixed at start-up - and so cannot pass
  * b2f_gemm_fp8 a split-K workspace.  Same arguments and results as b2f_gemm_fp8 with
- * split-K (`workspace` / `workspace_bytes` are ignored; `splits` 0 selects 4, else 2..8;
+ * split-K (`workspace` / `workspace_bytes` are ignored; `splits` 0 selects 2, else 2..8;
  * `tile_n` 0 / 128 / 256).  The scratch is a file-scope device array of 8 MiB + 16 KiB
  * that every GPU which loads the library holds until the process exits; a call whose
  * splits * ceil(m/128)*128 * ceil(n/256)*256 * 4 bytes exceed 8 MiB is rejected with
