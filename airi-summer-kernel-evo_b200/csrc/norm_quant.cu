@@ -424,10 +424,21 @@ __global__ void __launch_bounds__(256, 3) norm_stream_kernel(const NormParams p,
     for (; issued < c.stages && issued < nrows; ++issued) issue(issued);
   const bool has_b = kind == 1 && p.bias != nullptr;
   {
-    const int n16 = p.cols * (wdt == kF32 ? 4 : 2) / 16;
-    for (int i = t; i < n16; i += blockDim.x) {
-      reinterpret_cast<uint4*>(sw)[i] = reinterpret_cast<const uint4*>(p.weight)[i];
-      if (has_b) reinterpret_cast<uint4*>(sb)[i] = reinterpret_cast<const uint4*>(p.bias)[i];
+    // Gamma (plus the RMSNorm weight offset, the same f32 addition the formula makes) and
+    // the LayerNorm bias, staged as f32: no per-element conversion or offset add later.
+    const float woff = kind == 1 ? 0.0f : p.w_offset;
+    for (int i = t; i < nvec; i += blockDim.x) {
+      float v[8];
+      load8(p.weight, wdt, (long long)i * 8, 1.0f, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] += woff;
+      reinterpret_cast<float4*>(sw)[2 * i] = make_float4(v[0], v[1], v[2], v[3]);
+      reinterpret_cast<float4*>(sw)[2 * i + 1] = make_float4(v[4], v[5], v[6], v[7]);
+      if (has_b) {
+        load8(p.bias, wdt, (long long)i * 8, 1.0f, v);
+        reinterpret_cast<float4*>(sb)[2 * i] = make_float4(v[0], v[1], v[2], v[3]);
+        reinterpret_cast<float4*>(sb)[2 * i + 1] = make_float4(v[4], v[5], v[6], v[7]);
+      }
     }
   }
   // (the first row-wait's barrier below publishes the staged gamma / bias)
@@ -544,11 +555,11 @@ __global__ void __launch_bounds__(256, 3) norm_stream_kernel(const NormParams p,
       const int vi = t + tpr * i;
       if (FULL || vi < nvec) {
         float w[8], y[8];
-        ld8<WDT>(sw, wdt, (long long)vi * 8, w);
+        ld8<kF32>(sw, kF32, (long long)vi * 8, w);
         if (kind == 1) {
           float b[8];
           if (has_b) {
-            ld8<WDT>(sb, wdt, (long long)vi * 8, b);
+            ld8<kF32>(sb, kF32, (long long)vi * 8, b);
           } else {
 #pragma unroll
             for (int j = 0; j < 8; ++j) b[j] = 0.f;
@@ -557,7 +568,7 @@ __global__ void __launch_bounds__(256, 3) norm_stream_kernel(const NormParams p,
           for (int j = 0; j < 8; ++j) y[j] = (h[i][j] - mean) * inv * w[j] + b[j];
         } else {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) y[j] = h[i][j] * inv * (w[j] + w_off);
+          for (int j = 0; j < 8; ++j) y[j] = h[i][j] * inv * w[j];  // w: gamma + offset
         }
         if (dyn1) {
           round_bf16(y);
@@ -855,7 +866,7 @@ bool plan_stream(const NormParams& p, bool pass2, StreamLaunch& L) {
       ((reinterpret_cast<uintptr_t>(c.src1) & 15) || (c.ld1 * esz(c.dt1)) % 16))
     return false;
   c.slot_bytes = c.bytes0 + c.bytes1;
-  c.wbytes = (uint32_t)((p.cols * (p.w_dtype == kF32 ? 4 : 2) + 15) / 16 * 16);
+  c.wbytes = (uint32_t)((p.cols * 4 + 15) / 16 * 16);  // f32 staging
   c.bbytes = (p.kind == 1 && p.bias != nullptr) ? c.wbytes : 0u;
   // About 32 KiB of rows in flight per CTA (at least two), several CTAs per SM.
   c.stages = (int)std::max<uint32_t>(
