@@ -43,10 +43,15 @@ def assert_ctx_close(ctx_q, ref_f32, scale, vmax):
     assert float(same.float().mean()) >= 0.95, float(same.float().mean())
 
 
+def _e4m3(x: torch.Tensor) -> torch.Tensor:
+    # torch's cast to float8_e4m3fn turns values beyond +-448 into NaN: clamp first
+    return x.clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+
+
 def _qkv(t, hq, hkv, d, g, scale=1 / 64.0):
-    q = (torch.randn((t, hq * d), generator=g) * 1.5 / scale).to(torch.float8_e4m3fn)
-    k = (torch.randn((t, hkv * d), generator=g) * 1.5 / scale).to(torch.float8_e4m3fn)
-    v = (torch.randn((t, hkv * d), generator=g) / scale).to(torch.float8_e4m3fn)
+    q = _e4m3(torch.randn((t, hq * d), generator=g) * 1.5 / scale)
+    k = _e4m3(torch.randn((t, hkv * d), generator=g) * 1.5 / scale)
+    v = _e4m3(torch.randn((t, hkv * d), generator=g) / scale)
     return q, k, v
 
 
@@ -75,6 +80,47 @@ def test_attention_matches_oracle(batch, seq, hq, hkv, d, causal, vtype):
     ctx = ops.attention_fp8(q.cuda(), k.cuda(), vd, batch=batch,
                             heads=hq, kv_heads=hkv, head_dim=d, causal=causal, q_scale=s,
                             k_scale=s, v_scale=s, ctx_scale=s)
+    torch.cuda.synchronize()
+    assert_ctx_close(ctx, ref, s, float(vf.abs().max()))
+
+
+@pytest.mark.parametrize("gdt", ["e4m3", "bf16"])
+@pytest.mark.parametrize("batch,seq,hq,hkv,d,causal", [
+    (1, 200, 4, 2, 64, True),     # paired GQA heads, ragged sequence, 64-byte gate rows
+    (2, 256, 6, 6, 64, False),    # MHA, non-causal
+    (1, 384, 8, 2, 128, True),    # Qwen-like GQA, 128-byte gate rows
+    (1, 130, 3, 3, 128, True),    # odd head count, one partial query tile
+])
+def test_attention_gate_tiles_match_oracle(batch, seq, hq, hkv, d, causal, gdt):
+    """Sigmoid output gate read from a column block of a wider projection (as the blocks
+    lay it out): e4m3 gates arrive as TMA tiles in shared memory (128- or 64-byte swizzled
+    rows), bf16 gates are read per row."""
+    g = gen(3000 + seq + hq + d)
+    s = 1 / 64.0
+    t = batch * seq
+    q, k, v = _qkv(t, hq, hkv, d, g, s)
+    gate_vals = torch.randn((t, hq * d), generator=g) * 3.0
+    if gdt == "e4m3":
+        gate_st = _e4m3(gate_vals / s)
+        gate_f = gate_st.float() * s
+        gs = s
+    else:
+        gate_st = gate_vals.to(torch.bfloat16)
+        gate_f = gate_st.float()
+        gs = 1.0
+    # the gate as columns [64, 64 + hq*d) of a wider row-major buffer
+    wide = torch.zeros((t, hq * d + 128), dtype=gate_st.dtype)
+    wide[:, 64:64 + hq * d] = gate_st
+    vf = v.float().view(t, hkv, d) * s
+    ref = oatt.attention(q.float().view(t, hq, d) * s, k.float().view(t, hkv, d) * s, vf,
+                         batch=batch, causal=causal,
+                         gate=gate_f.view(t, hq, d)).reshape(t, hq * d)
+    ops = _ops()
+    wide_d = wide.cuda()
+    ctx = ops.attention_fp8(q.cuda(), k.cuda(), ops.fp8_to_bf16(v.cuda()), batch=batch,
+                            heads=hq, kv_heads=hkv, head_dim=d, causal=causal, q_scale=s,
+                            k_scale=s, v_scale=s, gate=wide_d[:, 64:64 + hq * d],
+                            gate_scale=gs, ctx_scale=s)
     torch.cuda.synchronize()
     assert_ctx_close(ctx, ref, s, float(vf.abs().max()))
 
