@@ -1,16 +1,21 @@
 // Fused FP8 attention on 5th-generation tensor cores (C ABI: b2f_attention_fp8).
 //
-// One CTA owns 128 queries of one (sequence, query head):
+// Per query tile of 128 rows and key tile j:
 //   S_j  = Q . K_j^T            tcgen05.mma kind::f8f6f4 (e4m3 x e4m3 -> f32 in TMEM)
 //   P_j  = exp2(S_j * scale*log2e - m)  in registers, online softmax with lazy rescaling
 //          (the running max only moves when it grows by more than 2^8), P rounded to bf16
-//   O   += P_j . V_j            tcgen05.mma kind::f16 (bf16 x bf16 -> f32 in TMEM);
-//                               V is bf16 (exact image of the e4m3 values) read MN-major
+//          (f16 with f16 V) and written back to TMEM over S_j
+//   O   += P_j . V_j            tcgen05.mma kind::f16, P from TMEM, V (exact bf16 / f16
+//                               image of the e4m3 values) MN-major from shared memory
 //   ctx  = e4m3( O / l * sigmoid(gate) / ctx_scale )   fused epilogue
-// Roles (192 threads): warp 0 TMA producer (Q once, K/V ring), warp 1 MMA issuer,
-// warps 2-5 softmax + epilogue (one query row per thread).  S is double-buffered in TMEM
-// so Q.K_{j+1}^T runs while the softmax of tile j is computed.  Causal tiles above the
-// diagonal are never visited; GQA maps query head h to KV head h / (Hq / Hkv).
+// Two kernels:
+//   attention2_kernel<D, VF16> (head_dim 64 / 128): two query tiles per CTA alternating
+//     with the tensor core (320 threads: TMA producer warp, MMA warp, two softmax
+//     warpgroups); GQA head pairs share K / V; e4m3 gate tiles arrive by TMA.
+//   attention_kernel<256> (head_dim 256): one query tile per CTA (192 threads), S
+//     double-buffered in TMEM so Q.K_{j+1}^T runs while the softmax of tile j is computed.
+// Causal tiles above the diagonal are never visited; GQA maps query head h to KV head
+// h / (Hq / Hkv).
 //
 // Reference math: tasks/model_gpt2_small_transformer_block_fp8/starter.py:428-453 (GPT-2),
 // tasks/model_qwen35_4b_full_attention_block_fp8/starter.py:354-392 (Qwen, gated GQA),
@@ -405,7 +410,8 @@ __global__ void __launch_bounds__(192, 1)
 // with the tensor core: while A exponentiates S_A(j) the MMA warp runs S_B(j) and
 // P_B(j-1).V, and vice versa.  With causal masking the pair is (i, n-1-i), so every CTA
 // walks n+1 key tiles in total (balanced grid); without masking it is (2c, 2c+1).
-// TMEM: S_A | S_B | O_A | O_B.  P_A, P_B live in shared memory (bf16, 128B swizzle).
+// TMEM: S_A | S_B | O_A | O_B; P_X is written back over the first BKV/2 columns of S_X
+// (bf16 or f16 pairs) and read from there by the P.V MMA.
 #ifdef B2F_TRACE
 // Debug-only timeline of attention2: [cta][key step][slot] globaltimer stamps.
 __device__ unsigned long long g_atrace[8][16][16];
