@@ -148,19 +148,30 @@ def test_attention_gated_interleaved_qwen_reference_layout():
     assert_ctx_close(ctx, ref, s, float(vf.abs().max()))
 
 
-@pytest.mark.parametrize("d,rot", [(256, 64), (128, 128), (64, 64)])
-def test_head_norm_rope(d, rot):
-    t, h, seq = 256, 4, 128
-    g = gen(7 + d)
+@pytest.mark.parametrize("d,rot,h,wide", [
+    (256, 64, 4, False), (128, 128, 4, False), (64, 64, 4, False),
+    (128, 128, 32, True),   # Qwen q: 32 heads inside the fused projection (4-head groups)
+    (128, 128, 6, True),    # head count not a multiple of 4: per-head kernel
+    (128, 0, 16, True),     # norm only, 4-head groups
+])
+def test_head_norm_rope(d, rot, h, wide):
+    t, seq = 256, 128
+    g = gen(7 + d + h)
     s = 1 / 64.0
-    x = (torch.randn((t, h * d), generator=g) / s).to(torch.float8_e4m3fn)
+    x = _e4m3(torch.randn((t, h * d), generator=g) / s)
     w = torch.randn((d,), generator=g) * 0.02
-    cos, sin = oatt.rope_tables(seq, rot, 1e6, batch=t // seq)
+    cos, sin = oatt.rope_tables(seq, rot, 1e6, batch=t // seq) if rot else (None, None)
     ref = oatt.head_rmsnorm_rope(x.float().view(t, h, d) * s, w, cos, sin, rot)
     ref_q = (ref.reshape(t, h * d) / s).to(torch.float8_e4m3fn)
-    out = _ops().head_norm_rope(x.cuda(), heads=h, head_dim=d, in_scale=s, out_scale=s,
-                                weight=w.cuda(), cos=cos[:seq].contiguous().cuda(),
-                                sin=sin[:seq].contiguous().cuda(), rotary_dim=rot, seq=seq)
+    xd = x.cuda()
+    if wide:  # columns [256, 256 + h*d) of a wider row-major projection
+        buf = torch.zeros((t, h * d + 512), dtype=torch.uint8, device="cuda")
+        buf[:, 256:256 + h * d] = xd.view(torch.uint8)
+        xd = buf[:, 256:256 + h * d].view(torch.float8_e4m3fn)
+    tab = (lambda z: None if z is None else z[:seq].contiguous().cuda())  # noqa: E731
+    out = _ops().head_norm_rope(xd, heads=h, head_dim=d, in_scale=s, out_scale=s,
+                                weight=w.cuda(), cos=tab(cos), sin=tab(sin), rotary_dim=rot,
+                                seq=seq)
     torch.cuda.synchronize()
     diff = e4m3_ulp_diff(out.cpu(), ref_q)
     assert int(diff.max()) <= 1
