@@ -103,8 +103,8 @@ int launch_gemm(const b2f_gemm_args* a, EpilogueParams ep, cudaStream_t stream) 
   int splits = a->splits;
   if (splits == 0) {
     // Automatic choice: two K slices when the tiles fill at most half of the SMs, K is
-    // long and the caller passed a workspace (M=128, N=K=8192 on B200: 25.8 us unsplit,
-    // 24.0 us in two slices, 32.5 us in three -- each extra slice adds a partial-tile
+    // long and the caller passed a workspace (M=128, N=K=8192 on B200: 25.7 us unsplit,
+    // 23.3 us in two slices, 31.4 us in three -- each extra slice adds a partial-tile
     // store and read); otherwise none.
     const bool ws_ok = a->workspace != nullptr &&
                        a->workspace_bytes >= b2f_gemm_workspace_bytes(a->m, a->n);
@@ -436,7 +436,7 @@ extern "C" int b2f_gemm_fp8_static(const b2f_gemm_args* a, b2f_stream_t stream) 
     return fail(B2F_ERR_ARG, "gemm_fp8_static: misaligned output, bias or col_scale");
   const int num_kb = (a->k + 127) / 128;
   int splits = a->splits;
-  if (splits == 0) splits = 2;  // fastest measured (M=128, N=K=8192: 24.0 us vs 32.1 us at 4)
+  if (splits == 0) splits = 2;  // fastest measured (M=128, N=K=8192: two slices 23.3 us)
   if (splits < 2 || splits > kMaxSplits || splits > num_kb)
     return fail(B2F_ERR_ARG, "gemm_fp8_static: splits must be in [2, min(8, K/128)]");
   const int tn = a->tile_n == 0 ? 256 : a->tile_n;

@@ -288,6 +288,36 @@ __device__ __forceinline__ void splitk_store(const EpilogueParams& ep, uint32_t 
   }
 }
 
+// Two-slice split-K, second slice: adds the other slice's partial tile (workspace slice
+// `sk`) into this warp's 32 rows x HALF columns of the tensor-memory accumulator, which then
+// drains through the normal epilogue (two addends: the same bits in either order).
+template <int HALF>
+__device__ __forceinline__ void splitk_accumulate(const EpilogueParams& ep, uint32_t t_row,
+                                                  int row0, int col_base, int sk) {
+  const int lane = threadIdx.x & 31;
+  const float* w = ep.ws + (long long)sk * ep.ws_slice;
+#pragma unroll 1
+  for (int c = 0; c < HALF; c += 32) {
+    uint32_t r[32];
+    tmem_ld32_async(t_row + c, r);
+    const float* blk = w + splitk_block(ep, row0, col_base + c) + lane * 4;
+    float4 pv[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) pv[j] = __ldcg(reinterpret_cast<const float4*>(blk + j * 128));
+    tmem_ld_wait_regs(r);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      r[4 * j] = __float_as_uint(__uint_as_float(r[4 * j]) + pv[j].x);
+      r[4 * j + 1] = __float_as_uint(__uint_as_float(r[4 * j + 1]) + pv[j].y);
+      r[4 * j + 2] = __float_as_uint(__uint_as_float(r[4 * j + 2]) + pv[j].z);
+      r[4 * j + 3] = __float_as_uint(__uint_as_float(r[4 * j + 3]) + pv[j].w);
+    }
+    tmem_st16p(t_row + c, r);
+    tmem_st16p(t_row + c + 16, r + 16);
+  }
+  tmem_st_wait();
+}
+
 // Pulls this lane's residual row segment [col_base, col_base + HALF) into L2 while the
 // accumulator is still being computed, so the epilogue's residual loads hit L2.
 template <int HALF>
@@ -317,15 +347,15 @@ __device__ __forceinline__ void epi_lane_vectors(const EpilogueParams& ep, int c
 // stores (full 128-byte lines, clipped at the M/N edges by the TMA unit).  `stage` points
 // at this warp's 4 KB staging area (1024-byte aligned).
 //
-// SPLIT: the last K slice of a split-K tile to finish; the accumulator chunks come from the
-// workspace, the slices summed in order 0..splits-1, instead of from tensor memory.
-template <int BN, bool SPLIT = false>
+// SRC selects where the accumulator chunks come from: 0 = tensor memory; 1 = the workspace,
+// K slices 0..slice_arg-1 summed in order (the last slice of a split-K tile).
+template <int BN, int SRC = 0>
 __device__ __forceinline__ void epilogue_tile(const EpilogueParams& ep, const CUtensorMap* tmap_out,
                                               float alpha, uint32_t t_row, int row, int row0,
                                               int col_base, int M, int N, uint8_t* stage,
                                               int& buf, float& rowsum, float& amax_local,
                                               const float (&lbv)[BN / 32],
-                                              const float (&lcv)[BN / 32], int splits = 1) {
+                                              const float (&lcv)[BN / 32], int slice_arg = 0) {
   const int lane = threadIdx.x & 31;
   const bool tma = ep.out_vec && ep.mode == kModeStore;
   const int esz = out_esize(ep.out_dtype);
@@ -348,13 +378,13 @@ __device__ __forceinline__ void epilogue_tile(const EpilogueParams& ep, const CU
 #pragma unroll
       for (int x = 1; x < BN / 32; ++x)
         if (uu == x) { lb = lbv[x]; lc = lcv[x]; }
-      if constexpr (SPLIT) {
+      if constexpr (SRC == 1) {
         float sum[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) sum[j] = 0.f;
         const float* blk = ep.ws + splitk_block(ep, row0, col0) + lane * 4;
 #pragma unroll 1
-        for (int sk = 0; sk < splits; ++sk) {
+        for (int sk = 0; sk < slice_arg; ++sk) {
           const float* bs = blk + (long long)sk * ep.ws_slice;
 #pragma unroll
           for (int j = 0; j < 32; j += 4) {
@@ -451,7 +481,9 @@ __global__ void __launch_bounds__(320, 1)
   const int num_units = num_tiles * splits;  // unit u: tile u / splits, K slice u % splits
   uint64_t* split_done = drain_bar + 8;       // 8 epilogue warps finished their partials
   uint64_t* split_flag_bar = split_done + 1;  // "is this the tile's last slice" published
+  uint64_t* split_ready = split_flag_bar + 1; // two slices: the other slice's partial is in
   volatile int* split_last = abort_flag + 1;
+  volatile int* split_ok = abort_flag + 2;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -464,6 +496,7 @@ __global__ void __launch_bounds__(320, 1)
     }
     mbar_init(split_done, 8);
     mbar_init(split_flag_bar, 1);
+    mbar_init(split_ready, 1);
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
     fence_mbarrier_init();
@@ -600,16 +633,83 @@ __global__ void __launch_bounds__(320, 1)
       const int col_base = nb * BN + chalf * (BN / 2);
       float rowsum = 0.0f;
       const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + acc * BN + chalf * (BN / 2);
+      bool slice_last = splits == 1;  // this CTA writes the tile's output
+      bool drain_tmem = splits == 1;  // the output leaves from this CTA's accumulator
       if (splits == 1) {
 #ifdef B2F_TRACE
         if (warp == 2 && lane == 0) g_epi_it = it;
 #endif
-        epilogue_tile<BN / 2>(ep, &tmap_out, alpha, t_row, row, row0, col_base, M, N, stage,
-                              buf, rowsum, amax_local, lbv, lcv);
-        tc_fence_before();
-        __syncwarp();
-        if (warp == 2 && lane == 0) B2F_STAMP(it, 4);
-        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      } else if (splits == 2) {
+        // Two K slices: arrival order is settled first.  The first slice stores its partial
+        // tile and then sets the ready bit; the second waits for it (the first is resident
+        // and waits on nothing, so the wait ends) and adds that partial to its own
+        // accumulator on the way through the epilogue.  counters[t]: +1 per arrival, +4
+        // once the partial is visible; the second slice resets it.
+        const uint32_t sp = it & 1;
+        const int sk = u - t * splits;
+        if (ew == 0) {
+          if (lane == 0) {
+            const unsigned old = atomicAdd(&ep.counters[t], 1u);
+            *split_last = (old & 3u) == 1u;
+            mbar_arrive(split_flag_bar);
+          }
+          __syncwarp();
+        }
+        if (!__all_sync(0xffffffffu,
+                        mbar_wait(split_flag_bar, sp, kDevTimeoutEpilogue, abort_flag)))
+          break;
+        slice_last = *split_last;
+        if (!slice_last) {
+          splitk_store<BN / 2>(ep, t_row, row0, col_base, sk);
+          tc_fence_before();
+          __threadfence();  // this thread's partials are visible before the ready bit
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(&tempty_bar[acc]);
+            mbar_arrive(split_done);
+          }
+          if (ew == 0) {
+            const bool okw = mbar_wait(split_done, sp, kDevTimeoutEpilogue, abort_flag);
+            if (lane == 0) {
+              if (okw) {
+                __threadfence();
+                atomicAdd(&ep.counters[t], 4u);
+              }
+              mbar_arrive(split_ready);
+            }
+            __syncwarp();
+          }
+        } else {
+          if (ew == 0) {
+            if (lane == 0) {
+              int okr = 0;
+              const uint64_t t0 = globaltimer();
+              while (true) {
+                if (atomicAdd(&ep.counters[t], 0u) & 4u) { okr = 1; break; }  // L2-coherent read
+                if (*abort_flag || globaltimer() - t0 > B2F_WAIT_NS) {
+                  record_error(kDevTimeoutEpilogue);
+                  *abort_flag = 1;
+                  break;
+                }
+              }
+              if (okr) {
+                __threadfence();
+                ep.counters[t] = 0u;  // both slices arrived and the first is done with it
+              }
+              *split_ok = okr;
+              mbar_arrive(split_ready);
+            }
+            __syncwarp();
+          }
+          if (!__all_sync(0xffffffffu,
+                          mbar_wait(split_ready, sp, kDevTimeoutEpilogue, abort_flag)) ||
+              !*split_ok)
+            break;
+          __threadfence();
+          splitk_accumulate<BN / 2>(ep, t_row, row0, col_base, 1 - sk);
+          if (lane == 0) mbar_arrive(split_done);  // (keeps the phase in step with `it`)
+          drain_tmem = true;
+        }
       } else {
         splitk_store<BN / 2>(ep, t_row, row0, col_base, u - t * splits);
         tc_fence_before();
@@ -642,14 +742,23 @@ __global__ void __launch_bounds__(320, 1)
                         mbar_wait(split_flag_bar, sp, kDevTimeoutEpilogue, abort_flag)))
           break;
         if (warp == 2 && lane == 0) B2F_STAMP(it, 6);
-        if (*split_last) {
+        slice_last = *split_last;
+        if (slice_last) {
           __threadfence();
-          epilogue_tile<BN / 2, true>(ep, &tmap_out, alpha, t_row, row, row0, col_base, M, N,
-                                      stage, buf, rowsum, amax_local, lbv, lcv, splits);
+          epilogue_tile<BN / 2, 1>(ep, &tmap_out, alpha, t_row, row, row0, col_base, M, N,
+                                   stage, buf, rowsum, amax_local, lbv, lcv, splits);
           if (warp == 2 && lane == 0) B2F_STAMP(it, 7);
         }
       }
-      if (ep.mode == kModeRowSum && row < M && (splits == 1 || *split_last))
+      if (drain_tmem) {
+        epilogue_tile<BN / 2>(ep, &tmap_out, alpha, t_row, row, row0, col_base, M, N, stage,
+                              buf, rowsum, amax_local, lbv, lcv);
+        tc_fence_before();
+        __syncwarp();
+        if (warp == 2 && lane == 0) B2F_STAMP(it, 4);
+        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      }
+      if (ep.mode == kModeRowSum && row < M && slice_last)
         atomicAdd(reinterpret_cast<float*>(ep.out) + row, rowsum * ep.out_inv_scale);
     }
     if (lane == 0) bulk_wait_all();  // output stores complete before the CTA exits
