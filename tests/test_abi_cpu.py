@@ -112,3 +112,14 @@ def test_ops_refuse_cpu_tensors():
     a = torch.zeros((128, 128), dtype=torch.float8_e4m3fn)
     with pytest.raises(ValueError, match="CUDA"):
         ops.gemm_fp8(a, a)
+
+
+def test_auto_split_rule(monkeypatch):
+    """The Python layer hands its cached split-K workspace to the shapes b2f_gemm_fp8's
+    automatic choice may split (few 128 x 128 tiles, K >= 4096); the rest get none."""
+    from b200fp8 import ops
+    monkeypatch.setattr(ops, "_sm_count", lambda index: 148)
+    assert ops._auto_split(128, 8192, 8192, "cuda:0")        # BASELINE configs[0]
+    assert not ops._auto_split(128, 8192, 2048, "cuda:0")    # short K
+    assert not ops._auto_split(128, 32768, 8192, "cuda:0")   # 256 tiles fill the GPU
+    assert not ops._auto_split(8192, 8192, 8192, "cuda:0")   # large M: CTA pairs
