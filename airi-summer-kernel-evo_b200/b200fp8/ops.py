@@ -71,13 +71,14 @@ def _auto_split(m: int, n: int, k: int, device) -> bool:
     workspace."""
     dev = torch.device(device)
     tiles = ((m + 127) // 128) * ((n + 127) // 128)
-    return m <= 128 and k >= 32 * 128 and tiles * 2 <= _sm_count(dev.index or 0)
+    return (k + 127) // 128 >= 32 and tiles * 2 <= _sm_count(dev.index or 0)
 
 
 def gemm_workspace(m: int, n: int, device) -> torch.Tensor:
-    """Split-K workspace for an m x n GEMM output on ``device``: zero-filled once (its tile
-    counters must start at zero; every call leaves them zero), cached per device and grown
-    on demand.  One workspace per device means split-K GEMMs on one device must not
+    """Split-K workspace for an m x n GEMM output on ``device``: zero-filled once, cached per
+    device and grown on demand.  Its tile counters carry a per-call tag, so a call that
+    timed out and left them mid-protocol does not mislead the next call.  One workspace per
+    device means split-K GEMMs on one device must not
     overlap in time (the library issues them on the caller's single stream)."""
     need = int(_lib.lib().b2f_gemm_workspace_bytes(m, n))
     dev = torch.device(device)

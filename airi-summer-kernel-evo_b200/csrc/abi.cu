@@ -22,7 +22,27 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeTiledFn g_encode = nullptr;
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+CtxGetCurrentFn g_ctx_get = nullptr;
 }  // namespace
+
+unsigned long long context_token() {
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g_ctx_get == nullptr) {
+      void* fn = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &fn, 12000, cudaEnableDefault,
+                                           &q) != cudaSuccess ||
+          fn == nullptr || q != cudaDriverEntryPointSuccess)
+        return 0;
+      g_ctx_get = reinterpret_cast<CtxGetCurrentFn>(fn);
+    }
+  }
+  CUcontext c = nullptr;
+  if (g_ctx_get(&c) != CUDA_SUCCESS) return 0;
+  return reinterpret_cast<unsigned long long>(c);
+}
 
 void set_error(const std::string& msg) { t_last_error = msg; }
 

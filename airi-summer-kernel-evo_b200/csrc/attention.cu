@@ -412,17 +412,6 @@ __global__ void __launch_bounds__(192, 1)
 // walks n+1 key tiles in total (balanced grid); without masking it is (2c, 2c+1).
 // TMEM: S_A | S_B | O_A | O_B; P_X is written back over the first BKV/2 columns of S_X
 // (bf16 or f16 pairs) and read from there by the P.V MMA.
-#ifdef B2F_TRACE
-// Debug-only timeline of attention2: [cta][key step][slot] globaltimer stamps.
-__device__ unsigned long long g_atrace[8][16][16];
-#define B2F_ASTAMP(j, slot)                                                         \
-  do {                                                                              \
-    const int _cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z); \
-    if (_cta < 8 && (j) < 16) g_atrace[_cta][(j)][(slot)] = globaltimer();           \
-  } while (0)
-#else
-#define B2F_ASTAMP(j, slot) do {} while (0)
-#endif
 
 __device__ __forceinline__ float ex2_hw(float x) {
   float y;
@@ -487,7 +476,6 @@ __global__ void __launch_bounds__(320, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) B2F_ASTAMP(15, 12);
   const int n_qt = (p.seq + BQ - 1) / BQ;
   int qt[2], hx[2];
   bool act[2];
@@ -549,7 +537,6 @@ __global__ void __launch_bounds__(320, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (threadIdx.x == 0) B2F_ASTAMP(15, 13);
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
@@ -651,7 +638,6 @@ __global__ void __launch_bounds__(320, 1)
       };
       auto issue_pv = [&](int x, int j) -> bool {
         if (!mbar_wait(&p_full[x], j & 1, kDevTimeoutMma, abort_flag)) return false;
-        if (x == 1) B2F_ASTAMP(j, 8);
         const int vs = j % VST;
         if (x == 0 || j >= nkv[0]) {  // first reader of V(j)
           if (!mbar_wait(&v_full[vs], (j / VST) & 1, kDevTimeoutMma, abort_flag)) return false;
@@ -684,13 +670,10 @@ __global__ void __launch_bounds__(320, 1)
           }
         }
         if (!(ok = issue_pv(1, j))) break;
-        B2F_ASTAMP(j, 9);
         mma_commit(&v_empty[j % VST]);  // both P.V of this key tile issued before it
         if (j + 1 < nkv[1]) {
           if (!(ok = mbar_wait(&s_free[1], j & 1, kDevTimeoutMma, abort_flag))) break;
-          B2F_ASTAMP(j, 10);
           if (!(ok = issue_s(1, j + 1))) break;
-          B2F_ASTAMP(j, 11);
         }
       }
       mma_commit(drain);
@@ -715,7 +698,6 @@ __global__ void __launch_bounds__(320, 1)
     for (int j = 0; j < nkv[x] && ok; ++j) {
       ok = __all_sync(0xffffffffu, mbar_wait(&s_full[x], j & 1, kDevTimeoutEpilogue, abort_flag));
       if (!ok) break;
-      if (lane == 0 && (warp == 2 || warp == 6)) B2F_ASTAMP(j, x * 4 + 0);
       tc_fence_after();
       const int k0 = j * BKV;
       // keys k0 + kk with kk > klim are masked (past the sequence end or, causal, past qi)
@@ -772,7 +754,6 @@ __global__ void __launch_bounds__(320, 1)
           m_used = mt;
         }
         const float mref = (m_used == -INFINITY) ? 0.0f : m_used;
-        if (lane == 0 && (warp == 2 || warp == 6)) B2F_ASTAMP(j, x * 4 + 1);
         // P = 2^(S*c - m), written back to tensor memory over the S columns (P column k/2
         // < S column k; the row is already in registers): the A operand of P.V.  P(j-1)
         // is no longer read there: S(j) was written after P(j-1).V in the tensor pipe's
@@ -817,7 +798,6 @@ __global__ void __launch_bounds__(320, 1)
         }
         lt = (ls[0] + ls[1]) + (ls[2] + ls[3]);
       }
-      if (lane == 0 && (warp == 2 || warp == 6)) B2F_ASTAMP(j, x * 4 + 2);
       tmem_st_wait();
       // O *= corr once P(j-1).V has landed (before P(j).V is released below).
       if (j > 0) {
@@ -834,12 +814,10 @@ __global__ void __launch_bounds__(320, 1)
         mbar_arrive(&s_free[x]);
         mbar_arrive(&p_full[x]);
       }
-      if (lane == 0 && (warp == 2 || warp == 6)) B2F_ASTAMP(j, x * 4 + 3);
     }
     // ---------------------------------------------------------------- epilogue
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[x], (nkv[x] - 1) & 1,
                                                   kDevTimeoutEpilogue, abort_flag));
-    if (lane == 0 && warp == 4) B2F_ASTAMP(15, 14);
     if (ok) {
       tc_fence_after();
       const long long row = (long long)b * p.seq + qi;
@@ -935,7 +913,6 @@ __global__ void __launch_bounds__(320, 1)
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
-  if (threadIdx.x == 0) B2F_ASTAMP(15, 15);
 }
 
 template <int D, bool PAIR>
@@ -1040,17 +1017,6 @@ bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 }  // namespace
 }  // namespace b2f
 
-#ifdef B2F_TRACE
-extern "C" int b2f_atrace_read(void* host, unsigned long long bytes, int reset) {
-  if (bytes > sizeof(b2f::g_atrace)) bytes = sizeof(b2f::g_atrace);
-  if (cudaMemcpyFromSymbol(host, b2f::g_atrace, bytes) != cudaSuccess) return -1;
-  if (reset) {
-    static unsigned long long zeros[8 * 16 * 16] = {};
-    cudaMemcpyToSymbol(b2f::g_atrace, zeros, sizeof(zeros));
-  }
-  return 0;
-}
-#endif
 
 extern "C" {
 

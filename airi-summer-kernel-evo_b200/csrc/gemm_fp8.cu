@@ -1,4 +1,5 @@
 // Host launcher of the tcgen05 e4m3 GEMM (C ABI: b2f_gemm_fp8).
+#include <atomic>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -41,8 +42,21 @@ int encode_out_map(const b2f_gemm_args* a, EpilogueParams& ep, int half_cols, CU
   return B2F_OK;
 }
 
+// Split-K calls tag their tile counters with a per-call epoch (24 bits, never 0), so a
+// counter left mid-protocol by a call that timed out reads as zero in the next call.
+std::atomic<unsigned> g_splitk_epoch{0};
+
+unsigned next_splitk_epoch() {
+  unsigned e;
+  do {
+    e = (g_splitk_epoch.fetch_add(1u, std::memory_order_relaxed) + 1u) & 0xFFFFFFu;
+  } while (e == 0u);
+  return e;
+}
+
 EpilogueParams make_epilogue(const b2f_gemm_args* a) {
   EpilogueParams ep;
+  ep.epoch = next_splitk_epoch();
   ep.alpha = a->alpha;
   ep.alpha_ptr = a->alpha_ptr;
   ep.col_scale = a->col_scale;
@@ -308,17 +322,6 @@ int b2f_gemm_fp8(const b2f_gemm_args* a, b2f_stream_t stream) {
 
 }  // extern "C"
 
-#ifdef B2F_TRACE
-extern "C" int b2f_trace_read(void* host, unsigned long long bytes, int reset) {
-  if (bytes > sizeof(b2f::g_trace)) bytes = sizeof(b2f::g_trace);
-  if (cudaMemcpyFromSymbol(host, b2f::g_trace, bytes) != cudaSuccess) return -1;
-  if (reset) {
-    static unsigned long long zeros[160 * 64] = {};
-    cudaMemcpyToSymbol(b2f::g_trace, zeros, sizeof(zeros));
-  }
-  return 0;
-}
-#endif
 
 // ---------------------------------------------------------------------------------------
 // Allocation-free split-K GEMM (b2f_gemm_fp8_static).
@@ -332,8 +335,9 @@ extern "C" int b2f_trace_read(void* host, unsigned long long bytes, int reset) {
 // kStaticScratchBytes (8 MiB of f32 partial tiles + 16 KiB of tile counters) lives on
 // every GPU that loads this library until the process exits.  Host code only ever sees
 // the array's host-side shadow symbol, which is not a device address: the device address
-// is looked up with cudaGetSymbolAddress once per device, with that device current, on
-// the first call made on the device (so make that first call before any stream capture).
+// is looked up with cudaGetSymbolAddress once per device and context, with that device
+// current, on the first call made on the device (so make that first call before any
+// stream capture); after a cudaDeviceReset the next call looks it up again.
 // Every call shares the one array and keeps the last call's partial tiles; the counters
 // that must start at zero are cleared (cudaMemsetAsync on the call's stream) at the start
 // of every call.  Calls that overlap on the GPU - on two streams, or from two host
@@ -345,27 +349,41 @@ constexpr long long kStaticScratchBytes = kCounterBytes + 8ll * 1024 * 1024;
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
 std::mutex g_static_mu;
-std::vector<void*> g_static_ptr;  // device address of g_static_scratch, per device
+// Per device: the device address of g_static_scratch and the context it was looked up in
+// (a context reset invalidates both the address and the kernels' shared-memory attribute).
+struct StaticSlot {
+  unsigned long long ctx = 0;
+  void* ptr = nullptr;
+  bool attr256 = false, attr128 = false;
+};
+constexpr int kMaxDevices = 64;
+StaticSlot g_static_slots[kMaxDevices];  // fixed storage: callers keep pointers into it
 
-int static_scratch_address(void** out) {
+int static_scratch_address(void** out, bool** attr_done, int bn) {
   int dev = 0;
   B2F_CUDA_TRY(cudaGetDevice(&dev));
+  const unsigned long long ctx = context_token();
   std::lock_guard<std::mutex> lk(g_static_mu);
-  if ((int)g_static_ptr.size() <= dev) g_static_ptr.resize(dev + 1, nullptr);
-  if (g_static_ptr[dev] == nullptr) {
+  if (dev < 0 || dev >= kMaxDevices) return fail(B2F_ERR_UNSUPPORTED, "gemm_fp8_static: device ordinal");
+  StaticSlot& slot = g_static_slots[dev];
+  if (slot.ptr == nullptr || slot.ctx != ctx || ctx == 0) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
     if (e != cudaSuccess || p == nullptr)
       return cuda_fail(e != cudaSuccess ? e : cudaErrorInvalidSymbol,
                        "cudaGetSymbolAddress(g_static_scratch)");
-    g_static_ptr[dev] = p;
+    slot = StaticSlot{};
+    slot.ptr = p;
+    slot.ctx = ctx;
   }
-  *out = g_static_ptr[dev];
+  *out = slot.ptr;
+  *attr_done = bn == 256 ? &slot.attr256 : &slot.attr128;
   return B2F_OK;
 }
 
 template <int BN>
-int launch_gemm_static(const b2f_gemm_args* a, int splits, void* scratch, cudaStream_t stream) {
+int launch_gemm_static(const b2f_gemm_args* a, int splits, void* scratch, bool* attr_done,
+                       cudaStream_t stream) {
   using Cfg = GemmCfg<BN>;
   CUtensorMap ta, tb;
   std::string err;
@@ -398,9 +416,12 @@ int launch_gemm_static(const b2f_gemm_args* a, int splits, void* scratch, cudaSt
   GemmShape shape{a->m, a->n, a->k, splits};
   const int units = num_tiles * splits;
   const int grid = units < sms ? units : sms;
-  B2F_CUDA_TRY(cudaFuncSetAttribute(gemm_fp8_kernel<BN>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    Cfg::SMEM_BYTES));
+  if (!*attr_done) {
+    B2F_CUDA_TRY(cudaFuncSetAttribute(gemm_fp8_kernel<BN>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      Cfg::SMEM_BYTES));
+    *attr_done = true;
+  }
   CUtensorMap to;
   if (int rc = encode_out_map(a, ep, BN / 2, &to)) return rc;
   // Tile counters must start at zero: clear them on the call's stream.
@@ -452,8 +473,9 @@ extern "C" int b2f_gemm_fp8_static(const b2f_gemm_args* a, b2f_stream_t stream) 
                     std::to_string(need - kCounterBytes) +
                     " exceeds the 8 MiB static scratch; use b2f_gemm_fp8 with a workspace");
   void* scratch = nullptr;
-  if (int rc = static_scratch_address(&scratch)) return rc;
+  bool* attr_done = nullptr;
+  if (int rc = static_scratch_address(&scratch, &attr_done, tn)) return rc;
   cudaStream_t s = (cudaStream_t)stream;
-  if (tn == 256) return launch_gemm_static<256>(a, splits, scratch, s);
-  return launch_gemm_static<128>(a, splits, scratch, s);
+  if (tn == 256) return launch_gemm_static<256>(a, splits, scratch, attr_done, s);
+  return launch_gemm_static<128>(a, splits, scratch, attr_done, s);
 }

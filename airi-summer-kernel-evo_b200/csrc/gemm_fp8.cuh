@@ -22,21 +22,6 @@
 
 namespace b2f {
 
-#ifdef B2F_TRACE
-// Debug-only timeline: per CTA, per tile (first 8), globaltimer stamps of each role.
-__device__ unsigned long long g_trace[160][8][8];
-#define B2F_STAMP(tile, slot)                                                   \
-  do {                                                                          \
-    if ((tile) < 8 && blockIdx.x < 160) g_trace[blockIdx.x][(tile)][(slot)] = globaltimer(); \
-  } while (0)
-#else
-#define B2F_STAMP(tile, slot) do {} while (0)
-#endif
-#ifdef B2F_TRACE
-static __device__ __forceinline__ int& epi_it_ref() { static __shared__ int v; return v; }
-#define g_epi_it (epi_it_ref())
-#endif
-
 enum : int { kOutF32 = 0, kOutBF16 = 1, kOutE4M3 = 2 };
 enum : int { kActNone = 0, kActRelu = 1, kActGeluTanh = 2, kActLeakyRelu = 3, kActSilu = 4 };
 enum : int { kModeStore = 0, kModeRowSum = 1 };
@@ -66,8 +51,30 @@ struct EpilogueParams {
   float* ws;               // split-K: f32 partial tiles [splits][rows_pad][ws_ld]
   long long ws_ld;
   long long ws_slice;      // elements per split slice (rows_pad * ws_ld)
-  unsigned int* counters;  // split-K: arrivals per output tile, zero between calls
+  unsigned int* counters;  // split-K: per output tile, (epoch << 8) | arrival state
+  unsigned int epoch;      // split-K: this call's 24-bit tag (a counter whose tag differs
+                           // is stale, left by an aborted call, and reads as zero)
 };
+
+// Split-K tile counter update: adds `add` to the tile's arrival state for this call and
+// returns the state before the update.  A counter whose epoch tag is not this call's
+// (a call that timed out or aborted left it mid-protocol) counts as zero, so one failed
+// call cannot mislead the next one that shares the workspace.
+__device__ __forceinline__ unsigned splitk_arrive(unsigned int* c, unsigned epoch, unsigned add) {
+  unsigned old = atomicAdd(c, 0u);  // L2-coherent read
+  while (true) {
+    const unsigned state = (old >> 8) == epoch ? (old & 0xFFu) : 0u;
+    const unsigned prev = atomicCAS(c, old, (epoch << 8) | (state + add));
+    if (prev == old) return state;
+    old = prev;
+  }
+}
+
+// Reads the tile's arrival state for this call (zero when the tag is stale).
+__device__ __forceinline__ unsigned splitk_state(unsigned int* c, unsigned epoch) {
+  const unsigned v = atomicAdd(c, 0u);
+  return (v >> 8) == epoch ? (v & 0xFFu) : 0u;
+}
 
 struct GemmShape {
   int M, N, K;
@@ -125,10 +132,7 @@ struct GemmCfg {
 // Tile order: groups of GROUP_M row-blocks sweep all column blocks, so the CTAs that run
 // concurrently share A rows and B columns in L2.
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
-#ifndef B2F_GROUP_M
-#define B2F_GROUP_M 16
-#endif
-  constexpr int GROUP_M = B2F_GROUP_M;
+  constexpr int GROUP_M = 16;
   const int per_group = GROUP_M * num_n;
   const int g = t / per_group;
   const int first_m = g * GROUP_M;
@@ -398,14 +402,8 @@ __device__ __forceinline__ void epilogue_tile(const EpilogueParams& ep, const CU
         tmem_ld32_async(t_row + uu * 32, cur);
         tmem_ld_wait_regs(cur);
       }
-#ifdef B2F_TRACE
-      if (uu == 0 && (threadIdx.x >> 5) == 2 && (threadIdx.x & 31) == 0) B2F_STAMP(g_epi_it, 5);
-#endif
       float v[32];
       epi_values(ep, alpha, row, col0, M, N, cur, v, rowsum, amax_local, lb, lc);
-#ifdef B2F_TRACE
-      if (uu == 0 && (threadIdx.x >> 5) == 2 && (threadIdx.x & 31) == 0) B2F_STAMP(g_epi_it, 6);
-#endif
       if (ep.mode == kModeRowSum) continue;
       if (!tma) {
         if (row < M) epi_store_direct(ep, row, col0, N, v);
@@ -431,9 +429,6 @@ __device__ __forceinline__ void epilogue_tile(const EpilogueParams& ep, const CU
               make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
         }
       }
-#ifdef B2F_TRACE
-      if (uu == 0 && (threadIdx.x >> 5) == 2 && (threadIdx.x & 31) == 0) B2F_STAMP(g_epi_it, 7);
-#endif
       if (sub == subs - 1 || uu == units - 1) {
         fence_async_shared();
         __syncwarp();
@@ -513,13 +508,8 @@ __global__ void __launch_bounds__(320, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------------------ producer
-#if defined(B2F_EXP) && B2F_EXP == 3
-      const uint64_t pol_a = policy_evict_normal();
-      const uint64_t pol_b = policy_evict_normal();
-#else
       const uint64_t pol_a = policy_evict_last();
       const uint64_t pol_b = policy_evict_last();
-#endif
       int stage = 0;
       uint32_t phase = 0;
       long long issued = 0;
@@ -534,7 +524,6 @@ __global__ void __launch_bounds__(320, 1)
             ok = false;
             break;
           }
-          if (kb == kb0) B2F_STAMP((u - (int)blockIdx.x) / (int)gridDim.x, 0);
           mbar_arrive_expect_tx(&full_bar[stage], Cfg::STAGE_BYTES);
           tma_load_2d(smem_a + stage * Cfg::A_BYTES, &tmap_a, &full_bar[stage], kb * Cfg::BK,
                       mb * Cfg::BM, pol_a);
@@ -568,7 +557,6 @@ __global__ void __launch_bounds__(320, 1)
         const int acc = it & 1;
         const uint32_t acc_phase = (it >> 1) & 1;
         if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1, kDevTimeoutMma, abort_flag)) break;
-        B2F_STAMP(it, 1);
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = kb0; kb < kb1; ++kb) {
@@ -589,7 +577,6 @@ __global__ void __launch_bounds__(320, 1)
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
         if (ok) mma_commit(&tfull_bar[acc]);
-        B2F_STAMP(it, 2);
       }
       // Drain: wait until every issued MMA retired before TMEM is released.
       mma_commit(drain_bar);
@@ -626,7 +613,6 @@ __global__ void __launch_bounds__(320, 1)
       if (!__all_sync(0xffffffffu,
                       mbar_wait(&tfull_bar[acc], acc_phase, kDevTimeoutEpilogue, abort_flag)))
         break;
-      if (warp == 2 && lane == 0) B2F_STAMP(it, 3);
       tc_fence_after();
       const int row0 = mb * Cfg::BM + q * 32;
       const int row = row0 + lane;
@@ -635,11 +621,7 @@ __global__ void __launch_bounds__(320, 1)
       const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + acc * BN + chalf * (BN / 2);
       bool slice_last = splits == 1;  // this CTA writes the tile's output
       bool drain_tmem = splits == 1;  // the output leaves from this CTA's accumulator
-      if (splits == 1) {
-#ifdef B2F_TRACE
-        if (warp == 2 && lane == 0) g_epi_it = it;
-#endif
-      } else if (splits == 2) {
+      if (splits == 2) {
         // Two K slices: arrival order is settled first.  The first slice stores its partial
         // tile and then sets the ready bit; the second waits for it (the first is resident
         // and waits on nothing, so the wait ends) and adds that partial to its own
@@ -649,7 +631,7 @@ __global__ void __launch_bounds__(320, 1)
         const int sk = u - t * splits;
         if (ew == 0) {
           if (lane == 0) {
-            const unsigned old = atomicAdd(&ep.counters[t], 1u);
+            const unsigned old = splitk_arrive(&ep.counters[t], ep.epoch, 1u);
             *split_last = (old & 3u) == 1u;
             mbar_arrive(split_flag_bar);
           }
@@ -673,7 +655,7 @@ __global__ void __launch_bounds__(320, 1)
             if (lane == 0) {
               if (okw) {
                 __threadfence();
-                atomicAdd(&ep.counters[t], 4u);
+                splitk_arrive(&ep.counters[t], ep.epoch, 4u);
               }
               mbar_arrive(split_ready);
             }
@@ -685,7 +667,7 @@ __global__ void __launch_bounds__(320, 1)
               int okr = 0;
               const uint64_t t0 = globaltimer();
               while (true) {
-                if (atomicAdd(&ep.counters[t], 0u) & 4u) { okr = 1; break; }  // L2-coherent read
+                if (splitk_state(&ep.counters[t], ep.epoch) & 4u) { okr = 1; break; }
                 if (*abort_flag || globaltimer() - t0 > B2F_WAIT_NS) {
                   record_error(kDevTimeoutEpilogue);
                   *abort_flag = 1;
@@ -710,12 +692,11 @@ __global__ void __launch_bounds__(320, 1)
           if (lane == 0) mbar_arrive(split_done);  // (keeps the phase in step with `it`)
           drain_tmem = true;
         }
-      } else {
+      } else if (splits > 2) {
         splitk_store<BN / 2>(ep, t_row, row0, col_base, u - t * splits);
         tc_fence_before();
         __threadfence();  // this thread's partials are visible before the tile counter moves
         __syncwarp();
-        if (warp == 2 && lane == 0) B2F_STAMP(it, 5);
         if (lane == 0) {
           mbar_arrive(&tempty_bar[acc]);
           mbar_arrive(split_done);
@@ -727,7 +708,7 @@ __global__ void __launch_bounds__(320, 1)
             int last = 0;
             if (okw) {
               __threadfence();
-              last = atomicAdd(&ep.counters[t], 1u) == (unsigned)(splits - 1);
+              last = splitk_arrive(&ep.counters[t], ep.epoch, 1u) == (unsigned)(splits - 1);
               if (last) {
                 __threadfence();
                 ep.counters[t] = 0u;  // reset for the next call (every slice has arrived)
@@ -741,13 +722,11 @@ __global__ void __launch_bounds__(320, 1)
         if (!__all_sync(0xffffffffu,
                         mbar_wait(split_flag_bar, sp, kDevTimeoutEpilogue, abort_flag)))
           break;
-        if (warp == 2 && lane == 0) B2F_STAMP(it, 6);
         slice_last = *split_last;
         if (slice_last) {
           __threadfence();
           epilogue_tile<BN / 2, 1>(ep, &tmap_out, alpha, t_row, row, row0, col_base, M, N,
                                    stage, buf, rowsum, amax_local, lbv, lcv, splits);
-          if (warp == 2 && lane == 0) B2F_STAMP(it, 7);
         }
       }
       if (drain_tmem) {
@@ -755,7 +734,6 @@ __global__ void __launch_bounds__(320, 1)
                               buf, rowsum, amax_local, lbv, lcv);
         tc_fence_before();
         __syncwarp();
-        if (warp == 2 && lane == 0) B2F_STAMP(it, 4);
         if (lane == 0) mbar_arrive(&tempty_bar[acc]);
       }
       if (ep.mode == kModeRowSum && row < M && slice_last)

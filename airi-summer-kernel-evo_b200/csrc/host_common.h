@@ -14,6 +14,10 @@ void set_error(const std::string& msg);
 int fail(int code, const std::string& msg);
 int cuda_fail(cudaError_t e, const char* what);
 int sm_count();
+// Identifies the CUDA context current on this thread (0 when unknown).  Per-device caches
+// of device addresses or function attributes compare it so that they are rebuilt after a
+// cudaDeviceReset or a primary-context reset instead of handing out stale values.
+unsigned long long context_token();
 
 // Encode a 2-D (or 3-D) tiled tensor map for an 8- or 16-bit row-major tensor.
 // dims/strides are innermost first; strides are in bytes for dims 1..rank-1.

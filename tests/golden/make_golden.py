@@ -20,7 +20,7 @@ and prints its PASS line (or raises).  The script records, per task:
     for the GEMM tasks, the full output (f16) for the decoder blocks.
 
 Run from the repository root in a container that has the reference checkout:
-    python tests/golden/make_golden.py [--reference PATH] [--tasks a,b,...]
+    python tests/golden/make_golden.py --reference PATH [--tasks a,b,...]
 It needs no GPU.  The committed fixtures let the GPU tests run without the reference.
 """
 from __future__ import annotations
@@ -265,9 +265,12 @@ def _samples(out: torch.Tensor, n=2048, seed=7):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("B2F_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("B2F_REFERENCE"),
+                    help="path of the reference checkout (or set B2F_REFERENCE)")
     ap.add_argument("--tasks", default="")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference PATH or set B2F_REFERENCE to the reference checkout")
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     wanted = set(filter(None, args.tasks.split(",")))
     path_json = os.path.join(HERE, "reference_pass.json")

@@ -123,3 +123,7 @@ def test_auto_split_rule(monkeypatch):
     assert not ops._auto_split(128, 8192, 2048, "cuda:0")    # short K
     assert not ops._auto_split(128, 32768, 8192, "cuda:0")   # 256 tiles fill the GPU
     assert not ops._auto_split(8192, 8192, 8192, "cuda:0")   # large M: CTA pairs
+    assert ops._auto_split(256, 4096, 8192, "cuda:0")         # 64 tiles, long K, M > 128
+    assert not ops._auto_split(256, 8192, 8192, "cuda:0")     # 128 tiles: more than half
+    assert ops._auto_split(128, 8192, 3969, "cuda:0")         # ceil(K / 128) = 32
+    assert not ops._auto_split(128, 8192, 3968, "cuda:0")     # ceil(K / 128) = 31

@@ -161,7 +161,8 @@ def test_gemm_split_k_matches_oracle_and_is_reproducible(m, n, k, splits):
     assert torch.equal(outs[0], outs[1])  # fixed-order slice sums: bitwise reproducible
 
 
-def test_gemm_split_k_rowsum_and_e4m3_out():
+@pytest.mark.parametrize("splits", [2, 4])
+def test_gemm_split_k_rowsum_and_e4m3_out(splits):
     from b200fp8 import ops
     m, n, k = 128, 2048, 4096
     g = gen(11)
@@ -169,14 +170,77 @@ def test_gemm_split_k_rowsum_and_e4m3_out():
     b, sb = fp8_amax((n, k), g, 0.1)
     ref = og.gemm_epilogue(a, b, sa, sb, post_mul=0.5, rowsum=True, out_scale=1.0 / 1.5)
     out = ops.gemm_fp8(a.cuda(), b.cuda(), scale_a=sa, scale_b=sb, post_mul=0.5, rowsum=True,
-                       out_scale=1.0 / 1.5, splits=4)
+                       out_scale=1.0 / 1.5, splits=splits)
     torch.cuda.synchronize()
     assert (out.cpu() - ref).abs().max().item() < 1e-3 * (1 + ref.abs().max().item())
     v0 = og.gemm_epilogue(a, b, sa, sb)
     s_out = float(v0.abs().max()) / 448.0  # keep the e4m3 output in range (torch: NaN above)
     v = v0 / s_out
     q = ops.gemm_fp8(a.cuda(), b.cuda(), scale_a=sa, scale_b=sb, out_dtype=torch.float8_e4m3fn,
-                     out_scale=s_out, splits=4)
+                     out_scale=s_out, splits=splits)
     torch.cuda.synchronize()
     d = e4m3_ulp_diff(q.cpu(), v.to(torch.float8_e4m3fn))
     assert int(d.max()) <= 1 and float((d > 0).float().mean()) < 0.01
+
+
+@pytest.mark.parametrize("splits", [2, 4])
+def test_gemm_split_k_ignores_counters_left_by_an_aborted_call(splits):
+    """A split-K call that timed out leaves its tile counters mid-protocol (e.g. 1, 5 or 6
+    in the two-slice scheme).  The counters carry a per-call tag, so the next call on the
+    same workspace still produces the oracle's result."""
+    from b200fp8 import ops
+    m, n, k = 128, 4096, 4096
+    g = gen(31 + splits)
+    a, sa = fp8_amax((m, k), g, 0.1)
+    b, sb = fp8_amax((n, k), g, 0.1)
+    bias = randn((n,), g, 0.02)
+    ref = og.gemm_epilogue(a, b, sa, sb, bias=bias, act="relu")
+    ws = torch.zeros(int(ops._lib.lib().b2f_gemm_workspace_bytes(m, n)), dtype=torch.uint8,
+                     device="cuda")
+    counters = ws[:16384].view(torch.int32)
+    stale = torch.tensor([1, 5, 6, 2, 3, 7], dtype=torch.int32)
+    counters.copy_(stale.repeat(4096 // 6 + 1)[:4096].cuda())
+    counters[::7] = torch.randint(0, 2**30, (len(range(0, 4096, 7)),), generator=g,
+                                  dtype=torch.int32).cuda()
+    for _ in range(2):
+        out = ops.gemm_fp8(a.cuda(), b.cuda(), scale_a=sa, scale_b=sb, bias=bias.cuda(),
+                           act="relu", out_dtype=torch.float32, splits=splits, workspace=ws)
+        torch.cuda.synchronize()
+        err = (out.cpu() - ref).abs().max().item()
+        assert err < 1e-4 * (1 + ref.abs().max().item()), err
+    from b200fp8 import device_status
+    assert device_status() == 0
+
+
+def test_gemm_bias_relu_bench_path_128x8192x8192():
+    """BASELINE configs[0] exactly as bench.py runs it: automatic split (two K slices with
+    the cached workspace), bf16 output, X and W from N(0,1) x 0.1 with amax scales."""
+    from b200fp8 import ops
+    m, n, k = 128, 8192, 8192
+    g = gen(20260726)
+    a, sa = fp8_amax((m, k), g, 0.1)
+    b, sb = fp8_amax((n, k), g, 0.1)
+    bias = randn((n,), g, 0.02)
+    assert ops._auto_split(m, n, k, "cuda:0")
+    ref = og.gemm_epilogue(a, b, sa, sb, bias=bias, act="relu")
+    out = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+    for _ in range(2):
+        ops.gemm_fp8(a.cuda(), b.cuda(), scale_a=sa, scale_b=sb, bias=bias.cuda(), act="relu",
+                     out=out)
+        torch.cuda.synchronize()
+        _close_bf16(out, ref, k)
+
+
+@pytest.mark.parametrize("n", [8192, 16384])
+def test_square_gemm_bf16_bench_sizes_sampled_rows(n):
+    """BASELINE configs[1] at the bench's sizes, bf16 output: every column of a spread of
+    rows (first, last, and one in each 256-row CTA-pair band position) against the f64
+    oracle."""
+    g = gen(20260726 + n)
+    a, sa = fp8_amax((n, n), g)
+    b, sb = fp8_amax((n, n), g)
+    out = _ops().gemm_fp8(a.cuda(), b.cuda(), scale_a=sa, scale_b=sb)
+    torch.cuda.synchronize()
+    rows = sorted({0, 1, 127, 128, 255, 256, 1000, n // 2 + 77, n - 129, n - 1})
+    ref = og.scaled_mm(a[rows], b, sa, sb)
+    _close_bf16(out[rows], ref, n)

@@ -15,7 +15,7 @@ import ctypes
 import pytest
 import torch
 
-from helpers import fp8_amax, gen, randn
+from helpers import e4m3_ulp_diff, fp8_amax, gen, randn
 
 pytestmark = pytest.mark.gpu
 
@@ -52,6 +52,37 @@ def test_static_scratch_split_k_matches_existing_entry_point_twice():
         torch.cuda.synchronize()
         err = (got - ref).abs().max().item()
         assert err <= 1e-4 * (1.0 + ref.abs().max().item()), (m, n, k, err)
+    assert L.device_status() == 0
+
+
+def test_static_scratch_e4m3_output_with_amax():
+    """The two-slice drain also requantises to e4m3 and reduces amax: same codes and the
+    same amax as the workspace entry point."""
+    from b200fp8 import _lib as L
+    lib = L.lib()
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    m, n, k = 128, 2048, 8192
+    g = gen(3)
+    a, sa = fp8_amax((m, k), g, 0.1)
+    b, sb = fp8_amax((n, k), g, 0.1)
+    bias = randn((n,), g, 0.02).cuda()
+    a, b = a.cuda(), b.cuda()
+    outs, amaxes = [], []
+    for entry, splits in ((lib.b2f_gemm_fp8, 1), (lib.b2f_gemm_fp8_static, 2)):
+        out = torch.zeros((m, n), dtype=torch.uint8, device="cuda")
+        amax = torch.zeros(1, device="cuda")
+        args = _args(L, a, b, bias, out, sa, sb, splits)
+        args.out_dtype, args.out_ld, args.out_scale = L.DTYPE_E4M3, n, 1.0 / 256.0
+        args.amax = amax.data_ptr()
+        L.check(entry(ctypes.byref(args), stream))
+        torch.cuda.synchronize()
+        outs.append(out.cpu())
+        amaxes.append(float(amax))
+    # the two forms add the same partial products in a different order (f32): at most one
+    # e4m3 code apart, and rarely
+    d = e4m3_ulp_diff(outs[0].view(torch.float8_e4m3fn), outs[1].view(torch.float8_e4m3fn))
+    assert int(d.max()) <= 1 and float((d > 0).float().mean()) < 0.01
+    assert abs(amaxes[0] - amaxes[1]) <= 1e-5 * amaxes[0]
     assert L.device_status() == 0
 
 
