@@ -63,6 +63,15 @@ def _v_convert(src: torch.Tensor, dst: torch.Tensor) -> None:
 _DTC = {torch.float32: 0, torch.bfloat16: 1, torch.float8_e4m3fn: 2, torch.float16: 3}
 
 
+def _mark(marks: Optional[list], name: str) -> None:
+    """Stage boundary of an eager forward: records a CUDA event on the current stream when
+    the caller collects per-stage timings (``marks`` is a list of (stage, event))."""
+    if marks is not None:
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        marks.append((name, ev))
+
+
 def _p(t: Optional[torch.Tensor]) -> Optional[int]:
     return None if t is None else t.data_ptr()
 
@@ -105,6 +114,22 @@ class _Graphable:
     def replay(self) -> torch.Tensor:
         self._graph.replay()
         return self._g_out
+
+    def stage_times(self, hidden: torch.Tensor, hidden_scale: float = 1.0,
+                    reps: int = 5) -> dict:
+        """Mean device time (ms) of each stage of the forward, from CUDA events between the
+        stages of eager forwards.  A device-side sleep is queued first so that the host has
+        issued every launch before the GPU reaches them: the intervals are device time, not
+        host launch gaps."""
+        acc = {}
+        for _ in range(reps):
+            marks = []
+            torch.cuda._sleep(4_000_000)
+            self.forward(hidden, hidden_scale, marks=marks)
+            torch.cuda.synchronize()
+            for (_, e0), (name, e1) in zip(marks, marks[1:]):
+                acc.setdefault(name, []).append(e0.elapsed_time(e1))
+        return {k: sum(v) / len(v) for k, v in acc.items()}
 
 
 class GPT2Block(_Graphable):
@@ -157,13 +182,20 @@ class GPT2Block(_Graphable):
         attn = (2 if self.causal else 4) * self.batch * self.heads * s * s * self.hd
         return float(gemm + attn)
 
-    def forward(self, hidden: torch.Tensor, hidden_scale: float = 1.0) -> torch.Tensor:
+    def forward(self, hidden: torch.Tensor, hidden_scale: float = 1.0,
+                marks: Optional[list] = None) -> torch.Tensor:
+        """One forward; with ``marks`` (a list) every stage ends with a recorded CUDA event
+        (eager per-stage timing; not for graph capture)."""
         d = self.d
+        _mark(marks, "start")
         ops.norm_quant(hidden, self.ln1_w, kind="layer", bias=self.ln1_b, eps=self.eps,
                        x_scale=hidden_scale, q_out=self.n1, q_scale=self.ns)
+        _mark(marks, "ln1")
         _gemm(self.n1, self.qkv_w, scale_a=self.ns, scale_b=self.qkv_s, bias=self.qkv_b,
               out=self.qkv, out_scale=self.qs)
+        _mark(marks, "qkv_gemm")
         _v_convert(self.qkv[:, 2 * d:], self.v16)
+        _mark(marks, "v_convert")
         q, k = self.qkv[:, :d], self.qkv[:, d:2 * d]
         if self.rope:
             for src, dst in ((q, self.q_rot), (k, self.k_rot)):
@@ -171,19 +203,25 @@ class GPT2Block(_Graphable):
                                    out_scale=self.qs, cos=self.cos, sin=self.sin,
                                    rotary_dim=self.hd, seq=self.seq, out=dst)
             q, k = self.q_rot, self.k_rot
+            _mark(marks, "rope")
         ops.attention_fp8(q, k, self.v16, batch=self.batch,
                           heads=self.heads, kv_heads=self.heads, head_dim=self.hd,
                           causal=self.causal,
                           q_scale=self.qs, k_scale=self.qs, v_scale=self.qs, ctx=self.ctx,
                           ctx_scale=self.cs)
+        _mark(marks, "attention")
         _gemm(self.ctx, self.out_w, scale_a=self.cs, scale_b=self.out_s, bias=self.out_b,
               residual=hidden, residual_scale=hidden_scale, out=self.r1)
+        _mark(marks, "out_gemm")
         ops.norm_quant(self.r1, self.ln2_w, kind="layer", bias=self.ln2_b, eps=self.eps,
                        q_out=self.n2, q_scale=self.ns)
+        _mark(marks, "ln2")
         _gemm(self.n2, self.fc_w, scale_a=self.ns, scale_b=self.fc_s, bias=self.fc_b,
               act="gelu_tanh", out=self.h, out_scale=self.ms)
+        _mark(marks, "fc_gemm")
         _gemm(self.h, self.proj_w, scale_a=self.ms, scale_b=self.proj_s, bias=self.proj_b,
               residual=self.r1, out=self.out)
+        _mark(marks, "proj_gemm")
         return self.out
 
     def forward_abi(self, hidden: torch.Tensor, hidden_scale: float = 1.0) -> torch.Tensor:
@@ -282,12 +320,18 @@ class QwenBlock(_Graphable):
         attn = 2 * self.batch * self.h * self.seq * self.seq * self.dh
         return float(gemm + attn)
 
-    def forward(self, hidden: torch.Tensor, hidden_scale: float = 1.0) -> torch.Tensor:
+    def forward(self, hidden: torch.Tensor, hidden_scale: float = 1.0,
+                marks: Optional[list] = None) -> torch.Tensor:
+        """One forward; with ``marks`` (a list) every stage ends with a recorded CUDA event
+        (eager per-stage timing; not for graph capture)."""
         h, hk, dh = self.h, self.hk, self.dh
+        _mark(marks, "start")
         ops.norm_quant(hidden, self.in_norm, kind="rms", weight_offset=1.0, eps=self.eps,
                        x_scale=hidden_scale, q_out=self.n1, q_scale=self.ns)
+        _mark(marks, "in_norm")
         _gemm(self.n1, self.w_cat, col_scale=self.cs_cat, out=self.proj,
               out_scale=self.qs)
+        _mark(marks, "qgkv_gemm")
         ops.head_norm_rope(self.proj[:, self.q_off:], heads=h, head_dim=dh, in_scale=self.qs,
                            out_scale=self.qs, head_stride=self.q_hstride, weight=self.q_norm,
                            weight_offset=1.0, eps=self.eps, cos=self.cos, sin=self.sin,
@@ -296,15 +340,19 @@ class QwenBlock(_Graphable):
                            out_scale=self.qs, weight=self.k_norm, weight_offset=1.0,
                            eps=self.eps, cos=self.cos, sin=self.sin, rotary_dim=self.rot,
                            seq=self.seq, out=self.k)
+        _mark(marks, "qk_norm_rope")
         _v_convert(self.proj[:, self.v_off:self.v_off + hk * dh], self.v16)
+        _mark(marks, "v_convert")
         ops.attention_fp8(self.q, self.k, self.v16, batch=self.batch, heads=h, kv_heads=hk,
                           head_dim=dh, causal=True, q_scale=self.qs, k_scale=self.qs,
                           v_scale=self.qs, gate=self.proj[:, self.g_off:], gate_scale=self.qs,
                           gate_head_stride=self.q_hstride, ctx=self.ctx, ctx_scale=self.cs)
+        _mark(marks, "attention")
         r1 = self.r1 if self.has_mlp else self.out
         _gemm(self.ctx, self.o_w, scale_a=self.cs, scale_b=self.o_s,
               residual=hidden if self.add_residual else None,
               residual_scale=hidden_scale, out=r1)
+        _mark(marks, "o_gemm")
         if not self.has_mlp:
             return self.out
         ops.norm_quant(r1, self.post_norm, kind="rms", weight_offset=1.0, eps=self.eps,
@@ -314,6 +362,7 @@ class QwenBlock(_Graphable):
                        out_scale=self.mas, out=self.act)
         _gemm(self.act, self.down_w, scale_a=self.mas, scale_b=self.down_s, residual=r1,
               out=self.out)
+        _mark(marks, "mlp")
         return self.out
 
     def forward_abi(self, hidden: torch.Tensor, hidden_scale: float = 1.0) -> torch.Tensor:
