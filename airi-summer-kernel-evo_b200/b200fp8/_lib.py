@@ -71,6 +71,8 @@ class GemmArgs(ctypes.Structure):
         ("splits", ctypes.c_int),
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_longlong),
+        ("gate", ctypes.c_void_p), ("gate_dtype", ctypes.c_int),
+        ("gate_ld", ctypes.c_longlong),
     ]
 
 
@@ -92,6 +94,19 @@ class NormArgs(ctypes.Structure):
         ("q_scale", ctypes.c_float), ("dynamic_scale", ctypes.c_int),
         ("amax", ctypes.c_void_p), ("scale_out", ctypes.c_void_p),
         ("schedule", ctypes.c_int), ("row_stats", ctypes.c_void_p),
+    ]
+
+
+class LnRowsArgs(ctypes.Structure):
+    """Mirror of ``b2f_lnrows_args`` (include/b200fp8.h)."""
+
+    _fields_ = [
+        ("rows", ctypes.c_int), ("cols", ctypes.c_longlong),
+        ("x", ctypes.c_void_p), ("x_dtype", ctypes.c_int), ("x_ld", ctypes.c_longlong),
+        ("x_scale", ctypes.c_float), ("weight", ctypes.c_void_p), ("bias", ctypes.c_void_p),
+        ("eps", ctypes.c_float), ("out", ctypes.c_void_p), ("out_dtype", ctypes.c_int),
+        ("out_ld", ctypes.c_longlong), ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_longlong),
     ]
 
 
@@ -200,6 +215,7 @@ EXPORTED_SYMBOLS = (
     "b2f_norm_args_init", "b2f_norm_quant", "b2f_norm_plan", "b2f_attn_args_init", "b2f_attention_fp8",
     "b2f_head_norm_rope", "b2f_fp8_to_bf16", "b2f_fp8_to_f16", "b2f_swiglu_fp8",
     "b2f_quant_args_init", "b2f_quantize_fp8",
+    "b2f_lnrows_args_init", "b2f_layer_norm_rows_workspace_bytes", "b2f_layer_norm_rows",
     "b2f_gpt2_block_args_init", "b2f_gpt2_block_workspace_bytes", "b2f_gpt2_block",
     "b2f_qwen_block_args_init", "b2f_qwen_block_workspace_bytes", "b2f_qwen_block",
     "b2f_registry_lookup", "b2f_registry_size", "b2f_registry_at",
@@ -241,6 +257,12 @@ def _declare(lib: ctypes.CDLL) -> None:
         getattr(lib, f"b2f_{nm}_block_workspace_bytes").restype = ctypes.c_longlong
         getattr(lib, f"b2f_{nm}_block").argtypes = [ctypes.POINTER(st), vp]
         getattr(lib, f"b2f_{nm}_block").restype = ctypes.c_int
+    lib.b2f_lnrows_args_init.argtypes = [ctypes.POINTER(LnRowsArgs)]
+    lib.b2f_lnrows_args_init.restype = None
+    lib.b2f_layer_norm_rows_workspace_bytes.argtypes = [ctypes.c_int, ctypes.c_longlong]
+    lib.b2f_layer_norm_rows_workspace_bytes.restype = ctypes.c_longlong
+    lib.b2f_layer_norm_rows.argtypes = [ctypes.POINTER(LnRowsArgs), vp]
+    lib.b2f_layer_norm_rows.restype = ctypes.c_int
     lib.b2f_norm_plan.argtypes = [ctypes.POINTER(NormArgs)]
     lib.b2f_norm_plan.restype = ctypes.c_int
     lib.b2f_attn_args_init.argtypes = [ctypes.POINTER(AttnArgs)]

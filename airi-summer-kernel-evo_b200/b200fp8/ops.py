@@ -107,15 +107,19 @@ def gemm_fp8(a: torch.Tensor, b_nk: torch.Tensor, *, scale_a: float = 1.0,
              out_dtype: torch.dtype = torch.bfloat16, out_scale: float = 1.0,
              amax: Optional[torch.Tensor] = None, rowsum: bool = False,
              tile_n: int = 0, splits: Optional[int] = None,
-             workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+             workspace: Optional[torch.Tensor] = None,
+             gate: Optional[torch.Tensor] = None) -> torch.Tensor:
     """out = epilogue(scale_a*scale_b * A . B_nk^T)  (see b2f_gemm_fp8).
+
+    ``gate`` (f32 or bf16 [M, N]) multiplies the value after ``post_mul``, before the
+    residual is added: the gated-residual epilogue.
 
     ``out_scale`` is the quantisation scale of an e4m3 output (stored = v / out_scale).
     With ``rowsum=True`` the output is f32 [M] holding sum over columns of v / out_scale.
     ``splits`` > 1 selects split-K with that many K slices (using ``workspace`` or the cached
     one of :func:`gemm_workspace`); None / 1 = off.
     """
-    _check_cuda(a, b_nk, bias, residual, out, amax, alpha_tensor, col_scale)
+    _check_cuda(a, b_nk, bias, residual, out, amax, alpha_tensor, col_scale, gate)
     _fp8_rows(a, "a")
     _fp8_rows(b_nk, "b_nk")
     m, k = a.shape
@@ -154,6 +158,11 @@ def gemm_fp8(a: torch.Tensor, b_nk: torch.Tensor, *, scale_a: float = 1.0,
         args.residual_dtype = _DT[residual.dtype]
         args.residual_ld = residual.stride(0)
         args.residual_scale = residual_scale
+    if gate is not None:
+        if gate.dim() != 2 or gate.stride(1) != 1 or gate.dtype not in (torch.float32,
+                                                                        torch.bfloat16):
+            raise ValueError("gate must be a row-major 2-D f32 or bf16 tensor")
+        args.gate, args.gate_dtype, args.gate_ld = gate.data_ptr(), _DT[gate.dtype], gate.stride(0)
     args.out = out.data_ptr()
     args.out_dtype = _DT[out.dtype]
     args.out_ld = out.stride(0) if out.dim() == 2 else 1
@@ -250,6 +259,45 @@ def norm_quant(x: torch.Tensor, weight: torch.Tensor, *, kind: str = "rms",
         return {0: "stream", 1: "rowgroup", 2: "warp"}[rc]
     check(_lib.lib().b2f_norm_quant(ctypes.byref(args), _stream()))
     return q_out, scale_out
+
+
+_LN_WS = {}
+
+
+def layer_norm_rows(x: torch.Tensor, *, out: Optional[torch.Tensor] = None,
+                    x_scale: float = 1.0, eps: float = 1e-5,
+                    weight: Optional[torch.Tensor] = None, bias: Optional[torch.Tensor] = None,
+                    out_dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """LayerNorm over each row of a 2-D tensor with very long rows (b2f_layer_norm_rows):
+    every row is split over many CTAs.  ``x`` e4m3 (value = stored * x_scale), bf16 or f32;
+    ``out`` f32 or bf16; optional f32 ``weight`` / ``bias`` [cols]."""
+    _check_cuda(x, out, weight, bias)
+    if x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError("x must be a row-major 2-D tensor")
+    rows, cols = x.shape
+    if out is None:
+        out = torch.empty((rows, cols), device=x.device, dtype=out_dtype)
+    if out.shape != x.shape or out.stride(1) != 1:
+        raise ValueError("out must match x's shape, row-major")
+    for t, nm in ((weight, "weight"), (bias, "bias")):
+        if t is not None and (t.dtype != torch.float32 or not t.is_contiguous() or t.numel() != cols):
+            raise TypeError(f"{nm} must be contiguous float32 [cols]")
+    L = _lib.lib()
+    need = int(L.b2f_layer_norm_rows_workspace_bytes(rows, cols))
+    key = x.device.index if x.device.index is not None else torch.cuda.current_device()
+    ws = _LN_WS.get(key)
+    if ws is None or ws.numel() < need:
+        ws = torch.empty((max(need, 4096),), dtype=torch.uint8, device=x.device)
+        _LN_WS[key] = ws
+    a = _lib.LnRowsArgs()
+    L.b2f_lnrows_args_init(ctypes.byref(a))
+    a.rows, a.cols = rows, cols
+    a.x, a.x_dtype, a.x_ld, a.x_scale = x.data_ptr(), _DT[x.dtype], x.stride(0), float(x_scale)
+    a.weight, a.bias, a.eps = _ptr(weight), _ptr(bias), float(eps)
+    a.out, a.out_dtype, a.out_ld = out.data_ptr(), _DT[out.dtype], out.stride(0)
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    check(L.b2f_layer_norm_rows(ctypes.byref(a), _stream()))
+    return out
 
 
 def attention_fp8(q: torch.Tensor, k: torch.Tensor, v_bf16: torch.Tensor, *, batch: int,

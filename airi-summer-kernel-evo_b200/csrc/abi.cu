@@ -141,6 +141,7 @@ const b2f_op g_ops[] = {
     {"gpt2_block", B2F_ABI_VERSION, (void*)&b2f_gpt2_block, "b2f_gpt2_block_args"},
     {"qwen_block", B2F_ABI_VERSION, (void*)&b2f_qwen_block, "b2f_qwen_block_args"},
     {"quantize_fp8", B2F_ABI_VERSION, (void*)&b2f_quantize_fp8, "b2f_quant_args"},
+    {"layer_norm_rows", B2F_ABI_VERSION, (void*)&b2f_layer_norm_rows, "b2f_lnrows_args"},
 };
 }
 

@@ -66,6 +66,14 @@ EpilogueParams make_epilogue(const b2f_gemm_args* a) {
   ep.act = a->act;
   ep.act_param = a->act_param;
   ep.post_mul = a->post_mul;
+  ep.gate = a->gate;
+  ep.gate_dtype = a->gate_dtype;
+  ep.gate_ld = a->gate_ld;
+  {
+    const int gsz = a->gate_dtype == B2F_DTYPE_F32 ? 4 : 2;
+    ep.gate_vec = a->gate == nullptr ||
+                  ((((uintptr_t)a->gate) % 16 == 0) && ((a->gate_ld * gsz) % 16 == 0));
+  }
   ep.residual = a->residual;
   ep.res_dtype = a->residual_dtype;
   ep.res_ld = a->residual_ld;
@@ -240,6 +248,9 @@ void b2f_gemm_args_init(b2f_gemm_args* a) {
   a->out_scale = 1.0f;
   a->mode = B2F_GEMM_STORE;
   a->tile_n = 0;
+  a->gate = nullptr;
+  a->gate_dtype = B2F_DTYPE_F32;
+  a->gate_ld = 0;
 }
 
 int b2f_gemm_pair_capacity(void) { return b2f::g_pair_capacity; }
@@ -276,6 +287,10 @@ int b2f_gemm_fp8(const b2f_gemm_args* a, b2f_stream_t stream) {
   if (((uintptr_t)a->out) % esz != 0) return fail(B2F_ERR_ARG, "gemm_fp8: misaligned out");
   if (a->residual != nullptr && a->residual_ld < a->n)
     return fail(B2F_ERR_ARG, "gemm_fp8: residual_ld < n");
+  if (a->gate != nullptr &&
+      ((a->gate_dtype != B2F_DTYPE_F32 && a->gate_dtype != B2F_DTYPE_BF16) || a->gate_ld < a->n ||
+       ((uintptr_t)a->gate) % (a->gate_dtype == B2F_DTYPE_F32 ? 4 : 2) != 0))
+    return fail(B2F_ERR_ARG, "gemm_fp8: gate must be f32 or bf16 with gate_ld >= n");
   if (a->col_scale != nullptr && ((uintptr_t)a->col_scale) % 16 != 0)
     return fail(B2F_ERR_ARG, "gemm_fp8: col_scale must be 16-byte aligned");
   if (a->bias != nullptr && ((uintptr_t)a->bias) % 16 != 0)
@@ -449,7 +464,9 @@ extern "C" int b2f_gemm_fp8_static(const b2f_gemm_args* a, b2f_stream_t stream) 
       (a->mode == B2F_GEMM_ROWSUM && a->out_dtype != B2F_DTYPE_F32))
     return fail(B2F_ERR_ARG, "gemm_fp8_static: bad dtype, activation or mode");
   if ((a->mode == B2F_GEMM_STORE && a->out_ld < a->n) || a->out_scale == 0.0f ||
-      (a->residual != nullptr && a->residual_ld < a->n))
+      (a->residual != nullptr && a->residual_ld < a->n) ||
+      (a->gate != nullptr && ((a->gate_dtype != B2F_DTYPE_F32 && a->gate_dtype != B2F_DTYPE_BF16) ||
+                              a->gate_ld < a->n)))
     return fail(B2F_ERR_ARG, "gemm_fp8_static: bad output / residual layout or scale");
   const int esz = a->out_dtype == B2F_DTYPE_F32 ? 4 : (a->out_dtype == B2F_DTYPE_BF16 ? 2 : 1);
   if (((uintptr_t)a->out) % esz != 0 || (a->bias != nullptr && !aligned16(a->bias)) ||

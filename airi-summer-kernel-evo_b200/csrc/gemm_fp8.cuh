@@ -35,7 +35,11 @@ struct EpilogueParams {
   int act;                 // activation applied after the affine step
   float act_param;         // LeakyReLU negative slope
   float post_mul;          // v *= post_mul after the activation
-  const void* residual;    // optional [M, res_ld] tensor added after post_mul
+  const void* gate;        // optional f32 / bf16 [M, gate_ld]: v *= gate after post_mul
+  int gate_dtype;
+  long long gate_ld;
+  int gate_vec;            // gate base and row pitch 16-byte aligned: vector loads
+  const void* residual;    // optional [M, res_ld] tensor added after the gate
   int res_dtype;           // kOutF32 / kOutBF16 / kOutE4M3
   long long res_ld;
   float res_scale;         // residual value = stored * res_scale
@@ -168,6 +172,38 @@ __device__ __forceinline__ void epi_values(const EpilogueParams& ep, float alpha
     default: act_affine32<kActNone>(v, ep.pre_mul, ep.pre_add, ep.act_param, ep.post_mul); break;
   }
   const bool in_n = row_ok && (col0 + 32 <= N);
+  if (ep.gate != nullptr && row_ok) {
+    const bool full = in_n && ep.gate_vec;
+    if (ep.gate_dtype == kOutF32) {
+      const float* gp = reinterpret_cast<const float*>(ep.gate) + (long long)row * ep.gate_ld + col0;
+      if (full) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          const float4 q = __ldcs(reinterpret_cast<const float4*>(gp + j));
+          v[j] *= q.x; v[j + 1] *= q.y; v[j + 2] *= q.z; v[j + 3] *= q.w;
+        }
+      } else {
+        for (int j = 0; j < 32; ++j)
+          if (col0 + j < N) v[j] *= gp[j];
+      }
+    } else {
+      const __nv_bfloat16* gp =
+          reinterpret_cast<const __nv_bfloat16*>(ep.gate) + (long long)row * ep.gate_ld + col0;
+      if (full) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          const uint4 q = __ldcs(reinterpret_cast<const uint4*>(gp + j));
+          const float2 a = unpack_bf16x2(q.x), b = unpack_bf16x2(q.y), c = unpack_bf16x2(q.z),
+                       d = unpack_bf16x2(q.w);
+          v[j] *= a.x; v[j + 1] *= a.y; v[j + 2] *= b.x; v[j + 3] *= b.y;
+          v[j + 4] *= c.x; v[j + 5] *= c.y; v[j + 6] *= d.x; v[j + 7] *= d.y;
+        }
+      } else {
+        for (int j = 0; j < 32; ++j)
+          if (col0 + j < N) v[j] *= __bfloat162float(gp[j]);
+      }
+    }
+  }
   if (ep.residual != nullptr && row_ok) {
     const bool full = in_n && ep.res_vec;
     if (ep.res_dtype == kOutBF16) {
@@ -327,13 +363,22 @@ __device__ __forceinline__ void splitk_accumulate(const EpilogueParams& ep, uint
 template <int HALF>
 __device__ __forceinline__ void epi_prefetch_residual(const EpilogueParams& ep, int row,
                                                       int col_base, int M, int N) {
-  if (ep.residual == nullptr || row >= M || col_base >= N) return;
-  const int esz = ep.res_dtype == kOutF32 ? 4 : (ep.res_dtype == kOutBF16 ? 2 : 1);
+  if (row >= M || col_base >= N) return;
   const int cols = min(HALF, N - col_base);
-  const uint8_t* p = reinterpret_cast<const uint8_t*>(ep.residual) +
-                     ((long long)row * ep.res_ld + col_base) * esz;
-  for (int off = 0; off < cols * esz; off += 32)
-    asm volatile("prefetch.global.L2 [%0];" ::"l"(p + off));
+  if (ep.residual != nullptr) {
+    const int esz = ep.res_dtype == kOutF32 ? 4 : (ep.res_dtype == kOutBF16 ? 2 : 1);
+    const uint8_t* p = reinterpret_cast<const uint8_t*>(ep.residual) +
+                       ((long long)row * ep.res_ld + col_base) * esz;
+    for (int off = 0; off < cols * esz; off += 32)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p + off));
+  }
+  if (ep.gate != nullptr) {
+    const int esz = ep.gate_dtype == kOutF32 ? 4 : 2;
+    const uint8_t* p = reinterpret_cast<const uint8_t*>(ep.gate) +
+                       ((long long)row * ep.gate_ld + col_base) * esz;
+    for (int off = 0; off < cols * esz; off += 32)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(p + off));
+  }
 }
 
 // Per-lane epilogue vectors for the 32 columns starting at col0 (one coalesced load each).

@@ -120,14 +120,23 @@ typedef struct b2f_gemm_args {
   /* Split-K (few output tiles, long K): `splits` K slices per tile, at most 8 (0 =
    * automatic: two slices when a large-enough workspace is given, the 128 x 128 tiles fill
    * at most half of the SMs and K >= 4096; otherwise none).  The workspace holds a fixed
-   * 16 KB region of per-tile arrival counters, then one f32 partial tile per slice; the
-   * counters must be zero before the first use (zero-fill the buffer once) and every call
-   * leaves them zero, so one workspace serves calls of any shape (at most 4096 tiles).
-   * Slices are summed in a fixed order, so results are bitwise reproducible.
+   * 16 KB region of per-tile arrival counters, then one f32 partial tile per slice; zero-fill
+   * the buffer once before its first use.  Each call tags the counters it uses with its own
+   * epoch and leaves them zero, and a counter with another call's tag (left by a call that
+   * timed out) reads as zero, so one workspace serves calls of any shape (at most 4096
+   * tiles).  Slices are summed in a fixed order, so results are bitwise reproducible.
    * Size: b2f_gemm_workspace_bytes(m, n). */
   int splits;
   void* workspace;
   long long workspace_bytes;
+  /* Optional elementwise gate, f32 or bf16 [m, gate_ld] (null = none): after post_mul the
+   * value is multiplied by gate[row, col], then the residual is added, i.e.
+   *   out = (A.B^T * alpha) * gate + residual
+   * Replaces the epilogue of gemm_gated_residual (cute_kernels/fused_gemm_gated_residual_fp8/
+   * submission.py:234-256, reference check :383-394). */
+  const void* gate;
+  int gate_dtype;
+  long long gate_ld;
 } b2f_gemm_args;
 
 /* Fill `args` with neutral defaults (alpha 1, pre_mul 1, post_mul 1, out_scale 1, bf16 out). */
@@ -166,8 +175,8 @@ int b2f_gemm_pair_capacity(void);
  * Replaces: residual_rmsnorm (cute_kernels/fused_residual_rmsnorm_fp8/submission.py:57-106,
  *   formula :139-145), the Qwen rms_norm step (tasks/model_qwen35_4b_full_attention_block_fp8/
  *   starter.py:167-171, used at :347-348 and :402-403), the GPT-2 LayerNorm steps
- *   (tasks/model_gpt2_small_transformer_block_fp8/starter.py:407-416, 461-470) and
- *   layer_norm (tasks/level1_40_layer_norm_fp8/starter.py).
+ *   (tasks/model_gpt2_small_transformer_block_fp8/starter.py:407-416, 461-470); long rows
+ *   such as layer_norm's (tasks/level1_40_layer_norm_fp8) go to b2f_layer_norm_rows.
  * dynamic_scale selects the scale:
  *   B2F_SCALE_STATIC        s = q_scale, one pass;
  *   B2F_SCALE_DYNAMIC       both passes below on this device;
@@ -230,6 +239,39 @@ int b2f_norm_quant(const b2f_norm_args* args, b2f_stream_t stream);
  * row (short bf16 rows, static scale, no residual), or -code when the arguments are
  * invalid.  Launches nothing; needs the current device. */
 int b2f_norm_plan(const b2f_norm_args* args);
+
+/* ------------------------------------------------------------------ long-row LayerNorm
+ * y[r, :] = (x[r, :] * x_scale - mean_r) * rsqrt(var_r + eps) [* weight + bias]
+ *   over rows of up to millions of columns: every row is cut into 65536-element chunks, one
+ *   CTA each (pass 1: chunk sums; pass 2: the row's sums combined in f64, then the chunk
+ *   normalised), so a handful of rows still streams through all SMs.
+ *   x: e4m3, bf16 or f32 [rows, x_ld]; out: f32 or bf16 [rows, out_ld]; weight / bias
+ *   optional f32 [cols]; workspace: b2f_layer_norm_rows_workspace_bytes(rows, cols) bytes,
+ *   8-byte aligned (per-chunk f64 sums; no zeroing needed).
+ * Replaces: layer_norm of tasks/level1_40_layer_norm_fp8 (evaluator starter.py:84-166,
+ *   [16 x 4,194,304] e4m3 at 1/448, eps 1e-5, f32 out; CuTe submission
+ *   cute_kernels/level1_40_layer_norm_fp8/submission.py:71-134, one CTA per row).
+ */
+typedef struct b2f_lnrows_args {
+  int rows;
+  long long cols;
+  const void* x;
+  int x_dtype;
+  long long x_ld;
+  float x_scale;
+  const float* weight;
+  const float* bias;
+  float eps;
+  void* out;
+  int out_dtype;
+  long long out_ld;
+  void* workspace;
+  long long workspace_bytes;
+} b2f_lnrows_args;
+
+void b2f_lnrows_args_init(b2f_lnrows_args* args);
+long long b2f_layer_norm_rows_workspace_bytes(int rows, long long cols);
+int b2f_layer_norm_rows(const b2f_lnrows_args* args, b2f_stream_t stream);
 
 /* ------------------------------------------------------------------ attention
  * ctx[t, h*D:(h+1)*D] = e4m3( softmax(q_h k_g^T * sm_scale [causal]) v_g * sigmoid(gate) / ctx_scale )

@@ -10,6 +10,8 @@ scale_a, scale_b, out_dtype=float32)``:
                     tasks/level2_40_*/starter.py:125  lin * 0.5 + lin
                     tasks/level2_63_*/starter.py:125  relu(lin) / 2
   - block linears   ``_cute_harness_scaled_linear`` in the block tasks' starter.py.
+  - gated residual  cute_kernels/fused_gemm_gated_residual_fp8/submission.py:383-394
+                    (_scaled_mm(a, b.t()) * gate + residual)
 e4m3 x e4m3 products are exact in f32; this oracle accumulates them in f64 and rounds
 once, so it is at least as accurate as any f32 accumulation order.
 """
@@ -44,13 +46,15 @@ def activation(v: torch.Tensor, act: Optional[str], act_param: float = 0.0) -> t
 
 def gemm_epilogue(a_fp8, b_nk_fp8, scale_a=1.0, scale_b=1.0, bias=None, pre_mul=1.0,
                   pre_add=0.0, act=None, act_param=0.0, post_mul=1.0, residual=None,
-                  residual_scale=1.0, rowsum=False, out_scale=1.0) -> torch.Tensor:
+                  residual_scale=1.0, rowsum=False, out_scale=1.0, gate=None) -> torch.Tensor:
     """f32 value of the fused epilogue before the output cast (see b2f_gemm_fp8)."""
     v = scaled_mm(a_fp8, b_nk_fp8, scale_a, scale_b)
     if bias is not None:
         v = v + bias.float()
     v = v * pre_mul + pre_add
     v = activation(v, act, act_param) * post_mul
+    if gate is not None:
+        v = v * gate.float()
     if residual is not None:
         v = v + residual.float() * residual_scale
     if rowsum:

@@ -49,3 +49,19 @@ def residual_rmsnorm_amax_quant(x, residual, gamma, eps=1e-6):
     s = amax / 448.0 if amax > 0 else 1.0
     q = (y / s).to(torch.float8_e4m3fn)
     return q, s, h.to(torch.bfloat16)
+
+
+def layer_norm_rows(x: torch.Tensor, eps: float = 1e-5, weight: Optional[torch.Tensor] = None,
+                    bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """LayerNorm over each whole row (tasks/level1_40_layer_norm_fp8/starter.py:134-144:
+    F.layer_norm over the normalized shape [64, 256, 256], i.e. one 4,194,304-element row per
+    batch item, no affine); statistics in f64.  x: values (already dequantised).  f32 out."""
+    xd = x.double()
+    mean = xd.mean(dim=-1, keepdim=True)
+    var = (xd - mean).square().mean(dim=-1, keepdim=True)
+    y = (xd - mean) * torch.rsqrt(var + eps)
+    if weight is not None:
+        y = y * weight.double()
+    if bias is not None:
+        y = y + bias.double()
+    return y.float()

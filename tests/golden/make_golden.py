@@ -205,6 +205,98 @@ def qwen_candidate(ns):
     return cand
 
 
+def layer_norm_candidate(ns):
+    from oracle import norm as onorm
+
+    def cand(inp, out):
+        x = _e(inp).float() * ns["_CUTE_HARNESS_INPUT_SCALE"]
+        out.copy_(onorm.layer_norm_rows(x, ns["_CUTE_HARNESS_EPSILON"]))
+    return cand
+
+
+def gated_candidate(ns):
+    def cand(a, b, gate, residual, out):
+        out.copy_(og.gemm_epilogue(_e(a), _e(b), ns["SCALE_A"], ns["SCALE_B"], gate=gate,
+                                   residual=residual))
+    return cand
+
+
+class _Any:
+    """Stands in for every CuTe-DSL object a submission touches at import time (types,
+    decorators, struct annotations); calling it on a function returns the function."""
+
+    def __getattr__(self, name):
+        return _Any()
+
+    def __call__(self, *a, **k):
+        if len(a) == 1 and callable(a[0]) and not k:
+            return a[0]
+        return _Any()
+
+    def __getitem__(self, key):
+        return _Any()
+
+
+class _AnyModule(types.ModuleType):
+    def __getattr__(self, name):
+        return _Any()
+
+
+def _run_submission(path, make_candidate):
+    """Executes a whole standalone CuTe submission script (kernel definitions and its own
+    main() check) on CPU: the DSL's modules are permissive stand-ins, ``cute.compile``
+    returns the oracle candidate, torch runs on CPU.  Returns (stdout, captured args)."""
+    captured = {}
+    holder = {}
+
+    def compile_fn(entry_fn, *args):
+        def run(*call_args):
+            args_u = [_unwrap(a) for a in call_args]
+            captured["args"] = args_u
+            holder["c"](*args_u)
+        return run
+
+    base = _make_modules(compile_fn)
+    mods = {}
+    for name in ("cutlass", "cutlass.cute", "cutlass.pipeline", "cutlass.utils",
+                 "cutlass.utils.blackwell_helpers", "cutlass.cute.nvgpu", "cutlass.cute.runtime"):
+        m = _AnyModule(name)
+        if name in base:
+            m.__dict__.update({k: v for k, v in base[name].__dict__.items()
+                               if not k.startswith("__")})
+        mods[name] = m
+    mods["cutlass"].cute = mods["cutlass.cute"]
+    mods["cutlass"].utils = mods["cutlass.utils"]
+    mods["cutlass"].pipeline = mods["cutlass.pipeline"]
+    mods["cutlass.cute"].nvgpu = mods["cutlass.cute.nvgpu"]
+    mods["cutlass.cute"].runtime = mods["cutlass.cute.runtime"]
+    mods["cutlass.utils"].blackwell_helpers = mods["cutlass.utils.blackwell_helpers"]
+    shim = _TorchShim()
+    real_import = builtins.__import__
+
+    def fake_import(name, globals=None, locals=None, fromlist=(), level=0):
+        if name == "torch" or name.startswith("torch."):
+            if fromlist:
+                return real_import(name, globals, locals, fromlist, level)
+            return shim
+        if name == "cutlass" or name.startswith("cutlass."):
+            if fromlist:
+                return mods[name]
+            return mods["cutlass"]
+        return real_import(name, globals, locals, fromlist, level)
+
+    text = open(path).read().rstrip()
+    assert text.endswith("main()"), "submission must end with main()"
+    ns = {"__builtins__": dict(builtins.__dict__, __import__=fake_import),
+          "__name__": "__cute_submission__"}
+    exec(compile(text[: -len("main()")], path, "exec"), ns)
+    holder["c"] = make_candidate(ns)
+    out = io.StringIO()
+    with contextlib.redirect_stdout(out):
+        ns["main"]()
+    return out.getvalue().strip(), captured
+
+
 # ---------------------------------------------------------------------------- tasks
 GEMM_TASKS = {
     # task: (seed, entry, epilogue, regeneration)
@@ -241,6 +333,13 @@ BLOCK_TASKS = {
         lambda: ti.gpt2_block(hidden=1024, mlp=4096, vision=True)),
     "model_qwen35_4b_full_attention_block_fp8": (
         20260801, "qwen35_full_attention_block", "qwen", lambda: ti.qwen_block()),
+}
+NORM_TASKS = {
+    "level1_40_layer_norm_fp8": (20260726, "layer_norm", lambda: ti.layer_norm_task()),
+}
+# standalone CuTe submissions whose own main() checks the kernel (no task evaluator)
+SUBMISSIONS = {
+    "fused_gemm_gated_residual_fp8": (gated_candidate, lambda: ti.gated_residual()),
 }
 
 
@@ -293,6 +392,22 @@ def main():
                     (7, "out_w"), (11, "down_w"), (12, "cos"), (13, "sin")]
             mk = qwen_candidate
         jobs.append((task, seed, entry, mk, regen_fn, keys, True))
+    for task, (seed, entry, regen_fn) in NORM_TASKS.items():
+        jobs.append((task, seed, entry, layer_norm_candidate, regen_fn, [(0, "x")], False))
+    for name, (mk, regen_fn) in SUBMISSIONS.items():
+        if wanted and name not in wanted:
+            continue
+        t0 = time.time()
+        path = os.path.join(args.reference, "cute_kernels", name, "submission.py")
+        line, cap = _run_submission(path, mk)
+        _check_regen(cap, regen_fn(), [(0, "a"), (1, "b"), (2, "gate"), (3, "residual")])
+        fix = _samples(cap["args"][-1])
+        torch.save(fix, os.path.join(HERE, name + ".pt"))
+        results[name] = {"seed": "SEED of the submission", "evaluator_line": line,
+                         "inputs_regenerated": True, "seconds": round(time.time() - t0, 1)}
+        print(name, "->", line, flush=True)
+        with open(path_json, "w") as f:
+            json.dump(results, f, indent=1, sort_keys=True)
     for task, seed, entry, mk, regen_fn, keys, full in jobs:
         if wanted and task not in wanted:
             continue

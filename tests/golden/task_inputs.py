@@ -134,3 +134,24 @@ def qwen_weights_from(inp, heads=16, kv_heads=4, head_dim=256, rotary=64):
     w.mlp_up_w, w.mlp_up_s = inp["up_w"], inp["up_s"]
     w.mlp_down_w, w.mlp_down_s = inp["down_w"], inp["down_s"]
     return w
+
+
+def layer_norm_task(seed=20260726, batch=16, row=64 * 256 * 256):
+    """tasks/level1_40_layer_norm_fp8/starter.py:88-109: U(0,1) * 448 -> e4m3, read at 1/448."""
+    torch.manual_seed(seed)
+    src = torch.rand((batch, row), dtype=torch.float32)
+    return {"x": (src * FP8_MAX).to(E4M3), "x_scale": 1 / FP8_MAX, "eps": 1e-5}
+
+
+def gated_residual(seed=20260731, m=2048, n=4096, k=4096):
+    """cute_kernels/fused_gemm_gated_residual_fp8/submission.py:325-350: A ~ U(-1,1),
+    B ~ U(+-K^-1/2), gate and residual ~ N(0,1) f32."""
+    torch.manual_seed(seed)
+    bound = k ** -0.5
+    a = torch.empty((m, k), dtype=torch.float32).uniform_(-1.0, 1.0)
+    b = torch.empty((n, k), dtype=torch.float32).uniform_(-bound, bound)
+    gate = torch.randn((m, n), dtype=torch.float32)
+    residual = torch.randn((m, n), dtype=torch.float32)
+    return {"a": (a * FP8_MAX).to(E4M3), "b": (b * (FP8_MAX / bound)).to(E4M3),
+            "scale_a": 1 / FP8_MAX, "scale_b": bound / FP8_MAX, "gate": gate,
+            "residual": residual}

@@ -244,3 +244,43 @@ def test_square_gemm_bf16_bench_sizes_sampled_rows(n):
     rows = sorted({0, 1, 127, 128, 255, 256, 1000, n // 2 + 77, n - 129, n - 1})
     ref = og.scaled_mm(a[rows], b, sa, sb)
     _close_bf16(out[rows], ref, n)
+
+
+@pytest.mark.parametrize("gdt", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("m,n,k", [(256, 512, 1024), (200, 776, 528), (1024, 2048, 4096)])
+def test_gemm_gate_epilogue(m, n, k, gdt):
+    """out = (A.B^T * alpha + bias) * gate + residual with C-shaped gate and residual."""
+    from b200fp8 import ops
+    g = gen(77 + m + n)
+    a, sa = fp8_amax((m, k), g)
+    b, sb = fp8_amax((n, k), g, 0.1)
+    bias = randn((n,), g, 0.02)
+    gate = randn((m, n), g).to(gdt)
+    res = randn((m, n), g)
+    ref = og.gemm_epilogue(a, b, sa, sb, bias=bias, gate=gate, residual=res)
+    out = ops.gemm_fp8(a.cuda(), b.cuda(), scale_a=sa, scale_b=sb, bias=bias.cuda(),
+                       gate=gate.cuda(), residual=res.cuda(), out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    err = (out.cpu() - ref).abs().max().item()
+    assert err < 1e-4 * (1 + ref.abs().max().item()), err
+
+
+def test_gated_residual_reference_shape_golden():
+    """cute_kernels/fused_gemm_gated_residual_fp8 at its own shape (2048 x 4096 x 4096, f32
+    gate and residual) against the golden samples, with the submission's 0.002 bar."""
+    import os
+    import sys
+    from conftest import ROOT
+    from b200fp8 import ops
+    gdir = os.path.join(ROOT, "tests", "golden")
+    if gdir not in sys.path:
+        sys.path.insert(0, gdir)
+    import task_inputs as ti
+    fix = torch.load(os.path.join(gdir, "fused_gemm_gated_residual_fp8.pt"))
+    inp = ti.gated_residual()
+    out = ops.gemm_fp8(inp["a"].cuda(), inp["b"].cuda(), scale_a=inp["scale_a"],
+                       scale_b=inp["scale_b"], gate=inp["gate"].cuda(),
+                       residual=inp["residual"].cuda(), out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    got = out.cpu().reshape(-1)[fix["index"]]
+    assert float((got - fix["value"]).abs().max()) <= 0.002

@@ -22,7 +22,8 @@ TASKS = [
     "level2_40_matmul_scaling_residual_add_fp8", "level2_63_gemm_relu_divide_fp8",
     "level2_76_gemm_add_relu_fp8", "model_gpt2_small_qkv_projection_fp8",
     "model_gpt2_small_transformer_block_fp8", "model_qwen35_4b_full_attention_block_fp8",
-    "model_qwen35_4b_vision_block_fp8",
+    "model_qwen35_4b_vision_block_fp8", "level1_40_layer_norm_fp8",
+    "fused_gemm_gated_residual_fp8",
 ]
 
 
@@ -38,7 +39,7 @@ def test_reference_evaluator_accepted_oracle(task):
     res = _results()
     assert task in res, f"{task} missing from reference_pass.json"
     line = res[task]["evaluator_line"]
-    assert line.startswith("task=") and line.endswith(" PASS"), line
+    assert line.startswith(("task=", "kernel=")) and line.endswith(" PASS"), line
     assert res[task]["inputs_regenerated"]
     assert os.path.exists(os.path.join(GOLDEN, task + ".pt"))
 
@@ -65,6 +66,33 @@ def test_qkv_projection_fixture_matches_fresh_oracle_samples():
     full = torch.full(fix["shape"], float("nan"))
     full[rows] = sub
     got = full.reshape(-1)[idx]
+    m = ~torch.isnan(got)
+    assert m.any()
+    assert torch.allclose(got[m], fix["value"][m], atol=1e-5)
+
+
+def test_layer_norm_fixture_matches_fresh_oracle_samples():
+    import task_inputs as ti
+    from oracle import norm as onorm
+    fix = torch.load(os.path.join(GOLDEN, "level1_40_layer_norm_fp8.pt"))
+    inp = ti.layer_norm_task()
+    y = onorm.layer_norm_rows(inp["x"].float() * inp["x_scale"], inp["eps"])
+    assert list(y.shape) == fix["shape"]
+    assert torch.allclose(y.reshape(-1)[fix["index"]], fix["value"], atol=1e-5)
+
+
+def test_gated_residual_fixture_matches_fresh_oracle_samples():
+    import task_inputs as ti
+    from oracle import gemm as og
+    fix = torch.load(os.path.join(GOLDEN, "fused_gemm_gated_residual_fp8.pt"))
+    inp = ti.gated_residual()
+    n = fix["shape"][1]
+    rows = torch.unique(fix["index"] // n)[:48]
+    sub = og.gemm_epilogue(inp["a"][rows], inp["b"], inp["scale_a"], inp["scale_b"],
+                           gate=inp["gate"][rows], residual=inp["residual"][rows])
+    full = torch.full(fix["shape"], float("nan"))
+    full[rows] = sub
+    got = full.reshape(-1)[fix["index"]]
     m = ~torch.isnan(got)
     assert m.any()
     assert torch.allclose(got[m], fix["value"][m], atol=1e-5)

@@ -1,0 +1,177 @@
+"""The evaluator-compatible entry points (b200fp8.harness.make_entry) on the GPU.
+
+Each entry point is called the way the reference evaluator calls the compiled CuTe entry:
+positionally, inputs (e4m3 operands as uint8 storage, the rest f32), then the evaluator's
+workspaces (here zero-filled stand-ins of the evaluator's shapes, which the entries do not
+touch), then an uninitialised f32 ``output``.  Inputs are the evaluators' own draws
+(tests/golden/task_inputs.py, bit-identical, checked by make_golden.py) and outputs are
+held to the golden vectors with each task's own threshold (task.json ``validation``), as in
+tests/test_golden_gpu.py.  A second call on the same buffers must give the same bits (the
+evaluator's warm-up and timed repeats reuse them)."""
+from __future__ import annotations
+
+import os
+import sys
+
+import pytest
+import torch
+
+from conftest import ROOT
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(ROOT, "tests", "golden")
+
+
+def _ti():
+    if GOLDEN not in sys.path:
+        sys.path.insert(0, GOLDEN)
+    import task_inputs
+    return task_inputs
+
+
+def _fixture(task):
+    return torch.load(os.path.join(GOLDEN, task + ".pt"))
+
+
+def _u8(t):
+    return t.view(torch.uint8).cuda()
+
+
+def _ws(*shapes):
+    return [torch.zeros(s, dtype=torch.uint8, device="cuda") for s in shapes]
+
+
+GEMM = {
+    "level1_01_square_matrix_multiplication_fp8": (lambda t: t.square_gemm(), 0.125, False),
+    "level2_76_gemm_add_relu_fp8": (lambda t: t.gemm_epilogue_task(20260726), 0.01, True),
+    "level2_09_matmul_subtract_multiply_relu_fp8": (lambda t: t.gemm_epilogue_task(20260727), 0.01, True),
+    "level2_12_gemm_multiply_leaky_relu_fp8": (lambda t: t.gemm_epilogue_task(20260727), 0.01, True),
+    "level2_14_gemm_divide_sum_scaling_fp8": (
+        lambda t: t.gemm_epilogue_task(20260727, bias=False), 0.05, False),
+    "level2_40_matmul_scaling_residual_add_fp8": (lambda t: t.gemm_epilogue_task(20260727), 0.01, True),
+    "level2_63_gemm_relu_divide_fp8": (lambda t: t.gemm_epilogue_task(20260727), 0.01, True),
+    "model_gpt2_small_qkv_projection_fp8": (lambda t: t.qkv_projection(), 0.01, True),
+}
+
+
+@pytest.mark.parametrize("task", sorted(GEMM))
+def test_gemm_entry_points_against_golden(task):
+    from b200fp8 import harness
+    make, thr, has_bias = GEMM[task]
+    inp = make(_ti())
+    fix = _fixture(task)
+    entry = harness.make_entry(task)
+    m, n = inp["a"].shape[0], inp["b"].shape[0]
+    rowsum = harness.TASKS[task]["epilogue"].get("rowsum", False)
+    out = torch.full((m, 1) if rowsum else (m, n), float("nan"), device="cuda")
+    args = [_u8(inp["a"]), _u8(inp["b"])] + ([inp["bias"].cuda()] if has_bias else []) + [out]
+    entry(*args)
+    torch.cuda.synchronize()
+    first = out.clone()
+    entry(*args)  # warm-up and timed repeats reuse the buffers
+    torch.cuda.synchronize()
+    assert torch.equal(first, out)
+    got = out.cpu().reshape(-1)[fix["index"]]
+    assert float((got - fix["value"]).abs().max()) <= thr
+    assert abs(float(out.abs().max()) - fix["max_abs"]) <= thr
+
+
+def _block_check(out, fix, thr):
+    want = fix["output_f16"].float()
+    err = (out.float().cpu() - want).abs()
+    assert torch.isfinite(out).all()
+    assert bool((err <= thr + want.abs() * 2.0 ** -9).all()), float(err.max())
+
+
+def test_gpt2_block_entry_point_against_golden():
+    from b200fp8 import harness
+    inp = _ti().gpt2_block()
+    entry = harness.make_entry("model_gpt2_small_transformer_block_fp8")
+    t, d = inp["hidden"].shape
+    c = lambda k: inp[k].cuda()  # noqa: E731
+    out = torch.full((t, d), float("nan"), device="cuda")
+    ws = _ws((t, d), (t, 3 * d)) + [torch.zeros((12 * t, t), device="cuda")] * 2 + \
+        _ws((t, d)) + [torch.zeros((t, d), device="cuda")] + _ws((t, d), (t, 3072))
+    args = [_u8(inp["hidden"]), c("ln1_w"), c("ln1_b"), _u8(inp["qkv_w"]), c("qkv_b"),
+            _u8(inp["out_w"]), c("out_b"), c("ln2_w"), c("ln2_b"), _u8(inp["fc_w"]), c("fc_b"),
+            _u8(inp["proj_w"]), c("proj_b")] + ws + [out]
+    assert len(args) == 22
+    for _ in range(2):
+        entry(*args)
+    torch.cuda.synchronize()
+    _block_check(out, _fixture("model_gpt2_small_transformer_block_fp8"), 0.05)
+
+
+def test_vision_block_entry_point_against_golden():
+    from b200fp8 import harness
+    inp = _ti().gpt2_block(hidden=1024, mlp=4096, vision=True)
+    entry = harness.make_entry("model_qwen35_4b_vision_block_fp8")
+    t, d = inp["hidden"].shape
+    c = lambda k: inp[k].cuda()  # noqa: E731
+    out = torch.full((t, d), float("nan"), device="cuda")
+    ws = _ws(*([(t, d)] * 9))
+    args = [_u8(inp["hidden"]), c("ln1_w"), c("ln1_b"), _u8(inp["qkv_w"]), c("qkv_b"),
+            _u8(inp["out_w"]), c("out_b"), c("ln2_w"), c("ln2_b"), _u8(inp["fc_w"]), c("fc_b"),
+            _u8(inp["proj_w"]), c("proj_b"), c("cos"), c("sin")] + ws + [out]
+    assert len(args) == 25
+    for _ in range(2):
+        entry(*args)
+    torch.cuda.synchronize()
+    _block_check(out, _fixture("model_qwen35_4b_vision_block_fp8"), 0.06)
+
+
+def test_qwen_block_entry_point_against_golden():
+    from b200fp8 import harness
+    inp = _ti().qwen_block()
+    entry = harness.make_entry("model_qwen35_4b_full_attention_block_fp8")
+    t, d = inp["hidden"].shape
+    c = lambda k: inp[k].cuda()  # noqa: E731
+    out = torch.full((t, d), float("nan"), device="cuda")
+    ws = _ws(*([(t, d)] * 14))
+    args = [_u8(inp["hidden"]), c("in_norm_w"), c("q_norm_w"), c("k_norm_w"),
+            _u8(inp["q_gate_w"]), _u8(inp["k_w"]), _u8(inp["v_w"]), _u8(inp["out_w"]),
+            c("post_norm_w"), _u8(inp["gate_w"]), _u8(inp["up_w"]), _u8(inp["down_w"]),
+            c("cos"), c("sin")] + ws + [out]
+    assert len(args) == 29
+    for _ in range(2):
+        entry(*args)
+    torch.cuda.synchronize()
+    _block_check(out, _fixture("model_qwen35_4b_full_attention_block_fp8"), 0.08)
+
+
+def test_layer_norm_entry_point_against_golden():
+    from b200fp8 import harness
+    inp = _ti().layer_norm_task()
+    fix = _fixture("level1_40_layer_norm_fp8")
+    entry = harness.make_entry("level1_40_layer_norm_fp8")
+    out = torch.full(inp["x"].shape, float("nan"), device="cuda")
+    entry(_u8(inp["x"]), out)
+    torch.cuda.synchronize()
+    got = out.cpu().reshape(-1)[fix["index"]]
+    assert float((got - fix["value"]).abs().max()) <= 0.01
+
+
+def test_reporting_from_an_entry_point_timing():
+    """The evaluator's timing loop (median of CUDA-event repeats) around an entry point,
+    printed in the evaluator's PASS-line format and read back by the reporting record."""
+    from b200fp8 import harness, reporting
+    task = "level2_76_gemm_add_relu_fp8"
+    inp = _ti().gemm_epilogue_task(20260726)
+    entry = harness.make_entry(task)
+    out = torch.empty((1024, 8192), device="cuda")
+    args = [_u8(inp["a"]), _u8(inp["b"]), inp["bias"].cuda(), out]
+    for _ in range(2):
+        entry(*args)
+    times = []
+    for _ in range(5):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        entry(*args)
+        e.record()
+        e.synchronize()
+        times.append(s.elapsed_time(e))
+    t_ms = sorted(times)[len(times) // 2]
+    line = f"task=level2_76_gemm_add_relu full_max_abs=0 sample_max_abs=0 kernel_time_ms={t_ms:.6f} PASS"
+    res = reporting.evaluation_result(task, {"stdout": line, "success": True, "exit_code": 0})
+    assert res.passed and res.kernel_time_ms == pytest.approx(t_ms, rel=1e-5)
+    assert res.tflops > 100 and 0 < res.roofline_frac < 1.2

@@ -243,3 +243,50 @@ def test_stream_schedule_against_oracle_large(kind, static):
     if not static:
         assert abs(float(s.cpu()) - s_ref) <= 1e-6 * s_ref
     _assert_q(q, q_ref)
+
+
+@pytest.mark.parametrize("rows,cols,xdt,odt,affine", [
+    (3, 100000, torch.float8_e4m3fn, torch.float32, False),
+    (2, 65536 * 3 + 17, torch.bfloat16, torch.float32, True),
+    (5, 1000, torch.float32, torch.bfloat16, True),
+    (1, 131072, torch.float8_e4m3fn, torch.bfloat16, False),
+])
+def test_layer_norm_rows_against_oracle(rows, cols, xdt, odt, affine):
+    """Long-row LayerNorm (b2f_layer_norm_rows): each row split over many CTAs, ragged
+    chunk tails, f32 statistics per chunk combined in f64."""
+    ops = _ops()
+    g = gen(rows * 7 + cols)
+    src = torch.rand((rows, cols), generator=g)
+    if xdt == torch.float8_e4m3fn:
+        x, xs = (src * 448).to(xdt), 1 / 448.0
+    else:
+        x, xs = src.to(xdt), 1.0
+    w = (1 + 0.1 * randn((cols,), g)) if affine else None
+    b = 0.1 * randn((cols,), g) if affine else None
+    ref = onorm.layer_norm_rows(x.float() * xs, 1e-5, w, b)
+    out = ops.layer_norm_rows(x.cuda(), x_scale=xs, eps=1e-5, out_dtype=odt,
+                              weight=None if w is None else w.cuda(),
+                              bias=None if b is None else b.cuda())
+    torch.cuda.synchronize()
+    tol = 1e-4 if odt == torch.float32 else 2.0 ** -8 * float(ref.abs().max())
+    assert float((out.float().cpu() - ref).abs().max()) <= tol
+
+
+def test_layer_norm_rows_level1_40_golden():
+    """tasks/level1_40_layer_norm_fp8 at its shape [16 x 4,194,304], e4m3 at 1/448, f32
+    out: every element against the f64 oracle and the golden samples (task bar 0.01)."""
+    import os
+    import sys
+    from conftest import ROOT
+    gdir = os.path.join(ROOT, "tests", "golden")
+    if gdir not in sys.path:
+        sys.path.insert(0, gdir)
+    import task_inputs as ti
+    inp = ti.layer_norm_task()
+    fix = torch.load(os.path.join(gdir, "level1_40_layer_norm_fp8.pt"))
+    out = _ops().layer_norm_rows(inp["x"].cuda(), x_scale=inp["x_scale"], eps=inp["eps"])
+    torch.cuda.synchronize()
+    got = out.cpu()
+    assert float((got.reshape(-1)[fix["index"]] - fix["value"]).abs().max()) <= 1e-4
+    ref = onorm.layer_norm_rows(inp["x"].float() * inp["x_scale"], inp["eps"])
+    assert float((got - ref).abs().max()) <= 1e-4  # task bar: 0.01
