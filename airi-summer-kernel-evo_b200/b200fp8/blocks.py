@@ -47,10 +47,11 @@ def _gemm(*args, **kwargs):
 
 
 def _v_dtype(head_dim: int) -> torch.dtype:
-    """V operand type of the blocks: bf16 (P in bf16).  It holds e4m3 values exactly; the
-    f16 form the attention kernel also accepts (head_dim 64 / 128) measured slower on B200
-    (Qwen shape 237 vs 206 us, GPT-2 shape 69 vs 59 us)."""
-    return torch.bfloat16
+    """V operand type of the blocks: f16 for head_dim 64 / 128, so the attention rounds P
+    to f16 (2^-11 relative; measured as fast as bf16 P on B200, 179 us at the Qwen shape,
+    with six times fewer requantised codes off by one), bf16 for head_dim 256.  Both hold
+    the e4m3 values exactly."""
+    return torch.float16 if head_dim <= 128 else torch.bfloat16
 
 
 def _v_convert(src: torch.Tensor, dst: torch.Tensor) -> None:

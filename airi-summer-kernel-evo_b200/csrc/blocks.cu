@@ -33,8 +33,10 @@ struct Carve {
   }
 };
 
-// V operand of the blocks: bf16 (the f16 form measured slower on B200).
-int v_dtype(int /*head_dim*/) { return B2F_DTYPE_BF16; }
+// V operand of the blocks: f16 for head_dim 64 / 128 (P is then rounded to f16, 2^-11
+// relative, at the same speed as bf16 P), bf16 for head_dim 256 (the only form that
+// kernel takes).  Both hold the e4m3 values exactly.
+int v_dtype(int head_dim) { return head_dim <= 128 ? B2F_DTYPE_F16 : B2F_DTYPE_BF16; }
 
 int v_convert(const void* in, long long in_ld, void* out, long long rows, int cols, int dt,
               b2f_stream_t s) {

@@ -1,14 +1,19 @@
 """Parity of the fused tcgen05 attention (b2f_attention_fp8) and its operand prep
 (b2f_head_norm_rope, b2f_fp8_to_bf16, b2f_fp8_to_f16) with the CPU oracle.
 
-Bar for the e4m3 context, in value space against the oracle's unquantised f32 context:
-  |ctx - ref| <= half an e4m3 step at |ref|  (the requantisation itself)
-               + 2^-7 * max|v|               (P is rounded to bf16 before the P.V MMA,
-                                              (f16 with f16 V), the reference keeps f32;
-                                              f32 sum order)
-and at least 95% of the stored e4m3 codes equal the oracle's requantised codes.
-An e4m3 "ulp" count is not used: near-zero contexts change sign under tiny absolute
-errors, which spans many codes without being a meaningful error.
+Bars for the e4m3 context against the oracle's unquantised f32 context (reference math
+keeps P in f32; the kernel rounds P to f16 with f16 V, to bf16 with bf16 V, before P.V):
+  - every element: |ctx - ref| <= half an e4m3 step at |ref| (the requantisation itself)
+    + 2^-7 * max|v| (P rounding and f32 sum order), in value space;
+  - every element with |ref| >= 2^-8 * max|v| (in stored units; 2^-7 * max|v| with bf16 P,
+    whose rounding is 8x coarser): at most one e4m3 code from the oracle's requantised code
+    (the requirement for requantised outputs).  Below
+    that floor a context is a near-cancellation of +-v terms whose absolute error is far
+    below the e4m3 resolution of the larger values, and its code distance is not
+    meaningful (sign flips around zero);
+  - f16 V: >= 99 % of the codes equal the oracle's; bf16 V (2^-8 relative P rounding):
+    >= 94 %.
+The code-distance histogram is printed (pytest -s) for every case.
 """
 from __future__ import annotations
 
@@ -32,15 +37,23 @@ def e4m3_half_step(x: torch.Tensor) -> torch.Tensor:
     return torch.exp2(torch.floor(torch.log2(a)) - 3.0) * 0.5
 
 
-def assert_ctx_close(ctx_q, ref_f32, scale, vmax):
+def assert_ctx_close(ctx_q, ref_f32, scale, vmax, min_same=0.99):
+    """min_same 0.99 is the f16-P bar; the bf16-P callers pass 0.94 (and get the 2^-7
+    code floor)."""
     got = ctx_q.cpu().float()
     ref_units = ref_f32 / scale
     bound = e4m3_half_step(ref_units) + 2.0 ** -7 * vmax / scale
     err = (got - ref_units).abs()
     bad = err > bound
     assert not bad.any(), f"{int(bad.sum())} elements out of bound, max err {float(err.max())}"
-    same = (ctx_q.cpu().view(torch.uint8) == ref_units.to(torch.float8_e4m3fn).view(torch.uint8))
-    assert float(same.float().mean()) >= 0.95, float(same.float().mean())
+    codes = e4m3_ulp_diff(ctx_q.cpu(), ref_units.clamp(-448.0, 448.0).to(torch.float8_e4m3fn))
+    hist = [int((codes == i).sum()) for i in range(3)] + [int((codes >= 3).sum())]
+    floor = (2.0 ** -8 if min_same >= 0.99 else 2.0 ** -7) * vmax / scale
+    above = ref_units.abs() >= floor
+    print(f"e4m3 code distance histogram [0, 1, 2, >=3]: {hist}; "
+          f"max above floor {floor:.3g}: {int(codes[above].max()) if above.any() else 0}")
+    assert int(codes[above].max()) <= 1
+    assert float((codes == 0).float().mean()) >= min_same, hist
 
 
 def _e4m3(x: torch.Tensor) -> torch.Tensor:
@@ -81,7 +94,7 @@ def test_attention_matches_oracle(batch, seq, hq, hkv, d, causal, vtype):
                             heads=hq, kv_heads=hkv, head_dim=d, causal=causal, q_scale=s,
                             k_scale=s, v_scale=s, ctx_scale=s)
     torch.cuda.synchronize()
-    assert_ctx_close(ctx, ref, s, float(vf.abs().max()))
+    assert_ctx_close(ctx, ref, s, float(vf.abs().max()), 0.99 if vtype == "f16" else 0.94)
 
 
 @pytest.mark.parametrize("gdt", ["e4m3", "bf16"])
@@ -94,7 +107,7 @@ def test_attention_matches_oracle(batch, seq, hq, hkv, d, causal, vtype):
 def test_attention_gate_tiles_match_oracle(batch, seq, hq, hkv, d, causal, gdt):
     """Sigmoid output gate read from a column block of a wider projection (as the blocks
     lay it out): e4m3 gates arrive as TMA tiles in shared memory (128- or 64-byte swizzled
-    rows), bf16 gates are read per row."""
+    rows), bf16 gates are read per row.  f16 V, as the blocks run it."""
     g = gen(3000 + seq + hq + d)
     s = 1 / 64.0
     t = batch * seq
@@ -117,7 +130,7 @@ def test_attention_gate_tiles_match_oracle(batch, seq, hq, hkv, d, causal, gdt):
                          gate=gate_f.view(t, hq, d)).reshape(t, hq * d)
     ops = _ops()
     wide_d = wide.cuda()
-    ctx = ops.attention_fp8(q.cuda(), k.cuda(), ops.fp8_to_bf16(v.cuda()), batch=batch,
+    ctx = ops.attention_fp8(q.cuda(), k.cuda(), ops.fp8_to_f16(v.cuda()), batch=batch,
                             heads=hq, kv_heads=hkv, head_dim=d, causal=causal, q_scale=s,
                             k_scale=s, v_scale=s, gate=wide_d[:, 64:64 + hq * d],
                             gate_scale=gs, ctx_scale=s)
@@ -145,7 +158,7 @@ def test_attention_gated_interleaved_qwen_reference_layout():
                             kv_heads=hkv, head_dim=d, q_scale=s, k_scale=s, v_scale=s,
                             gate=qgc[:, d:], gate_scale=s, gate_head_stride=2 * d, ctx_scale=s)
     torch.cuda.synchronize()
-    assert_ctx_close(ctx, ref, s, float(vf.abs().max()))
+    assert_ctx_close(ctx, ref, s, float(vf.abs().max()), 0.94)  # head_dim 256: bf16 V
 
 
 @pytest.mark.parametrize("d,rot,h,wide", [

@@ -7,7 +7,8 @@ touch), then an uninitialised f32 ``output``.  Inputs are the evaluators' own dr
 (tests/golden/task_inputs.py, bit-identical, checked by make_golden.py) and outputs are
 held to the golden vectors with each task's own threshold (task.json ``validation``), as in
 tests/test_golden_gpu.py.  A second call on the same buffers must give the same bits (the
-evaluator's warm-up and timed repeats reuse them)."""
+evaluator's warm-up and timed repeats reuse them; the row-sum task, whose column tiles meet
+through f32 atomics, the same values to f32 rounding)."""
 from __future__ import annotations
 
 import os
@@ -70,7 +71,10 @@ def test_gemm_entry_points_against_golden(task):
     first = out.clone()
     entry(*args)  # warm-up and timed repeats reuse the buffers
     torch.cuda.synchronize()
-    assert torch.equal(first, out)
+    if rowsum:  # row sums gather column tiles with atomics: order-dependent f32 rounding
+        assert torch.allclose(first, out, rtol=1e-5, atol=1e-4)
+    else:
+        assert torch.equal(first, out)
     got = out.cpu().reshape(-1)[fix["index"]]
     assert float((got - fix["value"]).abs().max()) <= thr
     assert abs(float(out.abs().max()) - fix["max_abs"]) <= thr
