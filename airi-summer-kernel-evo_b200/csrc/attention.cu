@@ -4,14 +4,15 @@
 //   S_j  = Q . K_j^T            tcgen05.mma kind::f8f6f4 (e4m3 x e4m3 -> f32 in TMEM)
 //   P_j  = exp2(S_j * scale*log2e - m)  in registers, online softmax with lazy rescaling
 //          (the running max only moves when it grows by more than 2^8), P rounded to f16
-//          with f16 V (bf16 with bf16 V) and written back to TMEM over S_j
-//   O   += P_j . V_j            tcgen05.mma kind::f16, P from TMEM, V (exact bf16 / f16
-//                               image of the e4m3 values) MN-major from shared memory
+//          with f16 V (bf16 with bf16 V); P goes back to shared memory (two-tile kernel)
+//          or tensor memory over S_j (head_dim 256 kernel)
+//   O   += P_j . V_j            tcgen05.mma kind::f16, V (exact bf16 / f16 image of the
+//                               e4m3 values) MN-major from shared memory
 //   ctx  = e4m3( O / l * sigmoid(gate) / ctx_scale )   fused epilogue
 // Two kernels:
-//   attention2_kernel<D, VF16> (head_dim 64 / 128): two query tiles per CTA alternating
-//     with the tensor core (320 threads: TMA producer warp, MMA warp, two softmax
-//     warpgroups); GQA head pairs share K / V; e4m3 gate tiles arrive by TMA.
+//   attention2_kernel<D, VF16> (head_dim 64 / 128): two query tiles per CTA, 64-key tiles,
+//     S double-buffered in tensor memory per tile (320 threads: TMA producer warp, MMA
+//     warp, two softmax warpgroups); GQA head pairs share K / V; e4m3 gate tiles by TMA.
 //   attention_kernel<256> (head_dim 256): one query tile per CTA (192 threads), S
 //     double-buffered in TMEM so Q.K_{j+1}^T runs while the softmax of tile j is computed.
 // Causal tiles above the diagonal are never visited; GQA maps query head h to KV head
@@ -405,13 +406,16 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 // ---------------------------------------------------------------------------------------
-// Two query tiles per CTA (head_dim 64 / 128).  Query tiles A and B of the same (sequence,
-// head) share every K/V tile; softmax warpgroup A (warps 2-5) and B (warps 6-9) alternate
-// with the tensor core: while A exponentiates S_A(j) the MMA warp runs S_B(j) and
-// P_B(j-1).V, and vice versa.  With causal masking the pair is (i, n-1-i), so every CTA
-// walks n+1 key tiles in total (balanced grid); without masking it is (2c, 2c+1).
-// TMEM: S_A | S_B | O_A | O_B; P_X is written back over the first BKV/2 columns of S_X
-// (bf16 or f16 pairs) and read from there by the P.V MMA.
+// Two query tiles per CTA (head_dim 64 / 128), 64-key tiles.  Query tiles A and B share
+// every K/V tile; softmax warpgroup A (warps 2-5) and B (warps 6-9) each own one tile.
+// Each tile has two S buffers in tensor memory: the MMA warp computes S(j+2) while the
+// softmax works on S(j+1), so a tile's softmax never waits for its own P(j).V and next S
+// (the chain softmax -> P.V -> S -> softmax of a single buffer); the tensor core
+// alternates between the tiles' P.V and S MMAs.  With causal masking the pair is
+// (i, n-1-i) or, for GQA head pairs, the same query rows of two heads sharing K/V.
+// TMEM: S_A0 | S_A1 | S_B0 | S_B1 | O_A | O_B.  P(j) goes to a shared-memory tile per
+// query tile (f16 or bf16, the swizzled K-major layout of an MMA operand) once P(j-1).V
+// has retired, and P.V reads both operands from shared memory.
 
 __device__ __forceinline__ float ex2_hw(float x) {
   float y;
@@ -422,7 +426,10 @@ __device__ __forceinline__ float ex2_hw(float x) {
 template <int D>
 struct Attn2Cfg {
   static constexpr int BQ = 128;
-  static constexpr int BKV = 128;
+  // 64-key tiles: two S buffers per query tile fit in tensor memory next to both O
+  // accumulators (2 tiles x 2 x 64 + 2 x D <= 512 columns), so S(j+2) is computed while
+  // the softmax of S(j+1) runs and no query tile waits for its own P.V and next S.
+  static constexpr int BKV = 64;
   static constexpr int ROWB = (D >= 128) ? 128 : D;
   static constexpr int KB = (D >= 128) ? D / 128 : 1;
   static constexpr uint32_t LAYOUT8 = (ROWB == 128) ? 2u : 4u;
@@ -431,17 +438,22 @@ struct Attn2Cfg {
   static constexpr int K_BYTES = BKV * D;
   static constexpr int V_BYTES = BKV * D * 2;
   // Separate K and V rings: K(j) is released as soon as both S(j) MMAs are issued, so
-  // the K ring runs further ahead than the (larger) V ring.  P lives in tensor memory.
-  static constexpr int KST = (D >= 128) ? 4 : 6;
-  static constexpr int VST = (D >= 128) ? 3 : 4;
+  // the K ring runs further ahead than the (larger) V ring.
+  static constexpr int KST = (D >= 128) ? 6 : 8;
+  static constexpr int VST = (D >= 128) ? 4 : 6;
+  // P (16-bit, one 128-byte swizzled row of 64 keys per query row) in shared memory, one
+  // tile per query tile: the P.V MMA reads both operands from shared memory.  (With P in
+  // tensor memory that MMA ran at less than half rate while the softmax warps kept the
+  // SM's issue slots busy; the shared-memory form is unaffected.)
+  static constexpr int P_BYTES = BQ * BKV * 2;
   // e4m3 gate tiles (one per query tile, same shape as Q) for the gated epilogue.
   static constexpr int G_BYTES = Q_BYTES;
-  static constexpr int SMEM_BYTES =
-      2 * Q_BYTES + KST * K_BYTES + VST * V_BYTES + 2 * G_BYTES + 1024 + 512;
-  static constexpr int S_COL = 0;             // S_X at X * BKV
-  static constexpr int O_COL = 2 * BKV;       // O_X at O_COL + X * D
+  static constexpr int SMEM_BYTES = 2 * Q_BYTES + KST * K_BYTES + VST * V_BYTES +
+                                    2 * P_BYTES + 2 * G_BYTES + 1024 + 512;
+  static constexpr int S_COL = 0;             // S_X buffer b at X * 2 * BKV + b * BKV
+  static constexpr int O_COL = 4 * BKV;       // O_X at O_COL + X * D
   static constexpr int TMEM_COLS = 512;
-  static_assert(D > 128 || 2 * BKV + 2 * D <= 512, "TMEM budget");
+  static_assert(D > 128 || 4 * BKV + 2 * D <= 512, "TMEM budget");
   static_assert(D > 128 || SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 
@@ -459,18 +471,18 @@ __global__ void __launch_bounds__(320, 1)
   uint8_t* sq = smem;                            // [2][Q_BYTES]
   uint8_t* sk = sq + 2 * C::Q_BYTES;             // [KST][K_BYTES]
   uint8_t* sv = sk + KST * C::K_BYTES;           // [VST][V_BYTES]
-  uint8_t* sg = sv + VST * C::V_BYTES;           // [2][G_BYTES]
+  uint8_t* sp = sv + VST * C::V_BYTES;           // [2][P_BYTES]
+  uint8_t* sg = sp + 2 * C::P_BYTES;             // [2][G_BYTES]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sg + 2 * C::G_BYTES);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
   uint64_t* k_empty = k_full + KST;
   uint64_t* v_full = k_empty + KST;
   uint64_t* v_empty = v_full + VST;
-  uint64_t* s_full = v_empty + VST;  // [2] per query tile
-  uint64_t* s_free = s_full + 2;
-  uint64_t* p_full = s_free + 2;
-  uint64_t* pv_done = p_full + 2;
-  uint64_t* drain = pv_done + 2;
+  uint64_t* s_full = v_empty + VST;  // [tile][S buffer]: S(j) landed in buffer j & 1
+  uint64_t* p_full = s_full + 4;     // [tile][buffer]: the softmax wrote P(j) over S(j)
+  uint64_t* pv_done = p_full + 4;    // [tile][buffer]: P(j).V retired
+  uint64_t* drain = pv_done + 4;
   uint64_t* g_full = drain + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g_full + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -518,9 +530,8 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < 4; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 4);
       mbar_init(&p_full[i], 4);
       mbar_init(&pv_done[i], 1);
     }
@@ -612,69 +623,77 @@ __global__ void __launch_bounds__(320, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------------------------------------------------------- MMA issuer
+      // Order per key tile j: P_A(j).V, P_B(j).V, then S_A(j+2), S_B(j+2) into the S
+      // buffers the softmax finished reading before it released P(j).  S(j+1) was issued
+      // one step earlier, so each softmax finds its next S ready.
       constexpr uint32_t idesc_s = make_idesc_f8(BQ, BKV);
       constexpr uint32_t idesc_pv = VF16 ? make_idesc_f16(BQ, D, 1) : make_idesc_bf16(BQ, D, 1);
       bool ok = mbar_wait(q_full, 0, kDevTimeoutMma, abort_flag);
-      auto issue_s = [&](int x, int j) -> bool {
-        const int st = j % KST;
-        if (!mbar_wait(&k_full[st], (j / KST) & 1, kDevTimeoutMma, abort_flag)) return false;
-        tc_fence_after();
-        const uint32_t q_addr = smem_u32(sq + x * C::Q_BYTES);
-        const uint32_t k_addr = smem_u32(sk + st * C::K_BYTES);
+      auto s_tmem = [&](int x, int j) -> uint32_t {
+        return tmem + C::S_COL + x * 2 * BKV + (j & 1) * BKV;
+      };
+      auto wait_k = [&](int j) -> bool {
+        return mbar_wait(&k_full[j % KST], (j / KST) & 1, kDevTimeoutMma, abort_flag);
+      };
+      // Shared-memory descriptors are built once: a descriptor's low 14 bits hold the
+      // address / 16 (every address here is below 256 KB, so adding an offset / 16 never
+      // carries out of the field), so each MMA's operands are the base plus an immediate.
+      // A lean issue loop matters: with the softmax warps keeping the SM's issue slots
+      // busy, descriptor arithmetic between 16-bit MMAs left the tensor core idle.
+      const uint64_t q_desc[2] = {make_sdesc(smem_u32(sq), C::LAYOUT8, 16, C::SBO8),
+                                  make_sdesc(smem_u32(sq + C::Q_BYTES), C::LAYOUT8, 16, C::SBO8)};
+      const uint64_t k_desc0 = make_sdesc(smem_u32(sk), C::LAYOUT8, 16, C::SBO8);
+      const uint64_t p_desc[2] = {make_sdesc(smem_u32(sp), 2, 16, 1024),
+                                  make_sdesc(smem_u32(sp + C::P_BYTES), 2, 16, 1024)};
+      const uint64_t v_desc0 = make_sdesc(smem_u32(sv), 2, BKV * 128, 1024);
+      auto issue_s = [&](int x, int j) {
+        const uint64_t qd = q_desc[x];
+        const uint64_t kd = k_desc0 + uint64_t((j % KST) * (C::K_BYTES >> 4));
+        const uint32_t d = s_tmem(x, j);
 #pragma unroll
         for (int kb = 0; kb < C::KB; ++kb) {
 #pragma unroll
-          for (int k = 0; k < C::ROWB / 32; ++k) {
-            const uint64_t ad =
-                make_sdesc(q_addr + kb * BQ * C::ROWB + k * 32, C::LAYOUT8, 16, C::SBO8);
-            const uint64_t bd =
-                make_sdesc(k_addr + kb * BKV * C::ROWB + k * 32, C::LAYOUT8, 16, C::SBO8);
-            mma_f8(tmem + C::S_COL + x * BKV, ad, bd, idesc_s, (kb | k) != 0);
-          }
+          for (int k = 0; k < C::ROWB / 32; ++k)
+            mma_f8(d, qd + ((kb * BQ * C::ROWB + k * 32) >> 4),
+                   kd + ((kb * BKV * C::ROWB + k * 32) >> 4), idesc_s, (kb | k) != 0);
         }
-        mma_commit(&s_full[x]);
-        if (x == 1) mma_commit(&k_empty[st]);  // tile 1 is the last reader of K(j)
+        mma_commit(&s_full[x * 2 + (j & 1)]);
+      };
+      // S(j) of both tiles (tile 0 only while its causal rows still reach key tile j).
+      auto issue_s_pair = [&](int j) -> bool {
+        if (!wait_k(j)) return false;
+        tc_fence_after();
+        if (act[0] && j < nkv[0]) issue_s(0, j);
+        issue_s(1, j);
+        mma_commit(&k_empty[j % KST]);  // both readers of K(j) issued before it
         return true;
       };
       auto issue_pv = [&](int x, int j) -> bool {
-        if (!mbar_wait(&p_full[x], j & 1, kDevTimeoutMma, abort_flag)) return false;
+        if (!mbar_wait(&p_full[x * 2 + (j & 1)], (j >> 1) & 1, kDevTimeoutMma, abort_flag))
+          return false;
         const int vs = j % VST;
         if (x == 0 || j >= nkv[0]) {  // first reader of V(j)
           if (!mbar_wait(&v_full[vs], (j / VST) & 1, kDevTimeoutMma, abort_flag)) return false;
         }
         tc_fence_after();
-        // P(j) sits in tensor memory over the first BKV/2 columns of S_x (bf16 pairs).
-        const uint32_t p_tmem = tmem + C::S_COL + x * BKV;
-        const uint32_t v_addr = smem_u32(sv + vs * C::V_BYTES);
+        // P(j): 128 query rows x 64 keys of 16-bit weights, K-major, 128-byte swizzled
+        // rows in shared memory; 16 keys (32 bytes of P, 2 KB of V) per MMA.
+        const uint64_t pd = p_desc[x];
+        const uint64_t vd = v_desc0 + uint64_t(vs * (C::V_BYTES >> 4));
+        const uint32_t o = tmem + C::O_COL + x * D;
+        mma_bf16(o, pd, vd, idesc_pv, j != 0);
 #pragma unroll
-        for (int kb = 0; kb < BKV / 64; ++kb) {
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int ks = kb * 4 + k;  // 16 keys per MMA
-            const uint64_t bd = make_sdesc(v_addr + ks * 2048, 2, BKV * 128, 1024);
-            mma_bf16_ts(tmem + C::O_COL + x * D, p_tmem + ks * 8, bd, idesc_pv,
-                        (j | kb | k) != 0);
-          }
-        }
-        mma_commit(&pv_done[x]);
+        for (int ks = 1; ks < BKV / 16; ++ks)
+          mma_bf16(o, pd + ((ks * 32) >> 4), vd + ((ks * 2048) >> 4), idesc_pv, 1u);
+        mma_commit(&pv_done[x * 2 + (j & 1)]);
         return true;
       };
-      if (ok && act[0]) ok = issue_s(0, 0);
-      if (ok) ok = issue_s(1, 0);
+      for (int j = 0; j < 2 && j < nkv[1] && ok; ++j) ok = issue_s_pair(j);
       for (int j = 0; j < nkv[1] && ok; ++j) {
-        if (j < nkv[0]) {
-          if (!(ok = issue_pv(0, j))) break;
-          if (j + 1 < nkv[0]) {
-            if (!(ok = mbar_wait(&s_free[0], j & 1, kDevTimeoutMma, abort_flag))) break;
-            if (!(ok = issue_s(0, j + 1))) break;
-          }
-        }
+        if (j < nkv[0] && !(ok = issue_pv(0, j))) break;
         if (!(ok = issue_pv(1, j))) break;
         mma_commit(&v_empty[j % VST]);  // both P.V of this key tile issued before it
-        if (j + 1 < nkv[1]) {
-          if (!(ok = mbar_wait(&s_free[1], j & 1, kDevTimeoutMma, abort_flag))) break;
-          if (!(ok = issue_s(1, j + 1))) break;
-        }
+        if (j + 2 < nkv[1] && !(ok = issue_s_pair(j + 2))) break;
       }
       mma_commit(drain);
       const uint64_t t0 = globaltimer();
@@ -689,34 +708,29 @@ __global__ void __launch_bounds__(320, 1)
     const int q0 = qt[x] * BQ;
     const int qi = q0 + r;
     const uint32_t t_lane = tmem + (uint32_t(qd * 32) << 16);
-    const uint32_t s_col = C::S_COL + x * BKV;
     const uint32_t o_col = C::O_COL + x * D;
     const float c = p.qk_scale_log2;
     float m_used = -INFINITY;
     float l = 0.f;
     bool ok = act[x];
     for (int j = 0; j < nkv[x] && ok; ++j) {
-      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[x], j & 1, kDevTimeoutEpilogue, abort_flag));
+      const int sb = x * 2 + (j & 1);  // this step's S buffer / barrier slot
+      ok = __all_sync(0xffffffffu,
+                      mbar_wait(&s_full[sb], (j >> 1) & 1, kDevTimeoutEpilogue, abort_flag));
       if (!ok) break;
       tc_fence_after();
+      const uint32_t s_col = C::S_COL + x * 2 * BKV + (j & 1) * BKV;
       const int k0 = j * BKV;
       // keys k0 + kk with kk > klim are masked (past the sequence end or, causal, past qi)
       const int klim = min(p.seq - 1, p.causal ? qi : p.seq - 1) - k0;
       const bool need_mask = klim < BKV - 1;
-      // The whole S row (128 f32 columns) in registers: four loads in flight, one wait;
-      // S is read from tensor memory once per key tile.
-      uint32_t s0[32], s1[32], s2[32], s3[32];
+      // The whole S row (64 f32 columns) in registers: two loads in flight, one wait.
+      uint32_t s0[32], s1[32];
       tmem_ld32_async(t_lane + s_col, s0);
       tmem_ld32_async(t_lane + s_col + 32, s1);
-      tmem_ld32_async(t_lane + s_col + 64, s2);
-      tmem_ld32_async(t_lane + s_col + 96, s3);
       tmem_ld_wait_regs(s0);
       reg_fence32(s1);
-      reg_fence32(s2);
-      reg_fence32(s3);
-      auto sv = [&](int u) -> uint32_t& {
-        return u < 32 ? s0[u] : u < 64 ? s1[u - 32] : u < 96 ? s2[u - 64] : s3[u - 96];
-      };
+      auto sv = [&](int u) -> uint32_t& { return u < 32 ? s0[u] : s1[u - 32]; };
       if (need_mask) {
 #pragma unroll
         for (int u = 0; u < BKV; ++u)
@@ -736,6 +750,7 @@ __global__ void __launch_bounds__(320, 1)
       };
       float corr = 1.0f, lt;
       bool rescale = false;
+      uint32_t pk[BKV / 2];  // this row's P(j) as 16-bit pairs
       {
         // Row max of S * c: 4 independent partial maxima over 3-input max.
         float mp[4];
@@ -754,67 +769,62 @@ __global__ void __launch_bounds__(320, 1)
           m_used = mt;
         }
         const float mref = (m_used == -INFINITY) ? 0.0f : m_used;
-        // P = 2^(S*c - m), written back to tensor memory over the S columns (P column k/2
-        // < S column k; the row is already in registers): the A operand of P.V.  P(j-1)
-        // is no longer read there: S(j) was written after P(j-1).V in the tensor pipe's
-        // order.  Each weight is exponentiated in f32 and rounded to f16 (f16 V) or bf16
+        // P = 2^(S*c - m) in registers, stored below to the shared-memory P tile (the A
+        // operand of P.V).  Each weight is exponentiated in f32 and rounded to f16 (f16 V) or bf16
         // (bf16 V); the row sum accumulates the f32 weights.  Masked keys hold -inf, whose
         // weight is 0.
-        float ls[4] = {0.f, 0.f, 0.f, 0.f};
+        // Scale, offset and row sum as packed pair operations (half the issue slots of
+        // scalar FFMA / FADD: the softmax warps share the SM's issue slots with the MMA
+        // warp, and 16-bit MMAs fed late leave the tensor core idle).
+        const float2 c2 = make_float2(c, c), nm2 = make_float2(-mref, -mref);
+        float2 acc2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-        for (int cc = 0; cc < BKV; cc += 32) {
-          uint32_t pk[16];
+        for (int e = 0; e < BKV / 2; ++e) {
+          const float2 xv = ffma2(make_float2(__uint_as_float(sv(2 * e)),
+                                              __uint_as_float(sv(2 * e + 1))), c2, nm2);
+          const float e0 = ex2_hw(xv.x), e1 = ex2_hw(xv.y);
+          acc2[e & 1] = fadd2(acc2[e & 1], make_float2(e0, e1));
           if constexpr (VF16) {
             // f32 exponentials packed to f16 pairs: the same instruction cost as the bf16
             // form (ex2.approx.f16x2 yields no more exponentials per clock than the f32 one
             // on B200), with a 2^-11 instead of 2^-8 relative rounding of each weight
             // (weights are <= 2^8 after the lazy max update, inside f16's range).
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const int u = cc + 2 * e;
-              const float v0 = fmaf(__uint_as_float(sv(u)), c, -mref);
-              const float v1 = fmaf(__uint_as_float(sv(u + 1)), c, -mref);
-              const float e0 = ex2_hw(v0), e1 = ex2_hw(v1);
-              ls[e & 3] += e0 + e1;
-              pk[e] = pack_f16x2(e0, e1);
-            }
+            pk[e] = pack_f16x2(e0, e1);
           } else {
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const int u = cc + 2 * e;
-              const float v0 = fmaf(__uint_as_float(sv(u)), c, -mref);
-              const float v1 = fmaf(__uint_as_float(sv(u + 1)), c, -mref);
-              const float e0 = ex2_hw(v0), e1 = ex2_hw(v1);
-              const __nv_bfloat162 bb = __floats2bfloat162_rn(e0, e1);
-              // row sum from the f32 weights: the P.V MMA sees them rounded to bf16
-              // (relative 2^-9 per weight, averaging out over the row)
-              ls[e & 3] += e0 + e1;
-              pk[e] = *reinterpret_cast<const uint32_t*>(&bb);
-            }
+            // the row sum keeps the f32 weights; the P.V MMA sees them rounded to bf16
+            pk[e] = pack_bf16x2(e0, e1);
           }
-          tmem_st16(t_lane + s_col + cc / 2, pk);
         }
-        lt = (ls[0] + ls[1]) + (ls[2] + ls[3]);
+        lt = (acc2[0].x + acc2[0].y) + (acc2[1].x + acc2[1].y);
       }
-      tmem_st_wait();
-      // O *= corr once P(j-1).V has landed (before P(j).V is released below).
+      // P(j-1).V has landed before P(j) overwrites the shared-memory P tile and before O is
+      // rescaled (P(j).V is released below).
       if (j > 0) {
-        ok = __all_sync(0xffffffffu,
-                        mbar_wait(&pv_done[x], (j - 1) & 1, kDevTimeoutEpilogue, abort_flag));
+        const int pj = j - 1;
+        ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[x * 2 + (pj & 1)], (pj >> 1) & 1,
+                                               kDevTimeoutEpilogue, abort_flag));
         if (!ok) break;
         tc_fence_after();
         if (__any_sync(0xffffffffu, rescale)) rescale_o(corr);
       }
+      {
+        // Row r of the P tile: eight 16-byte chunks of 8 keys, 128-byte swizzle (chunk c
+        // at position c ^ (r % 8)), the layout of a K-major SW128 MMA operand.
+        uint8_t* prow = sp + x * C::P_BYTES + r * 128;
+#pragma unroll
+        for (int c8 = 0; c8 < BKV / 8; ++c8)
+          *reinterpret_cast<uint4*>(prow + ((c8 ^ (r & 7)) << 4)) =
+              make_uint4(pk[4 * c8], pk[4 * c8 + 1], pk[4 * c8 + 2], pk[4 * c8 + 3]);
+        fence_async_shared();  // generic-proxy writes visible to the tensor core
+      }
       l = l * corr + lt;
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&s_free[x]);
-        mbar_arrive(&p_full[x]);
-      }
+      if (lane == 0) mbar_arrive(&p_full[sb]);
     }
     // ---------------------------------------------------------------- epilogue
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[x], (nkv[x] - 1) & 1,
+    const int lj = nkv[x] - 1;
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[x * 2 + (lj & 1)], (lj >> 1) & 1,
                                                   kDevTimeoutEpilogue, abort_flag));
     if (ok) {
       tc_fence_after();
