@@ -11,8 +11,9 @@
 //   ctx  = e4m3( O / l * sigmoid(gate) / ctx_scale )   fused epilogue
 // Two kernels:
 //   attention2_kernel<D, VF16> (head_dim 64 / 128): two query tiles per CTA, 64-key tiles,
-//     S double-buffered in tensor memory per tile (320 threads: TMA producer warp, MMA
-//     warp, two softmax warpgroups); GQA head pairs share K / V; e4m3 gate tiles by TMA.
+//     P through shared memory, S released as soon as the softmax loaded it (384 threads:
+//     TMA producer warp, MMA warp, two idle warps, two softmax warpgroups holding the
+//     registers the others give up); GQA head pairs share K / V; e4m3 gate tiles by TMA.
 //   attention_kernel<256> (head_dim 256): one query tile per CTA (192 threads), S
 //     double-buffered in TMEM so Q.K_{j+1}^T runs while the softmax of tile j is computed.
 // Causal tiles above the diagonal are never visited; GQA maps query head h to KV head
@@ -406,16 +407,14 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 // ---------------------------------------------------------------------------------------
-// Two query tiles per CTA (head_dim 64 / 128), 64-key tiles.  Query tiles A and B share
-// every K/V tile; softmax warpgroup A (warps 2-5) and B (warps 6-9) each own one tile.
-// Each tile has two S buffers in tensor memory: the MMA warp computes S(j+2) while the
-// softmax works on S(j+1), so a tile's softmax never waits for its own P(j).V and next S
-// (the chain softmax -> P.V -> S -> softmax of a single buffer); the tensor core
-// alternates between the tiles' P.V and S MMAs.  With causal masking the pair is
-// (i, n-1-i) or, for GQA head pairs, the same query rows of two heads sharing K/V.
-// TMEM: S_A0 | S_A1 | S_B0 | S_B1 | O_A | O_B.  P(j) goes to a shared-memory tile per
-// query tile (f16 or bf16, the swizzled K-major layout of an MMA operand) once P(j-1).V
-// has retired, and P.V reads both operands from shared memory.
+// Two query tiles per CTA (head_dim 64 / 128).  Query tiles A and B share every K/V tile;
+// softmax warpgroup A (warps 2-5) and B (warps 6-9) each own one tile.  Each softmax step
+// loads its S row into registers and releases the S columns at once, so the MMA warp
+// computes S(j+1) while the exponentials of S(j) run; P(j) goes to a shared-memory tile
+// per query tile (once P(j-1).V has retired) and P.V reads both operands from shared
+// memory.  A tile's softmax therefore never waits for its own P.V and next QK^T.  With
+// causal masking the pair is (i, n-1-i), or, for GQA head pairs, the same query rows of
+// two heads sharing K/V.  TMEM: S_A | S_B | O_A | O_B.
 
 __device__ __forceinline__ float ex2_hw(float x) {
   float y;
@@ -423,13 +422,31 @@ __device__ __forceinline__ float ex2_hw(float x) {
   return y;
 }
 
+// 2^x for a pair, on the FMA and integer pipes instead of the exponential unit (Cody-Waite
+// style range reduction + polynomial): x = n + f with n = rint(x) (the round-to-nearest of
+// adding 1.5 * 2^23 leaves n in the low mantissa bits), f in [-0.5, 0.5]; 2^f by a cubic
+// fitted for minimal relative error on that interval (max 7.5e-5, 2^-13.7, below the 2^-11
+// rounding of the f16 weights it feeds); 2^n added to the exponent field.  Inputs are
+// clamped to >= -125 (masked keys' -inf gives 2^-125, a weight of zero in f16 and
+// negligible against the row sum).
+__device__ __forceinline__ float2 ex2_poly2(float2 x) {
+  x.x = fmaxf(x.x, -125.0f);
+  x.y = fmaxf(x.y, -125.0f);
+  const float2 t = fadd2(x, make_float2(12582912.0f, 12582912.0f));
+  const float2 n = fadd2(t, make_float2(-12582912.0f, -12582912.0f));
+  const float2 f = ffma2(n, make_float2(-1.0f, -1.0f), x);
+  float2 p = ffma2(make_float2(0.05517132f, 0.05517132f), f,
+                   make_float2(0.24261054f, 0.24261054f));
+  p = ffma2(p, f, make_float2(0.69326097f, 0.69326097f));
+  p = ffma2(p, f, make_float2(0.99992812f, 0.99992812f));
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
+}
+
 template <int D>
 struct Attn2Cfg {
   static constexpr int BQ = 128;
-  // 64-key tiles: two S buffers per query tile fit in tensor memory next to both O
-  // accumulators (2 tiles x 2 x 64 + 2 x D <= 512 columns), so S(j+2) is computed while
-  // the softmax of S(j+1) runs and no query tile waits for its own P.V and next S.
-  static constexpr int BKV = 64;
+  static constexpr int BKV = 128;
   static constexpr int ROWB = (D >= 128) ? 128 : D;
   static constexpr int KB = (D >= 128) ? D / 128 : 1;
   static constexpr uint32_t LAYOUT8 = (ROWB == 128) ? 2u : 4u;
@@ -437,28 +454,29 @@ struct Attn2Cfg {
   static constexpr int Q_BYTES = BQ * D;  // per query tile
   static constexpr int K_BYTES = BKV * D;
   static constexpr int V_BYTES = BKV * D * 2;
-  // Separate K and V rings: K(j) is released as soon as both S(j) MMAs are issued, so
-  // the K ring runs further ahead than the (larger) V ring.
-  static constexpr int KST = (D >= 128) ? 6 : 8;
-  static constexpr int VST = (D >= 128) ? 4 : 6;
-  // P (16-bit, one 128-byte swizzled row of 64 keys per query row) in shared memory, one
-  // tile per query tile: the P.V MMA reads both operands from shared memory.  (With P in
-  // tensor memory that MMA ran at less than half rate while the softmax warps kept the
-  // SM's issue slots busy; the shared-memory form is unaffected.)
+  // Separate K and V rings: K(j) is released as soon as both S(j) MMAs are issued.
+  static constexpr int KST = (D >= 128) ? 2 : 4;
+  static constexpr int VST = (D >= 128) ? 2 : 3;
+  // P (16-bit) in shared memory, one tile per query tile: [2 key blocks of 64][128 rows]
+  // [128-byte swizzled row], the K-major layout of an MMA operand.  The P.V MMA reads both
+  // operands from shared memory (with P in tensor memory that MMA ran at less than half
+  // rate while the softmax warps kept the SM's issue slots busy), and the S columns are
+  // free as soon as the softmax has loaded them: S(j+1) is computed during the
+  // exponentials of S(j).
   static constexpr int P_BYTES = BQ * BKV * 2;
   // e4m3 gate tiles (one per query tile, same shape as Q) for the gated epilogue.
   static constexpr int G_BYTES = Q_BYTES;
   static constexpr int SMEM_BYTES = 2 * Q_BYTES + KST * K_BYTES + VST * V_BYTES +
                                     2 * P_BYTES + 2 * G_BYTES + 1024 + 512;
-  static constexpr int S_COL = 0;             // S_X buffer b at X * 2 * BKV + b * BKV
-  static constexpr int O_COL = 4 * BKV;       // O_X at O_COL + X * D
+  static constexpr int S_COL = 0;             // S_X at X * BKV
+  static constexpr int O_COL = 2 * BKV;       // O_X at O_COL + X * D
   static constexpr int TMEM_COLS = 512;
-  static_assert(D > 128 || 4 * BKV + 2 * D <= 512, "TMEM budget");
+  static_assert(D > 128 || 2 * BKV + 2 * D <= 512, "TMEM budget");
   static_assert(D > 128 || SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 
 template <int D, bool VF16>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(384, 1)
     attention2_kernel(const __grid_constant__ CUtensorMap tm_q,
                       const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v,
@@ -479,10 +497,11 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* k_empty = k_full + KST;
   uint64_t* v_full = k_empty + KST;
   uint64_t* v_empty = v_full + VST;
-  uint64_t* s_full = v_empty + VST;  // [tile][S buffer]: S(j) landed in buffer j & 1
-  uint64_t* p_full = s_full + 4;     // [tile][buffer]: the softmax wrote P(j) over S(j)
-  uint64_t* pv_done = p_full + 4;    // [tile][buffer]: P(j).V retired
-  uint64_t* drain = pv_done + 4;
+  uint64_t* s_full = v_empty + VST;  // [tile]: S(j) landed
+  uint64_t* s_free = s_full + 2;     // [tile]: the softmax loaded S(j) into registers
+  uint64_t* p_full = s_free + 2;     // [tile]: P(j) stored in shared memory
+  uint64_t* pv_done = p_full + 2;    // [tile]: P(j).V retired
+  uint64_t* drain = pv_done + 2;
   uint64_t* g_full = drain + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g_full + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -530,8 +549,9 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);
       mbar_init(&p_full[i], 4);
       mbar_init(&pv_done[i], 1);
     }
@@ -549,6 +569,11 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Register split (per warpgroup): the producer / MMA warpgroup (warps 0-3, two of them
+  // idle) gives up registers to the two softmax warpgroups, which hold a 128-column S row.
+  // 128 x 56 + 256 x 224 = 384 x 168, the block's launch allocation.
+  if (warp < 4) setmaxnreg_dec<56>();
+  else setmaxnreg_inc<224>();
 
   if (warp == 0) {
     // ---------------------------------------------------------------- producers
@@ -623,18 +648,12 @@ __global__ void __launch_bounds__(320, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------------------------------------------------------- MMA issuer
-      // Order per key tile j: P_A(j).V, P_B(j).V, then S_A(j+2), S_B(j+2) into the S
-      // buffers the softmax finished reading before it released P(j).  S(j+1) was issued
-      // one step earlier, so each softmax finds its next S ready.
+      // Per key tile j: S_A(j+1), S_B(j+1) as soon as each softmax has loaded S(j) into
+      // registers (the exponentials of S(j) then overlap the next QK^T), then P_A(j).V and
+      // P_B(j).V once the softmax stored P(j).
       constexpr uint32_t idesc_s = make_idesc_f8(BQ, BKV);
       constexpr uint32_t idesc_pv = VF16 ? make_idesc_f16(BQ, D, 1) : make_idesc_bf16(BQ, D, 1);
       bool ok = mbar_wait(q_full, 0, kDevTimeoutMma, abort_flag);
-      auto s_tmem = [&](int x, int j) -> uint32_t {
-        return tmem + C::S_COL + x * 2 * BKV + (j & 1) * BKV;
-      };
-      auto wait_k = [&](int j) -> bool {
-        return mbar_wait(&k_full[j % KST], (j / KST) & 1, kDevTimeoutMma, abort_flag);
-      };
       // Shared-memory descriptors are built once: a descriptor's low 14 bits hold the
       // address / 16 (every address here is below 256 KB, so adding an offset / 16 never
       // carries out of the field), so each MMA's operands are the base plus an immediate.
@@ -649,7 +668,7 @@ __global__ void __launch_bounds__(320, 1)
       auto issue_s = [&](int x, int j) {
         const uint64_t qd = q_desc[x];
         const uint64_t kd = k_desc0 + uint64_t((j % KST) * (C::K_BYTES >> 4));
-        const uint32_t d = s_tmem(x, j);
+        const uint32_t d = tmem + C::S_COL + x * BKV;
 #pragma unroll
         for (int kb = 0; kb < C::KB; ++kb) {
 #pragma unroll
@@ -657,52 +676,61 @@ __global__ void __launch_bounds__(320, 1)
             mma_f8(d, qd + ((kb * BQ * C::ROWB + k * 32) >> 4),
                    kd + ((kb * BKV * C::ROWB + k * 32) >> 4), idesc_s, (kb | k) != 0);
         }
-        mma_commit(&s_full[x * 2 + (j & 1)]);
+        mma_commit(&s_full[x]);
       };
-      // S(j) of both tiles (tile 0 only while its causal rows still reach key tile j).
+      // S(j) of both tiles (tile 0 only while its causal rows still reach key tile j); for
+      // j > 0 each waits until its softmax has loaded S(j-1).
       auto issue_s_pair = [&](int j) -> bool {
-        if (!wait_k(j)) return false;
+        if (!mbar_wait(&k_full[j % KST], (j / KST) & 1, kDevTimeoutMma, abort_flag))
+          return false;
+        if (act[0] && j < nkv[0]) {
+          if (j > 0 && !mbar_wait(&s_free[0], (j - 1) & 1, kDevTimeoutMma, abort_flag))
+            return false;
+          tc_fence_after();
+          issue_s(0, j);
+        }
+        if (j > 0 && !mbar_wait(&s_free[1], (j - 1) & 1, kDevTimeoutMma, abort_flag))
+          return false;
         tc_fence_after();
-        if (act[0] && j < nkv[0]) issue_s(0, j);
         issue_s(1, j);
         mma_commit(&k_empty[j % KST]);  // both readers of K(j) issued before it
         return true;
       };
       auto issue_pv = [&](int x, int j) -> bool {
-        if (!mbar_wait(&p_full[x * 2 + (j & 1)], (j >> 1) & 1, kDevTimeoutMma, abort_flag))
-          return false;
+        if (!mbar_wait(&p_full[x], j & 1, kDevTimeoutMma, abort_flag)) return false;
         const int vs = j % VST;
         if (x == 0 || j >= nkv[0]) {  // first reader of V(j)
           if (!mbar_wait(&v_full[vs], (j / VST) & 1, kDevTimeoutMma, abort_flag)) return false;
         }
         tc_fence_after();
-        // P(j): 128 query rows x 64 keys of 16-bit weights, K-major, 128-byte swizzled
-        // rows in shared memory; 16 keys (32 bytes of P, 2 KB of V) per MMA.
+        // P(j): 128 query rows x 128 keys of 16-bit weights in two 64-key blocks of
+        // 128-byte swizzled rows; 16 keys (32 bytes of P, 2 KB of V) per MMA.
         const uint64_t pd = p_desc[x];
         const uint64_t vd = v_desc0 + uint64_t(vs * (C::V_BYTES >> 4));
         const uint32_t o = tmem + C::O_COL + x * D;
         mma_bf16(o, pd, vd, idesc_pv, j != 0);
 #pragma unroll
         for (int ks = 1; ks < BKV / 16; ++ks)
-          mma_bf16(o, pd + ((ks * 32) >> 4), vd + ((ks * 2048) >> 4), idesc_pv, 1u);
-        mma_commit(&pv_done[x * 2 + (j & 1)]);
+          mma_bf16(o, pd + (((ks >> 2) * BQ * 128 + (ks & 3) * 32) >> 4),
+                   vd + ((ks * 2048) >> 4), idesc_pv, 1u);
+        mma_commit(&pv_done[x]);
         return true;
       };
-      for (int j = 0; j < 2 && j < nkv[1] && ok; ++j) ok = issue_s_pair(j);
+      if (ok) ok = issue_s_pair(0);
       for (int j = 0; j < nkv[1] && ok; ++j) {
+        if (j + 1 < nkv[1] && !(ok = issue_s_pair(j + 1))) break;
         if (j < nkv[0] && !(ok = issue_pv(0, j))) break;
         if (!(ok = issue_pv(1, j))) break;
         mma_commit(&v_empty[j % VST]);  // both P.V of this key tile issued before it
-        if (j + 2 < nkv[1] && !(ok = issue_s_pair(j + 2))) break;
       }
       mma_commit(drain);
       const uint64_t t0 = globaltimer();
       while (!mbar_test(drain, 0))
         if (globaltimer() - t0 > B2F_WAIT_NS) { record_error(kDevTimeoutDrain); break; }
     }
-  } else {
+  } else if (warp >= 4) {
     // ------------------------------------------------------------------ softmax + epilogue
-    const int x = (warp - 2) >> 2;   // query tile handled by this warpgroup
+    const int x = (warp - 4) >> 2;   // query tile handled by this warpgroup
     const int qd = warp & 3;         // TMEM lane quadrant
     const int r = qd * 32 + lane;
     const int q0 = qt[x] * BQ;
@@ -713,24 +741,32 @@ __global__ void __launch_bounds__(320, 1)
     float m_used = -INFINITY;
     float l = 0.f;
     bool ok = act[x];
+    const uint32_t s_col = C::S_COL + x * BKV;
     for (int j = 0; j < nkv[x] && ok; ++j) {
-      const int sb = x * 2 + (j & 1);  // this step's S buffer / barrier slot
-      ok = __all_sync(0xffffffffu,
-                      mbar_wait(&s_full[sb], (j >> 1) & 1, kDevTimeoutEpilogue, abort_flag));
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[x], j & 1, kDevTimeoutEpilogue, abort_flag));
       if (!ok) break;
       tc_fence_after();
-      const uint32_t s_col = C::S_COL + x * 2 * BKV + (j & 1) * BKV;
       const int k0 = j * BKV;
       // keys k0 + kk with kk > klim are masked (past the sequence end or, causal, past qi)
       const int klim = min(p.seq - 1, p.causal ? qi : p.seq - 1) - k0;
       const bool need_mask = klim < BKV - 1;
-      // The whole S row (64 f32 columns) in registers: two loads in flight, one wait.
-      uint32_t s0[32], s1[32];
+      // The whole S row (128 f32 columns) in registers: four loads in flight, one wait;
+      // then the S columns are released for S(j+1).
+      uint32_t s0[32], s1[32], s2[32], s3[32];
       tmem_ld32_async(t_lane + s_col, s0);
       tmem_ld32_async(t_lane + s_col + 32, s1);
+      tmem_ld32_async(t_lane + s_col + 64, s2);
+      tmem_ld32_async(t_lane + s_col + 96, s3);
       tmem_ld_wait_regs(s0);
       reg_fence32(s1);
-      auto sv = [&](int u) -> uint32_t& { return u < 32 ? s0[u] : s1[u - 32]; };
+      reg_fence32(s2);
+      reg_fence32(s3);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[x]);
+      auto sv = [&](int u) -> uint32_t& {
+        return u < 32 ? s0[u] : u < 64 ? s1[u - 32] : u < 96 ? s2[u - 64] : s3[u - 96];
+      };
       if (need_mask) {
 #pragma unroll
         for (int u = 0; u < BKV; ++u)
@@ -750,7 +786,6 @@ __global__ void __launch_bounds__(320, 1)
       };
       float corr = 1.0f, lt;
       bool rescale = false;
-      uint32_t pk[BKV / 2];  // this row's P(j) as 16-bit pairs
       {
         // Row max of S * c: 4 independent partial maxima over 3-input max.
         float mp[4];
@@ -769,10 +804,12 @@ __global__ void __launch_bounds__(320, 1)
           m_used = mt;
         }
         const float mref = (m_used == -INFINITY) ? 0.0f : m_used;
-        // P = 2^(S*c - m) in registers, stored below to the shared-memory P tile (the A
-        // operand of P.V).  Each weight is exponentiated in f32 and rounded to f16 (f16 V) or bf16
+        // P = 2^(S*c - m), stored below to the shared-memory P tile (the A operand of
+        // P.V).  Each weight is exponentiated in f32 and rounded to f16 (f16 V) or bf16
         // (bf16 V); the row sum accumulates the f32 weights.  Masked keys hold -inf, whose
-        // weight is 0.
+        // weight is 0.  The 16-bit pairs overwrite the S registers they came from (pair e
+        // goes to S slot e, already consumed), which keeps the row within the register
+        // budget.
         // Scale, offset and row sum as packed pair operations (half the issue slots of
         // scalar FFMA / FADD: the softmax warps share the SM's issue slots with the MMA
         // warp, and 16-bit MMAs fed late leave the tensor core idle).
@@ -782,17 +819,27 @@ __global__ void __launch_bounds__(320, 1)
         for (int e = 0; e < BKV / 2; ++e) {
           const float2 xv = ffma2(make_float2(__uint_as_float(sv(2 * e)),
                                               __uint_as_float(sv(2 * e + 1))), c2, nm2);
-          const float e0 = ex2_hw(xv.x), e1 = ex2_hw(xv.y);
+          // Three of every eight pairs go through the polynomial: the exponential unit (16
+          // results per clock per SM) is the softmax's bound, the FMA pipe has room.
+          float e0, e1;
+          if ((e & 7) < 3) {
+            const float2 pe = ex2_poly2(xv);
+            e0 = pe.x;
+            e1 = pe.y;
+          } else {
+            e0 = ex2_hw(xv.x);
+            e1 = ex2_hw(xv.y);
+          }
           acc2[e & 1] = fadd2(acc2[e & 1], make_float2(e0, e1));
           if constexpr (VF16) {
             // f32 exponentials packed to f16 pairs: the same instruction cost as the bf16
             // form (ex2.approx.f16x2 yields no more exponentials per clock than the f32 one
             // on B200), with a 2^-11 instead of 2^-8 relative rounding of each weight
             // (weights are <= 2^8 after the lazy max update, inside f16's range).
-            pk[e] = pack_f16x2(e0, e1);
+            sv(e) = pack_f16x2(e0, e1);
           } else {
             // the row sum keeps the f32 weights; the P.V MMA sees them rounded to bf16
-            pk[e] = pack_bf16x2(e0, e1);
+            sv(e) = pack_bf16x2(e0, e1);
           }
         }
         lt = (acc2[0].x + acc2[0].y) + (acc2[1].x + acc2[1].y);
@@ -800,31 +847,30 @@ __global__ void __launch_bounds__(320, 1)
       // P(j-1).V has landed before P(j) overwrites the shared-memory P tile and before O is
       // rescaled (P(j).V is released below).
       if (j > 0) {
-        const int pj = j - 1;
-        ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[x * 2 + (pj & 1)], (pj >> 1) & 1,
-                                               kDevTimeoutEpilogue, abort_flag));
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait(&pv_done[x], (j - 1) & 1, kDevTimeoutEpilogue, abort_flag));
         if (!ok) break;
         tc_fence_after();
         if (__any_sync(0xffffffffu, rescale)) rescale_o(corr);
       }
       {
-        // Row r of the P tile: eight 16-byte chunks of 8 keys, 128-byte swizzle (chunk c
-        // at position c ^ (r % 8)), the layout of a K-major SW128 MMA operand.
+        // Row r of the P tile: sixteen 16-byte chunks of 8 keys in two 64-key blocks of
+        // 128-byte rows, swizzled (chunk c at position c ^ (r % 8) of its row), the layout
+        // of a K-major SW128 MMA operand.
         uint8_t* prow = sp + x * C::P_BYTES + r * 128;
 #pragma unroll
         for (int c8 = 0; c8 < BKV / 8; ++c8)
-          *reinterpret_cast<uint4*>(prow + ((c8 ^ (r & 7)) << 4)) =
-              make_uint4(pk[4 * c8], pk[4 * c8 + 1], pk[4 * c8 + 2], pk[4 * c8 + 3]);
+          *reinterpret_cast<uint4*>(prow + (c8 >> 3) * (BQ * 128) + (((c8 & 7) ^ (r & 7)) << 4)) =
+              make_uint4(sv(4 * c8), sv(4 * c8 + 1), sv(4 * c8 + 2), sv(4 * c8 + 3));
         fence_async_shared();  // generic-proxy writes visible to the tensor core
       }
       l = l * corr + lt;
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[sb]);
+      if (lane == 0) mbar_arrive(&p_full[x]);
     }
     // ---------------------------------------------------------------- epilogue
-    const int lj = nkv[x] - 1;
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[x * 2 + (lj & 1)], (lj >> 1) & 1,
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[x], (nkv[x] - 1) & 1,
                                                   kDevTimeoutEpilogue, abort_flag));
     if (ok) {
       tc_fence_after();
@@ -1004,9 +1050,9 @@ int launch_attention(const b2f_attn_args* a, cudaStream_t stream) {
     p.pair_heads = (a->hq / a->hkv) % 2 == 0;
     dim3 grid(p.pair_heads ? n_qt : (n_qt + 1) / 2, p.pair_heads ? a->hq / 2 : a->hq, a->batch);
     if (a->v_dtype == B2F_DTYPE_F16)
-      attention2_kernel<D, true><<<grid, 320, SMEM, stream>>>(tq, tk, tv, tg, p);
+      attention2_kernel<D, true><<<grid, 384, SMEM, stream>>>(tq, tk, tv, tg, p);
     else
-      attention2_kernel<D, false><<<grid, 320, SMEM, stream>>>(tq, tk, tv, tg, p);
+      attention2_kernel<D, false><<<grid, 384, SMEM, stream>>>(tq, tk, tv, tg, p);
   } else {
     if (attr_dev[0][slot] != dev) {
       B2F_CUDA_TRY(cudaFuncSetAttribute(attention_kernel<D>,
