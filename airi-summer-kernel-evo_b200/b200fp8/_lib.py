@@ -213,7 +213,7 @@ EXPORTED_SYMBOLS = (
     "b2f_debug_bounded_wait", "b2f_gemm_args_init", "b2f_gemm_fp8", "b2f_gemm_pair_capacity",
     "b2f_gemm_workspace_bytes", "b2f_gemm_fp8_static",
     "b2f_norm_args_init", "b2f_norm_quant", "b2f_norm_plan", "b2f_attn_args_init", "b2f_attention_fp8",
-    "b2f_head_norm_rope", "b2f_fp8_to_bf16", "b2f_fp8_to_f16", "b2f_swiglu_fp8",
+    "b2f_head_norm_rope", "b2f_attn_prep", "b2f_fp8_to_bf16", "b2f_fp8_to_f16", "b2f_swiglu_fp8",
     "b2f_quant_args_init", "b2f_quantize_fp8",
     "b2f_lnrows_args_init", "b2f_layer_norm_rows_workspace_bytes", "b2f_layer_norm_rows",
     "b2f_gpt2_block_args_init", "b2f_gpt2_block_workspace_bytes", "b2f_gpt2_block",
@@ -271,6 +271,10 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.b2f_attention_fp8.restype = ctypes.c_int
     lib.b2f_head_norm_rope.argtypes = [ctypes.POINTER(RopeArgs), vp]
     lib.b2f_head_norm_rope.restype = ctypes.c_int
+    lib.b2f_attn_prep.argtypes = [ctypes.POINTER(RopeArgs), ctypes.POINTER(RopeArgs), vp,
+                                  ctypes.c_longlong, vp, ctypes.c_longlong, ctypes.c_int,
+                                  ctypes.c_int, vp]
+    lib.b2f_attn_prep.restype = ctypes.c_int
     lib.b2f_fp8_to_bf16.argtypes = [vp, ctypes.c_longlong, vp, ctypes.c_longlong, ctypes.c_int,
                                     ctypes.c_int, ctypes.c_float, vp]
     lib.b2f_fp8_to_bf16.restype = ctypes.c_int

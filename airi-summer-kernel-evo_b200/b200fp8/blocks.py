@@ -313,6 +313,15 @@ class QwenBlock(_Graphable):
         self.out = torch.empty((t, self.hidden), device=device, dtype=out_dtype)
         self._init_graph()
 
+    @property
+    def launches_per_forward(self) -> int:
+        """Kernel launches of one forward: the q / k / V preparations are one launch when
+        b2f_attn_prep covers the shape (head_dim 128, head counts in four-head groups)."""
+        fused = (self.dh == 128 and self.h % 4 == 0 and self.hk % 4 == 0 and self.h <= 32
+                 and self.rot in (0, 128))
+        n = 5 if fused else 7
+        return n + (4 if self.has_mlp else 0)
+
     def flops(self) -> float:
         t, hd = self.t, self.hidden
         gemm = 2 * t * hd * self.n_cat + 2 * t * self.h * self.dh * hd
@@ -333,17 +342,25 @@ class QwenBlock(_Graphable):
         _gemm(self.n1, self.w_cat, col_scale=self.cs_cat, out=self.proj,
               out_scale=self.qs)
         _mark(marks, "qgkv_gemm")
-        ops.head_norm_rope(self.proj[:, self.q_off:], heads=h, head_dim=dh, in_scale=self.qs,
-                           out_scale=self.qs, head_stride=self.q_hstride, weight=self.q_norm,
-                           weight_offset=1.0, eps=self.eps, cos=self.cos, sin=self.sin,
-                           rotary_dim=self.rot, seq=self.seq, out=self.q)
-        ops.head_norm_rope(self.proj[:, self.k_off:], heads=hk, head_dim=dh, in_scale=self.qs,
-                           out_scale=self.qs, weight=self.k_norm, weight_offset=1.0,
-                           eps=self.eps, cos=self.cos, sin=self.sin, rotary_dim=self.rot,
-                           seq=self.seq, out=self.k)
-        _mark(marks, "qk_norm_rope")
-        _v_convert(self.proj[:, self.v_off:self.v_off + hk * dh], self.v16)
-        _mark(marks, "v_convert")
+        vsrc = self.proj[:, self.v_off:self.v_off + hk * dh]
+        fused = ops.attn_prep(
+            self.proj[:, self.q_off:], self.proj[:, self.k_off:], vsrc, q_heads=h,
+            k_heads=hk, head_dim=dh, in_scale=self.qs, out_scale=self.qs,
+            q_head_stride=self.q_hstride, q_weight=self.q_norm, k_weight=self.k_norm,
+            weight_offset=1.0, eps=self.eps, cos=self.cos, sin=self.sin,
+            rotary_dim=self.rot, seq=self.seq, q_out=self.q, k_out=self.k, v_out=self.v16)
+        if not fused:
+            ops.head_norm_rope(self.proj[:, self.q_off:], heads=h, head_dim=dh,
+                               in_scale=self.qs, out_scale=self.qs, head_stride=self.q_hstride,
+                               weight=self.q_norm, weight_offset=1.0, eps=self.eps,
+                               cos=self.cos, sin=self.sin, rotary_dim=self.rot, seq=self.seq,
+                               out=self.q)
+            ops.head_norm_rope(self.proj[:, self.k_off:], heads=hk, head_dim=dh,
+                               in_scale=self.qs, out_scale=self.qs, weight=self.k_norm,
+                               weight_offset=1.0, eps=self.eps, cos=self.cos, sin=self.sin,
+                               rotary_dim=self.rot, seq=self.seq, out=self.k)
+            _v_convert(vsrc, self.v16)
+        _mark(marks, "qkv_prep")
         ops.attention_fp8(self.q, self.k, self.v16, batch=self.batch, heads=h, kv_heads=hk,
                           head_dim=dh, causal=True, q_scale=self.qs, k_scale=self.qs,
                           v_scale=self.qs, gate=self.proj[:, self.g_off:], gate_scale=self.qs,

@@ -341,13 +341,8 @@ def attention_fp8(q: torch.Tensor, k: torch.Tensor, v_bf16: torch.Tensor, *, bat
     return ctx
 
 
-def head_norm_rope(x: torch.Tensor, *, heads: int, head_dim: int, in_scale: float,
-                   out_scale: float, head_stride: Optional[int] = None,
-                   weight: Optional[torch.Tensor] = None, weight_offset: float = 1.0,
-                   eps: float = 1e-6, cos: Optional[torch.Tensor] = None,
-                   sin: Optional[torch.Tensor] = None, rotary_dim: int = 0, seq: int = 0,
-                   out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Per-head RMSNorm (w + weight_offset) + rotate-half RoPE + e4m3 requantisation."""
+def _rope_args(x, heads, head_dim, in_scale, out_scale, head_stride, weight, weight_offset,
+               eps, cos, sin, rotary_dim, seq, out):
     _check_cuda(x, weight, cos, sin, out)
     _fp8_rows(x, "x")
     rows = x.shape[0]
@@ -364,8 +359,44 @@ def head_norm_rope(x: torch.Tensor, *, heads: int, head_dim: int, in_scale: floa
     a.weight, a.weight_offset, a.eps = _ptr(weight), weight_offset, eps
     a.cos, a.sin, a.rotary_dim, a.seq = _ptr(cos), _ptr(sin), rotary_dim, seq
     a.out, a.out_ld, a.out_scale = out.data_ptr(), out.stride(0), out_scale
+    return a, out
+
+
+def head_norm_rope(x: torch.Tensor, *, heads: int, head_dim: int, in_scale: float,
+                   out_scale: float, head_stride: Optional[int] = None,
+                   weight: Optional[torch.Tensor] = None, weight_offset: float = 1.0,
+                   eps: float = 1e-6, cos: Optional[torch.Tensor] = None,
+                   sin: Optional[torch.Tensor] = None, rotary_dim: int = 0, seq: int = 0,
+                   out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Per-head RMSNorm (w + weight_offset) + rotate-half RoPE + e4m3 requantisation."""
+    a, out = _rope_args(x, heads, head_dim, in_scale, out_scale, head_stride, weight,
+                        weight_offset, eps, cos, sin, rotary_dim, seq, out)
     check(_lib.lib().b2f_head_norm_rope(ctypes.byref(a), _stream()))
     return out
+
+
+def attn_prep(q_src: torch.Tensor, k_src: torch.Tensor, v_src: torch.Tensor, *, q_heads: int,
+              k_heads: int, head_dim: int, in_scale: float, out_scale: float,
+              q_head_stride: Optional[int] = None, q_weight=None, k_weight=None,
+              weight_offset: float = 1.0, eps: float = 1e-6, cos=None, sin=None,
+              rotary_dim: int = 0, seq: int = 0, q_out=None, k_out=None,
+              v_out: torch.Tensor = None) -> bool:
+    """q / k head norm + RoPE (as :func:`head_norm_rope`) and the e4m3 -> 16-bit V copy
+    (as :func:`fp8_to_f16` / :func:`fp8_to_bf16`, by ``v_out``'s dtype) in one launch
+    (b2f_attn_prep).  Returns False, having done nothing, for shapes that launch does not
+    cover (the caller then runs the three operations)."""
+    _check_cuda(v_src, v_out)
+    qa, q_out = _rope_args(q_src, q_heads, head_dim, in_scale, out_scale, q_head_stride,
+                           q_weight, weight_offset, eps, cos, sin, rotary_dim, seq, q_out)
+    ka, k_out = _rope_args(k_src, k_heads, head_dim, in_scale, out_scale, None, k_weight,
+                           weight_offset, eps, cos, sin, rotary_dim, seq, k_out)
+    rc = _lib.lib().b2f_attn_prep(ctypes.byref(qa), ctypes.byref(ka), v_src.data_ptr(),
+                                  v_src.stride(0), v_out.data_ptr(), v_out.stride(0),
+                                  v_src.shape[1], _DT[v_out.dtype], _stream())
+    if rc == _lib.B2F_ERR_UNSUPPORTED:
+        return False
+    check(rc)
+    return True
 
 
 def quantize_fp8(x: torch.Tensor, *, scale: Optional[float] = None,

@@ -443,6 +443,15 @@ __device__ __forceinline__ float2 ex2_poly2(float2 x) {
                      __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
 }
 
+// sigmoid of a pair, 1 / (1 + 2^(-g log2 e)): the exponential on the FMA pipe (ex2_poly2,
+// its argument clamped to <= 126 so 2^x stays finite) and one reciprocal on the exponential
+// unit instead of two exponential-unit operations per gate value.
+__device__ __forceinline__ float2 sigmoid2(float a, float b) {
+  const float2 e = ex2_poly2(make_float2(fminf(a * -1.4426950408889634f, 126.0f),
+                                         fminf(b * -1.4426950408889634f, 126.0f)));
+  return make_float2(__fdividef(1.0f, 1.0f + e.x), __fdividef(1.0f, 1.0f + e.y));
+}
+
 template <int D>
 struct Attn2Cfg {
   static constexpr int BQ = 128;
@@ -784,7 +793,7 @@ __global__ void __launch_bounds__(384, 1)
         }
         tmem_st_wait();
       };
-      float corr = 1.0f, lt;
+      float corr = 1.0f, lt, mref;
       bool rescale = false;
       {
         // Row max of S * c: 4 independent partial maxima over 3-input max.
@@ -803,49 +812,11 @@ __global__ void __launch_bounds__(384, 1)
           }
           m_used = mt;
         }
-        const float mref = (m_used == -INFINITY) ? 0.0f : m_used;
-        // P = 2^(S*c - m), stored below to the shared-memory P tile (the A operand of
-        // P.V).  Each weight is exponentiated in f32 and rounded to f16 (f16 V) or bf16
-        // (bf16 V); the row sum accumulates the f32 weights.  Masked keys hold -inf, whose
-        // weight is 0.  The 16-bit pairs overwrite the S registers they came from (pair e
-        // goes to S slot e, already consumed), which keeps the row within the register
-        // budget.
-        // Scale, offset and row sum as packed pair operations (half the issue slots of
-        // scalar FFMA / FADD: the softmax warps share the SM's issue slots with the MMA
-        // warp, and 16-bit MMAs fed late leave the tensor core idle).
-        const float2 c2 = make_float2(c, c), nm2 = make_float2(-mref, -mref);
-        float2 acc2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-#pragma unroll
-        for (int e = 0; e < BKV / 2; ++e) {
-          const float2 xv = ffma2(make_float2(__uint_as_float(sv(2 * e)),
-                                              __uint_as_float(sv(2 * e + 1))), c2, nm2);
-          // Three of every eight pairs go through the polynomial: the exponential unit (16
-          // results per clock per SM) is the softmax's bound, the FMA pipe has room.
-          float e0, e1;
-          if ((e & 7) < 3) {
-            const float2 pe = ex2_poly2(xv);
-            e0 = pe.x;
-            e1 = pe.y;
-          } else {
-            e0 = ex2_hw(xv.x);
-            e1 = ex2_hw(xv.y);
-          }
-          acc2[e & 1] = fadd2(acc2[e & 1], make_float2(e0, e1));
-          if constexpr (VF16) {
-            // f32 exponentials packed to f16 pairs: the same instruction cost as the bf16
-            // form (ex2.approx.f16x2 yields no more exponentials per clock than the f32 one
-            // on B200), with a 2^-11 instead of 2^-8 relative rounding of each weight
-            // (weights are <= 2^8 after the lazy max update, inside f16's range).
-            sv(e) = pack_f16x2(e0, e1);
-          } else {
-            // the row sum keeps the f32 weights; the P.V MMA sees them rounded to bf16
-            sv(e) = pack_bf16x2(e0, e1);
-          }
-        }
-        lt = (acc2[0].x + acc2[0].y) + (acc2[1].x + acc2[1].y);
+        mref = (m_used == -INFINITY) ? 0.0f : m_used;
       }
       // P(j-1).V has landed before P(j) overwrites the shared-memory P tile and before O is
-      // rescaled (P(j).V is released below).
+      // rescaled (P(j).V is released below).  Waiting here, before the exponentials, lets
+      // the first half of P(j) be stored while the second half is computed.
       if (j > 0) {
         ok = __all_sync(0xffffffffu,
                         mbar_wait(&pv_done[x], (j - 1) & 1, kDevTimeoutEpilogue, abort_flag));
@@ -854,15 +825,49 @@ __global__ void __launch_bounds__(384, 1)
         if (__any_sync(0xffffffffu, rescale)) rescale_o(corr);
       }
       {
-        // Row r of the P tile: sixteen 16-byte chunks of 8 keys in two 64-key blocks of
-        // 128-byte rows, swizzled (chunk c at position c ^ (r % 8) of its row), the layout
-        // of a K-major SW128 MMA operand.
+        // P = 2^(S*c - m) to the shared-memory P tile (the A operand of P.V), 64 keys at a
+        // time: row r of the tile is sixteen 16-byte chunks of 8 keys in two 64-key blocks
+        // of 128-byte rows, swizzled (chunk c at position c ^ (r % 8) of its row), the
+        // layout of a K-major SW128 MMA operand.  Each weight is exponentiated in f32 and
+        // rounded to f16 (f16 V; 2^-11 relative, the conversion is not on the exponential
+        // unit) or bf16 (bf16 V); the row sum accumulates the f32 weights.  Masked keys
+        // hold -inf, whose weight is 0.  Scale, offset and row sum are packed pair
+        // operations (half the issue slots of scalar FFMA / FADD: the softmax warps share
+        // the SM's issue slots with the MMA warp, and 16-bit MMAs fed late leave the tensor
+        // core idle).  The 16-bit pairs overwrite the S registers they came from (pair e
+        // goes to S slot e, already consumed), which keeps the row within the register
+        // budget.
+        const float2 c2 = make_float2(c, c), nm2 = make_float2(-mref, -mref);
+        float2 acc2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
         uint8_t* prow = sp + x * C::P_BYTES + r * 128;
 #pragma unroll
-        for (int c8 = 0; c8 < BKV / 8; ++c8)
-          *reinterpret_cast<uint4*>(prow + (c8 >> 3) * (BQ * 128) + (((c8 & 7) ^ (r & 7)) << 4)) =
-              make_uint4(sv(4 * c8), sv(4 * c8 + 1), sv(4 * c8 + 2), sv(4 * c8 + 3));
+        for (int hb = 0; hb < BKV / 64; ++hb) {
+#pragma unroll
+          for (int e = hb * 32; e < hb * 32 + 32; ++e) {
+            const float2 xv = ffma2(make_float2(__uint_as_float(sv(2 * e)),
+                                                __uint_as_float(sv(2 * e + 1))), c2, nm2);
+            // Three of every eight pairs go through the polynomial: the exponential unit
+            // (16 results per clock per SM) bounds the softmax, the FMA pipe has room.
+            float e0, e1;
+            if ((e & 7) < 3) {
+              const float2 pe = ex2_poly2(xv);
+              e0 = pe.x;
+              e1 = pe.y;
+            } else {
+              e0 = ex2_hw(xv.x);
+              e1 = ex2_hw(xv.y);
+            }
+            acc2[e & 1] = fadd2(acc2[e & 1], make_float2(e0, e1));
+            if constexpr (VF16) sv(e) = pack_f16x2(e0, e1);
+            else sv(e) = pack_bf16x2(e0, e1);
+          }
+#pragma unroll
+          for (int c8 = hb * 8; c8 < hb * 8 + 8; ++c8)
+            *reinterpret_cast<uint4*>(prow + hb * (BQ * 128) + (((c8 & 7) ^ (r & 7)) << 4)) =
+                make_uint4(sv(4 * c8), sv(4 * c8 + 1), sv(4 * c8 + 2), sv(4 * c8 + 3));
+        }
         fence_async_shared();  // generic-proxy writes visible to the tensor core
+        lt = (acc2[0].x + acc2[0].y) + (acc2[1].x + acc2[1].y);
       }
       l = l * corr + lt;
       tc_fence_before();
@@ -911,10 +916,12 @@ __global__ void __launch_bounds__(384, 1)
                   const float2 a = e4m3x2_to_f32x2(w4[t] & 0xFFFF);
                   const float2 bb = e4m3x2_to_f32x2(w4[t] >> 16);
                   const int u = h16 * 16 + 4 * t;
-                  v[u] *= sigmoid_fast(a.x * p.gate_scale);
-                  v[u + 1] *= sigmoid_fast(a.y * p.gate_scale);
-                  v[u + 2] *= sigmoid_fast(bb.x * p.gate_scale);
-                  v[u + 3] *= sigmoid_fast(bb.y * p.gate_scale);
+                  const float2 s01 = sigmoid2(a.x * p.gate_scale, a.y * p.gate_scale);
+                  const float2 s23 = sigmoid2(bb.x * p.gate_scale, bb.y * p.gate_scale);
+                  v[u] *= s01.x;
+                  v[u + 1] *= s01.y;
+                  v[u + 2] *= s23.x;
+                  v[u + 3] *= s23.y;
                 }
               }
             } else {

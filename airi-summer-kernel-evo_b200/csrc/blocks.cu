@@ -307,19 +307,33 @@ int b2f_qwen_block(const b2f_qwen_block_args* a, b2f_stream_t s) {
     g.g.col_scale = a->qgkv_col_scale; g.g.out_scale = qs;
     if ((rc = b2f_gemm_fp8(&g.g, s))) return rc;
   }
-  for (int which = 0; which < 2; ++which) {
-    b2f_rope_args r;
-    std::memset(&r, 0, sizeof(r));
-    r.rows = t; r.heads = which == 0 ? h : hk; r.head_dim = dh;
-    r.in = b.proj + (which == 0 ? q_off : k_off); r.in_ld = ncat;
-    r.in_head_stride = which == 0 ? q_hstride : dh; r.in_scale = qs;
-    r.weight = which == 0 ? a->q_norm_w : a->k_norm_w; r.weight_offset = 1.0f; r.eps = a->eps;
-    r.cos = a->rope_cos; r.sin = a->rope_sin; r.rotary_dim = a->rotary_dim; r.seq = a->seq;
-    r.out = which == 0 ? b.q : b.k; r.out_ld = (which == 0 ? h : hk) * dh; r.out_scale = qs;
-    if ((rc = b2f_head_norm_rope(&r, s))) return rc;
-  }
   const int vdt = v_dtype(dh);
-  if ((rc = v_convert(b.proj + v_off, ncat, b.v, t, hk * dh, vdt, s))) return rc;
+  {
+    // q / k head norm + RoPE and the V conversion: one launch when the shapes allow it
+    // (head_dim 128, four-head groups), else the three operations one by one.
+    b2f_rope_args r[2];
+    for (int which = 0; which < 2; ++which) {
+      std::memset(&r[which], 0, sizeof(r[which]));
+      r[which].rows = t; r[which].heads = which == 0 ? h : hk; r[which].head_dim = dh;
+      r[which].in = b.proj + (which == 0 ? q_off : k_off); r[which].in_ld = ncat;
+      r[which].in_head_stride = which == 0 ? q_hstride : dh; r[which].in_scale = qs;
+      r[which].weight = which == 0 ? a->q_norm_w : a->k_norm_w;
+      r[which].weight_offset = 1.0f; r[which].eps = a->eps;
+      r[which].cos = a->rope_cos; r[which].sin = a->rope_sin;
+      r[which].rotary_dim = a->rotary_dim; r[which].seq = a->seq;
+      r[which].out = which == 0 ? b.q : b.k; r[which].out_ld = (which == 0 ? h : hk) * dh;
+      r[which].out_scale = qs;
+    }
+    rc = b2f_attn_prep(&r[0], &r[1], b.proj + v_off, ncat, b.v, (long long)hk * dh, hk * dh,
+                       vdt, s);
+    if (rc == B2F_ERR_UNSUPPORTED) {
+      for (int which = 0; which < 2; ++which)
+        if ((rc = b2f_head_norm_rope(&r[which], s))) return rc;
+      if ((rc = v_convert(b.proj + v_off, ncat, b.v, t, hk * dh, vdt, s))) return rc;
+    } else if (rc) {
+      return rc;
+    }
+  }
   {
     b2f_attn_args at;
     b2f_attn_args_init(&at);

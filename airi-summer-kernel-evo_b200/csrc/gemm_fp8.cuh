@@ -592,6 +592,9 @@ __global__ void __launch_bounds__(320, 1)
     if (lane == 0) {
       // ------------------------------------------------------------ MMA issuer
       constexpr uint32_t idesc = make_idesc_f8(Cfg::BM, BN);
+      // Operand descriptors built once (stage 0); each MMA adds an immediate.
+      const uint64_t a_desc0 = make_sdesc_sw128(smem_u32(smem_a), 1024);
+      const uint64_t b_desc0 = make_sdesc_sw128(smem_u32(smem_b), 1024);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
@@ -610,14 +613,13 @@ __global__ void __launch_bounds__(320, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem_a + stage * Cfg::A_BYTES);
-          const uint32_t b_addr = smem_u32(smem_b + stage * Cfg::B_BYTES);
+          // descriptor = stage-0 descriptor + (byte offset / 16) in the address field
+          const uint64_t ad0 = a_desc0 + uint64_t(stage * (Cfg::A_BYTES >> 4));
+          const uint64_t bd0 = b_desc0 + uint64_t(stage * (Cfg::B_BYTES >> 4));
+          mma_f8(d_tmem, ad0, bd0, idesc, kb != kb0 ? 1u : 0u);
 #pragma unroll
-          for (int k = 0; k < Cfg::BK / 32; ++k) {
-            const uint64_t ad = make_sdesc_sw128(a_addr + k * 32, 1024);
-            const uint64_t bd = make_sdesc_sw128(b_addr + k * 32, 1024);
-            mma_f8(d_tmem, ad, bd, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
-          }
+          for (int k = 1; k < Cfg::BK / 32; ++k)
+            mma_f8(d_tmem, ad0 + 2 * k, bd0 + 2 * k, idesc, 1u);
           mma_commit(&empty_bar[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
@@ -917,6 +919,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
     if (lane == 0 && rank == 0) {
       // ------------------------------------------------------------ MMA issuer (leader)
       constexpr uint32_t idesc = make_idesc_f8(2 * Cfg::BM, BN);
+      const uint64_t a_desc0 = make_sdesc_sw128(smem_u32(smem_a), 1024);
+      const uint64_t b_desc0 = make_sdesc_sw128(smem_u32(smem_b), 1024);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
@@ -933,14 +937,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem_a + stage * Cfg::A_BYTES);
-          const uint32_t b_addr = smem_u32(smem_b + stage * Cfg::B_BYTES);
+          const uint64_t ad0 = a_desc0 + uint64_t(stage * (Cfg::A_BYTES >> 4));
+          const uint64_t bd0 = b_desc0 + uint64_t(stage * (Cfg::B_BYTES >> 4));
+          mma_f8_pair(d_tmem, ad0, bd0, idesc, kb != 0);
 #pragma unroll
-          for (int k = 0; k < Cfg::BK / 32; ++k) {
-            const uint64_t ad = make_sdesc_sw128(a_addr + k * 32, 1024);
-            const uint64_t bd = make_sdesc_sw128(b_addr + k * 32, 1024);
-            mma_f8_pair(d_tmem, ad, bd, idesc, (kb | k) != 0);
-          }
+          for (int k = 1; k < Cfg::BK / 32; ++k)
+            mma_f8_pair(d_tmem, ad0 + 2 * k, bd0 + 2 * k, idesc, 1u);
           mma_commit_pair(&empty_bar[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }

@@ -150,10 +150,7 @@ __global__ void __launch_bounds__(256) head_norm_rope_kernel(const RopeParams p)
 // (element i +- 64) sits in lane l ^ 4.  Same formulas as head_norm_rope_kernel (the
 // f32 sum of squares runs in another order).
 template <int G>
-__global__ void __launch_bounds__(256) head_norm_rope128_kernel(const RopeParams p) {
-  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (t >= p.rows) return;
+__device__ __forceinline__ void head_norm_rope128_token(const RopeParams& p, int t, int lane) {
   const int sub = lane & 7;
   const int hg = lane >> 3;
   const int i0 = sub * 16;
@@ -230,11 +227,17 @@ __global__ void __launch_bounds__(256) head_norm_rope128_kernel(const RopeParams
   }
 }
 
+template <int G>
+__global__ void __launch_bounds__(256) head_norm_rope128_kernel(const RopeParams p) {
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (t < p.rows) head_norm_rope128_token<G>(p, t, threadIdx.x & 31);
+}
+
 template <bool F16>
-__global__ void fp8_to_bf16_kernel(const uint8_t* in, long long in_ld, uint16_t* out,
-                                   long long out_ld, int rows, int cols, float scale) {
+__device__ __forceinline__ void fp8_convert8(const uint8_t* in, long long in_ld, uint16_t* out,
+                                             long long out_ld, int rows, int cols, float scale,
+                                             long long i) {
   const int vec_per_row = cols / 8;
-  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (long long)rows * vec_per_row) return;
   const int r = int(i / vec_per_row);
   const int c = int(i - (long long)r * vec_per_row) * 8;
@@ -254,6 +257,44 @@ __global__ void fp8_to_bf16_kernel(const uint8_t* in, long long in_ld, uint16_t*
     o.w = pack_bf16x2(d.x * scale, d.y * scale);
   }
   *reinterpret_cast<uint4*>(out + (long long)r * out_ld + c) = o;
+}
+
+template <bool F16>
+__global__ void fp8_to_bf16_kernel(const uint8_t* in, long long in_ld, uint16_t* out,
+                                   long long out_ld, int rows, int cols, float scale) {
+  fp8_convert8<F16>(in, in_ld, out, out_ld, rows, cols, scale,
+                    (long long)blockIdx.x * blockDim.x + threadIdx.x);
+}
+
+// The three operand preparations of a gated GQA block in one launch: blocks [0, nq) run
+// the q head norm + RoPE (GQ four-head groups per token), [nq, nq + nk) the k one (GK
+// groups), the rest convert V to f16 / bf16.  One launch instead of three: each of them
+// alone is too short to fill the GPU past its ramp and tail.
+struct VConvertParams {
+  const uint8_t* in;
+  long long in_ld;
+  uint16_t* out;
+  long long out_ld;
+  int rows, cols;
+  int f16;
+};
+
+template <int GQ, int GK>
+__global__ void __launch_bounds__(256, 2) attn_prep_kernel(const RopeParams q, const RopeParams k,
+                                                        const VConvertParams v, int nq, int nk) {
+  const int b = blockIdx.x;
+  const int lane = threadIdx.x & 31;
+  if (b < nq) {
+    const int t = b * 8 + (threadIdx.x >> 5);
+    if (t < q.rows) head_norm_rope128_token<GQ>(q, t, lane);
+  } else if (b < nq + nk) {
+    const int t = (b - nq) * 8 + (threadIdx.x >> 5);
+    if (t < k.rows) head_norm_rope128_token<GK>(k, t, lane);
+  } else {
+    const long long i = (long long)(b - nq - nk) * blockDim.x + threadIdx.x;
+    if (v.f16) fp8_convert8<true>(v.in, v.in_ld, v.out, v.out_ld, v.rows, v.cols, 1.0f, i);
+    else fp8_convert8<false>(v.in, v.in_ld, v.out, v.out_ld, v.rows, v.cols, 1.0f, i);
+  }
 }
 
 // out = e4m3( silu(gate * in_scale) * (up * in_scale) / out_scale ), 8 elements per thread.
@@ -309,8 +350,12 @@ int b2f_swiglu_fp8(const void* gate, long long gate_ld, const void* up, long lon
   return B2F_OK;
 }
 
-int b2f_head_norm_rope(const b2f_rope_args* a, b2f_stream_t stream) {
-  using namespace b2f;
+}  // extern "C"
+
+namespace b2f {
+namespace {
+// Validates a b2f_head_norm_rope argument block and fills the kernel parameters.
+int rope_params(const b2f_rope_args* a, RopeParams& p) {
   if (a == nullptr) return fail(B2F_ERR_ARG, "head_norm_rope: null args");
   if (a->rows <= 0 || a->heads <= 0) return fail(B2F_ERR_ARG, "head_norm_rope: empty shape");
   const int d = a->head_dim;
@@ -329,7 +374,6 @@ int b2f_head_norm_rope(const b2f_rope_args* a, b2f_stream_t stream) {
       ((uintptr_t)a->out % al))
     return fail(B2F_ERR_ARG, "head_norm_rope: pointers and pitches must be multiples of head_dim/32");
   if (!(a->out_scale > 0.f)) return fail(B2F_ERR_ARG, "head_norm_rope: out_scale must be > 0");
-  RopeParams p;
   p.in = reinterpret_cast<const uint8_t*>(a->in);
   p.in_ld = a->in_ld; p.in_hstride = a->in_head_stride; p.in_scale = a->in_scale;
   p.weight = a->weight; p.w_offset = a->weight_offset; p.eps = a->eps;
@@ -342,16 +386,35 @@ int b2f_head_norm_rope(const b2f_rope_args* a, b2f_stream_t stream) {
       (a->cos != nullptr && ((reinterpret_cast<uintptr_t>(a->cos) & 7) ||
                              (reinterpret_cast<uintptr_t>(a->sin) & 7) || (a->rotary_dim % 2))))
     return fail(B2F_ERR_ARG, "head_norm_rope: weight / cos / sin must be 8-byte aligned");
+  return B2F_OK;
+}
+
+bool al16p(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; }
+
+// The 128-wide layout (four heads per 16-byte lane load) applies: head_dim 128, heads a
+// multiple of 4, full-width or no RoPE, 16-byte aligned rows, heads and tables.
+bool rope128_ok(const b2f_rope_args* a) {
+  return a->head_dim == 128 && a->heads % 4 == 0 && a->heads <= 32 &&
+         (a->cos == nullptr || a->rotary_dim == 128) && a->in_ld % 16 == 0 &&
+         a->in_head_stride % 16 == 0 && a->out_ld % 16 == 0 && al16p(a->in) &&
+         al16p(a->out) && (a->weight == nullptr || al16p(a->weight)) &&
+         (a->cos == nullptr || (al16p(a->cos) && al16p(a->sin)));
+}
+}  // namespace
+}  // namespace b2f
+
+extern "C" {
+
+int b2f_head_norm_rope(const b2f_rope_args* a, b2f_stream_t stream) {
+  using namespace b2f;
+  RopeParams p;
+  if (int rc = rope_params(a, p)) return rc;
+  const int d = a->head_dim;
   const int grid = (a->rows + 7) / 8;  // one warp per token
   cudaStream_t s = (cudaStream_t)stream;
-  auto al16p = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
   // 4-head groups pay off from 16 heads (measured [8192 tokens]: 32 heads 25.6 -> 21.1 us;
   // 8 heads 8.0 -> 11.8 us, the extra registers costing more than the wider loads gain)
-  const bool fast128 = d == 128 && a->heads % 4 == 0 && a->heads >= 16 && a->heads <= 32 &&
-                       (a->cos == nullptr || a->rotary_dim == 128) && a->in_ld % 16 == 0 &&
-                       a->in_head_stride % 16 == 0 && a->out_ld % 16 == 0 && al16p(a->in) &&
-                       al16p(a->out) && (a->weight == nullptr || al16p(a->weight)) &&
-                       (a->cos == nullptr || (al16p(a->cos) && al16p(a->sin)));
+  const bool fast128 = rope128_ok(a) && a->heads >= 16;
   if (fast128) {
     switch (a->heads / 4) {
       case 4: head_norm_rope128_kernel<4><<<grid, 256, 0, s>>>(p); break;
@@ -365,6 +428,44 @@ int b2f_head_norm_rope(const b2f_rope_args* a, b2f_stream_t stream) {
   else head_norm_rope_kernel<256><<<grid, 256, 0, s>>>(p);
   B2F_CUDA_TRY(cudaGetLastError());
   return B2F_OK;
+}
+
+int b2f_attn_prep(const b2f_rope_args* q, const b2f_rope_args* k, const void* v_in,
+                  long long v_in_ld, void* v_out, long long v_out_ld, int v_cols, int v_dtype,
+                  b2f_stream_t stream) {
+  using namespace b2f;
+  if (q == nullptr || k == nullptr) return fail(B2F_ERR_ARG, "attn_prep: null args");
+  RopeParams pq, pk;
+  if (int rc = rope_params(q, pq)) return rc;
+  if (int rc = rope_params(k, pk)) return rc;
+  if (!rope128_ok(q) || !rope128_ok(k) || q->rows != k->rows)
+    return fail(B2F_ERR_UNSUPPORTED,
+                "attn_prep: q and k need head_dim 128, heads a multiple of 4 (<= 32), full or "
+                "no RoPE, 16-byte aligned rows, and the same token count");
+  if (v_in == nullptr || v_out == nullptr || v_cols <= 0 || v_cols % 8 || v_in_ld % 8 ||
+      v_out_ld % 8 || ((uintptr_t)v_in & 7) || ((uintptr_t)v_out & 15) ||
+      (v_dtype != B2F_DTYPE_F16 && v_dtype != B2F_DTYPE_BF16))
+    return fail(B2F_ERR_ARG, "attn_prep: V must be e4m3 -> f16 / bf16, cols and pitches "
+                             "multiples of 8, aligned");
+  VConvertParams pv{reinterpret_cast<const uint8_t*>(v_in), v_in_ld,
+                    reinterpret_cast<uint16_t*>(v_out), v_out_ld, q->rows, v_cols,
+                    v_dtype == B2F_DTYPE_F16 ? 1 : 0};
+  const int nq = (q->rows + 7) / 8, nk = (k->rows + 7) / 8;
+  const long long nv = ((long long)q->rows * (v_cols / 8) + 255) / 256;
+  const int grid = (int)(nq + nk + nv);
+  cudaStream_t s = (cudaStream_t)stream;
+  const int gq = q->heads / 4, gk = k->heads / 4;
+#define B2F_PREP(GQ, GK)                                                        \
+  if (gq == GQ && gk == GK) {                                                   \
+    attn_prep_kernel<GQ, GK><<<grid, 256, 0, s>>>(pq, pk, pv, nq, nk);          \
+    B2F_CUDA_TRY(cudaGetLastError());                                           \
+    return B2F_OK;                                                              \
+  }
+  B2F_PREP(8, 2) B2F_PREP(4, 1) B2F_PREP(8, 1) B2F_PREP(4, 2) B2F_PREP(2, 1) B2F_PREP(8, 8)
+  B2F_PREP(4, 4)
+#undef B2F_PREP
+  return fail(B2F_ERR_UNSUPPORTED, "attn_prep: head counts (q, k) not in the compiled set "
+                                   "{(32,8), (16,4), (32,4), (16,8), (8,4), (32,32), (16,16)}");
 }
 
 static int fp8_convert(const void* in, long long in_ld, void* out, long long out_ld, int rows,

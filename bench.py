@@ -13,7 +13,8 @@ other BASELINE config measured in the same run, each with its roofline, e2e, par
 of the timed output and (N=1) CPU baseline:
   N=1: GEMM+bias+ReLU 128x8192x8192; square GEMM n = 4096 / 8192 / 16384
        (configs[1]); residual RMSNorm + amax quant 16384x4096; GPT-2 block
-       B8 x S1024; Qwen block with pure N-way heads (N>1 only).
+       B8 x S1024; the reference tasks' long-row LayerNorm (level1_40,
+       [16 x 4194304]) and gated-residual GEMM (2048 x 4096 x 4096).
   N>1: the same global problems split over the ranks (strong scaling): GEMM 8192^3 along N
        (no communication), norm by rows (one f32 MAX all-reduce), GPT-2 by sequences (no
        communication), Qwen with every rank in one head group (tp = N).
@@ -458,6 +459,188 @@ class NormWorkload:
                           f"on CPU, {t:.2f} s"}
 
 
+class LayerNormRowsWorkload:
+    """The reference task level1_40 (tasks/level1_40_layer_norm_fp8): LayerNorm over each of
+    16 rows of 4,194,304 e4m3 values read at 1/448, eps 1e-5, f32 output
+    (b2f_layer_norm_rows: every row split over 64 CTAs).  Inputs U(0,1) * 448 as the task's
+    evaluator draws them, from a CPU generator."""
+
+    unit = "GB/s"
+    bound = "hbm"
+    scaling = "strong"
+    name = "layer_norm_rows_16x4194304"
+    launches = 2
+
+    def __init__(self, rank: int, world: int = 1, rows: int = 16, cols: int = 64 * 256 * 256):
+        g = torch.Generator("cpu").manual_seed(20260726)
+        self.world, self.rank = world, rank
+        self.rows, self.cols = rows, cols
+        self.x_cpu = (torch.rand((rows, cols), generator=g) * 448.0).to(torch.float8_e4m3fn)
+        self.x = self.x_cpu.cuda()
+        self.out = torch.empty((rows, cols), device="cuda")
+        self.work = float(rows * cols * (1 + 4))
+        self.algo_bytes = self.work
+
+    def config(self):
+        return {"workload": f"layer norm [{self.rows} x {self.cols}] e4m3 (1/448) -> f32",
+                "rows": self.rows, "cols": self.cols, "eps": 1e-5,
+                "l2": "output 268 MB > 126 MB L2 (the 67 MB input is re-read from L2 by "
+                      "the second pass)"}
+
+    def parallelism(self):
+        return "single GPU"
+
+    def step(self):
+        from b200fp8 import ops
+        ops.layer_norm_rows(self.x, out=self.out, x_scale=1 / 448.0, eps=1e-5)
+        return 2
+
+    def roofline(self, per_launch_ms):
+        return ("ln_rows_stats_kernel + ln_rows_apply_kernel", self.algo_bytes / 1e9, "GB/s",
+                HBM, f"{PEAKS['basis']} HBM copy bandwidth")
+
+    def parity(self):
+        from oracle import norm as onorm
+        ref = onorm.layer_norm_rows(self.x_cpu.float() / 448.0, 1e-5)
+        err = float((self.out.cpu() - ref).abs().max())
+        return {"status": "pass" if err <= 0.01 else "fail", "max_abs_err": err,
+                "bar": "0.01 (task level1_40's full_max_absolute_error_vs_torch)",
+                "check": "every element of the timed output vs the f64 oracle"}
+
+    def e2e_setup(self):
+        self.hx = self.x_cpu.view(torch.uint8).pin_memory()
+        self.ho = torch.empty((self.rows, self.cols)).pin_memory()
+        self.sx = [self.x, torch.empty_like(self.x)]
+        self.so = [self.out, torch.empty_like(self.out)]
+
+    def e2e_h2d(self, slot):
+        self.sx[slot].view(torch.uint8).copy_(self.hx, non_blocking=True)
+
+    def e2e_compute(self, slot):
+        from b200fp8 import ops
+        ops.layer_norm_rows(self.sx[slot], out=self.so[slot], x_scale=1 / 448.0, eps=1e-5)
+
+    def e2e_d2h(self, slot):
+        self.ho.copy_(self.so[slot], non_blocking=True)
+
+    def e2e_bytes(self):
+        return self.rows * self.cols, self.rows * self.cols * 4
+
+    def e2e_release(self):
+        del self.sx, self.so
+
+    def cpu_sample(self, target_s: float):
+        from oracle import norm as onorm
+        threads = _threads()
+        torch.set_num_threads(threads)
+        t0 = time.perf_counter()
+        onorm.layer_norm_rows(self.x_cpu[:2].float() / 448.0, 1e-5)
+        t = time.perf_counter() - t0
+        return {"value": 2 * self.cols * 5 / t / 1e9, "unit": "GB/s", "cores": threads,
+                "kind": "port", "sample": f"2 of {self.rows} rows through the f64 oracle, {t:.2f} s"}
+
+
+class GatedGemmWorkload:
+    """The gated-residual GEMM of cute_kernels/fused_gemm_gated_residual_fp8 (2048 x 4096 x
+    4096, out = A.B^T * scale * gate + residual, f32 gate / residual / output), inputs drawn
+    as that submission draws them, from a CPU generator."""
+
+    unit = "TFLOP/s"
+    bound = "tensor"
+    scaling = "strong"
+    name = "gemm_gated_residual_fp8_2048x4096x4096"
+    launches = 1
+
+    def __init__(self, rank: int, world: int = 1, m=2048, n=4096, k=4096):
+        g = torch.Generator("cpu").manual_seed(20260731)
+        bound = k ** -0.5
+        a = torch.empty((m, k)).uniform_(-1.0, 1.0, generator=g)
+        b = torch.empty((n, k)).uniform_(-bound, bound, generator=g)
+        self.gate_cpu = torch.randn((m, n), generator=g)
+        self.res_cpu = torch.randn((m, n), generator=g)
+        self.a_cpu, self.b_cpu = (a * 448.0).to(torch.float8_e4m3fn), (b * (448.0 / bound)).to(torch.float8_e4m3fn)
+        self.sa, self.sb = 1 / 448.0, bound / 448.0
+        self.m, self.n, self.k = m, n, k
+        self.a, self.b = self.a_cpu.cuda(), self.b_cpu.cuda()
+        self.gate, self.res = self.gate_cpu.cuda(), self.res_cpu.cuda()
+        self.out = torch.empty((m, n), device="cuda")
+        self.work = 2.0 * m * n * k
+        self.world, self.rank = world, rank
+
+    def config(self):
+        return {"workload": f"gated-residual GEMM M={self.m} N={self.n} K={self.k} e4m3 -> f32",
+                "M": self.m, "N": self.n, "K": self.k,
+                "l2": "A, B, gate, residual and output: 109 MB per call, about the L2 size"}
+
+    def parallelism(self):
+        return "single GPU"
+
+    def step(self):
+        from b200fp8 import ops
+        ops.gemm_fp8(self.a, self.b, scale_a=self.sa, scale_b=self.sb, gate=self.gate,
+                     residual=self.res, out=self.out, out_dtype=torch.float32)
+        return 1
+
+    def roofline(self, per_launch_ms):
+        return ("gemm_fp8 (gate + residual epilogue)", self.work / 1e12, "TFLOP/s", FP8_PEAK,
+                f"2 x {PEAKS['basis']} cuBLAS bf16 burst ({BF16_PEAK} TFLOP/s)")
+
+    def parity(self):
+        from oracle import gemm as og
+        rows = [0, 1, 511, 1024, 2047]
+        ref = og.gemm_epilogue(self.a_cpu[rows], self.b_cpu, self.sa, self.sb,
+                               gate=self.gate_cpu[rows], residual=self.res_cpu[rows])
+        err = float((self.out[rows].cpu() - ref).abs().max())
+        return {"status": "pass" if err <= 0.002 else "fail", "max_abs_err": err,
+                "bar": "0.002 (the submission's own check)",
+                "check": "5 rows x all columns of the timed output vs the f64 oracle"}
+
+    def e2e_setup(self):
+        self.ha = self.a_cpu.view(torch.uint8).pin_memory()
+        self.hb = self.b_cpu.view(torch.uint8).pin_memory()
+        self.hg, self.hr = self.gate_cpu.pin_memory(), self.res_cpu.pin_memory()
+        self.ho = torch.empty((self.m, self.n)).pin_memory()
+        self.s = [[torch.empty_like(t) for t in (self.a, self.b, self.gate, self.res, self.out)]
+                  for _ in range(2)]
+
+    def e2e_h2d(self, slot):
+        a, b, gt, r, _ = self.s[slot]
+        a.view(torch.uint8).copy_(self.ha, non_blocking=True)
+        b.view(torch.uint8).copy_(self.hb, non_blocking=True)
+        gt.copy_(self.hg, non_blocking=True)
+        r.copy_(self.hr, non_blocking=True)
+
+    def e2e_compute(self, slot):
+        from b200fp8 import ops
+        a, b, gt, r, o = self.s[slot]
+        ops.gemm_fp8(a, b, scale_a=self.sa, scale_b=self.sb, gate=gt, residual=r, out=o,
+                     out_dtype=torch.float32)
+
+    def e2e_d2h(self, slot):
+        self.ho.copy_(self.s[slot][4], non_blocking=True)
+
+    def e2e_bytes(self):
+        mk, nk, mn = self.m * self.k, self.n * self.k, self.m * self.n
+        return mk + nk + 8 * mn, 4 * mn
+
+    def e2e_release(self):
+        del self.s
+
+    def cpu_sample(self, target_s: float):
+        from oracle import gemm as og
+        threads = _threads()
+        torch.set_num_threads(threads)
+        rows = 256
+        t0 = time.perf_counter()
+        v = og.cpu_fast_scaled_mm(self.a_cpu[:rows], self.b_cpu, self.sa, self.sb)
+        v = v * self.gate_cpu[:rows] + self.res_cpu[:rows]
+        t = time.perf_counter() - t0
+        return {"value": 2.0 * rows * self.n * self.k / t / 1e12, "unit": "TFLOP/s",
+                "cores": threads, "kind": "port",
+                "sample": f"{rows} of {self.m} rows, f32 dequantise + torch.matmul + gate + "
+                          f"residual on CPU, {t:.2f} s"}
+
+
 def _nq(shape, g, std=0.02):
     w = torch.randn(shape, generator=g) * std
     s = float(w.abs().max()) / 448.0
@@ -523,6 +706,7 @@ def _stage_model(kind, blk):
     return {
         "in_norm": (0.0, t * hid * 3.0, FP8_PEAK),
         "qgkv_gemm": (2.0 * t * hid * nc, t * hid + nc * hid + t * nc + 0.0, FP8_PEAK),
+        "qkv_prep": (0.0, 2.0 * t * (h + hk) * dh + 3.0 * t * hk * dh, FP8_PEAK),
         "qk_norm_rope": (0.0, 2.0 * t * (h + hk) * dh, FP8_PEAK),
         "v_convert": (0.0, 3.0 * t * hk * dh, FP8_PEAK),
         "attention": (2.0 * b * h * s * s * dh, t * dh * (3.0 * h + 4.0 * hk), ATTN_PEAK),
@@ -556,7 +740,6 @@ class BlockWorkload:
             self.dp, self.tp = sharding.plan_block_parallel(world, self.batch, 32, 8, tp=tp)
             self.name = "qwen_gated_attention_block_fp8_b4_s2048" + (
                 f"_heads_tp{self.tp}" if tp else "")
-            self.launches = 7
         if world > 1:
             d, self.tp_rank, self.group = sharding.tp_groups(world, self.tp)
         else:
@@ -578,6 +761,8 @@ class BlockWorkload:
         else:
             self.blk = blocks.QwenBlock(self.w, **kw)
             self.local = self.blk
+        if kind != "gpt2":
+            self.launches = self.local.launches_per_forward
         self.x = self.x_cpu.cuda()
         self.blk.capture(self.x)
         self.blk.graph_input.copy_(self.x)
@@ -717,6 +902,10 @@ def make_workload(name: str, rank: int, world: int = 1, tp=None, n: int = 8192):
         return BlockWorkload(name, rank, world, tp)
     if name == "qwen_heads":
         return BlockWorkload("qwen", rank, world, tp=world)
+    if name == "layer_norm_rows":
+        return LayerNormRowsWorkload(rank, world)
+    if name == "gated_gemm":
+        return GatedGemmWorkload(rank, world)
     raise SystemExit(f"unknown workload {name}")
 
 
@@ -967,7 +1156,9 @@ def run_ours(args):
             plan += [(("gemm", n), None, side_soak, args.steps, side_cpu)
                      for n in (4096, 8192, 16384)]
             plan += [("norm", None, side_soak, args.steps, side_cpu),
-                     ("gpt2", None, side_soak, args.steps, side_cpu)]
+                     ("gpt2", None, side_soak, args.steps, side_cpu),
+                     ("layer_norm_rows", None, side_soak, args.steps, side_cpu),
+                     ("gated_gemm", None, side_soak, args.steps, side_cpu)]
         else:
             plan += [("qwen_heads", None, side_soak, args.steps, 0),
                      (("gemm", 8192), None, side_soak, args.steps, 0),

@@ -347,6 +347,17 @@ typedef struct b2f_rope_args {
 
 int b2f_head_norm_rope(const b2f_rope_args* args, b2f_stream_t stream);
 
+/* The three operand preparations of a gated GQA attention in one launch: q and k as
+ * b2f_head_norm_rope (head_dim 128, heads a multiple of 4, full or no RoPE, 16-byte aligned
+ * rows; the same token count) and V [q->rows, v_cols] e4m3 -> f16 or bf16 (v_dtype,
+ * exact).  B2F_ERR_UNSUPPORTED for other shapes (call the three operations separately).
+ * Replaces: the q / k normalisation, RoPE and V requantisation steps of
+ *   qwen35_full_attention_block (tasks/model_qwen35_4b_full_attention_block_fp8/starter.py:
+ *   365-376), fused into one launch. */
+int b2f_attn_prep(const b2f_rope_args* q, const b2f_rope_args* k, const void* v_in,
+                  long long v_in_ld, void* v_out, long long v_out_ld, int v_cols, int v_dtype,
+                  b2f_stream_t stream);
+
 /* out (bf16) = in (e4m3 bytes) * scale, [rows, cols] with row pitches in elements.
  * Produces the bf16 V operand of b2f_attention_fp8 (exact: bf16 holds every e4m3 value). */
 int b2f_fp8_to_bf16(const void* in, long long in_ld, void* out, long long out_ld, int rows,

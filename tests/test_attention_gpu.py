@@ -205,3 +205,38 @@ def test_fp8_to_bf16_exact():
     out = _ops().fp8_to_bf16(x.cuda(), scale=1 / 64.0)
     torch.cuda.synchronize()
     assert torch.equal(out.cpu(), (x.float() / 64.0).to(torch.bfloat16))
+
+
+@pytest.mark.parametrize("hq,hkv", [(32, 8), (16, 4)])
+def test_attn_prep_one_launch_matches_separate_ops(hq, hkv):
+    """b2f_attn_prep (q / k head norm + RoPE and the V copy in one launch) against the
+    oracle (q, k within one e4m3 code, as test_head_norm_rope) and the exact V image."""
+    t, seq, d = 512, 256, 128
+    g = gen(11 + hq)
+    s = 1 / 64.0
+    ncat = (2 * hq + 2 * hkv) * d
+    proj = _e4m3(torch.randn((t, ncat), generator=g) / s)
+    wq = torch.randn((d,), generator=g) * 0.02
+    wk = torch.randn((d,), generator=g) * 0.02
+    cos, sin = oatt.rope_tables(seq, d, 1e6, batch=t // seq)
+    q_src = proj[:, :hq * d].float().view(t, hq, d) * s
+    k_src = proj[:, 2 * hq * d:(2 * hq + hkv) * d].float().view(t, hkv, d) * s
+    q_ref = (oatt.head_rmsnorm_rope(q_src, wq, cos, sin, d).reshape(t, hq * d) / s).to(torch.float8_e4m3fn)
+    k_ref = (oatt.head_rmsnorm_rope(k_src, wk, cos, sin, d).reshape(t, hkv * d) / s).to(torch.float8_e4m3fn)
+    ops = _ops()
+    pd = proj.cuda()
+    qo = torch.empty((t, hq * d), dtype=torch.float8_e4m3fn, device="cuda")
+    ko = torch.empty((t, hkv * d), dtype=torch.float8_e4m3fn, device="cuda")
+    vo = torch.empty((t, hkv * d), dtype=torch.float16, device="cuda")
+    tab = lambda z: z[:seq].contiguous().cuda()  # noqa: E731
+    ok = ops.attn_prep(pd[:, :], pd[:, 2 * hq * d:], pd[:, (2 * hq + hkv) * d:],
+                       q_heads=hq, k_heads=hkv, head_dim=d, in_scale=s, out_scale=s,
+                       q_weight=wq.cuda(), k_weight=wk.cuda(), cos=tab(cos), sin=tab(sin),
+                       rotary_dim=d, seq=seq, q_out=qo, k_out=ko, v_out=vo)
+    torch.cuda.synchronize()
+    assert ok
+    for got, ref in ((qo, q_ref), (ko, k_ref)):
+        diff = e4m3_ulp_diff(got.cpu(), ref)
+        assert int(diff.max()) <= 1 and float((diff > 0).float().mean()) < 0.01
+    v_ref = proj[:, (2 * hq + hkv) * d:].float().to(torch.float16)
+    assert torch.equal(vo.cpu(), v_ref)
