@@ -196,6 +196,23 @@ class RopeArgs(ctypes.Structure):
     ]
 
 
+class HeadPrepArgs(ctypes.Structure):
+    """Mirror of ``b2f_head_prep_args`` (include/b200fp8.h)."""
+
+    _fields_ = [
+        ("q_off", ctypes.c_int), ("q_head_stride", ctypes.c_int), ("q_heads", ctypes.c_int),
+        ("k_off", ctypes.c_int), ("k_heads", ctypes.c_int),
+        ("v_off", ctypes.c_int), ("v_heads", ctypes.c_int),
+        ("q_out", ctypes.c_void_p), ("q_ld", ctypes.c_longlong),
+        ("k_out", ctypes.c_void_p), ("k_ld", ctypes.c_longlong),
+        ("v_out", ctypes.c_void_p), ("v_ld", ctypes.c_longlong), ("v_dtype", ctypes.c_int),
+        ("q_norm_w", ctypes.c_void_p), ("k_norm_w", ctypes.c_void_p),
+        ("weight_offset", ctypes.c_float), ("eps", ctypes.c_float),
+        ("rope_cos", ctypes.c_void_p), ("rope_sin", ctypes.c_void_p), ("seq", ctypes.c_int),
+        ("out_scale", ctypes.c_float),
+    ]
+
+
 class Op(ctypes.Structure):
     """Mirror of ``b2f_op``."""
 
@@ -211,7 +228,7 @@ class Op(ctypes.Structure):
 EXPORTED_SYMBOLS = (
     "b2f_version", "b2f_last_error", "b2f_num_sms", "b2f_status_read",
     "b2f_debug_bounded_wait", "b2f_gemm_args_init", "b2f_gemm_fp8", "b2f_gemm_pair_capacity",
-    "b2f_gemm_workspace_bytes", "b2f_gemm_fp8_static",
+    "b2f_gemm_workspace_bytes", "b2f_gemm_fp8_static", "b2f_gemm_fp8_head_prep",
     "b2f_norm_args_init", "b2f_norm_quant", "b2f_norm_plan", "b2f_attn_args_init", "b2f_attention_fp8",
     "b2f_head_norm_rope", "b2f_attn_prep", "b2f_fp8_to_bf16", "b2f_fp8_to_f16", "b2f_swiglu_fp8",
     "b2f_quant_args_init", "b2f_quantize_fp8",
@@ -239,6 +256,8 @@ def _declare(lib: ctypes.CDLL) -> None:
     lib.b2f_gemm_fp8.restype = ctypes.c_int
     lib.b2f_gemm_pair_capacity.restype = ctypes.c_int
     lib.b2f_gemm_fp8_static.argtypes = [ctypes.POINTER(GemmArgs), vp]
+    lib.b2f_gemm_fp8_head_prep.argtypes = [ctypes.POINTER(GemmArgs), ctypes.POINTER(HeadPrepArgs), vp]
+    lib.b2f_gemm_fp8_head_prep.restype = ctypes.c_int
     lib.b2f_gemm_fp8_static.restype = ctypes.c_int
     lib.b2f_gemm_workspace_bytes.argtypes = [ctypes.c_int, ctypes.c_int]
     lib.b2f_gemm_workspace_bytes.restype = ctypes.c_longlong

@@ -134,7 +134,6 @@ class _Graphable:
 
 
 class GPT2Block(_Graphable):
-    launches_per_forward = 8
 
     def __init__(self, w, *, batch: int, seq: int, residual_dtype=torch.float32,
                  out_dtype=torch.float32, device="cuda", causal: bool = True,
@@ -174,7 +173,10 @@ class GPT2Block(_Graphable):
             self.sin = _dev(rope_sin[:seq], device, f32)
             self.q_rot = torch.empty((t, d), device=device, dtype=_E4M3)
             self.k_rot = torch.empty((t, d), device=device, dtype=_E4M3)
-            self.launches_per_forward = 10
+        # LN1, QKV GEMM (+ the V copy when d is a multiple of 128, else a separate launch),
+        # [q / k RoPE], attention, out GEMM, LN2, FC GEMM, proj GEMM
+        self.launches_per_forward = (7 if d % 128 == 0 and t >= 128 else 8) + \
+            (2 if self.rope else 0)
         self._init_graph()
 
     def flops(self) -> float:
@@ -192,11 +194,18 @@ class GPT2Block(_Graphable):
         ops.norm_quant(hidden, self.ln1_w, kind="layer", bias=self.ln1_b, eps=self.eps,
                        x_scale=hidden_scale, q_out=self.n1, q_scale=self.ns)
         _mark(marks, "ln1")
-        _gemm(self.n1, self.qkv_w, scale_a=self.ns, scale_b=self.qkv_s, bias=self.qkv_b,
-              out=self.qkv, out_scale=self.qs)
-        _mark(marks, "qkv_gemm")
-        _v_convert(self.qkv[:, 2 * d:], self.v16)
-        _mark(marks, "v_convert")
+        if d % 128 == 0 and self.t >= 128 and ops.gemm_fp8_head_prep(
+                self.n1, self.qkv_w, scale_a=self.ns, scale_b=self.qkv_s, bias=self.qkv_b,
+                out=self.qkv, out_scale=self.qs, q_out=None, k_out=None, v_out=self.v16,
+                q_off=0, q_heads=0, k_off=0, k_heads=0, v_off=2 * d, v_heads=d // 128):
+            # the 16-bit V image leaves the QKV GEMM's epilogue directly
+            _mark(marks, "qkv_gemm_v")
+        else:
+            _gemm(self.n1, self.qkv_w, scale_a=self.ns, scale_b=self.qkv_s, bias=self.qkv_b,
+                  out=self.qkv, out_scale=self.qs)
+            _mark(marks, "qkv_gemm")
+            _v_convert(self.qkv[:, 2 * d:], self.v16)
+            _mark(marks, "v_convert")
         q, k = self.qkv[:, :d], self.qkv[:, d:2 * d]
         if self.rope:
             for src, dst in ((q, self.q_rot), (k, self.k_rot)):
@@ -314,12 +323,28 @@ class QwenBlock(_Graphable):
         self._init_graph()
 
     @property
+    def v_copy_in_gemm(self) -> bool:
+        """The 16-bit V image leaves the projection GEMM's epilogue (b2f_gemm_fp8_head_prep
+        with V blocks only: >= 256 tokens, V columns in whole 128-column blocks).  (The q / k
+        norm + RoPE can run in that epilogue too, but measured slower than a separate
+        launch: each epilogue thread owns one row, so its rotary-table loads do not
+        coalesce.)"""
+        return self.t >= 256 and (self.hk * self.dh) % 128 == 0 and self.v_off % 128 == 0
+
+    @property
+    def _qk_one_launch(self) -> bool:
+        return (self.dh == 128 and self.h % 4 == 0 and self.hk % 4 == 0 and self.h <= 32
+                and self.rot in (0, 128))
+
+    @property
     def launches_per_forward(self) -> int:
-        """Kernel launches of one forward: the q / k / V preparations are one launch when
-        b2f_attn_prep covers the shape (head_dim 128, head counts in four-head groups)."""
-        fused = (self.dh == 128 and self.h % 4 == 0 and self.hk % 4 == 0 and self.h <= 32
-                 and self.rot in (0, 128))
-        n = 5 if fused else 7
+        """Kernel launches of one forward: in-norm, projection GEMM, q / k (/ V)
+        preparation (one b2f_attn_prep launch where it covers the shape, else one per
+        operand), attention, o-projection, and the MLP's four."""
+        if self._qk_one_launch:
+            n = 5
+        else:
+            n = 6 if self.v_copy_in_gemm else 7
         return n + (4 if self.has_mlp else 0)
 
     def flops(self) -> float:
@@ -330,25 +355,17 @@ class QwenBlock(_Graphable):
         attn = 2 * self.batch * self.h * self.seq * self.seq * self.dh
         return float(gemm + attn)
 
-    def forward(self, hidden: torch.Tensor, hidden_scale: float = 1.0,
-                marks: Optional[list] = None) -> torch.Tensor:
-        """One forward; with ``marks`` (a list) every stage ends with a recorded CUDA event
-        (eager per-stage timing; not for graph capture)."""
+    def _qk_prep(self, vsrc):
+        """q / k head norm + RoPE, plus the V copy from ``vsrc`` unless it is None (V already
+        written): one b2f_attn_prep launch where it covers the shape, else one per operand."""
         h, hk, dh = self.h, self.hk, self.dh
-        _mark(marks, "start")
-        ops.norm_quant(hidden, self.in_norm, kind="rms", weight_offset=1.0, eps=self.eps,
-                       x_scale=hidden_scale, q_out=self.n1, q_scale=self.ns)
-        _mark(marks, "in_norm")
-        _gemm(self.n1, self.w_cat, col_scale=self.cs_cat, out=self.proj,
-              out_scale=self.qs)
-        _mark(marks, "qgkv_gemm")
-        vsrc = self.proj[:, self.v_off:self.v_off + hk * dh]
         fused = ops.attn_prep(
             self.proj[:, self.q_off:], self.proj[:, self.k_off:], vsrc, q_heads=h,
             k_heads=hk, head_dim=dh, in_scale=self.qs, out_scale=self.qs,
             q_head_stride=self.q_hstride, q_weight=self.q_norm, k_weight=self.k_norm,
             weight_offset=1.0, eps=self.eps, cos=self.cos, sin=self.sin,
-            rotary_dim=self.rot, seq=self.seq, q_out=self.q, k_out=self.k, v_out=self.v16)
+            rotary_dim=self.rot, seq=self.seq, q_out=self.q, k_out=self.k,
+            v_out=None if vsrc is None else self.v16)
         if not fused:
             ops.head_norm_rope(self.proj[:, self.q_off:], heads=h, head_dim=dh,
                                in_scale=self.qs, out_scale=self.qs, head_stride=self.q_hstride,
@@ -359,8 +376,37 @@ class QwenBlock(_Graphable):
                                in_scale=self.qs, out_scale=self.qs, weight=self.k_norm,
                                weight_offset=1.0, eps=self.eps, cos=self.cos, sin=self.sin,
                                rotary_dim=self.rot, seq=self.seq, out=self.k)
-            _v_convert(vsrc, self.v16)
+            if vsrc is not None:
+                _v_convert(vsrc, self.v16)
+
+    def _qgkv_unfused(self, marks):
+        """Projection GEMM, then the q / k / V preparations (one b2f_attn_prep launch where
+        it covers the shape, else three)."""
+        h, hk, dh = self.h, self.hk, self.dh
+        _gemm(self.n1, self.w_cat, col_scale=self.cs_cat, out=self.proj,
+              out_scale=self.qs)
+        _mark(marks, "qgkv_gemm")
+        self._qk_prep(self.proj[:, self.v_off:self.v_off + hk * dh])
         _mark(marks, "qkv_prep")
+
+    def forward(self, hidden: torch.Tensor, hidden_scale: float = 1.0,
+                marks: Optional[list] = None) -> torch.Tensor:
+        """One forward; with ``marks`` (a list) every stage ends with a recorded CUDA event
+        (eager per-stage timing; not for graph capture)."""
+        h, hk, dh = self.h, self.hk, self.dh
+        _mark(marks, "start")
+        ops.norm_quant(hidden, self.in_norm, kind="rms", weight_offset=1.0, eps=self.eps,
+                       x_scale=hidden_scale, q_out=self.n1, q_scale=self.ns)
+        _mark(marks, "in_norm")
+        if self.v_copy_in_gemm and ops.gemm_fp8_head_prep(
+                self.n1, self.w_cat, col_scale=self.cs_cat, out=self.proj, out_scale=self.qs,
+                q_out=None, k_out=None, v_out=self.v16, q_off=0, q_heads=0, k_off=0,
+                k_heads=0, v_off=self.v_off, v_heads=hk * dh // 128):
+            _mark(marks, "qgkv_gemm_v")
+            self._qk_prep(None)
+            _mark(marks, "qk_prep")
+        else:
+            self._qgkv_unfused(marks)
         ops.attention_fp8(self.q, self.k, self.v16, batch=self.batch, heads=h, kv_heads=hk,
                           head_dim=dh, causal=True, q_scale=self.qs, k_scale=self.qs,
                           v_scale=self.qs, gate=self.proj[:, self.g_off:], gate_scale=self.qs,

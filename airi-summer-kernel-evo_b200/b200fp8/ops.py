@@ -178,6 +178,68 @@ def gemm_fp8(a: torch.Tensor, b_nk: torch.Tensor, *, scale_a: float = 1.0,
     return out
 
 
+def gemm_fp8_head_prep(a: torch.Tensor, b_nk: torch.Tensor, *, out: torch.Tensor,
+                       out_scale: float, q_out: Optional[torch.Tensor],
+                       k_out: Optional[torch.Tensor], v_out: Optional[torch.Tensor],
+                       q_off: int, q_heads: int, k_off: int, k_heads: int, v_off: int,
+                       v_heads: int, q_head_stride: int = 128, scale_a: float = 1.0,
+                       scale_b: float = 1.0, col_scale: Optional[torch.Tensor] = None,
+                       bias: Optional[torch.Tensor] = None,
+                       q_norm_w: Optional[torch.Tensor] = None,
+                       k_norm_w: Optional[torch.Tensor] = None, weight_offset: float = 0.0,
+                       eps: float = 1e-6, cos: Optional[torch.Tensor] = None,
+                       sin: Optional[torch.Tensor] = None, seq: int = 0,
+                       qk_out_scale: Optional[float] = None) -> bool:
+    """q / gate / k / v projection with the attention-operand preparation in its epilogue
+    (b2f_gemm_fp8_head_prep): the result of :func:`gemm_fp8` (e4m3 ``out`` at ``out_scale``)
+    followed by :func:`attn_prep`, except that only the non-head columns (the gate) are
+    written to ``out``.  Head dim 128, full-head RoPE; with ``q_heads = k_heads = 0`` only
+    the V copy is fused (any head size: v "heads" are 128-column blocks).  Returns False,
+    having done nothing, for shapes the fused kernel does not cover."""
+    _check_cuda(a, b_nk, out, q_out, k_out, v_out, col_scale, bias, q_norm_w, k_norm_w, cos,
+                sin)
+    _fp8_rows(a, "a")
+    _fp8_rows(b_nk, "b_nk")
+    m, k = a.shape
+    n, k2 = b_nk.shape
+    if k != k2:
+        raise ValueError(f"K mismatch: {k} vs {k2}")
+    if out.dtype != torch.float8_e4m3fn:
+        raise TypeError("out must be e4m3")
+    if col_scale is not None and (col_scale.dtype != torch.float32 or not col_scale.is_contiguous()
+                                  or col_scale.numel() != n):
+        raise TypeError("col_scale must be contiguous float32 [n]")
+    args = GemmArgs()
+    L = _lib.lib()
+    L.b2f_gemm_args_init(ctypes.byref(args))
+    args.m, args.n, args.k = m, n, k
+    args.a, args.lda = a.data_ptr(), a.stride(0)
+    args.b, args.ldb = b_nk.data_ptr(), b_nk.stride(0)
+    args.alpha = float(scale_a) * float(scale_b)
+    args.col_scale = _ptr(col_scale)
+    if bias is not None and (bias.dtype != torch.float32 or not bias.is_contiguous()):
+        raise TypeError("bias must be contiguous float32")
+    args.bias = _ptr(bias)
+    args.out, args.out_dtype, args.out_ld = out.data_ptr(), _DT[out.dtype], out.stride(0)
+    args.out_scale = out_scale
+    hp = _lib.HeadPrepArgs()
+    hp.q_off, hp.q_head_stride, hp.q_heads = q_off, q_head_stride, q_heads
+    hp.k_off, hp.k_heads, hp.v_off, hp.v_heads = k_off, k_heads, v_off, v_heads
+    hp.q_out, hp.q_ld = _ptr(q_out), (q_out.stride(0) if q_out is not None else 0)
+    hp.k_out, hp.k_ld = _ptr(k_out), (k_out.stride(0) if k_out is not None else 0)
+    hp.v_out, hp.v_ld = _ptr(v_out), (v_out.stride(0) if v_out is not None else 0)
+    hp.v_dtype = _DT[v_out.dtype] if v_out is not None else _lib.DTYPE_F16
+    hp.q_norm_w, hp.k_norm_w = _ptr(q_norm_w), _ptr(k_norm_w)
+    hp.weight_offset, hp.eps = weight_offset, eps
+    hp.rope_cos, hp.rope_sin, hp.seq = _ptr(cos), _ptr(sin), seq
+    hp.out_scale = out_scale if qk_out_scale is None else qk_out_scale
+    rc = L.b2f_gemm_fp8_head_prep(ctypes.byref(args), ctypes.byref(hp), _stream())
+    if rc == _lib.B2F_ERR_UNSUPPORTED:
+        return False
+    check(rc)
+    return True
+
+
 def norm_quant(x: torch.Tensor, weight: torch.Tensor, *, kind: str = "rms",
                bias: Optional[torch.Tensor] = None, weight_offset: float = 0.0,
                eps: float = 1e-6, x_scale: float = 1.0,
@@ -375,7 +437,8 @@ def head_norm_rope(x: torch.Tensor, *, heads: int, head_dim: int, in_scale: floa
     return out
 
 
-def attn_prep(q_src: torch.Tensor, k_src: torch.Tensor, v_src: torch.Tensor, *, q_heads: int,
+def attn_prep(q_src: torch.Tensor, k_src: torch.Tensor, v_src: Optional[torch.Tensor], *,
+              q_heads: int,
               k_heads: int, head_dim: int, in_scale: float, out_scale: float,
               q_head_stride: Optional[int] = None, q_weight=None, k_weight=None,
               weight_offset: float = 1.0, eps: float = 1e-6, cos=None, sin=None,
@@ -386,13 +449,18 @@ def attn_prep(q_src: torch.Tensor, k_src: torch.Tensor, v_src: torch.Tensor, *, 
     (b2f_attn_prep).  Returns False, having done nothing, for shapes that launch does not
     cover (the caller then runs the three operations)."""
     _check_cuda(v_src, v_out)
+    if (v_src is None) != (v_out is None):
+        raise ValueError("v_src and v_out go together (both None: no V copy)")
     qa, q_out = _rope_args(q_src, q_heads, head_dim, in_scale, out_scale, q_head_stride,
                            q_weight, weight_offset, eps, cos, sin, rotary_dim, seq, q_out)
     ka, k_out = _rope_args(k_src, k_heads, head_dim, in_scale, out_scale, None, k_weight,
                            weight_offset, eps, cos, sin, rotary_dim, seq, k_out)
-    rc = _lib.lib().b2f_attn_prep(ctypes.byref(qa), ctypes.byref(ka), v_src.data_ptr(),
-                                  v_src.stride(0), v_out.data_ptr(), v_out.stride(0),
-                                  v_src.shape[1], _DT[v_out.dtype], _stream())
+    if v_src is None:
+        vargs = (None, 0, None, 0, 0, _lib.DTYPE_F16)
+    else:
+        vargs = (v_src.data_ptr(), v_src.stride(0), v_out.data_ptr(), v_out.stride(0),
+                 v_src.shape[1], _DT[v_out.dtype])
+    rc = _lib.lib().b2f_attn_prep(ctypes.byref(qa), ctypes.byref(ka), *vargs, _stream())
     if rc == _lib.B2F_ERR_UNSUPPORTED:
         return False
     check(rc)

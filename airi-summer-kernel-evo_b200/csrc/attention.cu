@@ -846,17 +846,10 @@ __global__ void __launch_bounds__(384, 1)
           for (int e = hb * 32; e < hb * 32 + 32; ++e) {
             const float2 xv = ffma2(make_float2(__uint_as_float(sv(2 * e)),
                                                 __uint_as_float(sv(2 * e + 1))), c2, nm2);
-            // Three of every eight pairs go through the polynomial: the exponential unit
-            // (16 results per clock per SM) bounds the softmax, the FMA pipe has room.
-            float e0, e1;
-            if ((e & 7) < 3) {
-              const float2 pe = ex2_poly2(xv);
-              e0 = pe.x;
-              e1 = pe.y;
-            } else {
-              e0 = ex2_hw(xv.x);
-              e1 = ex2_hw(xv.y);
-            }
+            // Every exponential on the exponential unit: moving three of eight pairs to
+            // an FMA-pipe polynomial (ex2_poly2) measured slower here (Qwen shape 223 vs
+            // 205 us): the softmax is bound by issue slots, which the polynomial adds.
+            const float e0 = ex2_hw(xv.x), e1 = ex2_hw(xv.y);
             acc2[e & 1] = fadd2(acc2[e & 1], make_float2(e0, e1));
             if constexpr (VF16) sv(e) = pack_f16x2(e0, e1);
             else sv(e) = pack_bf16x2(e0, e1);

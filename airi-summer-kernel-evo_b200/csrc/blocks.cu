@@ -164,14 +164,29 @@ int b2f_gpt2_block(const b2f_gpt2_block_args* a, b2f_stream_t s) {
     n.q_out = b.n1; n.q_ld = d; n.q_scale = ns;
     if ((rc = b2f_norm_quant(&n, s))) return rc;
   }
-  // QKV + bias -> e4m3
+  // QKV + bias -> e4m3, the 16-bit V image from the same epilogue where the V columns are
+  // whole 128-column blocks, else by a separate conversion
+  const int vdt = v_dtype(hd);
   {
     Gemm g(t, 3 * d, d, b.n1, a->qkv_w, b.qkv, B2F_DTYPE_E4M3);
     g.g.alpha = alpha_of(ns, a->qkv_s); g.g.bias = a->qkv_b; g.g.out_scale = qs;
-    if ((rc = b2f_gemm_fp8(&g.g, s))) return rc;
+    bool fused = false;
+    if (d % 128 == 0) {
+      b2f_head_prep_args hp;
+      std::memset(&hp, 0, sizeof(hp));
+      hp.q_head_stride = 128;
+      hp.v_off = 2 * d; hp.v_heads = d / 128;
+      hp.v_out = b.v; hp.v_ld = d; hp.v_dtype = vdt;
+      hp.out_scale = qs;
+      rc = b2f_gemm_fp8_head_prep(&g.g, &hp, s);
+      if (rc == B2F_OK) fused = true;
+      else if (rc != B2F_ERR_UNSUPPORTED) return rc;
+    }
+    if (!fused) {
+      if ((rc = b2f_gemm_fp8(&g.g, s))) return rc;
+      if ((rc = v_convert(b.qkv + 2 * d, 3 * d, b.v, t, d, vdt, s))) return rc;
+    }
   }
-  const int vdt = v_dtype(hd);
-  if ((rc = v_convert(b.qkv + 2 * d, 3 * d, b.v, t, d, vdt, s))) return rc;
   const char* q = b.qkv;
   const char* k = b.qkv + d;
   long long q_ld = 3 * d, k_ld = 3 * d;
@@ -302,15 +317,32 @@ int b2f_qwen_block(const b2f_qwen_block_args* a, b2f_stream_t s) {
     n.q_out = b.n1; n.q_ld = hid; n.q_scale = ns;
     if ((rc = b2f_norm_quant(&n, s))) return rc;
   }
-  {
+  const int vdt = v_dtype(dh);
+  // The 16-bit V image from the projection GEMM's epilogue where the V columns are whole
+  // 128-column blocks (the q / k norm + RoPE stay a separate launch: in the epilogue each
+  // thread owns one row and its rotary-table loads would not coalesce).
+  bool v_done = false;
+  if ((long long)hk * dh % 128 == 0 && v_off % 128 == 0) {
+    Gemm g(t, ncat, hid, b.n1, a->qgkv_w, b.proj, B2F_DTYPE_E4M3);
+    g.g.col_scale = a->qgkv_col_scale; g.g.out_scale = qs;
+    b2f_head_prep_args hp;
+    std::memset(&hp, 0, sizeof(hp));
+    hp.q_head_stride = 128;
+    hp.v_off = v_off; hp.v_heads = hk * dh / 128;
+    hp.v_out = b.v; hp.v_ld = (long long)hk * dh; hp.v_dtype = vdt;
+    hp.out_scale = qs;
+    rc = b2f_gemm_fp8_head_prep(&g.g, &hp, s);
+    if (rc == B2F_OK) v_done = true;
+    else if (rc != B2F_ERR_UNSUPPORTED) return rc;
+  }
+  if (!v_done) {
     Gemm g(t, ncat, hid, b.n1, a->qgkv_w, b.proj, B2F_DTYPE_E4M3);
     g.g.col_scale = a->qgkv_col_scale; g.g.out_scale = qs;
     if ((rc = b2f_gemm_fp8(&g.g, s))) return rc;
   }
-  const int vdt = v_dtype(dh);
   {
-    // q / k head norm + RoPE and the V conversion: one launch when the shapes allow it
-    // (head_dim 128, four-head groups), else the three operations one by one.
+    // q / k head norm + RoPE (and the V conversion unless the GEMM wrote V): one launch
+    // when the shapes allow it (head_dim 128, four-head groups), else one per operation.
     b2f_rope_args r[2];
     for (int which = 0; which < 2; ++which) {
       std::memset(&r[which], 0, sizeof(r[which]));
@@ -324,12 +356,13 @@ int b2f_qwen_block(const b2f_qwen_block_args* a, b2f_stream_t s) {
       r[which].out = which == 0 ? b.q : b.k; r[which].out_ld = (which == 0 ? h : hk) * dh;
       r[which].out_scale = qs;
     }
-    rc = b2f_attn_prep(&r[0], &r[1], b.proj + v_off, ncat, b.v, (long long)hk * dh, hk * dh,
-                       vdt, s);
+    rc = v_done ? b2f_attn_prep(&r[0], &r[1], nullptr, 0, nullptr, 0, 0, vdt, s)
+                : b2f_attn_prep(&r[0], &r[1], b.proj + v_off, ncat, b.v, (long long)hk * dh,
+                                hk * dh, vdt, s);
     if (rc == B2F_ERR_UNSUPPORTED) {
       for (int which = 0; which < 2; ++which)
         if ((rc = b2f_head_norm_rope(&r[which], s))) return rc;
-      if ((rc = v_convert(b.proj + v_off, ncat, b.v, t, hk * dh, vdt, s))) return rc;
+      if (!v_done && (rc = v_convert(b.proj + v_off, ncat, b.v, t, hk * dh, vdt, s))) return rc;
     } else if (rc) {
       return rc;
     }

@@ -96,6 +96,20 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// mbar_test that may suspend the thread (until the phase completes, or about 20 us) instead
+// of returning at once: waiting warps stop taking issue slots from the working ones.
+__device__ __forceinline__ bool mbar_test_suspend(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(20000u)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait for the phase with the given parity to complete.  Returns false (and
 // records `code`) when the limit expires or when another role already aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int code,
@@ -103,7 +117,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
   if (mbar_test(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
-    if (mbar_test(bar, parity)) return true;
+    if (mbar_test_suspend(bar, parity)) return true;
     if (abort_flag != nullptr && *abort_flag) return false;
     if (globaltimer() - t0 > B2F_WAIT_NS) {
       record_error(code);
@@ -444,6 +458,16 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
   asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
       "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
       "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
       : "=f"(d.x), "=f"(d.y)
       : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
   return d;

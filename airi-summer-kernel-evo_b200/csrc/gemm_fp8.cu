@@ -88,6 +88,7 @@ EpilogueParams make_epilogue(const b2f_gemm_args* a) {
   ep.ws_ld = 0;
   ep.ws_slice = 0;
   ep.counters = nullptr;
+  ep.hp = HeadPrepParams{};
   const int esz = a->out_dtype == B2F_DTYPE_F32 ? 4 : (a->out_dtype == B2F_DTYPE_BF16 ? 2 : 1);
   const int rsz =
       a->residual_dtype == B2F_DTYPE_F32 ? 4 : (a->residual_dtype == B2F_DTYPE_BF16 ? 2 : 1);
@@ -172,8 +173,9 @@ int launch_gemm(const b2f_gemm_args* a, EpilogueParams ep, cudaStream_t stream) 
   return B2F_OK;
 }
 
+template <int PBN>
 int launch_gemm_pair(const b2f_gemm_args* a, EpilogueParams ep, cudaStream_t stream) {
-  using Cfg = Gemm2Cfg;
+  using Cfg = Gemm2Cfg<PBN>;
   CUtensorMap ta, tb;
   std::string err;
   {
@@ -194,11 +196,11 @@ int launch_gemm_pair(const b2f_gemm_args* a, EpilogueParams ep, cudaStream_t str
   }
   GemmShape shape{a->m, a->n, a->k, 1};
   const int num_tiles = ((a->m + 255) / 256) * ((a->n + Cfg::BN - 1) / Cfg::BN);
-  static thread_local int cached_dev = -1, cached_pairs = 0;
+  static thread_local int cached_dev = -1, cached_pairs = 0;  // per instance
   int dev = 0;
   B2F_CUDA_TRY(cudaGetDevice(&dev));
   if (cached_dev != dev) {
-    B2F_CUDA_TRY(cudaFuncSetAttribute(gemm_fp8_pair_kernel,
+    B2F_CUDA_TRY(cudaFuncSetAttribute(gemm_fp8_pair_kernel<PBN>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       Cfg::SMEM_BYTES));
     cudaLaunchConfig_t probe = {};
@@ -211,7 +213,7 @@ int launch_gemm_pair(const b2f_gemm_args* a, EpilogueParams ep, cudaStream_t str
     probe.attrs = &attr;
     probe.numAttrs = 1;
     int clusters = 0;
-    B2F_CUDA_TRY(cudaOccupancyMaxActiveClusters(&clusters, gemm_fp8_pair_kernel, &probe));
+    B2F_CUDA_TRY(cudaOccupancyMaxActiveClusters(&clusters, gemm_fp8_pair_kernel<PBN>, &probe));
     if (clusters <= 0) return fail(B2F_ERR_UNSUPPORTED, "gemm_fp8: no co-resident CTA pairs");
     cached_pairs = clusters;
     cached_dev = dev;
@@ -220,7 +222,7 @@ int launch_gemm_pair(const b2f_gemm_args* a, EpilogueParams ep, cudaStream_t str
   const int pairs = num_tiles < cached_pairs ? num_tiles : cached_pairs;
   CUtensorMap to;
   if (int rc = encode_out_map(a, ep, Cfg::BN / 2, &to)) return rc;
-  gemm_fp8_pair_kernel<<<2 * pairs, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, to, shape,
+  gemm_fp8_pair_kernel<PBN><<<2 * pairs, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, to, shape,
                                                                              ep);
   B2F_CUDA_TRY(cudaGetLastError());
   return B2F_OK;
@@ -228,42 +230,40 @@ int launch_gemm_pair(const b2f_gemm_args* a, EpilogueParams ep, cudaStream_t str
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-}  // namespace
-}  // namespace b2f
-
-extern "C" {
-
-void b2f_gemm_args_init(b2f_gemm_args* a) {
-  if (a == nullptr) return;
-  *a = b2f_gemm_args{};
-  a->alpha = 1.0f;
-  a->pre_mul = 1.0f;
-  a->pre_add = 0.0f;
-  a->act = B2F_ACT_NONE;
-  a->act_param = 0.0f;
-  a->post_mul = 1.0f;
-  a->residual_dtype = B2F_DTYPE_BF16;
-  a->residual_scale = 1.0f;
-  a->out_dtype = B2F_DTYPE_BF16;
-  a->out_scale = 1.0f;
-  a->mode = B2F_GEMM_STORE;
-  a->tile_n = 0;
-  a->gate = nullptr;
-  a->gate_dtype = B2F_DTYPE_F32;
-  a->gate_ld = 0;
+// Automatic tile choice of b2f_gemm_fp8 (tile_n = 0).
+int auto_tile_n(const b2f_gemm_args* a) {
+  int tn = 0;
+  // CTA-pair 256 x 256 tiles for large problems with a long K loop.  Short K loops (the
+  // K = 768 GEMMs of the GPT-2 block) run faster on single-CTA tiles (measured QKV 26.3
+  // -> 24.4 us, FC 45.4 -> 41.0 us at M=8192); between 128- and 256-wide tiles the
+  // choice weighs waves x tile width and takes 128 only when it saves a quarter
+  // (out-projection N=768: 21.3 -> 17.5 us).  Few-tile problems use 128-wide tiles to
+  // fill the 148 SMs.
+  const int sms = sm_count();
+  const long long rows128 = (a->m + 127) / 128;
+  const long long tiles256 = rows128 * ((a->n + 255) / 256);
+  const long long tiles128 = rows128 * ((a->n + 127) / 128);
+  const long long pair_tiles = (long long)((a->m + 255) / 256) * ((a->n + 255) / 256);
+  if (a->m > 128 && pair_tiles >= sms / 2 && a->k >= 2048) {
+    // 256 x 256 pair tiles.  (256 x 128 pair tiles, tile_n -128, would halve the wave
+    // quantisation of e.g. the 8192 x 2560 o-projection, but measured 1.5x slower there:
+    // 104 vs 70 us.)
+    tn = 512;
+  } else if (a->workspace != nullptr && a->splits > 1 && tiles256 * 2 <= sms) {
+    tn = 256;
+  } else if (tiles256 < sms) {
+    tn = 128;
+  } else {
+    const long long w256 = (tiles256 + sms - 1) / sms * 2;
+    const long long w128 = (tiles128 + sms - 1) / sms;
+    // (a tie goes to 128 for short K loops, where the epilogue dominates, and to 256 for
+    // long ones: GPT-2's proj, N=768 K=3072, 33.1 us at 256 vs 38.4 at 128)
+    tn = (a->k <= 1024 ? 4 * w128 <= 3 * w256 : 4 * w128 < 3 * w256) ? 128 : 256;
+  }
+  return tn;
 }
 
-int b2f_gemm_pair_capacity(void) { return b2f::g_pair_capacity; }
-
-long long b2f_gemm_workspace_bytes(int m, int n) {
-  if (m <= 0 || n <= 0) return 0;
-  const long long ld = (long long)((n + 255) / 256) * 256;   // column tiles of 256
-  const long long rows = (long long)((m + 127) / 128) * 128;  // row tiles of 128
-  return b2f::kCounterBytes + b2f::kMaxSplits * rows * ld * 4;
-}
-
-int b2f_gemm_fp8(const b2f_gemm_args* a, b2f_stream_t stream) {
-  using namespace b2f;
+int check_gemm_args(const b2f_gemm_args* a) {
   if (a == nullptr) return fail(B2F_ERR_ARG, "gemm_fp8: null args");
   if (a->m <= 0 || a->n <= 0 || a->k <= 0) return fail(B2F_ERR_ARG, "gemm_fp8: empty shape");
   if (a->a == nullptr || a->b == nullptr || a->out == nullptr)
@@ -295,36 +295,123 @@ int b2f_gemm_fp8(const b2f_gemm_args* a, b2f_stream_t stream) {
     return fail(B2F_ERR_ARG, "gemm_fp8: col_scale must be 16-byte aligned");
   if (a->bias != nullptr && ((uintptr_t)a->bias) % 16 != 0)
     return fail(B2F_ERR_ARG, "gemm_fp8: bias must be 16-byte aligned");
+  return B2F_OK;
+}
+
+
+}  // namespace
+}  // namespace b2f
+
+extern "C" {
+
+void b2f_gemm_args_init(b2f_gemm_args* a) {
+  if (a == nullptr) return;
+  *a = b2f_gemm_args{};
+  a->alpha = 1.0f;
+  a->pre_mul = 1.0f;
+  a->pre_add = 0.0f;
+  a->act = B2F_ACT_NONE;
+  a->act_param = 0.0f;
+  a->post_mul = 1.0f;
+  a->residual_dtype = B2F_DTYPE_BF16;
+  a->residual_scale = 1.0f;
+  a->out_dtype = B2F_DTYPE_BF16;
+  a->out_scale = 1.0f;
+  a->mode = B2F_GEMM_STORE;
+  a->tile_n = 0;
+  a->gate = nullptr;
+  a->gate_dtype = B2F_DTYPE_F32;
+  a->gate_ld = 0;
+}
+
+int b2f_gemm_fp8_head_prep(const b2f_gemm_args* a, const b2f_head_prep_args* h,
+                           b2f_stream_t stream) {
+  using namespace b2f;
+  if (a == nullptr || h == nullptr) return fail(B2F_ERR_ARG, "gemm_fp8_head_prep: null args");
+  if (a->out_dtype != B2F_DTYPE_E4M3 || a->mode != B2F_GEMM_STORE ||
+      a->act != B2F_ACT_NONE || a->residual != nullptr || a->gate != nullptr ||
+      a->amax != nullptr || a->splits > 1 || a->pre_mul != 1.0f || a->pre_add != 0.0f ||
+      a->post_mul != 1.0f)
+    return fail(B2F_ERR_ARG, "gemm_fp8_head_prep: e4m3 output with a plain epilogue (alpha, "
+                             "column scale, bias), no split-K");
+  auto head_ok = [&](int off, int stride, int heads) {
+    return heads >= 0 && off >= 0 && off % 128 == 0 && stride % 128 == 0 &&
+           (heads == 0 || off + (long long)(heads - 1) * stride + 128 <= a->n);
+  };
+  // every head must be a whole 128-column half of a 256-column tile: offsets multiples of
+  // 128 do that by construction
+  if (h->q_heads < 0 || h->k_heads < 0 || h->v_heads < 0 || h->q_head_stride < 128 ||
+      !head_ok(h->q_off, h->q_head_stride, h->q_heads) || !head_ok(h->k_off, 128, h->k_heads) ||
+      !head_ok(h->v_off, 128, h->v_heads))
+    return fail(B2F_ERR_ARG, "gemm_fp8_head_prep: head columns must be 128-aligned and inside n");
+  if ((h->q_heads && (h->q_out == nullptr || h->q_ld < 128LL * h->q_heads || h->q_ld % 16 ||
+                      ((uintptr_t)h->q_out & 15))) ||
+      (h->k_heads && (h->k_out == nullptr || h->k_ld < 128LL * h->k_heads || h->k_ld % 16 ||
+                      ((uintptr_t)h->k_out & 15))) ||
+      (h->v_heads && (h->v_out == nullptr || h->v_ld < 128LL * h->v_heads || h->v_ld % 8 ||
+                      ((uintptr_t)h->v_out & 15))))
+    return fail(B2F_ERR_ARG, "gemm_fp8_head_prep: q/k/v outputs: 16-byte aligned rows wide "
+                             "enough for their heads");
+  if (h->v_dtype != B2F_DTYPE_F16 && h->v_dtype != B2F_DTYPE_BF16)
+    return fail(B2F_ERR_ARG, "gemm_fp8_head_prep: v_dtype must be f16 or bf16");
+  if ((h->rope_cos == nullptr) != (h->rope_sin == nullptr) ||
+      (h->rope_cos != nullptr && (h->seq <= 0 || ((uintptr_t)h->rope_cos & 15) ||
+                                  ((uintptr_t)h->rope_sin & 15))))
+    return fail(B2F_ERR_ARG, "gemm_fp8_head_prep: rope tables [seq][128], 16-byte aligned");
+  if (((uintptr_t)h->q_norm_w & 15) || ((uintptr_t)h->k_norm_w & 15))
+    return fail(B2F_ERR_ARG, "gemm_fp8_head_prep: norm weights must be 16-byte aligned");
+  if (!(h->out_scale > 0.0f) || !(a->out_scale > 0.0f))
+    return fail(B2F_ERR_ARG, "gemm_fp8_head_prep: scales must be positive");
+  if (a->col_scale != nullptr && ((uintptr_t)a->col_scale) % 16 != 0)
+    return fail(B2F_ERR_ARG, "gemm_fp8: col_scale must be 16-byte aligned");
+  // the plain-GEMM argument checks (shape, operands, output)
+  b2f_gemm_args plain = *a;
+  plain.splits = 1;
+  plain.workspace = nullptr;
+  if (int rc = check_gemm_args(&plain)) return rc;
+  // 256-column tiles (each head one 128-column half): CTA pairs where the plain GEMM would
+  // use them, else single-CTA 128 x 256 tiles
+  const int auto_tn = auto_tile_n(&plain);
+  const bool pair = auto_tn == 512 || auto_tn == -128;
+  plain.tile_n = pair ? 512 : 256;
+  EpilogueParams ep = make_epilogue(&plain);
+  HeadPrepParams& p = ep.hp;
+  p.on = 1;
+  p.q_off = h->q_off; p.q_hstride = h->q_head_stride; p.q_heads = h->q_heads;
+  p.k_off = h->k_off; p.k_heads = h->k_heads;
+  p.v_off = h->v_off; p.v_heads = h->v_heads;
+  p.v_f16 = h->v_dtype == B2F_DTYPE_F16;
+  p.q_out = static_cast<uint8_t*>(h->q_out); p.q_ld = h->q_ld;
+  p.k_out = static_cast<uint8_t*>(h->k_out); p.k_ld = h->k_ld;
+  p.v_out = static_cast<uint16_t*>(h->v_out); p.v_ld = h->v_ld;
+  p.q_w = h->q_norm_w; p.k_w = h->k_norm_w;
+  p.w_offset = h->weight_offset; p.eps = h->eps;
+  p.cos = h->rope_cos; p.sin = h->rope_sin; p.seq = h->seq;
+  p.x_scale = a->out_scale;
+  p.out_inv_scale = 1.0f / h->out_scale;
+  return pair ? launch_gemm_pair<256>(&plain, ep, (cudaStream_t)stream)
+              : launch_gemm<256>(&plain, ep, (cudaStream_t)stream);
+}
+
+int b2f_gemm_pair_capacity(void) { return b2f::g_pair_capacity; }
+
+long long b2f_gemm_workspace_bytes(int m, int n) {
+  if (m <= 0 || n <= 0) return 0;
+  const long long ld = (long long)((n + 255) / 256) * 256;   // column tiles of 256
+  const long long rows = (long long)((m + 127) / 128) * 128;  // row tiles of 128
+  return b2f::kCounterBytes + b2f::kMaxSplits * rows * ld * 4;
+}
+
+int b2f_gemm_fp8(const b2f_gemm_args* a, b2f_stream_t stream) {
+  using namespace b2f;
+  if (int rc = check_gemm_args(a)) return rc;
   cudaStream_t s = (cudaStream_t)stream;
   int tn = a->tile_n;
-  if (tn == 0) {
-    // CTA-pair 256 x 256 tiles for large problems with a long K loop.  Short K loops (the
-    // K = 768 GEMMs of the GPT-2 block) run faster on single-CTA tiles (measured QKV 26.3
-    // -> 24.4 us, FC 45.4 -> 41.0 us at M=8192); between 128- and 256-wide tiles the
-    // choice weighs waves x tile width and takes 128 only when it saves a quarter
-    // (out-projection N=768: 21.3 -> 17.5 us).  Few-tile problems use 128-wide tiles to
-    // fill the 148 SMs.
-    const int sms = sm_count();
-    const long long rows128 = (a->m + 127) / 128;
-    const long long tiles256 = rows128 * ((a->n + 255) / 256);
-    const long long tiles128 = rows128 * ((a->n + 127) / 128);
-    const long long pair_tiles = (long long)((a->m + 255) / 256) * ((a->n + 255) / 256);
-    if (a->m > 128 && pair_tiles >= sms / 2 && a->k >= 2048) {
-      tn = 512;
-    } else if (a->workspace != nullptr && a->splits > 1 && tiles256 * 2 <= sms) {
-      tn = 256;
-    } else if (tiles256 < sms) {
-      tn = 128;
-    } else {
-      const long long w256 = (tiles256 + sms - 1) / sms * 2;
-      const long long w128 = (tiles128 + sms - 1) / sms;
-      tn = (4 * w128 <= 3 * w256) ? 128 : 256;
-    }
-  }
+  if (tn == 0) tn = auto_tile_n(a);
   const EpilogueParams ep = make_epilogue(a);
-  if (tn == 512) {
+  if (tn == 512 || tn == -256 || tn == -128) {
     if (a->splits > 1) return fail(B2F_ERR_UNSUPPORTED, "gemm_fp8: split-K uses tile_n 128 or 256");
-    return launch_gemm_pair(a, ep, s);
+    return tn == -128 ? launch_gemm_pair<128>(a, ep, s) : launch_gemm_pair<256>(a, ep, s);
   }
   if (tn == 256) return launch_gemm<256>(a, ep, s);
   if (tn == 128) return launch_gemm<128>(a, ep, s);
@@ -332,7 +419,8 @@ int b2f_gemm_fp8(const b2f_gemm_args* a, b2f_stream_t stream) {
     if (a->splits > 1) return fail(B2F_ERR_UNSUPPORTED, "gemm_fp8: split-K uses tile_n 128 or 256");
     return launch_gemm<64>(a, ep, s);
   }
-  return fail(B2F_ERR_ARG, "gemm_fp8: tile_n must be 0, 64, 128, 256 or 512 (CTA pair)");
+  return fail(B2F_ERR_ARG,
+              "gemm_fp8: tile_n must be 0, 64, 128, 256, or -128 / -256 / 512 (CTA pair)");
 }
 
 }  // extern "C"

@@ -26,6 +26,35 @@ enum : int { kOutF32 = 0, kOutBF16 = 1, kOutE4M3 = 2 };
 enum : int { kActNone = 0, kActRelu = 1, kActGeluTanh = 2, kActLeakyRelu = 3, kActSilu = 4 };
 enum : int { kModeStore = 0, kModeRowSum = 1 };
 
+// Attention-operand preparation fused into a q / gate / k / v projection's epilogue (CTA
+// pair kernel, 256-column tiles: each epilogue warp's 128-column half of a tile is one head
+// or one plain block of columns).  Half-tiles that are a q or k head are rounded to e4m3 at
+// the projection's scale (the values a separate GEMM would have stored), RMS-normalised
+// over the head, rotated (RoPE over the whole head) and stored as e4m3 in q_out / k_out;
+// half-tiles that are a v head are rounded the same way and stored as 16-bit codes in
+// v_out; every other column (the attention gate) takes the ordinary epilogue into `out`.
+struct HeadPrepParams {
+  int on;
+  int q_off, q_hstride, q_heads;  // q head h at columns q_off + h * q_hstride, 128 wide
+  int k_off, k_heads;             // k head h at k_off + 128 h
+  int v_off, v_heads;             // v head h at v_off + 128 h
+  int v_f16;                      // v_out holds f16 (else bf16) codes
+  uint8_t* q_out;
+  long long q_ld;
+  uint8_t* k_out;
+  long long k_ld;
+  uint16_t* v_out;
+  long long v_ld;
+  const float* q_w;  // [128] RMSNorm weight (+ w_offset), or null: no norm
+  const float* k_w;
+  float w_offset, eps;
+  const float* cos;  // [seq][128] rotary tables (sign of rotate_half not folded), or null
+  const float* sin;
+  int seq;               // rotary position = row % seq
+  float x_scale;         // one e4m3 code of the projection = x_scale (its out_scale)
+  float out_inv_scale;   // q / k codes = e4m3(y * out_inv_scale)
+};
+
 struct EpilogueParams {
   float alpha;             // scale_a * scale_b
   const float* alpha_ptr;  // optional device scalar multiplied into alpha (may be null)
@@ -58,6 +87,7 @@ struct EpilogueParams {
   unsigned int* counters;  // split-K: per output tile, (epoch << 8) | arrival state
   unsigned int epoch;      // split-K: this call's 24-bit tag (a counter whose tag differs
                            // is stale, left by an aborted call, and reads as zero)
+  HeadPrepParams hp;       // fused attention-operand preparation (pair kernel only)
 };
 
 // Split-K tile counter update: adds `add` to the tile's arrival state for this call and
@@ -101,22 +131,61 @@ __device__ __forceinline__ float gelu_tanh(float x) {
   return 0.5f * x * (1.0f + tanh_hw(u));
 }
 
-// Activation selected at compile time: a runtime switch inside the element loop gets
-// if-converted into evaluating every activation for every element.
+// Activation of a pair of values, selected at compile time (a runtime switch inside the
+// element loop gets if-converted into evaluating every activation for every element).
+// GELU-tanh: 0.5 x (1 + tanh(x (k0 + k0 k1 x^2))) with packed pair arithmetic and the
+// hardware tanh per element.
 template <int ACT>
-__device__ __forceinline__ float act_fn(float v, float p) {
-  if constexpr (ACT == kActRelu) return fmaxf(v, 0.0f);
-  else if constexpr (ACT == kActGeluTanh) return gelu_tanh(v);
-  else if constexpr (ACT == kActLeakyRelu) return v >= 0.0f ? v : v * p;
-  else if constexpr (ACT == kActSilu) return v / (1.0f + expf(-v));
-  else return v;
+__device__ __forceinline__ float2 act_pair(float2 v, float p) {
+  if constexpr (ACT == kActRelu) {
+    return make_float2(fmaxf(v.x, 0.0f), fmaxf(v.y, 0.0f));
+  } else if constexpr (ACT == kActGeluTanh) {
+    const float k0 = 0.7978845608028654f;
+    const float k0k1 = 0.7978845608028654f * 0.044715f;
+    const float2 x2 = fmul2(v, v);
+    const float2 u = fmul2(ffma2(x2, make_float2(k0k1, k0k1), make_float2(k0, k0)), v);
+    const float2 h = fmul2(v, make_float2(0.5f, 0.5f));
+    return ffma2(h, make_float2(tanh_hw(u.x), tanh_hw(u.y)), h);
+  } else if constexpr (ACT == kActLeakyRelu) {
+    return make_float2(v.x >= 0.0f ? v.x : v.x * p, v.y >= 0.0f ? v.y : v.y * p);
+  } else if constexpr (ACT == kActSilu) {
+    return make_float2(v.x / (1.0f + expf(-v.x)), v.y / (1.0f + expf(-v.y)));
+  } else {
+    return v;
+  }
+}
+
+// acc * m + a per column (m, a broadcast from the lanes that hold column j's values, or
+// uniform), then the activation, then post_mul: 16 pairs.
+template <int ACT, bool LANE_MUL, bool LANE_ADD>
+__device__ __forceinline__ void affine_act32(const uint32_t (&acc)[32], float (&v)[32],
+                                             float m, float a, float lane_mul, float lane_add,
+                                             float p, float post_mul) {
+#pragma unroll
+  for (int j = 0; j < 32; j += 2) {
+    const float2 m2 = LANE_MUL ? make_float2(__shfl_sync(0xffffffffu, lane_mul, j),
+                                             __shfl_sync(0xffffffffu, lane_mul, j + 1))
+                               : make_float2(m, m);
+    const float2 a2 = LANE_ADD ? make_float2(__shfl_sync(0xffffffffu, lane_add, j),
+                                             __shfl_sync(0xffffffffu, lane_add, j + 1))
+                               : make_float2(a, a);
+    float2 x = ffma2(make_float2(__uint_as_float(acc[j]), __uint_as_float(acc[j + 1])), m2, a2);
+    x = act_pair<ACT>(x, p);
+    if (post_mul != 1.0f) x = fmul2(x, make_float2(post_mul, post_mul));
+    v[j] = x.x;
+    v[j + 1] = x.y;
+  }
 }
 
 template <int ACT>
-__device__ __forceinline__ void act_affine32(float (&v)[32], float pre_mul, float pre_add,
-                                             float p, float post_mul) {
-#pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = act_fn<ACT>(fmaf(v[j], pre_mul, pre_add), p) * post_mul;
+__device__ __forceinline__ void affine_act32_sel(const EpilogueParams& ep, const uint32_t (&acc)[32],
+                                                 float (&v)[32], float m, float a,
+                                                 float lane_mul, float lane_add) {
+  const bool lm = ep.col_scale != nullptr, la = ep.bias != nullptr;
+  if (lm && la) affine_act32<ACT, true, true>(acc, v, m, a, lane_mul, lane_add, ep.act_param, ep.post_mul);
+  else if (lm) affine_act32<ACT, true, false>(acc, v, m, a, lane_mul, lane_add, ep.act_param, ep.post_mul);
+  else if (la) affine_act32<ACT, false, true>(acc, v, m, a, lane_mul, lane_add, ep.act_param, ep.post_mul);
+  else affine_act32<ACT, false, false>(acc, v, m, a, lane_mul, lane_add, ep.act_param, ep.post_mul);
 }
 
 template <int BN>
@@ -146,30 +215,25 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb
   nb = r / gsize;
 }
 
-// Epilogue math for 32 consecutive columns of one row: scale, bias, affine, activation,
-// residual; tracks |v| (amax) and the row sum.  Returns the f32 values before the store.
+// Epilogue math for 32 consecutive columns of one row:
+//   v = act(acc * m_c + a_c) * post_mul  [* gate]  [+ residual * res_scale]
+// with m_c = alpha * col_scale[c] * pre_mul and a_c = bias[c] * pre_mul + pre_add (the
+// affine step of (alpha acc col_scale + bias) pre_mul + pre_add folded per column; lane j
+// of the warp holds column col0 + j's m_c / a_c, broadcast by shuffle); tracks |v| (amax)
+// and the row sum.  Returns the f32 values before the store.
 __device__ __forceinline__ void epi_values(const EpilogueParams& ep, float alpha, int row,
                                            int col0, int M, int N, const uint32_t (&acc)[32],
                                            float (&v)[32], float& rowsum, float& amax_local,
-                                           float lane_bias, float lane_cscale) {
+                                           float lane_add, float lane_mul) {
   const bool row_ok = row < M;
-  // lane j of the warp holds bias / column scale of column col0 + j: broadcast by shuffle
-#pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(acc[j]) * alpha;
-  if (ep.col_scale != nullptr) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] *= __shfl_sync(0xffffffffu, lane_cscale, j);
-  }
-  if (ep.bias != nullptr) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] += __shfl_sync(0xffffffffu, lane_bias, j);
-  }
+  const float m = alpha * ep.pre_mul;  // uniform multiplier (no column scale)
+  const float a = ep.pre_add;          // uniform addend (no bias)
   switch (ep.act) {  // uniform branch, once per 32 columns
-    case kActRelu: act_affine32<kActRelu>(v, ep.pre_mul, ep.pre_add, ep.act_param, ep.post_mul); break;
-    case kActGeluTanh: act_affine32<kActGeluTanh>(v, ep.pre_mul, ep.pre_add, ep.act_param, ep.post_mul); break;
-    case kActLeakyRelu: act_affine32<kActLeakyRelu>(v, ep.pre_mul, ep.pre_add, ep.act_param, ep.post_mul); break;
-    case kActSilu: act_affine32<kActSilu>(v, ep.pre_mul, ep.pre_add, ep.act_param, ep.post_mul); break;
-    default: act_affine32<kActNone>(v, ep.pre_mul, ep.pre_add, ep.act_param, ep.post_mul); break;
+    case kActRelu: affine_act32_sel<kActRelu>(ep, acc, v, m, a, lane_mul, lane_add); break;
+    case kActGeluTanh: affine_act32_sel<kActGeluTanh>(ep, acc, v, m, a, lane_mul, lane_add); break;
+    case kActLeakyRelu: affine_act32_sel<kActLeakyRelu>(ep, acc, v, m, a, lane_mul, lane_add); break;
+    case kActSilu: affine_act32_sel<kActSilu>(ep, acc, v, m, a, lane_mul, lane_add); break;
+    default: affine_act32_sel<kActNone>(ep, acc, v, m, a, lane_mul, lane_add); break;
   }
   const bool in_n = row_ok && (col0 + 32 <= N);
   if (ep.gate != nullptr && row_ok) {
@@ -206,6 +270,7 @@ __device__ __forceinline__ void epi_values(const EpilogueParams& ep, float alpha
   }
   if (ep.residual != nullptr && row_ok) {
     const bool full = in_n && ep.res_vec;
+    const float2 rs2 = make_float2(ep.res_scale, ep.res_scale);
     if (ep.res_dtype == kOutBF16) {
       const __nv_bfloat16* rp =
           reinterpret_cast<const __nv_bfloat16*>(ep.residual) + (long long)row * ep.res_ld + col0;
@@ -213,12 +278,14 @@ __device__ __forceinline__ void epi_values(const EpilogueParams& ep, float alpha
 #pragma unroll
         for (int j = 0; j < 32; j += 8) {
           uint4 q = *reinterpret_cast<const uint4*>(rp + j);
-          float2 a = unpack_bf16x2(q.x), b = unpack_bf16x2(q.y), c = unpack_bf16x2(q.z),
-                 d = unpack_bf16x2(q.w);
-          v[j] += a.x * ep.res_scale; v[j + 1] += a.y * ep.res_scale;
-          v[j + 2] += b.x * ep.res_scale; v[j + 3] += b.y * ep.res_scale;
-          v[j + 4] += c.x * ep.res_scale; v[j + 5] += c.y * ep.res_scale;
-          v[j + 6] += d.x * ep.res_scale; v[j + 7] += d.y * ep.res_scale;
+          const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const float2 r = ffma2(unpack_bf16x2(w[t]), rs2,
+                                   make_float2(v[j + 2 * t], v[j + 2 * t + 1]));
+            v[j + 2 * t] = r.x;
+            v[j + 2 * t + 1] = r.y;
+          }
         }
       } else {
         for (int j = 0; j < 32; ++j)
@@ -229,9 +296,10 @@ __device__ __forceinline__ void epi_values(const EpilogueParams& ep, float alpha
       if (full) {
 #pragma unroll
         for (int j = 0; j < 32; j += 4) {
-          float4 q = *reinterpret_cast<const float4*>(rp + j);
-          v[j] += q.x * ep.res_scale; v[j + 1] += q.y * ep.res_scale;
-          v[j + 2] += q.z * ep.res_scale; v[j + 3] += q.w * ep.res_scale;
+          const float4 q = *reinterpret_cast<const float4*>(rp + j);
+          const float2 r0 = ffma2(make_float2(q.x, q.y), rs2, make_float2(v[j], v[j + 1]));
+          const float2 r1 = ffma2(make_float2(q.z, q.w), rs2, make_float2(v[j + 2], v[j + 3]));
+          v[j] = r0.x; v[j + 1] = r0.y; v[j + 2] = r1.x; v[j + 3] = r1.y;
         }
       } else {
         for (int j = 0; j < 32; ++j)
@@ -381,12 +449,16 @@ __device__ __forceinline__ void epi_prefetch_residual(const EpilogueParams& ep, 
   }
 }
 
-// Per-lane epilogue vectors for the 32 columns starting at col0 (one coalesced load each).
-__device__ __forceinline__ void epi_lane_vectors(const EpilogueParams& ep, int col0, int N,
-                                                 float& lane_bias, float& lane_cscale) {
+// Per-lane epilogue vectors for the 32 columns starting at col0 (one coalesced load each),
+// folded with the affine step: lane_add = bias[c] * pre_mul + pre_add and lane_mul =
+// alpha * col_scale[c] * pre_mul for this lane's column c.
+__device__ __forceinline__ void epi_lane_vectors(const EpilogueParams& ep, float alpha, int col0,
+                                                 int N, float& lane_add, float& lane_mul) {
   const int c = col0 + (threadIdx.x & 31);
-  lane_bias = (ep.bias != nullptr && c < N) ? __ldg(ep.bias + c) : 0.f;
-  lane_cscale = (ep.col_scale != nullptr && c < N) ? __ldg(ep.col_scale + c) : 1.f;
+  const float bias = (ep.bias != nullptr && c < N) ? __ldg(ep.bias + c) : 0.f;
+  const float cs = (ep.col_scale != nullptr && c < N) ? __ldg(ep.col_scale + c) : 1.f;
+  lane_add = fmaf(bias, ep.pre_mul, ep.pre_add);
+  lane_mul = alpha * cs * ep.pre_mul;
 }
 
 // Drains one 128 x BN accumulator (this warp: 32 TMEM lanes = 32 rows) through the fused
@@ -485,6 +557,193 @@ __device__ __forceinline__ void epilogue_tile(const EpilogueParams& ep, const CU
       }
     }
   }
+}
+
+// ---------------------------------------------------------------------------------------
+// Fused attention-operand preparation (HeadPrepParams) for one 128-column half-tile.
+
+// Which head (if any) the half-tile starting at column c0 is: 1 = q, 2 = k, 3 = v, 0 = none.
+__device__ __forceinline__ int head_prep_kind(const HeadPrepParams& h, int c0, int& head) {
+  if (!h.on) return 0;
+  if (c0 >= h.q_off && c0 < h.q_off + h.q_heads * h.q_hstride &&
+      (c0 - h.q_off) % h.q_hstride == 0) {
+    head = (c0 - h.q_off) / h.q_hstride;
+    return 1;
+  }
+  if (c0 >= h.k_off && c0 < h.k_off + h.k_heads * 128 && (c0 - h.k_off) % 128 == 0) {
+    head = (c0 - h.k_off) / 128;
+    return 2;
+  }
+  if (c0 >= h.v_off && c0 < h.v_off + h.v_heads * 128 && (c0 - h.v_off) % 128 == 0) {
+    head = (c0 - h.v_off) / 128;
+    return 3;
+  }
+  return 0;
+}
+
+// Columns [e0, e0 + 16) of this lane's row as the projection's e4m3 codes (as f32): acc *
+// (alpha * col_scale) + bias (the multiplier / addend of column e0 + j in lane (e0 + j) % 32
+// of `lane_mul` / `lane_add`), rounded to e4m3 at the projection's scale exactly as the
+// ordinary epilogue stores it.
+__device__ __forceinline__ void head_prep_codes16(uint32_t taddr, float lane_mul,
+                                                  float lane_add, bool add, int lo,
+                                                  float inv_scale, float (&code)[16]) {
+  uint32_t r[16];
+  tmem_ld16(taddr, r);
+#pragma unroll
+  for (int j = 0; j < 16; j += 2) {
+    const float2 m2 = make_float2(__shfl_sync(0xffffffffu, lane_mul, lo + j),
+                                  __shfl_sync(0xffffffffu, lane_mul, lo + j + 1));
+    const float2 a2 = add ? make_float2(__shfl_sync(0xffffffffu, lane_add, lo + j),
+                                        __shfl_sync(0xffffffffu, lane_add, lo + j + 1))
+                          : make_float2(0.f, 0.f);
+    const float2 v = ffma2(make_float2(__uint_as_float(r[j]), __uint_as_float(r[j + 1])), m2,
+                           a2);
+    const float2 c = e4m3x2_to_f32x2(f32x2_to_e4m3x2(v.x * inv_scale, v.y * inv_scale));
+    code[j] = c.x;
+    code[j + 1] = c.y;
+  }
+}
+
+// q / k half-tile: RMSNorm over the head (f32 sum of squares in the order of the standalone
+// head-norm kernel: eight 16-column partial sums combined pairwise), weight, RoPE
+// (rotate_half: column e pairs with e + 64), e4m3 store.  `lm` / `la` hold the lane multipliers /
+// addends of the half-tile's four 32-column chunks.
+__device__ __forceinline__ void head_prep_qk(const HeadPrepParams& h, uint32_t t_row, int row,
+                                             int M, const float* w, uint8_t* dst,
+                                             const float (&lm)[4], const float (&la)[4],
+                                             bool add, float inv_scale) {
+  float inv = 1.0f;
+  if (w != nullptr) {
+    float part[8];
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+      float code[16];
+      head_prep_codes16(t_row + s * 16, lm[s >> 1], la[s >> 1], add, (s & 1) * 16, inv_scale,
+                        code);
+      float ss = 0.f;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const float x = code[e] * h.x_scale;
+        ss = fmaf(x, x, ss);
+      }
+      part[s] = ss;
+    }
+    const float ss = ((part[0] + part[1]) + (part[2] + part[3])) +
+                     ((part[4] + part[5]) + (part[6] + part[7]));
+    inv = rsqrtf(ss / 128.0f + h.eps);
+  }
+  const bool rope = h.cos != nullptr;
+  const long long pos = rope ? (long long)(row % h.seq) * 128 : 0;
+#pragma unroll 1
+  for (int s = 0; s < 4; ++s) {  // columns [16 s, 16 s + 16) and their partners + 64
+    float a[16], b[16];
+    head_prep_codes16(t_row + s * 16, lm[s >> 1], la[s >> 1], add, (s & 1) * 16, inv_scale,
+                      a);
+    head_prep_codes16(t_row + 64 + s * 16, lm[2 + (s >> 1)], la[2 + (s >> 1)], add,
+                      (s & 1) * 16, inv_scale, b);
+    uint32_t oa[4], ob[4];
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const int e = s * 16 + g * 4;
+      float4 wa = make_float4(1.f, 1.f, 1.f, 1.f), wb = wa;
+      if (w != nullptr) {
+        wa = __ldg(reinterpret_cast<const float4*>(w + e));
+        wb = __ldg(reinterpret_cast<const float4*>(w + e + 64));
+        wa.x += h.w_offset; wa.y += h.w_offset; wa.z += h.w_offset; wa.w += h.w_offset;
+        wb.x += h.w_offset; wb.y += h.w_offset; wb.z += h.w_offset; wb.w += h.w_offset;
+      }
+      const float wav[4] = {wa.x, wa.y, wa.z, wa.w}, wbv[4] = {wb.x, wb.y, wb.z, wb.w};
+      float ya[4], yb[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        ya[t] = a[g * 4 + t] * h.x_scale;
+        yb[t] = b[g * 4 + t] * h.x_scale;
+        if (w != nullptr) {
+          ya[t] = ya[t] * inv * wav[t];
+          yb[t] = yb[t] * inv * wbv[t];
+        }
+      }
+      if (rope) {
+        // (each lane reads its own row's tables: these loads do not coalesce, which makes
+        // RoPE in this epilogue slower than in a separate launch)
+        const float4 ca = __ldg(reinterpret_cast<const float4*>(h.cos + pos + e));
+        const float4 sa = __ldg(reinterpret_cast<const float4*>(h.sin + pos + e));
+        const float4 cb = __ldg(reinterpret_cast<const float4*>(h.cos + pos + e + 64));
+        const float4 sb = __ldg(reinterpret_cast<const float4*>(h.sin + pos + e + 64));
+        const float cav[4] = {ca.x, ca.y, ca.z, ca.w}, sav[4] = {sa.x, sa.y, sa.z, sa.w};
+        const float cbv[4] = {cb.x, cb.y, cb.z, cb.w}, sbv[4] = {sb.x, sb.y, sb.z, sb.w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const float xa = ya[t], xb = yb[t];
+          ya[t] = xa * cav[t] + xb * (-1.0f * sav[t]);
+          yb[t] = xb * cbv[t] + xa * (1.0f * sbv[t]);
+        }
+      }
+      oa[g] = uint32_t(f32x2_to_e4m3x2(ya[0] * h.out_inv_scale, ya[1] * h.out_inv_scale)) |
+              (uint32_t(f32x2_to_e4m3x2(ya[2] * h.out_inv_scale, ya[3] * h.out_inv_scale)) << 16);
+      ob[g] = uint32_t(f32x2_to_e4m3x2(yb[0] * h.out_inv_scale, yb[1] * h.out_inv_scale)) |
+              (uint32_t(f32x2_to_e4m3x2(yb[2] * h.out_inv_scale, yb[3] * h.out_inv_scale)) << 16);
+    }
+    if (row < M) {
+      *reinterpret_cast<uint4*>(dst + s * 16) = make_uint4(oa[0], oa[1], oa[2], oa[3]);
+      *reinterpret_cast<uint4*>(dst + 64 + s * 16) = make_uint4(ob[0], ob[1], ob[2], ob[3]);
+    }
+  }
+}
+
+// v half-tile: the e4m3 codes as 16-bit floats (exact), 128 columns of this lane's row.
+__device__ __forceinline__ void head_prep_v(const HeadPrepParams& h, uint32_t t_row, int row,
+                                            int M, uint16_t* dst, const float (&lm)[4],
+                                            const float (&la)[4], bool add, float inv_scale) {
+#pragma unroll 1
+  for (int s = 0; s < 8; ++s) {
+    float code[16];
+    head_prep_codes16(t_row + s * 16, lm[s >> 1], la[s >> 1], add, (s & 1) * 16, inv_scale,
+                        code);
+    uint32_t o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      o[j] = h.v_f16 ? pack_f16x2(code[2 * j], code[2 * j + 1])
+                     : pack_bf16x2(code[2 * j], code[2 * j + 1]);
+    if (row < M) {
+      *reinterpret_cast<uint4*>(dst + s * 16) = make_uint4(o[0], o[1], o[2], o[3]);
+      *reinterpret_cast<uint4*>(dst + s * 16 + 8) = make_uint4(o[4], o[5], o[6], o[7]);
+    }
+  }
+}
+
+// One 128- or HALF-column half-tile of the accumulator to its destination: a q / k / v head
+// of a fused preparation (HeadPrepParams, 128-column halves only), else the ordinary
+// epilogue.
+template <int HALF>
+__device__ __forceinline__ void drain_half(const EpilogueParams& ep, const CUtensorMap* tmap_out,
+                                           float alpha, uint32_t t_row, int row, int row0,
+                                           int col_base, int M, int N, uint8_t* stage, int& buf,
+                                           float& rowsum, float& amax_local,
+                                           const float (&lbv)[HALF / 32],
+                                           const float (&lcv)[HALF / 32]) {
+  if constexpr (HALF == 128) {
+    int head = 0;
+    const int kind = head_prep_kind(ep.hp, col_base, head);
+    if (kind != 0) {
+      const HeadPrepParams& hp = ep.hp;
+      const bool add = ep.bias != nullptr;
+      if (kind == 3) {
+        head_prep_v(hp, t_row, row, M, hp.v_out + (long long)row * hp.v_ld + head * 128, lcv,
+                    lbv, add, ep.out_inv_scale);
+      } else {
+        const bool isq = kind == 1;
+        uint8_t* dst = isq ? hp.q_out + (long long)row * hp.q_ld + head * 128
+                           : hp.k_out + (long long)row * hp.k_ld + head * 128;
+        head_prep_qk(hp, t_row, row, M, isq ? hp.q_w : hp.k_w, dst, lcv, lbv, add,
+                     ep.out_inv_scale);
+      }
+      return;
+    }
+  }
+  epilogue_tile<HALF>(ep, tmap_out, alpha, t_row, row, row0, col_base, M, N, stage, buf, rowsum,
+                      amax_local, lbv, lcv);
 }
 
 template <int BN>
@@ -654,7 +913,7 @@ __global__ void __launch_bounds__(320, 1)
         const int cb0 = nb * BN + chalf * (BN / 2);
         epi_prefetch_residual<BN / 2>(ep, mb * Cfg::BM + q * 32 + lane, cb0, M, N);
 #pragma unroll
-        for (int x = 0; x < BN / 64; ++x) epi_lane_vectors(ep, cb0 + x * 32, N, lbv[x], lcv[x]);
+        for (int x = 0; x < BN / 64; ++x) epi_lane_vectors(ep, alpha, cb0 + x * 32, N, lbv[x], lcv[x]);
       }
       // tcgen05.ld is warp-collective: the whole warp leaves together or not at all.
       if (!__all_sync(0xffffffffu,
@@ -777,8 +1036,8 @@ __global__ void __launch_bounds__(320, 1)
         }
       }
       if (drain_tmem) {
-        epilogue_tile<BN / 2>(ep, &tmap_out, alpha, t_row, row, row0, col_base, M, N, stage,
-                              buf, rowsum, amax_local, lbv, lcv);
+        drain_half<BN / 2>(ep, &tmap_out, alpha, t_row, row, row0, col_base, M, N, stage, buf,
+                           rowsum, amax_local, lbv, lcv);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty_bar[acc]);
@@ -804,31 +1063,36 @@ __global__ void __launch_bounds__(320, 1)
 
 
 // ---------------------------------------------------------------------------------------
-// CTA-pair variant (cluster of 2, tcgen05 cta_group::2): the pair owns a 256 x 256 output
-// tile.  CTA r loads A rows [128 r, 128 r + 128) and B rows [128 r, 128 r + 128) of the
-// tile; the leader (r = 0) issues M=256, N=256, K=32 MMAs that read both CTAs' shared
-// memory, and each CTA's TMEM receives its own 128 rows x 256 columns.  Per SM this moves
+// CTA-pair variant (cluster of 2, tcgen05 cta_group::2): the pair owns a 256 x BN output
+// tile (BN 256, or 128 where 256-wide tiles leave most of a wave idle).  CTA r loads A rows
+// [128 r, 128 r + 128) and B rows [BN/2 r, BN/2 (r + 1)) of the tile; the leader (r = 0)
+// issues M=256, N=BN, K=32 MMAs that read both CTAs' shared memory, and each CTA's TMEM
+// receives its own 128 rows x BN columns.  Per SM this moves
 // half the B bytes of the single-CTA kernel for the same MMA work.  TMA loads are plain
 // (no multicast); only tcgen05.commit multicasts its arrive to both CTAs.
+template <int BN_>
 struct Gemm2Cfg {
   static constexpr int BM = 128;   // rows per CTA (256 per pair)
-  static constexpr int BN = 256;   // columns per pair tile (128 B rows per CTA)
+  static constexpr int BN = BN_;   // columns per pair tile (BN / 2 B rows per CTA)
   static constexpr int BK = 128;
-  static constexpr int STAGES = 6;
+  static constexpr int STAGES = BN == 256 ? 6 : 8;
   static constexpr int A_BYTES = BM * BK;
   static constexpr int B_BYTES = (BN / 2) * BK;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 4 * 8192 + 1024 + 256;
   static constexpr int THREADS = 320;  // producer, MMA, 8 epilogue warps
+  static_assert(BN == 128 || BN == 256, "pair tiles are 256 x 128 or 256 x 256");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
 };
 
+template <int PBN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
     gemm_fp8_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                          const __grid_constant__ CUtensorMap tmap_b,
                          const __grid_constant__ CUtensorMap tmap_out, const GemmShape shape,
                          const EpilogueParams ep) {
-  using Cfg = Gemm2Cfg;
+  using Cfg = Gemm2Cfg<PBN>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int BN = Cfg::BN;
   extern __shared__ uint8_t smem_raw[];
@@ -976,7 +1240,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
         epi_prefetch_residual<BN / 2>(ep, mb * 2 * Cfg::BM + rank * Cfg::BM + q * 32 + lane, cb0,
                                       M, N);
 #pragma unroll
-        for (int x = 0; x < BN / 64; ++x) epi_lane_vectors(ep, cb0 + x * 32, N, lbv[x], lcv[x]);
+        for (int x = 0; x < BN / 64; ++x) epi_lane_vectors(ep, alpha, cb0 + x * 32, N, lbv[x], lcv[x]);
       }
       // tcgen05.ld is warp-collective: the whole warp leaves together or not at all.
       if (!__all_sync(0xffffffffu,
@@ -987,8 +1251,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
       const int row = row0 + lane;
       float rowsum = 0.0f;
       const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + acc * BN + chalf * (BN / 2);
-      epilogue_tile<BN / 2>(ep, &tmap_out, alpha, t_row, row, row0, nb * BN + chalf * (BN / 2),
-                            M, N, stage, buf, rowsum, amax_local, lbv, lcv);
+      drain_half<BN / 2>(ep, &tmap_out, alpha, t_row, row, row0, nb * BN + chalf * (BN / 2), M,
+                         N, stage, buf, rowsum, amax_local, lbv, lcv);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(map_to_rank(&tempty_bar[acc], 0));

@@ -754,7 +754,180 @@ __global__ void __launch_bounds__(256) norm_warp_kernel(const NormParams p) {
   }
 }
 
+// Same warp-per-row arithmetic with the rows arriving through a shared-memory ring: each
+// warp owns `stages` row slots and its lane 0 keeps that many untiled bulk copies
+// (cp.async.bulk, completion on the slot's mbarrier) in flight ahead of the row being
+// normalised, so the bytes in flight per SM no longer sit in registers (the register
+// prefetch above holds two rows per warp in registers and runs one 256-thread CTA per SM
+// for 2560-column rows; here two CTAs fit and each warp has up to kRingMaxStages - 1 rows
+// outstanding while it normalises one).
+constexpr int kRingMaxStages = 4;
+
+// 16-byte shared-memory load that the compiler may not merge with an earlier one (the ring
+// slot is re-read after the warp reduction instead of keeping the row in registers).
+__device__ __forceinline__ uint4 lds16(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+constexpr int kRingWarps = 8;
+
+template <int NV, bool WF32>
+__global__ void __launch_bounds__(256, 2) norm_warp_ring_kernel(const NormParams p, int stages) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t full[kRingWarps][kRingMaxStages];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int nvec = p.cols / 8;
+  const uint32_t row_bytes = (uint32_t)nvec * 16;
+  constexpr int WV = WF32 ? 2 : 1;  // 16-byte words per 8 weights
+  uint4* sw = reinterpret_cast<uint4*>(smem);
+  const bool ln = p.kind == 1;
+  const bool has_b = ln && p.bias != nullptr;
+  uint4* sb = sw + nvec * WV;
+  uint8_t* ring = smem + (size_t)nvec * 16 * WV * (has_b ? 2 : 1) +
+                  (size_t)warp * stages * row_bytes;
+  const int nw = gridDim.x * kRingWarps;
+  const int row0 = blockIdx.x * kRingWarps + warp;
+  const int nrows = row0 < p.rows ? (p.rows - 1 - row0) / nw + 1 : 0;
+  const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(p.x);
+  const uint64_t pol = policy_evict_first();
+  auto issue = [&](int k) {
+    const int slot = k % stages;
+    const long long r = row0 + (long long)k * nw;
+    mbar_arrive_expect_tx(&full[warp][slot], row_bytes);
+    bulk_load(ring + (size_t)slot * row_bytes, xb + r * p.x_ld, row_bytes, &full[warp][slot], pol);
+  };
+  int issued = 0;
+  if (lane == 0) {
+    for (int i = 0; i < stages; ++i) mbar_init(&full[warp][i], 1);
+    fence_mbarrier_init();
+    for (; issued < stages && issued < nrows; ++issued) issue(issued);
+  }
+  for (int i = threadIdx.x; i < nvec * WV; i += blockDim.x) {
+    sw[i] = reinterpret_cast<const uint4*>(p.weight)[i];
+    if (has_b) sb[i] = reinterpret_cast<const uint4*>(p.bias)[i];
+  }
+  __syncthreads();  // weights staged; every warp's barriers initialised
+  auto wload = [&](const uint4* base, int vi, float (&o)[8]) {
+    if constexpr (WF32) {
+      const float4 a = reinterpret_cast<const float4*>(base)[2 * vi];
+      const float4 b = reinterpret_cast<const float4*>(base)[2 * vi + 1];
+      o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w; o[4] = b.x; o[5] = b.y; o[6] = b.z;
+      o[7] = b.w;
+    } else {
+      const uint4 q = base[vi];
+      const float2 a = unpack_bf16x2(q.x), b = unpack_bf16x2(q.y), c = unpack_bf16x2(q.z),
+                   d = unpack_bf16x2(q.w);
+      o[0] = a.x; o[1] = a.y; o[2] = b.x; o[3] = b.y; o[4] = c.x; o[5] = c.y; o[6] = d.x;
+      o[7] = d.y;
+    }
+  };
+  auto unpack = [&](const uint4& q, float (&v)[8]) {
+    const float2 a = unpack_bf16x2(q.x), b = unpack_bf16x2(q.y), c = unpack_bf16x2(q.z),
+                 d = unpack_bf16x2(q.w);
+    v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y; v[4] = c.x; v[5] = c.y; v[6] = d.x;
+    v[7] = d.y;
+    if (p.x_scale != 1.0f) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] *= p.x_scale;
+    }
+  };
+  const float n = float(p.cols);
+  const float qinv = 1.0f / p.q_scale;
+  int k = 0;
+  bool aborted = false;
+  for (; k < nrows; ++k) {
+    const int slot = k % stages;
+    const bool ok = mbar_wait(&full[warp][slot], (k / stages) & 1, kDevTimeoutProducer, nullptr);
+    if (!__all_sync(0xffffffffu, ok)) {
+      aborted = true;
+      break;
+    }
+    // The row is read from the slot twice (statistics, outputs) rather than held in
+    // registers across the warp reduction, which would spill at the longer rows.
+    const uint32_t src = smem_u32(ring + (size_t)slot * row_bytes);
+    auto cur = [&](int i) -> uint4 {
+      const int vi = lane + 32 * i;
+      return vi < nvec ? lds16(src + vi * 16) : make_uint4(0u, 0u, 0u, 0u);
+    };
+    const long long row = row0 + (long long)k * nw;
+    float mean = 0.f, s2 = 0.f;
+    if (ln) {
+      float s1 = 0.f;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        float v[8];
+        unpack(cur(i), v);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s1 += v[j];
+      }
+      mean = warp_sum(s1) / n;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        if (lane + 32 * i < nvec) {
+          float v[8];
+          unpack(cur(i), v);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float d = v[j] - mean;
+            s2 += d * d;
+          }
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        float v[8];
+        unpack(cur(i), v);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s2 += v[j] * v[j];
+      }
+    }
+    const float inv = rsqrtf(warp_sum(s2) / n + p.eps);
+    uint8_t* qrow = p.q_out + row * p.q_ld;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int vi = lane + 32 * i;
+      if (vi < nvec) {
+        float h[8], w[8], y[8];
+        unpack(cur(i), h);
+        wload(sw, vi, w);
+        if (ln) {
+          float bb[8];
+          if (has_b) {
+            wload(sb, vi, bb);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) bb[j] = 0.f;
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) y[j] = (h[j] - mean) * inv * w[j] + bb[j];
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) y[j] = h[j] * inv * (w[j] + p.w_offset);
+        }
+        __stcs(reinterpret_cast<uint2*>(qrow + vi * 8), quant8(y, qinv));
+      }
+    }
+    __syncwarp();  // every lane has read the slot: refill it
+    if (lane == 0 && issued < nrows) {
+      fence_proxy_async_smem();
+      issue(issued++);
+    }
+  }
+  if (aborted && lane == 0) {
+    // Let the copies still in flight land before the CTA's shared memory is released.
+    for (int j = k; j < issued; ++j)
+      mbar_wait(&full[warp][j % stages], (j / stages) & 1, kDevTimeoutDrain, nullptr);
+  }
+}
+
 using WarpFn = void (*)(const NormParams);
+using WarpRingFn = void (*)(const NormParams, int);
 
 template <bool WF32>
 WarpFn pick_warp(int nv) {
@@ -792,9 +965,65 @@ bool plan_warp(const NormParams& p) {
   return true;
 }
 
+template <bool WF32>
+WarpRingFn pick_warp_ring(int nv) {
+  switch (nv) {
+    case 1: return norm_warp_ring_kernel<1, WF32>;
+    case 2: return norm_warp_ring_kernel<2, WF32>;
+    case 3: return norm_warp_ring_kernel<3, WF32>;
+    case 4: return norm_warp_ring_kernel<4, WF32>;
+    case 5: return norm_warp_ring_kernel<5, WF32>;
+    case 6: return norm_warp_ring_kernel<6, WF32>;
+    case 7: return norm_warp_ring_kernel<7, WF32>;
+    case 8: return norm_warp_ring_kernel<8, WF32>;
+    case 9: return norm_warp_ring_kernel<9, WF32>;
+    case 10: return norm_warp_ring_kernel<10, WF32>;
+    case 11: return norm_warp_ring_kernel<11, WF32>;
+    default: return norm_warp_ring_kernel<12, WF32>;
+  }
+}
+
+// Ring depth for the bulk-copy schedule: as many row slots per warp (2..kRingMaxStages) as
+// fit two CTAs per SM; 0 when two slots do not fit (the register-prefetch kernel then runs).
+int warp_ring_stages(const NormParams& p) {
+  const size_t nvec = p.cols / 8;
+  const bool has_b = p.kind == 1 && p.bias != nullptr;
+  const size_t wbytes = nvec * 16 * (p.w_dtype == kF32 ? 2 : 1) * (has_b ? 2 : 1);
+  const size_t budget = 110 * 1024;  // two CTAs per SM, with room for the static barriers
+  if (wbytes >= budget) return 0;
+  const size_t per = (budget - wbytes) / ((size_t)kRingWarps * nvec * 16);
+  return per < 2 ? 0 : (int)std::min<size_t>(per, kRingMaxStages);
+}
+
 int launch_warp(const NormParams& p, cudaStream_t s) {
   const int nvec = p.cols / 8;
   const bool wf32 = p.w_dtype == kF32;
+  if (const int stages = warp_ring_stages(p)) {
+    const WarpRingFn fn =
+        wf32 ? pick_warp_ring<true>((nvec + 31) / 32) : pick_warp_ring<false>((nvec + 31) / 32);
+    const bool has_b = p.kind == 1 && p.bias != nullptr;
+    const size_t smem = (size_t)nvec * 16 * (wf32 ? 2 : 1) * (has_b ? 2 : 1) +
+                        (size_t)kRingWarps * stages * nvec * 16;
+    int per_sm = 0;
+    {
+      static std::mutex mu;
+      static std::map<std::pair<int, const void*>, bool> opted;
+      std::lock_guard<std::mutex> g(mu);
+      int dev = 0;
+      cudaGetDevice(&dev);
+      if (!opted[{dev, (const void*)fn}]) {
+        B2F_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          110 * 1024));
+        opted[{dev, (const void*)fn}] = true;
+      }
+    }
+    B2F_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 256, smem));
+    const int grid = std::max(1, std::min((p.rows + kRingWarps - 1) / kRingWarps,
+                                          sm_count() * std::max(per_sm, 1)));
+    fn<<<grid, 256, smem, s>>>(p, stages);
+    B2F_CUDA_TRY(cudaGetLastError());
+    return B2F_OK;
+  }
   const WarpFn fn = wf32 ? pick_warp<true>((nvec + 31) / 32) : pick_warp<false>((nvec + 31) / 32);
   const size_t smem = (size_t)2 * nvec * 16 * (wf32 ? 2 : 1);
   int per_sm = 0;

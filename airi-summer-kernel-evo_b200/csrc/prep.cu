@@ -442,16 +442,18 @@ int b2f_attn_prep(const b2f_rope_args* q, const b2f_rope_args* k, const void* v_
     return fail(B2F_ERR_UNSUPPORTED,
                 "attn_prep: q and k need head_dim 128, heads a multiple of 4 (<= 32), full or "
                 "no RoPE, 16-byte aligned rows, and the same token count");
-  if (v_in == nullptr || v_out == nullptr || v_cols <= 0 || v_cols % 8 || v_in_ld % 8 ||
-      v_out_ld % 8 || ((uintptr_t)v_in & 7) || ((uintptr_t)v_out & 15) ||
-      (v_dtype != B2F_DTYPE_F16 && v_dtype != B2F_DTYPE_BF16))
+  const bool has_v = v_in != nullptr || v_out != nullptr || v_cols != 0;
+  if (has_v &&
+      (v_in == nullptr || v_out == nullptr || v_cols <= 0 || v_cols % 8 || v_in_ld % 8 ||
+       v_out_ld % 8 || ((uintptr_t)v_in & 7) || ((uintptr_t)v_out & 15) ||
+       (v_dtype != B2F_DTYPE_F16 && v_dtype != B2F_DTYPE_BF16)))
     return fail(B2F_ERR_ARG, "attn_prep: V must be e4m3 -> f16 / bf16, cols and pitches "
                              "multiples of 8, aligned");
   VConvertParams pv{reinterpret_cast<const uint8_t*>(v_in), v_in_ld,
                     reinterpret_cast<uint16_t*>(v_out), v_out_ld, q->rows, v_cols,
                     v_dtype == B2F_DTYPE_F16 ? 1 : 0};
   const int nq = (q->rows + 7) / 8, nk = (k->rows + 7) / 8;
-  const long long nv = ((long long)q->rows * (v_cols / 8) + 255) / 256;
+  const long long nv = has_v ? ((long long)q->rows * (v_cols / 8) + 255) / 256 : 0;
   const int grid = (int)(nq + nk + nv);
   cudaStream_t s = (cudaStream_t)stream;
   const int gq = q->heads / 4, gk = k->heads / 4;

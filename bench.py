@@ -694,6 +694,8 @@ def _stage_model(kind, blk):
         return {
             "ln1": (0.0, t * d * 3.0, FP8_PEAK),
             "qkv_gemm": (2.0 * t * d * 3 * d, t * d + 3 * d * d + 3 * t * d + 0.0, FP8_PEAK),
+            # QKV GEMM writing q, k (e4m3) and the 16-bit V image from its epilogue
+            "qkv_gemm_v": (2.0 * t * d * 3 * d, t * d + 3 * d * d + 4 * t * d + 0.0, FP8_PEAK),
             "v_convert": (0.0, t * d * 3.0, FP8_PEAK),
             "attention": (2.0 * b * h * s * s * hd, t * d * 5.0, ATTN_PEAK),
             "out_gemm": (2.0 * t * d * d, t * d + d * d + 4.0 * t * d, FP8_PEAK),
@@ -706,6 +708,10 @@ def _stage_model(kind, blk):
     return {
         "in_norm": (0.0, t * hid * 3.0, FP8_PEAK),
         "qgkv_gemm": (2.0 * t * hid * nc, t * hid + nc * hid + t * nc + 0.0, FP8_PEAK),
+        # projection with the q / k norm + RoPE and the V copy in its epilogue: reads A and
+        # the weights, writes the gate (e4m3), q and k (e4m3) and V (16-bit)
+        "qgkv_gemm_prep": (2.0 * t * hid * nc,
+                           t * hid + nc * hid + t * (nc - hk * dh) + 2.0 * t * hk * dh, FP8_PEAK),
         "qkv_prep": (0.0, 2.0 * t * (h + hk) * dh + 3.0 * t * hk * dh, FP8_PEAK),
         "qk_norm_rope": (0.0, 2.0 * t * (h + hk) * dh, FP8_PEAK),
         "v_convert": (0.0, 3.0 * t * hk * dh, FP8_PEAK),
@@ -733,7 +739,6 @@ class BlockWorkload:
             self.w = _gpt2_weights(g)
             self.dp, self.tp = sharding.plan_block_parallel(world, self.batch, 12, 12, tp=tp or 1)
             self.name = "gpt2_block_fp8_b8_s1024"
-            self.launches = 8
         else:
             self.batch, self.seq, self.hidden = 4, 2048, 2560
             self.w = _qwen_weights(g, self.seq)
@@ -761,8 +766,7 @@ class BlockWorkload:
         else:
             self.blk = blocks.QwenBlock(self.w, **kw)
             self.local = self.blk
-        if kind != "gpt2":
-            self.launches = self.local.launches_per_forward
+        self.launches = self.local.launches_per_forward
         self.x = self.x_cpu.cuda()
         self.blk.capture(self.x)
         self.blk.graph_input.copy_(self.x)

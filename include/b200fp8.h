@@ -116,7 +116,8 @@ typedef struct b2f_gemm_args {
   float out_scale;
   float* amax;
   int mode;
-  int tile_n; /* 0 = automatic, else 128, 256 or 512 (CTA-pair 256 x 256 tiles) */
+  int tile_n; /* 0 = automatic; 64, 128 or 256 (one CTA, 128-row tiles); -128 or -256 (CTA pair,
+                256-row tiles of 128 or 256 columns; 512 = -256) */
   /* Split-K (few output tiles, long K): `splits` K slices per tile, at most 8 (0 =
    * automatic: two slices when a large-enough workspace is given, the 128 x 128 tiles fill
    * at most half of the SMs and K >= 4096; otherwise none).  The workspace holds a fixed
@@ -143,6 +144,46 @@ typedef struct b2f_gemm_args {
 void b2f_gemm_args_init(b2f_gemm_args* args);
 
 int b2f_gemm_fp8(const b2f_gemm_args* args, b2f_stream_t stream);
+
+/* Attention-operand preparation fused into a q / gate / k / v projection GEMM.
+ * The GEMM is `args` (e4m3 output; alpha, column scale and bias only: no activation /
+ * residual / gate / amax / split-K; 256-column tiles, on CTA pairs where b2f_gemm_fp8 would
+ * use them, else on single CTAs).  Of its output columns:
+ *   q head h   = [q_off + h * q_head_stride, + 128): RMSNorm over the head (q_norm_w +
+ *                weight_offset; skipped when null), RoPE (rope_cos / rope_sin [seq][128],
+ *                rotate_half over the whole head, position = row % seq; skipped when null),
+ *                stored as e4m3 codes y / out_scale in q_out[row, 128 h ..] (q_ld bytes);
+ *   k head h   = [k_off + 128 h, + 128): the same with k_norm_w into k_out;
+ *   v head h   = [v_off + 128 h, + 128): the e4m3 codes as f16 / bf16 (v_dtype) into v_out;
+ *   the rest   (the attention gate) is stored as the plain GEMM would store it, in args->out.
+ * The q / k / v values are first rounded to e4m3 at args->out_scale, exactly the codes the
+ * plain GEMM would store, so the result equals b2f_gemm_fp8 followed by b2f_attn_prep up
+ * to the f32 rounding of the norm (at most one e4m3 step).  Offsets and head strides are
+ * multiples of 256 / 128 such that every head is one 128-column half of a 256-column tile;
+ * head_dim 128 only.  Replaces the reference block's q/gate/k/v projection followed by its
+ * q/k RMSNorm + RoPE (tasks/model_qwen35_4b_full_attention_block_fp8/starter.py:339-366). */
+typedef struct b2f_head_prep_args {
+  int q_off, q_head_stride, q_heads;
+  int k_off, k_heads;
+  int v_off, v_heads;
+  void* q_out;
+  long long q_ld;
+  void* k_out;
+  long long k_ld;
+  void* v_out;
+  long long v_ld; /* elements */
+  int v_dtype;    /* B2F_DTYPE_F16 or B2F_DTYPE_BF16 */
+  const float* q_norm_w;
+  const float* k_norm_w;
+  float weight_offset, eps;
+  const float* rope_cos;
+  const float* rope_sin;
+  int seq;
+  float out_scale; /* q / k codes = e4m3(y / out_scale) */
+} b2f_head_prep_args;
+
+int b2f_gemm_fp8_head_prep(const b2f_gemm_args* args, const b2f_head_prep_args* hp,
+                           b2f_stream_t stream);
 
 /* Split-K GEMM that allocates nothing (no counterpart in the reference).
  * For callers that cannot allocate device memory at call time - a library loaded as a
@@ -350,7 +391,9 @@ int b2f_head_norm_rope(const b2f_rope_args* args, b2f_stream_t stream);
 /* The three operand preparations of a gated GQA attention in one launch: q and k as
  * b2f_head_norm_rope (head_dim 128, heads a multiple of 4, full or no RoPE, 16-byte aligned
  * rows; the same token count) and V [q->rows, v_cols] e4m3 -> f16 or bf16 (v_dtype,
- * exact).  B2F_ERR_UNSUPPORTED for other shapes (call the three operations separately).
+ * exact; v_in = v_out = null and v_cols = 0 skip it, for a V image already written by
+ * b2f_gemm_fp8_head_prep).  B2F_ERR_UNSUPPORTED for other shapes (call the operations
+ * separately).
  * Replaces: the q / k normalisation, RoPE and V requantisation steps of
  *   qwen35_full_attention_block (tasks/model_qwen35_4b_full_attention_block_fp8/starter.py:
  *   365-376), fused into one launch. */

@@ -240,3 +240,113 @@ def test_attn_prep_one_launch_matches_separate_ops(hq, hkv):
         assert int(diff.max()) <= 1 and float((diff > 0).float().mean()) < 0.01
     v_ref = proj[:, (2 * hq + hkv) * d:].float().to(torch.float16)
     assert torch.equal(vo.cpu(), v_ref)
+
+
+@pytest.mark.parametrize("hq,hkv,interleaved,rope", [
+    (32, 8, False, True),    # the bench block's layout: q heads, gate heads, k, v
+    (16, 4, True, True),     # q / gate interleaved per head (head stride 256)
+    (8, 4, False, False),    # no RoPE
+])
+def test_gemm_head_prep_matches_gemm_then_prep(hq, hkv, interleaved, rope):
+    """b2f_gemm_fp8_head_prep (q / k norm + RoPE and the V copy in the projection GEMM's
+    epilogue) against the same GEMM's e4m3 output run through b2f_attn_prep: the gate
+    columns and the V image are bit-identical, q / k within one e4m3 code (the f32 norm is
+    summed in the same order; contraction choices may differ) and almost all equal."""
+    ops = _ops()
+    t, seq, d, hid = 512, 256, 128, 512
+    g = gen(31 + hq + int(interleaved))
+    s = 1 / 64.0
+    ncat = (2 * hq + 2 * hkv) * d
+    a = _e4m3(torch.randn((t, hid), generator=g) * 4)
+    w = _e4m3(torch.randn((ncat, hid), generator=g) * 4)
+    cs = (torch.rand((ncat,), generator=g) * 0.5 + 0.75) * (2.0 ** -9)
+    wq = torch.randn((d,), generator=g) * 0.02
+    wk = torch.randn((d,), generator=g) * 0.02
+    cos, sin = oatt.rope_tables(seq, d, 1e6, batch=1)
+    tab = lambda z: z[:seq].contiguous().cuda()  # noqa: E731
+    qh = 2 * d if interleaved else d
+    q_off, g_off = 0, (d if interleaved else hq * d)
+    k_off = 2 * hq * d
+    v_off = k_off + hkv * d
+    ad, wd, csd = a.cuda(), w.cuda(), cs.cuda()
+    rope_kw = dict(cos=tab(cos), sin=tab(sin)) if rope else {}
+
+    proj = ops.gemm_fp8(ad, wd, col_scale=csd, out_dtype=torch.float8_e4m3fn, out_scale=s)
+    q1 = torch.empty((t, hq * d), dtype=torch.float8_e4m3fn, device="cuda")
+    k1 = torch.empty((t, hkv * d), dtype=torch.float8_e4m3fn, device="cuda")
+    v1 = torch.empty((t, hkv * d), dtype=torch.float16, device="cuda")
+    assert ops.attn_prep(proj[:, q_off:], proj[:, k_off:], proj[:, v_off:v_off + hkv * d],
+                         q_heads=hq, k_heads=hkv, head_dim=d, in_scale=s, out_scale=s,
+                         q_head_stride=qh, q_weight=wq.cuda(), k_weight=wk.cuda(),
+                         rotary_dim=d if rope else 0, seq=seq, q_out=q1, k_out=k1, v_out=v1,
+                         **rope_kw)
+
+    proj2 = torch.zeros((t, ncat), dtype=torch.float8_e4m3fn, device="cuda")
+    q2 = torch.empty_like(q1)
+    k2 = torch.empty_like(k1)
+    v2 = torch.empty_like(v1)
+    assert ops.gemm_fp8_head_prep(ad, wd, col_scale=csd, out=proj2, out_scale=s, q_out=q2,
+                                  k_out=k2, v_out=v2, q_off=q_off, q_heads=hq,
+                                  q_head_stride=qh, k_off=k_off, k_heads=hkv, v_off=v_off,
+                                  v_heads=hkv, q_norm_w=wq.cuda(), k_norm_w=wk.cuda(),
+                                  weight_offset=1.0, eps=1e-6, seq=seq, **rope_kw)
+    torch.cuda.synchronize()
+    gate_cols = torch.cat([torch.arange(g_off + h * qh, g_off + h * qh + d) for h in range(hq)])
+    assert torch.equal(proj2.view(torch.uint8)[:, gate_cols].cpu(),
+                       proj.view(torch.uint8)[:, gate_cols].cpu())
+    assert torch.equal(v2.cpu(), v1.cpu())
+    for got, ref in ((q2, q1), (k2, k1)):
+        diff = e4m3_ulp_diff(got.cpu(), ref.cpu())
+        assert int(diff.max()) <= 1 and float((diff > 0).float().mean()) < 0.001
+
+
+@pytest.mark.parametrize("t,d", [(512, 768), (300, 1024)])
+def test_gemm_v_copy_in_epilogue_matches_gemm_then_convert(t, d):
+    """The GPT-2 / vision QKV GEMM (bias, single-CTA 256-column tiles) writing the 16-bit V
+    image from its epilogue (b2f_gemm_fp8_head_prep with V blocks only): q / k columns and
+    the V image bit-identical to the plain GEMM followed by the e4m3 -> f16 conversion."""
+    ops = _ops()
+    g = gen(7 + d)
+    s = 1 / 64.0
+    a = _e4m3(torch.randn((t, d), generator=g) * 4).cuda()
+    w = _e4m3(torch.randn((3 * d, d), generator=g) * 4).cuda()
+    bias = (torch.randn((3 * d,), generator=g) * 0.1).cuda()
+    kw = dict(scale_a=2.0 ** -5, scale_b=2.0 ** -6, bias=bias)
+    qkv = ops.gemm_fp8(a, w, out_dtype=torch.float8_e4m3fn, out_scale=s, **kw)
+    v1 = ops.fp8_to_f16(qkv[:, 2 * d:], out=torch.empty((t, d), dtype=torch.float16,
+                                                           device="cuda"))
+    qkv2 = torch.zeros_like(qkv)
+    v2 = torch.empty((t, d), dtype=torch.float16, device="cuda")
+    assert ops.gemm_fp8_head_prep(a, w, out=qkv2, out_scale=s, q_out=None, k_out=None,
+                                  v_out=v2, q_off=0, q_heads=0, k_off=0, k_heads=0,
+                                  v_off=2 * d, v_heads=d // 128, **kw)
+    torch.cuda.synchronize()
+    assert torch.equal(qkv2.view(torch.uint8)[:, :2 * d].cpu(), qkv.view(torch.uint8)[:, :2 * d].cpu())
+    assert torch.equal(v2.cpu(), v1.cpu())
+
+
+def test_attn_prep_without_v_copy():
+    """b2f_attn_prep with no V operand (the V image already written by the projection
+    GEMM's epilogue): q / k outputs identical to the call with the V copy."""
+    ops = _ops()
+    t, seq, d, hq, hkv = 512, 256, 128, 16, 4
+    g = gen(5)
+    s = 1 / 64.0
+    proj = _e4m3(torch.randn((t, (2 * hq + 2 * hkv) * d), generator=g) / s).cuda()
+    wq = (torch.randn((d,), generator=g) * 0.02).cuda()
+    wk = (torch.randn((d,), generator=g) * 0.02).cuda()
+    cos, sin = oatt.rope_tables(seq, d, 1e6, batch=1)
+    kw = dict(q_heads=hq, k_heads=hkv, head_dim=d, in_scale=s, out_scale=s, q_weight=wq,
+              k_weight=wk, cos=cos[:seq].contiguous().cuda(), sin=sin[:seq].contiguous().cuda(),
+              rotary_dim=d, seq=seq)
+    outs = []
+    for with_v in (True, False):
+        qo = torch.empty((t, hq * d), dtype=torch.float8_e4m3fn, device="cuda")
+        ko = torch.empty((t, hkv * d), dtype=torch.float8_e4m3fn, device="cuda")
+        vo = torch.empty((t, hkv * d), dtype=torch.float16, device="cuda") if with_v else None
+        vsrc = proj[:, (2 * hq + hkv) * d:] if with_v else None
+        assert ops.attn_prep(proj, proj[:, 2 * hq * d:], vsrc, q_out=qo, k_out=ko, v_out=vo, **kw)
+        outs.append((qo, ko))
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0][0].view(torch.uint8).cpu(), outs[1][0].view(torch.uint8).cpu())
+    assert torch.equal(outs[0][1].view(torch.uint8).cpu(), outs[1][1].view(torch.uint8).cpu())

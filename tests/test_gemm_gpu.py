@@ -33,7 +33,7 @@ def _close_bf16(out, ref, k):
     (128, 256, 128), (128, 128, 256), (256, 512, 1024), (1000, 777, 528),
     (8, 40, 64), (384, 2304, 768), (1024, 1024, 4096),
 ])
-@pytest.mark.parametrize("tile_n", [0, 64, 128, 256, 512])
+@pytest.mark.parametrize("tile_n", [0, 64, 128, 256, 512, -128])
 def test_gemm_bf16_out(m, n, k, tile_n):
     g = gen(20260726 + m + n + k)
     a, sa = fp8_amax((m, k), g)
@@ -104,7 +104,7 @@ def test_gemm_rowsum_level2_14():
     assert err < 1e-3 * (1 + ref.abs().max().item()), err
 
 
-@pytest.mark.parametrize("tile_n", [0, 64, 128, 256, 512])
+@pytest.mark.parametrize("tile_n", [0, 64, 128, 256, 512, -128])
 @pytest.mark.parametrize("res_dtype", [torch.bfloat16, torch.float32])
 def test_gemm_residual_requant_e4m3(res_dtype, tile_n):
     m, n, k = 512, 768, 768
