@@ -153,13 +153,17 @@ int launch_gemm(const b2f_gemm_args* a, EpilogueParams ep, cudaStream_t stream) 
   GemmShape shape{a->m, a->n, a->k, splits};
   const int units = num_tiles * splits;
   const int grid = units < sms ? units : sms;
-  auto kern = gemm_fp8_kernel<BN>;
+  auto kern = shape.splits > 1 ? gemm_fp8_kernel<BN, kFeatSplitK>
+                                : (ep.hp.on ? gemm_fp8_kernel<BN, kFeatHeadPrep>
+                                            : gemm_fp8_kernel<BN, 0>);
   static thread_local int attr_dev = -1;
   int dev = 0;
   B2F_CUDA_TRY(cudaGetDevice(&dev));
   if (attr_dev != dev) {
-    B2F_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      Cfg::SMEM_BYTES));
+    for (auto k : {gemm_fp8_kernel<BN, 0>, gemm_fp8_kernel<BN, kFeatSplitK>,
+                   gemm_fp8_kernel<BN, kFeatHeadPrep>})
+      B2F_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        Cfg::SMEM_BYTES));
     attr_dev = dev;
   }
   CUtensorMap to;
@@ -196,13 +200,14 @@ int launch_gemm_pair(const b2f_gemm_args* a, EpilogueParams ep, cudaStream_t str
   }
   GemmShape shape{a->m, a->n, a->k, 1};
   const int num_tiles = ((a->m + 255) / 256) * ((a->n + Cfg::BN - 1) / Cfg::BN);
-  static thread_local int cached_dev = -1, cached_pairs = 0;  // per instance
+  auto kern = ep.hp.on ? gemm_fp8_pair_kernel<PBN, kFeatHeadPrep> : gemm_fp8_pair_kernel<PBN, 0>;
+  static thread_local int cached_dev = -1, cached_pairs = 0;  // per tile width
   int dev = 0;
   B2F_CUDA_TRY(cudaGetDevice(&dev));
   if (cached_dev != dev) {
-    B2F_CUDA_TRY(cudaFuncSetAttribute(gemm_fp8_pair_kernel<PBN>,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      Cfg::SMEM_BYTES));
+    for (auto k : {gemm_fp8_pair_kernel<PBN, 0>, gemm_fp8_pair_kernel<PBN, kFeatHeadPrep>})
+      B2F_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        Cfg::SMEM_BYTES));
     cudaLaunchConfig_t probe = {};
     probe.gridDim = dim3(2 * 256, 1, 1);
     probe.blockDim = dim3(Cfg::THREADS, 1, 1);
@@ -213,7 +218,7 @@ int launch_gemm_pair(const b2f_gemm_args* a, EpilogueParams ep, cudaStream_t str
     probe.attrs = &attr;
     probe.numAttrs = 1;
     int clusters = 0;
-    B2F_CUDA_TRY(cudaOccupancyMaxActiveClusters(&clusters, gemm_fp8_pair_kernel<PBN>, &probe));
+    B2F_CUDA_TRY(cudaOccupancyMaxActiveClusters(&clusters, kern, &probe));
     if (clusters <= 0) return fail(B2F_ERR_UNSUPPORTED, "gemm_fp8: no co-resident CTA pairs");
     cached_pairs = clusters;
     cached_dev = dev;
@@ -222,8 +227,7 @@ int launch_gemm_pair(const b2f_gemm_args* a, EpilogueParams ep, cudaStream_t str
   const int pairs = num_tiles < cached_pairs ? num_tiles : cached_pairs;
   CUtensorMap to;
   if (int rc = encode_out_map(a, ep, Cfg::BN / 2, &to)) return rc;
-  gemm_fp8_pair_kernel<PBN><<<2 * pairs, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, to, shape,
-                                                                             ep);
+  kern<<<2 * pairs, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, to, shape, ep);
   B2F_CUDA_TRY(cudaGetLastError());
   return B2F_OK;
 }
@@ -520,7 +524,7 @@ int launch_gemm_static(const b2f_gemm_args* a, int splits, void* scratch, bool* 
   const int units = num_tiles * splits;
   const int grid = units < sms ? units : sms;
   if (!*attr_done) {
-    B2F_CUDA_TRY(cudaFuncSetAttribute(gemm_fp8_kernel<BN>,
+    B2F_CUDA_TRY(cudaFuncSetAttribute(gemm_fp8_kernel<BN, kFeatSplitK>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       Cfg::SMEM_BYTES));
     *attr_done = true;
@@ -529,7 +533,8 @@ int launch_gemm_static(const b2f_gemm_args* a, int splits, void* scratch, bool* 
   if (int rc = encode_out_map(a, ep, BN / 2, &to)) return rc;
   // Tile counters must start at zero: clear them on the call's stream.
   B2F_CUDA_TRY(cudaMemsetAsync(scratch, 0, kCounterBytes, stream));
-  gemm_fp8_kernel<BN><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, to, shape, ep);
+  gemm_fp8_kernel<BN, kFeatSplitK><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, to,
+                                                                                    shape, ep);
   B2F_CUDA_TRY(cudaGetLastError());
   return B2F_OK;
 }

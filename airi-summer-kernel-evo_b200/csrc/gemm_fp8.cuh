@@ -155,22 +155,38 @@ __device__ __forceinline__ float2 act_pair(float2 v, float p) {
   }
 }
 
-// acc * m + a per column (m, a broadcast from the lanes that hold column j's values, or
-// uniform), then the activation, then post_mul: 16 pairs.
-template <int ACT, bool LANE_MUL, bool LANE_ADD>
+// acc * m + a per column (m, a broadcast from the lanes that hold column j's values when
+// LANES, else uniform), then the activation, then post_mul: 16 pairs.  ACT is a compile-time
+// activation (none / ReLU / GELU); kActDyn selects the rarely used ones at run time.
+// Few instances on purpose: with one per (activation, bias, column scale) combination the
+// epilogue outgrew the instruction cache (instruction-fetch stalls in the short-K GEMMs).
+constexpr int kActDyn = -1;
+
+__device__ __forceinline__ float act_dyn(float v, int act, float p) {
+  switch (act) {
+    case kActRelu: return fmaxf(v, 0.0f);
+    case kActGeluTanh: return gelu_tanh(v);
+    case kActLeakyRelu: return v >= 0.0f ? v : v * p;
+    case kActSilu: return v / (1.0f + expf(-v));
+    default: return v;
+  }
+}
+
+template <int ACT, bool LANES>
 __device__ __forceinline__ void affine_act32(const uint32_t (&acc)[32], float (&v)[32],
                                              float m, float a, float lane_mul, float lane_add,
-                                             float p, float post_mul) {
+                                             int act, float p, float post_mul) {
 #pragma unroll
   for (int j = 0; j < 32; j += 2) {
-    const float2 m2 = LANE_MUL ? make_float2(__shfl_sync(0xffffffffu, lane_mul, j),
-                                             __shfl_sync(0xffffffffu, lane_mul, j + 1))
-                               : make_float2(m, m);
-    const float2 a2 = LANE_ADD ? make_float2(__shfl_sync(0xffffffffu, lane_add, j),
-                                             __shfl_sync(0xffffffffu, lane_add, j + 1))
-                               : make_float2(a, a);
+    const float2 m2 = LANES ? make_float2(__shfl_sync(0xffffffffu, lane_mul, j),
+                                          __shfl_sync(0xffffffffu, lane_mul, j + 1))
+                            : make_float2(m, m);
+    const float2 a2 = LANES ? make_float2(__shfl_sync(0xffffffffu, lane_add, j),
+                                          __shfl_sync(0xffffffffu, lane_add, j + 1))
+                            : make_float2(a, a);
     float2 x = ffma2(make_float2(__uint_as_float(acc[j]), __uint_as_float(acc[j + 1])), m2, a2);
-    x = act_pair<ACT>(x, p);
+    if constexpr (ACT == kActDyn) x = make_float2(act_dyn(x.x, act, p), act_dyn(x.y, act, p));
+    else x = act_pair<ACT>(x, p);
     if (post_mul != 1.0f) x = fmul2(x, make_float2(post_mul, post_mul));
     v[j] = x.x;
     v[j + 1] = x.y;
@@ -181,11 +197,12 @@ template <int ACT>
 __device__ __forceinline__ void affine_act32_sel(const EpilogueParams& ep, const uint32_t (&acc)[32],
                                                  float (&v)[32], float m, float a,
                                                  float lane_mul, float lane_add) {
-  const bool lm = ep.col_scale != nullptr, la = ep.bias != nullptr;
-  if (lm && la) affine_act32<ACT, true, true>(acc, v, m, a, lane_mul, lane_add, ep.act_param, ep.post_mul);
-  else if (lm) affine_act32<ACT, true, false>(acc, v, m, a, lane_mul, lane_add, ep.act_param, ep.post_mul);
-  else if (la) affine_act32<ACT, false, true>(acc, v, m, a, lane_mul, lane_add, ep.act_param, ep.post_mul);
-  else affine_act32<ACT, false, false>(acc, v, m, a, lane_mul, lane_add, ep.act_param, ep.post_mul);
+  // (lane_mul / lane_add hold alpha * pre_mul / pre_add in every lane when there is no
+  // column scale / bias, so either one alone takes the lane path)
+  if (ep.col_scale != nullptr || ep.bias != nullptr)
+    affine_act32<ACT, true>(acc, v, m, a, lane_mul, lane_add, ep.act, ep.act_param, ep.post_mul);
+  else
+    affine_act32<ACT, false>(acc, v, m, a, lane_mul, lane_add, ep.act, ep.act_param, ep.post_mul);
 }
 
 template <int BN>
@@ -229,11 +246,11 @@ __device__ __forceinline__ void epi_values(const EpilogueParams& ep, float alpha
   const float m = alpha * ep.pre_mul;  // uniform multiplier (no column scale)
   const float a = ep.pre_add;          // uniform addend (no bias)
   switch (ep.act) {  // uniform branch, once per 32 columns
+    case kActNone: affine_act32_sel<kActNone>(ep, acc, v, m, a, lane_mul, lane_add); break;
     case kActRelu: affine_act32_sel<kActRelu>(ep, acc, v, m, a, lane_mul, lane_add); break;
     case kActGeluTanh: affine_act32_sel<kActGeluTanh>(ep, acc, v, m, a, lane_mul, lane_add); break;
-    case kActLeakyRelu: affine_act32_sel<kActLeakyRelu>(ep, acc, v, m, a, lane_mul, lane_add); break;
-    case kActSilu: affine_act32_sel<kActSilu>(ep, acc, v, m, a, lane_mul, lane_add); break;
-    default: affine_act32_sel<kActNone>(ep, acc, v, m, a, lane_mul, lane_add); break;
+    default: affine_act32<kActDyn, true>(acc, v, m, a, lane_mul, lane_add, ep.act, ep.act_param,
+                                         ep.post_mul);
   }
   const bool in_n = row_ok && (col0 + 32 <= N);
   if (ep.gate != nullptr && row_ok) {
@@ -562,6 +579,11 @@ __device__ __forceinline__ void epilogue_tile(const EpilogueParams& ep, const CU
 // ---------------------------------------------------------------------------------------
 // Fused attention-operand preparation (HeadPrepParams) for one 128-column half-tile.
 
+// Kernel feature bits: each launch runs the instance with only the code it needs (the
+// split-K protocol and the head preparation would otherwise sit in every GEMM's instruction
+// stream; the short-K GEMMs measured instruction-fetch stalls as their largest stall).
+enum : int { kFeatSplitK = 1, kFeatHeadPrep = 2 };
+
 // Which head (if any) the half-tile starting at column c0 is: 1 = q, 2 = k, 3 = v, 0 = none.
 __device__ __forceinline__ int head_prep_kind(const HeadPrepParams& h, int c0, int& head) {
   if (!h.on) return 0;
@@ -716,14 +738,14 @@ __device__ __forceinline__ void head_prep_v(const HeadPrepParams& h, uint32_t t_
 // One 128- or HALF-column half-tile of the accumulator to its destination: a q / k / v head
 // of a fused preparation (HeadPrepParams, 128-column halves only), else the ordinary
 // epilogue.
-template <int HALF>
+template <int HALF, bool HP>
 __device__ __forceinline__ void drain_half(const EpilogueParams& ep, const CUtensorMap* tmap_out,
                                            float alpha, uint32_t t_row, int row, int row0,
                                            int col_base, int M, int N, uint8_t* stage, int& buf,
                                            float& rowsum, float& amax_local,
                                            const float (&lbv)[HALF / 32],
                                            const float (&lcv)[HALF / 32]) {
-  if constexpr (HALF == 128) {
+  if constexpr (HP && HALF == 128) {
     int head = 0;
     const int kind = head_prep_kind(ep.hp, col_base, head);
     if (kind != 0) {
@@ -746,7 +768,7 @@ __device__ __forceinline__ void drain_half(const EpilogueParams& ep, const CUten
                       amax_local, lbv, lcv);
 }
 
-template <int BN>
+template <int BN, int FEAT>
 __global__ void __launch_bounds__(320, 1)
     gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     const __grid_constant__ CUtensorMap tmap_b,
@@ -776,7 +798,7 @@ __global__ void __launch_bounds__(320, 1)
   const int num_n = (N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
   const int num_kb = (K + Cfg::BK - 1) / Cfg::BK;
-  const int splits = shape.splits;
+  const int splits = (FEAT & kFeatSplitK) ? shape.splits : 1;
   const int num_units = num_tiles * splits;  // unit u: tile u / splits, K slice u % splits
   uint64_t* split_done = drain_bar + 8;       // 8 epilogue warps finished their partials
   uint64_t* split_flag_bar = split_done + 1;  // "is this the tile's last slice" published
@@ -1036,7 +1058,7 @@ __global__ void __launch_bounds__(320, 1)
         }
       }
       if (drain_tmem) {
-        drain_half<BN / 2>(ep, &tmap_out, alpha, t_row, row, row0, col_base, M, N, stage, buf,
+        drain_half<BN / 2, (FEAT & kFeatHeadPrep) != 0>(ep, &tmap_out, alpha, t_row, row, row0, col_base, M, N, stage, buf,
                            rowsum, amax_local, lbv, lcv);
         tc_fence_before();
         __syncwarp();
@@ -1086,7 +1108,7 @@ struct Gemm2Cfg {
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
 };
 
-template <int PBN>
+template <int PBN, int FEAT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
     gemm_fp8_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                          const __grid_constant__ CUtensorMap tmap_b,
@@ -1251,8 +1273,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
       const int row = row0 + lane;
       float rowsum = 0.0f;
       const uint32_t t_row = tmem_base + (uint32_t(q * 32) << 16) + acc * BN + chalf * (BN / 2);
-      drain_half<BN / 2>(ep, &tmap_out, alpha, t_row, row, row0, nb * BN + chalf * (BN / 2), M,
-                         N, stage, buf, rowsum, amax_local, lbv, lcv);
+      drain_half<BN / 2, (FEAT & kFeatHeadPrep) != 0>(ep, &tmap_out, alpha, t_row, row, row0,
+                                                      nb * BN + chalf * (BN / 2), M, N, stage,
+                                                      buf, rowsum, amax_local, lbv, lcv);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(map_to_rank(&tempty_bar[acc], 0));

@@ -783,13 +783,12 @@ __global__ void __launch_bounds__(256, 2) norm_warp_ring_kernel(const NormParams
   const int warp = threadIdx.x >> 5;
   const int nvec = p.cols / 8;
   const uint32_t row_bytes = (uint32_t)nvec * 16;
-  constexpr int WV = WF32 ? 2 : 1;  // 16-byte words per 8 weights
-  uint4* sw = reinterpret_cast<uint4*>(smem);
   const bool ln = p.kind == 1;
   const bool has_b = ln && p.bias != nullptr;
-  uint4* sb = sw + nvec * WV;
-  uint8_t* ring = smem + (size_t)nvec * 16 * WV * (has_b ? 2 : 1) +
-                  (size_t)warp * stages * row_bytes;
+  // Gamma (RMSNorm: gamma + offset, added once here) and the LayerNorm bias, staged as f32.
+  float* sw = reinterpret_cast<float*>(smem);
+  float* sb = sw + p.cols;
+  uint8_t* ring = smem + (size_t)p.cols * 4 * (has_b ? 2 : 1) + (size_t)warp * stages * row_bytes;
   const int nw = gridDim.x * kRingWarps;
   const int row0 = blockIdx.x * kRingWarps + warp;
   const int nrows = row0 < p.rows ? (p.rows - 1 - row0) / nw + 1 : 0;
@@ -807,25 +806,22 @@ __global__ void __launch_bounds__(256, 2) norm_warp_ring_kernel(const NormParams
     fence_mbarrier_init();
     for (; issued < stages && issued < nrows; ++issued) issue(issued);
   }
-  for (int i = threadIdx.x; i < nvec * WV; i += blockDim.x) {
-    sw[i] = reinterpret_cast<const uint4*>(p.weight)[i];
-    if (has_b) sb[i] = reinterpret_cast<const uint4*>(p.bias)[i];
+  {
+    const float woff = ln ? 0.0f : p.w_offset;
+    for (int c = threadIdx.x; c < p.cols; c += blockDim.x) {
+      float wv, bv = 0.f;
+      if constexpr (WF32) {
+        wv = static_cast<const float*>(p.weight)[c];
+        if (has_b) bv = static_cast<const float*>(p.bias)[c];
+      } else {
+        wv = __bfloat162float(static_cast<const __nv_bfloat16*>(p.weight)[c]);
+        if (has_b) bv = __bfloat162float(static_cast<const __nv_bfloat16*>(p.bias)[c]);
+      }
+      sw[c] = ln ? wv : wv + woff;
+      if (has_b) sb[c] = bv;
+    }
   }
   __syncthreads();  // weights staged; every warp's barriers initialised
-  auto wload = [&](const uint4* base, int vi, float (&o)[8]) {
-    if constexpr (WF32) {
-      const float4 a = reinterpret_cast<const float4*>(base)[2 * vi];
-      const float4 b = reinterpret_cast<const float4*>(base)[2 * vi + 1];
-      o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w; o[4] = b.x; o[5] = b.y; o[6] = b.z;
-      o[7] = b.w;
-    } else {
-      const uint4 q = base[vi];
-      const float2 a = unpack_bf16x2(q.x), b = unpack_bf16x2(q.y), c = unpack_bf16x2(q.z),
-                   d = unpack_bf16x2(q.w);
-      o[0] = a.x; o[1] = a.y; o[2] = b.x; o[3] = b.y; o[4] = c.x; o[5] = c.y; o[6] = d.x;
-      o[7] = d.y;
-    }
-  };
   auto unpack = [&](const uint4& q, float (&v)[8]) {
     const float2 a = unpack_bf16x2(q.x), b = unpack_bf16x2(q.y), c = unpack_bf16x2(q.z),
                  d = unpack_bf16x2(q.w);
@@ -838,6 +834,7 @@ __global__ void __launch_bounds__(256, 2) norm_warp_ring_kernel(const NormParams
   };
   const float n = float(p.cols);
   const float qinv = 1.0f / p.q_scale;
+  const float2 qinv2 = make_float2(qinv, qinv);
   int k = 0;
   bool aborted = false;
   for (; k < nrows; ++k) {
@@ -855,6 +852,8 @@ __global__ void __launch_bounds__(256, 2) norm_warp_ring_kernel(const NormParams
       return vi < nvec ? lds16(src + vi * 16) : make_uint4(0u, 0u, 0u, 0u);
     };
     const long long row = row0 + (long long)k * nw;
+    // Statistics: the f32 sums in the order of the row-group kernels (one running sum per
+    // lane over its vectors, then the warp reduction), so the two schedules agree.
     float mean = 0.f, s2 = 0.f;
     if (ln) {
       float s1 = 0.f;
@@ -888,29 +887,44 @@ __global__ void __launch_bounds__(256, 2) norm_warp_ring_kernel(const NormParams
       }
     }
     const float inv = rsqrtf(warp_sum(s2) / n + p.eps);
+    const float2 inv2 = make_float2(inv, inv), nmean2 = make_float2(-mean, -mean);
     uint8_t* qrow = p.q_out + row * p.q_ld;
+    // Outputs in packed f32x2 arithmetic, the same operations per element as the scalar
+    // form: RMSNorm (h * inv) * w', LayerNorm ((h - mean) * inv) * w + b, then * 1/scale.
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const int vi = lane + 32 * i;
       if (vi < nvec) {
-        float h[8], w[8], y[8];
+        float h[8];
         unpack(cur(i), h);
-        wload(sw, vi, w);
-        if (ln) {
-          float bb[8];
-          if (has_b) {
-            wload(sb, vi, bb);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) bb[j] = 0.f;
-          }
-#pragma unroll
-          for (int j = 0; j < 8; ++j) y[j] = (h[j] - mean) * inv * w[j] + bb[j];
-        } else {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) y[j] = h[j] * inv * (w[j] + p.w_offset);
+        const float4 wa = reinterpret_cast<const float4*>(sw)[2 * vi];
+        const float4 wb = reinterpret_cast<const float4*>(sw)[2 * vi + 1];
+        const float2 w2[4] = {make_float2(wa.x, wa.y), make_float2(wa.z, wa.w),
+                              make_float2(wb.x, wb.y), make_float2(wb.z, wb.w)};
+        float2 b2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                        make_float2(0.f, 0.f)};
+        if (has_b) {
+          const float4 ba = reinterpret_cast<const float4*>(sb)[2 * vi];
+          const float4 bb = reinterpret_cast<const float4*>(sb)[2 * vi + 1];
+          b2[0] = make_float2(ba.x, ba.y); b2[1] = make_float2(ba.z, ba.w);
+          b2[2] = make_float2(bb.x, bb.y); b2[3] = make_float2(bb.z, bb.w);
         }
-        __stcs(reinterpret_cast<uint2*>(qrow + vi * 8), quant8(y, qinv));
+        uint32_t o16[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          float2 x = make_float2(h[2 * t], h[2 * t + 1]);
+          float2 y;
+          if (ln) {
+            x = fmul2(fadd2(x, nmean2), inv2);
+            y = ffma2(x, w2[t], b2[t]);
+          } else {
+            y = fmul2(fmul2(x, inv2), w2[t]);
+          }
+          y = fmul2(y, qinv2);
+          o16[t] = f32x2_to_e4m3x2(y.x, y.y);
+        }
+        __stcs(reinterpret_cast<uint2*>(qrow + vi * 8),
+               make_uint2(o16[0] | (o16[1] << 16), o16[2] | (o16[3] << 16)));
       }
     }
     __syncwarp();  // every lane has read the slot: refill it
@@ -988,7 +1002,7 @@ WarpRingFn pick_warp_ring(int nv) {
 int warp_ring_stages(const NormParams& p) {
   const size_t nvec = p.cols / 8;
   const bool has_b = p.kind == 1 && p.bias != nullptr;
-  const size_t wbytes = nvec * 16 * (p.w_dtype == kF32 ? 2 : 1) * (has_b ? 2 : 1);
+  const size_t wbytes = (size_t)p.cols * 4 * (has_b ? 2 : 1);  // f32 gamma (and bias)
   const size_t budget = 110 * 1024;  // two CTAs per SM, with room for the static barriers
   if (wbytes >= budget) return 0;
   const size_t per = (budget - wbytes) / ((size_t)kRingWarps * nvec * 16);
@@ -1002,7 +1016,7 @@ int launch_warp(const NormParams& p, cudaStream_t s) {
     const WarpRingFn fn =
         wf32 ? pick_warp_ring<true>((nvec + 31) / 32) : pick_warp_ring<false>((nvec + 31) / 32);
     const bool has_b = p.kind == 1 && p.bias != nullptr;
-    const size_t smem = (size_t)nvec * 16 * (wf32 ? 2 : 1) * (has_b ? 2 : 1) +
+    const size_t smem = (size_t)p.cols * 4 * (has_b ? 2 : 1) +
                         (size_t)kRingWarps * stages * nvec * 16;
     int per_sm = 0;
     {

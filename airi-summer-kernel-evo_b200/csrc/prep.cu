@@ -233,6 +233,109 @@ __global__ void __launch_bounds__(256) head_norm_rope128_kernel(const RopeParams
   if (t < p.rows) head_norm_rope128_token<G>(p, t, threadIdx.x & 31);
 }
 
+// q and k of one token in one warp (head_dim 128, rotate-half RoPE over the whole head or
+// none): lane (hg = lane / 8, sub = lane % 8) holds elements [8 sub, 8 sub + 8) and their
+// rotate-half partners [8 sub + 64, 8 sub + 72) of heads 4 g + hg, so the rotation needs no
+// shuffles; the token's cos / sin values are loaded once for the q and the k heads; all
+// arithmetic on f32 pairs (fma.rn.f32x2 / mul.rn.f32x2).  The per-head sum of squares runs
+// over the lane's 16 values (pairs) and then the 8 lanes of the head.
+struct QkLane {
+  float2 c[8], sn[8];  // cos / sin of the lane's elements: [0..3] low block, [4..7] high
+};
+
+template <int G>
+__device__ __forceinline__ void qk_heads128(const RopeParams& p, const QkLane& tb, bool rope,
+                                            int t, int hg, int e0) {
+  const uint8_t* src = p.in + (long long)t * p.in_ld + (long long)hg * p.in_hstride + e0;
+  uint2 lo[G], hi[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    lo[g] = *reinterpret_cast<const uint2*>(src + (long long)(4 * g) * p.in_hstride);
+    hi[g] = *reinterpret_cast<const uint2*>(src + (long long)(4 * g) * p.in_hstride + 64);
+  }
+  float2 w[8];
+#pragma unroll
+  for (int u = 0; u < 8; ++u) w[u] = make_float2(1.f, 1.f);
+  if (p.weight != nullptr) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p.weight + e0));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(p.weight + e0 + 4));
+    const float4 c = __ldg(reinterpret_cast<const float4*>(p.weight + e0 + 64));
+    const float4 d = __ldg(reinterpret_cast<const float4*>(p.weight + e0 + 68));
+    const float2 off = make_float2(p.w_offset, p.w_offset);
+    w[0] = fadd2(make_float2(a.x, a.y), off); w[1] = fadd2(make_float2(a.z, a.w), off);
+    w[2] = fadd2(make_float2(b.x, b.y), off); w[3] = fadd2(make_float2(b.z, b.w), off);
+    w[4] = fadd2(make_float2(c.x, c.y), off); w[5] = fadd2(make_float2(c.z, c.w), off);
+    w[6] = fadd2(make_float2(d.x, d.y), off); w[7] = fadd2(make_float2(d.z, d.w), off);
+  }
+  const float2 isc = make_float2(p.in_scale, p.in_scale);
+  const float2 osc = make_float2(p.out_inv_scale, p.out_inv_scale);
+  uint8_t* dst = p.out + (long long)t * p.out_ld + (long long)hg * 128 + e0;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float2 x[8];
+    const uint32_t wd[4] = {lo[g].x, lo[g].y, hi[g].x, hi[g].y};
+#pragma unroll
+    for (int q4 = 0; q4 < 4; ++q4) {
+      x[2 * q4] = fmul2(e4m3x2_to_f32x2(wd[q4] & 0xFFFF), isc);
+      x[2 * q4 + 1] = fmul2(e4m3x2_to_f32x2(wd[q4] >> 16), isc);
+    }
+    if (p.weight != nullptr) {
+      float2 ss = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) ss = ffma2(x[u], x[u], ss);
+      float sum = ss.x + ss.y;
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+      const float inv = rsqrtf(sum / 128.0f + p.eps);
+      const float2 inv2 = make_float2(inv, inv);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) x[u] = fmul2(fmul2(x[u], inv2), w[u]);
+    }
+    if (rope) {
+      // low element e: x_e cos_e - x_{e+64} sin_e; high element e+64: x_{e+64} cos + x_e sin
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float2 xl = x[u], xh = x[u + 4];
+        x[u] = ffma2(xh, make_float2(-tb.sn[u].x, -tb.sn[u].y), fmul2(xl, tb.c[u]));
+        x[u + 4] = ffma2(xl, tb.sn[u + 4], fmul2(xh, tb.c[u + 4]));
+      }
+    }
+    uint32_t o[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float2 a = fmul2(x[2 * u], osc), b = fmul2(x[2 * u + 1], osc);
+      o[u] = uint32_t(f32x2_to_e4m3x2(a.x, a.y)) | (uint32_t(f32x2_to_e4m3x2(b.x, b.y)) << 16);
+    }
+    *reinterpret_cast<uint2*>(dst + (long long)(4 * g) * 128) = make_uint2(o[0], o[1]);
+    *reinterpret_cast<uint2*>(dst + (long long)(4 * g) * 128 + 64) = make_uint2(o[2], o[3]);
+  }
+}
+
+template <int GQ, int GK>
+__device__ __forceinline__ void qk_token128(const RopeParams& q, const RopeParams& k, int t,
+                                            int lane) {
+  const int hg = lane >> 3, e0 = (lane & 7) * 8;
+  const bool rope = q.cos != nullptr;
+  QkLane tb;
+  if (rope) {
+    const long long base = (long long)(t % q.seq) * 128 + e0;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {  // low block, then the + 64 block
+      const float4 c0 = __ldg(reinterpret_cast<const float4*>(q.cos + base + 64 * h));
+      const float4 c1 = __ldg(reinterpret_cast<const float4*>(q.cos + base + 64 * h + 4));
+      const float4 s0 = __ldg(reinterpret_cast<const float4*>(q.sin + base + 64 * h));
+      const float4 s1 = __ldg(reinterpret_cast<const float4*>(q.sin + base + 64 * h + 4));
+      tb.c[4 * h] = make_float2(c0.x, c0.y); tb.c[4 * h + 1] = make_float2(c0.z, c0.w);
+      tb.c[4 * h + 2] = make_float2(c1.x, c1.y); tb.c[4 * h + 3] = make_float2(c1.z, c1.w);
+      tb.sn[4 * h] = make_float2(s0.x, s0.y); tb.sn[4 * h + 1] = make_float2(s0.z, s0.w);
+      tb.sn[4 * h + 2] = make_float2(s1.x, s1.y); tb.sn[4 * h + 3] = make_float2(s1.z, s1.w);
+    }
+  }
+  qk_heads128<GQ>(q, tb, rope, t, hg, e0);
+  qk_heads128<GK>(k, tb, rope, t, hg, e0);
+}
+
 template <bool F16>
 __device__ __forceinline__ void fp8_convert8(const uint8_t* in, long long in_ld, uint16_t* out,
                                              long long out_ld, int rows, int cols, float scale,
@@ -267,9 +370,9 @@ __global__ void fp8_to_bf16_kernel(const uint8_t* in, long long in_ld, uint16_t*
 }
 
 // The three operand preparations of a gated GQA block in one launch: blocks [0, nq) run
-// the q head norm + RoPE (GQ four-head groups per token), [nq, nq + nk) the k one (GK
-// groups), the rest convert V to f16 / bf16.  One launch instead of three: each of them
-// alone is too short to fill the GPU past its ramp and tail.
+// the q and k head norm + RoPE (one warp per token: GQ and GK four-head groups), the rest
+// convert V to f16 / bf16 (none when V was written elsewhere).  One launch instead of
+// three: each of them alone is too short to fill the GPU past its ramp and tail.
 struct VConvertParams {
   const uint8_t* in;
   long long in_ld;
@@ -281,17 +384,14 @@ struct VConvertParams {
 
 template <int GQ, int GK>
 __global__ void __launch_bounds__(256, 2) attn_prep_kernel(const RopeParams q, const RopeParams k,
-                                                        const VConvertParams v, int nq, int nk) {
+                                                        const VConvertParams v, int nq) {
   const int b = blockIdx.x;
   const int lane = threadIdx.x & 31;
   if (b < nq) {
     const int t = b * 8 + (threadIdx.x >> 5);
-    if (t < q.rows) head_norm_rope128_token<GQ>(q, t, lane);
-  } else if (b < nq + nk) {
-    const int t = (b - nq) * 8 + (threadIdx.x >> 5);
-    if (t < k.rows) head_norm_rope128_token<GK>(k, t, lane);
+    if (t < q.rows) qk_token128<GQ, GK>(q, k, t, lane);
   } else {
-    const long long i = (long long)(b - nq - nk) * blockDim.x + threadIdx.x;
+    const long long i = (long long)(b - nq) * blockDim.x + threadIdx.x;
     if (v.f16) fp8_convert8<true>(v.in, v.in_ld, v.out, v.out_ld, v.rows, v.cols, 1.0f, i);
     else fp8_convert8<false>(v.in, v.in_ld, v.out, v.out_ld, v.rows, v.cols, 1.0f, i);
   }
@@ -438,10 +538,11 @@ int b2f_attn_prep(const b2f_rope_args* q, const b2f_rope_args* k, const void* v_
   RopeParams pq, pk;
   if (int rc = rope_params(q, pq)) return rc;
   if (int rc = rope_params(k, pk)) return rc;
-  if (!rope128_ok(q) || !rope128_ok(k) || q->rows != k->rows)
+  if (!rope128_ok(q) || !rope128_ok(k) || q->rows != k->rows || q->cos != k->cos ||
+      q->sin != k->sin || (q->cos != nullptr && pq.seq != pk.seq))
     return fail(B2F_ERR_UNSUPPORTED,
                 "attn_prep: q and k need head_dim 128, heads a multiple of 4 (<= 32), full or "
-                "no RoPE, 16-byte aligned rows, and the same token count");
+                "no RoPE with the same tables, 16-byte aligned rows, and the same token count");
   const bool has_v = v_in != nullptr || v_out != nullptr || v_cols != 0;
   if (has_v &&
       (v_in == nullptr || v_out == nullptr || v_cols <= 0 || v_cols % 8 || v_in_ld % 8 ||
@@ -452,14 +553,14 @@ int b2f_attn_prep(const b2f_rope_args* q, const b2f_rope_args* k, const void* v_
   VConvertParams pv{reinterpret_cast<const uint8_t*>(v_in), v_in_ld,
                     reinterpret_cast<uint16_t*>(v_out), v_out_ld, q->rows, v_cols,
                     v_dtype == B2F_DTYPE_F16 ? 1 : 0};
-  const int nq = (q->rows + 7) / 8, nk = (k->rows + 7) / 8;
+  const int nq = (q->rows + 7) / 8;  // one warp per token does its q and k heads
   const long long nv = has_v ? ((long long)q->rows * (v_cols / 8) + 255) / 256 : 0;
-  const int grid = (int)(nq + nk + nv);
+  const int grid = (int)(nq + nv);
   cudaStream_t s = (cudaStream_t)stream;
   const int gq = q->heads / 4, gk = k->heads / 4;
 #define B2F_PREP(GQ, GK)                                                        \
   if (gq == GQ && gk == GK) {                                                   \
-    attn_prep_kernel<GQ, GK><<<grid, 256, 0, s>>>(pq, pk, pv, nq, nk);          \
+    attn_prep_kernel<GQ, GK><<<grid, 256, 0, s>>>(pq, pk, pv, nq);              \
     B2F_CUDA_TRY(cudaGetLastError());                                           \
     return B2F_OK;                                                              \
   }
