@@ -10,10 +10,12 @@
 //                               e4m3 values) MN-major from shared memory
 //   ctx  = e4m3( O / l * sigmoid(gate) / ctx_scale )   fused epilogue
 // Two kernels:
-//   attention2_kernel<D, VF16> (head_dim 64 / 128): two query tiles per CTA, 64-key tiles,
-//     P through shared memory, S released as soon as the softmax loaded it (384 threads:
-//     TMA producer warp, MMA warp, two idle warps, two softmax warpgroups holding the
-//     registers the others give up); GQA head pairs share K / V; e4m3 gate tiles by TMA.
+//   attention2_kernel<D, VF16> (head_dim 64 / 128): two query tiles per CTA, 128-key
+//     tiles, P through shared memory, S released as soon as the softmax loaded it (384
+//     threads: TMA producer warp, MMA warp, two idle warps, two softmax warpgroups holding
+//     the registers the others give up); the two tiles are GQA head pairs sharing K / V,
+//     or two heads with their own K / V at the same query rows (causal, head_dim 64), or
+//     causal query tiles (i, n-1-i) of one head; e4m3 gate tiles by TMA.
 //   attention_kernel<256> (head_dim 256): one query tile per CTA (192 threads), S
 //     double-buffered in TMEM so Q.K_{j+1}^T runs while the softmax of tile j is computed.
 // Causal tiles above the diagonal are never visited; GQA maps query head h to KV head
@@ -45,6 +47,9 @@ struct AttnParams {
   float ctx_inv_scale;
   float v_scale;        // V bf16 values are multiplied by v_scale in the epilogue
   int pair_heads;       // two-tile kernel: the tiles are query heads 2y, 2y+1 (same KV head)
+  int pair_kv;          // two-tile kernel, head_dim 64, causal, one KV head per query head:
+                        // the tiles are heads 2y, 2y+1 (each with its own K / V) at the same
+                        // query rows, both K (V) tiles in one ring stage
   int gate_tma;         // two-tile kernel: e4m3 gate tiles arrive in shared memory by TMA
 };
 
@@ -464,8 +469,9 @@ struct Attn2Cfg {
   static constexpr int K_BYTES = BKV * D;
   static constexpr int V_BYTES = BKV * D * 2;
   // Separate K and V rings: K(j) is released as soon as both S(j) MMAs are issued.
+  // Ring slots of one head's K / V tile; with pair_kv a stage is two slots (both heads).
   static constexpr int KST = (D >= 128) ? 2 : 4;
-  static constexpr int VST = (D >= 128) ? 2 : 3;
+  static constexpr int VST = (D >= 128) ? 2 : 4;
   // P (16-bit) in shared memory, one tile per query tile: [2 key blocks of 64][128 rows]
   // [128-byte swizzled row], the K-major layout of an MMA operand.  The P.V MMA reads both
   // operands from shared memory (with P in tensor memory that MMA ran at less than half
@@ -519,10 +525,11 @@ __global__ void __launch_bounds__(384, 1)
   const int n_qt = (p.seq + BQ - 1) / BQ;
   int qt[2], hx[2];
   bool act[2];
-  if (p.pair_heads) {
+  if (p.pair_heads || p.pair_kv) {
     // GQA: query heads 2y and 2y+1 read the same KV head; both tiles take the same query
-    // rows, so both stay active for every key tile and share each K / V load.  Longest
-    // causal rows first.
+    // rows, so both stay active for every key tile and share each K / V load.  (pair_kv:
+    // the same for two heads with their own K / V, loaded side by side.)  Longest causal
+    // rows first.
     qt[0] = qt[1] = n_qt - 1 - blockIdx.x;
     hx[0] = 2 * blockIdx.y;
     hx[1] = hx[0] + 1;
@@ -547,6 +554,9 @@ __global__ void __launch_bounds__(384, 1)
   }
   const int b = blockIdx.z;
   const int hk = hx[0] / (p.hq / p.hkv);
+  const int kv2 = p.pair_kv ? 2 : 1;     // heads per K / V ring stage
+  const int hkv[2] = {hk, p.pair_kv ? hx[1] : hk};
+  const int ks = KST / kv2, vsn = VST / kv2;  // ring stages
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -599,7 +609,7 @@ __global__ void __launch_bounds__(384, 1)
     }
     if (lane < 2) {
       const bool is_k = lane == 0;
-      const int NS = is_k ? KST : VST;
+      const int NS = is_k ? ks : vsn;
       uint64_t* fullb = is_k ? k_full : v_full;
       uint64_t* emptyb = is_k ? k_empty : v_empty;
       int stage = 0;
@@ -612,17 +622,21 @@ __global__ void __launch_bounds__(384, 1)
       for (int j = 0; j < nkv[1]; ++j) {
         if (!mbar_wait(&emptyb[stage], phase ^ 1, kDevTimeoutProducer, abort_flag)) break;
         if (is_k) {
-          uint8_t* dst = sk + stage * C::K_BYTES;
-          mbar_arrive_expect_tx(&fullb[stage], C::K_BYTES);
-          for (int kb = 0; kb < C::KB; ++kb)
-            tma_load_3d(dst + kb * BKV * C::ROWB, &tm_k, &fullb[stage], hk * D + kb * 128,
-                        j * BKV, b, pol);
+          mbar_arrive_expect_tx(&fullb[stage], kv2 * C::K_BYTES);
+          for (int h = 0; h < kv2; ++h) {
+            uint8_t* dst = sk + (stage * kv2 + h) * C::K_BYTES;
+            for (int kb = 0; kb < C::KB; ++kb)
+              tma_load_3d(dst + kb * BKV * C::ROWB, &tm_k, &fullb[stage], hkv[h] * D + kb * 128,
+                          j * BKV, b, pol);
+          }
         } else {
-          uint8_t* dst = sv + stage * C::V_BYTES;
-          mbar_arrive_expect_tx(&fullb[stage], C::V_BYTES);
-          for (int vb = 0; vb < D / 64; ++vb)
-            tma_load_3d(dst + vb * BKV * 128, &tm_v, &fullb[stage], hk * D + vb * 64, j * BKV,
-                        b, pol);
+          mbar_arrive_expect_tx(&fullb[stage], kv2 * C::V_BYTES);
+          for (int h = 0; h < kv2; ++h) {
+            uint8_t* dst = sv + (stage * kv2 + h) * C::V_BYTES;
+            for (int vb = 0; vb < D / 64; ++vb)
+              tma_load_3d(dst + vb * BKV * 128, &tm_v, &fullb[stage], hkv[h] * D + vb * 64,
+                          j * BKV, b, pol);
+          }
         }
         ++issued;
         if (++stage == NS) { stage = 0; phase ^= 1; }
@@ -676,7 +690,8 @@ __global__ void __launch_bounds__(384, 1)
       const uint64_t v_desc0 = make_sdesc(smem_u32(sv), 2, BKV * 128, 1024);
       auto issue_s = [&](int x, int j) {
         const uint64_t qd = q_desc[x];
-        const uint64_t kd = k_desc0 + uint64_t((j % KST) * (C::K_BYTES >> 4));
+        const uint64_t kd =
+            k_desc0 + uint64_t(((j % ks) * kv2 + (p.pair_kv ? x : 0)) * (C::K_BYTES >> 4));
         const uint32_t d = tmem + C::S_COL + x * BKV;
 #pragma unroll
         for (int kb = 0; kb < C::KB; ++kb) {
@@ -690,7 +705,7 @@ __global__ void __launch_bounds__(384, 1)
       // S(j) of both tiles (tile 0 only while its causal rows still reach key tile j); for
       // j > 0 each waits until its softmax has loaded S(j-1).
       auto issue_s_pair = [&](int j) -> bool {
-        if (!mbar_wait(&k_full[j % KST], (j / KST) & 1, kDevTimeoutMma, abort_flag))
+        if (!mbar_wait(&k_full[j % ks], (j / ks) & 1, kDevTimeoutMma, abort_flag))
           return false;
         if (act[0] && j < nkv[0]) {
           if (j > 0 && !mbar_wait(&s_free[0], (j - 1) & 1, kDevTimeoutMma, abort_flag))
@@ -702,20 +717,21 @@ __global__ void __launch_bounds__(384, 1)
           return false;
         tc_fence_after();
         issue_s(1, j);
-        mma_commit(&k_empty[j % KST]);  // both readers of K(j) issued before it
+        mma_commit(&k_empty[j % ks]);  // both readers of K(j) issued before it
         return true;
       };
       auto issue_pv = [&](int x, int j) -> bool {
         if (!mbar_wait(&p_full[x], j & 1, kDevTimeoutMma, abort_flag)) return false;
-        const int vs = j % VST;
+        const int vs = j % vsn;
         if (x == 0 || j >= nkv[0]) {  // first reader of V(j)
-          if (!mbar_wait(&v_full[vs], (j / VST) & 1, kDevTimeoutMma, abort_flag)) return false;
+          if (!mbar_wait(&v_full[vs], (j / vsn) & 1, kDevTimeoutMma, abort_flag)) return false;
         }
         tc_fence_after();
         // P(j): 128 query rows x 128 keys of 16-bit weights in two 64-key blocks of
         // 128-byte swizzled rows; 16 keys (32 bytes of P, 2 KB of V) per MMA.
         const uint64_t pd = p_desc[x];
-        const uint64_t vd = v_desc0 + uint64_t(vs * (C::V_BYTES >> 4));
+        const uint64_t vd =
+            v_desc0 + uint64_t((vs * kv2 + (p.pair_kv ? x : 0)) * (C::V_BYTES >> 4));
         const uint32_t o = tmem + C::O_COL + x * D;
         mma_bf16(o, pd, vd, idesc_pv, j != 0);
 #pragma unroll
@@ -730,7 +746,7 @@ __global__ void __launch_bounds__(384, 1)
         if (j + 1 < nkv[1] && !(ok = issue_s_pair(j + 1))) break;
         if (j < nkv[0] && !(ok = issue_pv(0, j))) break;
         if (!(ok = issue_pv(1, j))) break;
-        mma_commit(&v_empty[j % VST]);  // both P.V of this key tile issued before it
+        mma_commit(&v_empty[j % vsn]);  // both P.V of this key tile issued before it
       }
       mma_commit(drain);
       const uint64_t t0 = globaltimer();
@@ -1018,6 +1034,7 @@ int launch_attention(const b2f_attn_args* a, cudaStream_t stream) {
   p.ctx_inv_scale = 1.0f / a->ctx_scale;
   p.v_scale = a->v_scale;
   p.pair_heads = 0;
+  p.pair_kv = 0;
   p.gate_tma = 0;
   CUtensorMap tg = tq;  // (unused unless gate_tma)
   if (PAIR && a->gate != nullptr && a->gate_dtype == B2F_DTYPE_E4M3) {
@@ -1048,7 +1065,12 @@ int launch_attention(const b2f_attn_args* a, cudaStream_t stream) {
       attr_dev[1][slot] = dev;
     }
     p.pair_heads = (a->hq / a->hkv) % 2 == 0;
-    dim3 grid(p.pair_heads ? n_qt : (n_qt + 1) / 2, p.pair_heads ? a->hq / 2 : a->hq, a->batch);
+    // Causal attention with a KV head per query head (GPT-2): pair heads 2y, 2y+1 at the
+    // same query tile rather than query tiles (i, n-1-i) of one head, whose shorter tile
+    // leaves half of the CTA idle for most key tiles.
+    p.pair_kv = !p.pair_heads && D == 64 && a->causal && a->hq == a->hkv && a->hq % 2 == 0;
+    const bool two_heads = p.pair_heads || p.pair_kv;
+    dim3 grid(two_heads ? n_qt : (n_qt + 1) / 2, two_heads ? a->hq / 2 : a->hq, a->batch);
     if (a->v_dtype == B2F_DTYPE_F16)
       attention2_kernel<D, true><<<grid, 384, SMEM, stream>>>(tq, tk, tv, tg, p);
     else

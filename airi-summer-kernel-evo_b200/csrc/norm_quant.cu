@@ -626,338 +626,148 @@ StreamFn pick_stream(int kind, int dt0, int dt1, int wdt) {
 
 // ---------------------------------------------------------------------------------------
 // Short rows (the blocks' LayerNorms / input RMSNorms: <= 32 * 8 * kWarpMaxNV columns, bf16
-// x, bf16 or f32 weights, static scale, no residual / h / y outputs): one warp per row, persistent
-// warps striding over the rows, the next row's raw bf16 vectors loaded into registers while
-// the current row is normalised.  Gamma (and the LayerNorm bias) are staged once per CTA
-// in shared memory.  Lane l owns vectors l + 32 i, the order of the row-group kernels with
-// 32 threads per row.
+// x, bf16 or f32 weights, static scale, no residual / h / y outputs): one warp per row.
+// Lane l owns vectors l + 32 i, the order of the row-group kernels with 32 threads per row.
 constexpr int kWarpMaxNV = 12;
 
+// Warp per row without staging: the row's 16-byte vectors go straight into registers,
+// gamma / bias come through the L1 cache, and each warp takes one row (grid = rows / 8), so
+// a kernel of this size runs like a plain elementwise pass.  Measured in a CUDA graph on
+// [8192 x 768] LayerNorm: 7.0 us, where a shared-memory ring filled by one bulk copy per
+// row and a persistent kernel prefetching the next row into registers (weights staged per
+// CTA) took 9.5-10.8 us and a plain 25 MB copy 4.2 us.  Statistics in the row-group
+// kernels' order; outputs in packed f32x2 arithmetic, the same operations per element.
 template <int NV, bool WF32>
-__global__ void __launch_bounds__(256) norm_warp_kernel(const NormParams p) {
-  extern __shared__ __align__(16) uint8_t smem[];
+__global__ void __launch_bounds__(256, NV <= 6 ? 4 : 3) norm_warp_direct_kernel(const NormParams p) {
   const int lane = threadIdx.x & 31;
+  const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= p.rows) return;
   const int nvec = p.cols / 8;
-  constexpr int WV = WF32 ? 2 : 1;  // 16-byte words per 8 weights
-  uint4* sw = reinterpret_cast<uint4*>(smem);
-  uint4* sb = sw + nvec * WV;
   const bool ln = p.kind == 1;
   const bool has_b = ln && p.bias != nullptr;
-  for (int i = threadIdx.x; i < nvec * WV; i += blockDim.x) {
-    sw[i] = reinterpret_cast<const uint4*>(p.weight)[i];
-    if (has_b) sb[i] = reinterpret_cast<const uint4*>(p.bias)[i];
+  const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.x) + row * p.x_ld);
+  uint4 raw[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int vi = lane + 32 * i;
+    raw[i] = vi < nvec ? __ldcs(src + vi) : make_uint4(0u, 0u, 0u, 0u);
   }
-  __syncthreads();
-  // 8 weights of vector vi from shared memory as f32
-  auto wload = [&](const uint4* base, int vi, float (&o)[8]) {
+  // The row stays packed between passes: the fence keeps the compiler from carrying the
+  // unpacked f32 values (8 per vector) across the warp reductions, which spills.
+  auto fence = [&]() {
+#pragma unroll
+    for (int i = 0; i < NV; ++i)
+      asm volatile("" : "+r"(raw[i].x), "+r"(raw[i].y), "+r"(raw[i].z), "+r"(raw[i].w));
+  };
+  auto unpack = [&](const uint4& q, float (&v)[8]) {
+    const float2 a = unpack_bf16x2(q.x), b = unpack_bf16x2(q.y), c = unpack_bf16x2(q.z),
+                 d = unpack_bf16x2(q.w);
+    v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y; v[4] = c.x; v[5] = c.y; v[6] = d.x;
+    v[7] = d.y;
+    if (p.x_scale != 1.0f) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] *= p.x_scale;
+    }
+  };
+  auto load_w = [&](const void* base, int vi, float2 (&o)[4]) {
     if constexpr (WF32) {
-      const float4 a = reinterpret_cast<const float4*>(base)[2 * vi];
-      const float4 b = reinterpret_cast<const float4*>(base)[2 * vi + 1];
-      o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w; o[4] = b.x; o[5] = b.y; o[6] = b.z;
-      o[7] = b.w;
+      const float4 a = __ldg(reinterpret_cast<const float4*>(base) + 2 * vi);
+      const float4 b = __ldg(reinterpret_cast<const float4*>(base) + 2 * vi + 1);
+      o[0] = make_float2(a.x, a.y); o[1] = make_float2(a.z, a.w);
+      o[2] = make_float2(b.x, b.y); o[3] = make_float2(b.z, b.w);
     } else {
-      const uint4 q = base[vi];
-      const float2 a = unpack_bf16x2(q.x), b = unpack_bf16x2(q.y), c = unpack_bf16x2(q.z),
-                   d = unpack_bf16x2(q.w);
-      o[0] = a.x; o[1] = a.y; o[2] = b.x; o[3] = b.y; o[4] = c.x; o[5] = c.y; o[6] = d.x;
-      o[7] = d.y;
+      const uint4 q = __ldg(reinterpret_cast<const uint4*>(base) + vi);
+      o[0] = unpack_bf16x2(q.x); o[1] = unpack_bf16x2(q.y);
+      o[2] = unpack_bf16x2(q.z); o[3] = unpack_bf16x2(q.w);
     }
   };
-  const int wpc = blockDim.x >> 5;
-  const int nw = gridDim.x * wpc;
-  int row = blockIdx.x * wpc + (threadIdx.x >> 5);
-  const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(p.x);
-  uint4 cur[NV], nxt[NV];
-  auto load_row = [&](int r, uint4 (&d)[NV]) {
-    const uint4* src = reinterpret_cast<const uint4*>(xb + (long long)r * p.x_ld);
+  const float n = float(p.cols);
+  float mean = 0.f, s2 = 0.f;
+  if (ln) {
+    float s1 = 0.f;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      const int vi = lane + 32 * i;
-      d[i] = vi < nvec ? __ldcs(src + vi) : make_uint4(0u, 0u, 0u, 0u);
-    }
-  };
-  auto unpack = [&](const uint4& q, float (&v)[8]) {
-    const float2 a = unpack_bf16x2(q.x), b = unpack_bf16x2(q.y), c = unpack_bf16x2(q.z),
-                 d = unpack_bf16x2(q.w);
-    v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y; v[4] = c.x; v[5] = c.y; v[6] = d.x;
-    v[7] = d.y;
-    if (p.x_scale != 1.0f) {
+      float v[8];
+      unpack(raw[i], v);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] *= p.x_scale;
+      for (int j = 0; j < 8; ++j) s1 += v[j];
     }
-  };
-  if (row < p.rows) load_row(row, cur);
-  const float n = float(p.cols);
-  const float qinv = 1.0f / p.q_scale;
-  for (; row < p.rows; row += nw) {
-    if (row + nw < p.rows) load_row(row + nw, nxt);
-    float mean = 0.f, s2 = 0.f;
-    if (ln) {
-      float s1 = 0.f;
+    mean = warp_sum(s1) / n;
+    fence();
 #pragma unroll
-      for (int i = 0; i < NV; ++i) {
+    for (int i = 0; i < NV; ++i) {
+      if (lane + 32 * i < nvec) {
         float v[8];
-        unpack(cur[i], v);
+        unpack(raw[i], v);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) s1 += v[j];
-      }
-      mean = warp_sum(s1) / n;
-#pragma unroll
-      for (int i = 0; i < NV; ++i) {
-        if (lane + 32 * i < nvec) {
-          float v[8];
-          unpack(cur[i], v);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float d = v[j] - mean;
-            s2 += d * d;
-          }
+        for (int j = 0; j < 8; ++j) {
+          const float d = v[j] - mean;
+          s2 += d * d;
         }
       }
-    } else {
-#pragma unroll
-      for (int i = 0; i < NV; ++i) {
-        float v[8];
-        unpack(cur[i], v);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) s2 += v[j] * v[j];
-      }
     }
-    const float inv = rsqrtf(warp_sum(s2) / n + p.eps);
-    uint8_t* qrow = p.q_out + (long long)row * p.q_ld;
+  } else {
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      const int vi = lane + 32 * i;
-      if (vi < nvec) {
-        float h[8], w[8], y[8];
-        unpack(cur[i], h);
-        wload(sw, vi, w);
+      float v[8];
+      unpack(raw[i], v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s2 += v[j] * v[j];
+    }
+  }
+  const float inv = rsqrtf(warp_sum(s2) / n + p.eps);
+  fence();
+  const float qinv = 1.0f / p.q_scale;
+  const float2 inv2 = make_float2(inv, inv), nmean2 = make_float2(-mean, -mean);
+  const float2 qinv2 = make_float2(qinv, qinv), off2 = make_float2(p.w_offset, p.w_offset);
+  uint8_t* qrow = p.q_out + row * p.q_ld;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int vi = lane + 32 * i;
+    if (vi < nvec) {
+      float h[8];
+      unpack(raw[i], h);
+      float2 w2[4], b2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                             make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      load_w(p.weight, vi, w2);
+      if (has_b) load_w(p.bias, vi, b2);
+      uint32_t o16[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        float2 x = make_float2(h[2 * t], h[2 * t + 1]);
+        float2 y;
         if (ln) {
-          float bb[8];
-          if (has_b) {
-            wload(sb, vi, bb);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) bb[j] = 0.f;
-          }
-#pragma unroll
-          for (int j = 0; j < 8; ++j) y[j] = (h[j] - mean) * inv * w[j] + bb[j];
+          x = fmul2(fadd2(x, nmean2), inv2);
+          y = ffma2(x, w2[t], b2[t]);
         } else {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) y[j] = h[j] * inv * (w[j] + p.w_offset);
+          y = fmul2(fmul2(x, inv2), fadd2(w2[t], off2));
         }
-        __stcs(reinterpret_cast<uint2*>(qrow + vi * 8), quant8(y, qinv));
+        y = fmul2(y, qinv2);
+        o16[t] = f32x2_to_e4m3x2(y.x, y.y);
       }
+      __stcs(reinterpret_cast<uint2*>(qrow + vi * 8),
+             make_uint2(o16[0] | (o16[1] << 16), o16[2] | (o16[3] << 16)));
     }
-#pragma unroll
-    for (int i = 0; i < NV; ++i) cur[i] = nxt[i];
   }
 }
 
-// Same warp-per-row arithmetic with the rows arriving through a shared-memory ring: each
-// warp owns `stages` row slots and its lane 0 keeps that many untiled bulk copies
-// (cp.async.bulk, completion on the slot's mbarrier) in flight ahead of the row being
-// normalised, so the bytes in flight per SM no longer sit in registers (the register
-// prefetch above holds two rows per warp in registers and runs one 256-thread CTA per SM
-// for 2560-column rows; here two CTAs fit and each warp has up to kRingMaxStages - 1 rows
-// outstanding while it normalises one).
-constexpr int kRingMaxStages = 4;
-
-// 16-byte shared-memory load that the compiler may not merge with an earlier one (the ring
-// slot is re-read after the warp reduction instead of keeping the row in registers).
-__device__ __forceinline__ uint4 lds16(uint32_t addr) {
-  uint4 v;
-  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "r"(addr)
-               : "memory");
-  return v;
-}
-constexpr int kRingWarps = 8;
-
-template <int NV, bool WF32>
-__global__ void __launch_bounds__(256, 2) norm_warp_ring_kernel(const NormParams p, int stages) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ __align__(8) uint64_t full[kRingWarps][kRingMaxStages];
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const int nvec = p.cols / 8;
-  const uint32_t row_bytes = (uint32_t)nvec * 16;
-  const bool ln = p.kind == 1;
-  const bool has_b = ln && p.bias != nullptr;
-  // Gamma (RMSNorm: gamma + offset, added once here) and the LayerNorm bias, staged as f32.
-  float* sw = reinterpret_cast<float*>(smem);
-  float* sb = sw + p.cols;
-  uint8_t* ring = smem + (size_t)p.cols * 4 * (has_b ? 2 : 1) + (size_t)warp * stages * row_bytes;
-  const int nw = gridDim.x * kRingWarps;
-  const int row0 = blockIdx.x * kRingWarps + warp;
-  const int nrows = row0 < p.rows ? (p.rows - 1 - row0) / nw + 1 : 0;
-  const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(p.x);
-  const uint64_t pol = policy_evict_first();
-  auto issue = [&](int k) {
-    const int slot = k % stages;
-    const long long r = row0 + (long long)k * nw;
-    mbar_arrive_expect_tx(&full[warp][slot], row_bytes);
-    bulk_load(ring + (size_t)slot * row_bytes, xb + r * p.x_ld, row_bytes, &full[warp][slot], pol);
-  };
-  int issued = 0;
-  if (lane == 0) {
-    for (int i = 0; i < stages; ++i) mbar_init(&full[warp][i], 1);
-    fence_mbarrier_init();
-    for (; issued < stages && issued < nrows; ++issued) issue(issued);
-  }
-  {
-    const float woff = ln ? 0.0f : p.w_offset;
-    for (int c = threadIdx.x; c < p.cols; c += blockDim.x) {
-      float wv, bv = 0.f;
-      if constexpr (WF32) {
-        wv = static_cast<const float*>(p.weight)[c];
-        if (has_b) bv = static_cast<const float*>(p.bias)[c];
-      } else {
-        wv = __bfloat162float(static_cast<const __nv_bfloat16*>(p.weight)[c]);
-        if (has_b) bv = __bfloat162float(static_cast<const __nv_bfloat16*>(p.bias)[c]);
-      }
-      sw[c] = ln ? wv : wv + woff;
-      if (has_b) sb[c] = bv;
-    }
-  }
-  __syncthreads();  // weights staged; every warp's barriers initialised
-  auto unpack = [&](const uint4& q, float (&v)[8]) {
-    const float2 a = unpack_bf16x2(q.x), b = unpack_bf16x2(q.y), c = unpack_bf16x2(q.z),
-                 d = unpack_bf16x2(q.w);
-    v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y; v[4] = c.x; v[5] = c.y; v[6] = d.x;
-    v[7] = d.y;
-    if (p.x_scale != 1.0f) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] *= p.x_scale;
-    }
-  };
-  const float n = float(p.cols);
-  const float qinv = 1.0f / p.q_scale;
-  const float2 qinv2 = make_float2(qinv, qinv);
-  int k = 0;
-  bool aborted = false;
-  for (; k < nrows; ++k) {
-    const int slot = k % stages;
-    const bool ok = mbar_wait(&full[warp][slot], (k / stages) & 1, kDevTimeoutProducer, nullptr);
-    if (!__all_sync(0xffffffffu, ok)) {
-      aborted = true;
-      break;
-    }
-    // The row is read from the slot twice (statistics, outputs) rather than held in
-    // registers across the warp reduction, which would spill at the longer rows.
-    const uint32_t src = smem_u32(ring + (size_t)slot * row_bytes);
-    auto cur = [&](int i) -> uint4 {
-      const int vi = lane + 32 * i;
-      return vi < nvec ? lds16(src + vi * 16) : make_uint4(0u, 0u, 0u, 0u);
-    };
-    const long long row = row0 + (long long)k * nw;
-    // Statistics: the f32 sums in the order of the row-group kernels (one running sum per
-    // lane over its vectors, then the warp reduction), so the two schedules agree.
-    float mean = 0.f, s2 = 0.f;
-    if (ln) {
-      float s1 = 0.f;
-#pragma unroll
-      for (int i = 0; i < NV; ++i) {
-        float v[8];
-        unpack(cur(i), v);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) s1 += v[j];
-      }
-      mean = warp_sum(s1) / n;
-#pragma unroll
-      for (int i = 0; i < NV; ++i) {
-        if (lane + 32 * i < nvec) {
-          float v[8];
-          unpack(cur(i), v);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float d = v[j] - mean;
-            s2 += d * d;
-          }
-        }
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < NV; ++i) {
-        float v[8];
-        unpack(cur(i), v);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) s2 += v[j] * v[j];
-      }
-    }
-    const float inv = rsqrtf(warp_sum(s2) / n + p.eps);
-    const float2 inv2 = make_float2(inv, inv), nmean2 = make_float2(-mean, -mean);
-    uint8_t* qrow = p.q_out + row * p.q_ld;
-    // Outputs in packed f32x2 arithmetic, the same operations per element as the scalar
-    // form: RMSNorm (h * inv) * w', LayerNorm ((h - mean) * inv) * w + b, then * 1/scale.
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int vi = lane + 32 * i;
-      if (vi < nvec) {
-        float h[8];
-        unpack(cur(i), h);
-        const float4 wa = reinterpret_cast<const float4*>(sw)[2 * vi];
-        const float4 wb = reinterpret_cast<const float4*>(sw)[2 * vi + 1];
-        const float2 w2[4] = {make_float2(wa.x, wa.y), make_float2(wa.z, wa.w),
-                              make_float2(wb.x, wb.y), make_float2(wb.z, wb.w)};
-        float2 b2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
-                        make_float2(0.f, 0.f)};
-        if (has_b) {
-          const float4 ba = reinterpret_cast<const float4*>(sb)[2 * vi];
-          const float4 bb = reinterpret_cast<const float4*>(sb)[2 * vi + 1];
-          b2[0] = make_float2(ba.x, ba.y); b2[1] = make_float2(ba.z, ba.w);
-          b2[2] = make_float2(bb.x, bb.y); b2[3] = make_float2(bb.z, bb.w);
-        }
-        uint32_t o16[4];
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          float2 x = make_float2(h[2 * t], h[2 * t + 1]);
-          float2 y;
-          if (ln) {
-            x = fmul2(fadd2(x, nmean2), inv2);
-            y = ffma2(x, w2[t], b2[t]);
-          } else {
-            y = fmul2(fmul2(x, inv2), w2[t]);
-          }
-          y = fmul2(y, qinv2);
-          o16[t] = f32x2_to_e4m3x2(y.x, y.y);
-        }
-        __stcs(reinterpret_cast<uint2*>(qrow + vi * 8),
-               make_uint2(o16[0] | (o16[1] << 16), o16[2] | (o16[3] << 16)));
-      }
-    }
-    __syncwarp();  // every lane has read the slot: refill it
-    if (lane == 0 && issued < nrows) {
-      fence_proxy_async_smem();
-      issue(issued++);
-    }
-  }
-  if (aborted && lane == 0) {
-    // Let the copies still in flight land before the CTA's shared memory is released.
-    for (int j = k; j < issued; ++j)
-      mbar_wait(&full[warp][j % stages], (j / stages) & 1, kDevTimeoutDrain, nullptr);
-  }
-}
-
-using WarpFn = void (*)(const NormParams);
-using WarpRingFn = void (*)(const NormParams, int);
+using WarpDirectFn = void (*)(const NormParams);
 
 template <bool WF32>
-WarpFn pick_warp(int nv) {
+WarpDirectFn pick_warp_direct(int nv) {
   switch (nv) {
-    case 1: return norm_warp_kernel<1, WF32>;
-    case 2: return norm_warp_kernel<2, WF32>;
-    case 3: return norm_warp_kernel<3, WF32>;
-    case 4: return norm_warp_kernel<4, WF32>;
-    case 5: return norm_warp_kernel<5, WF32>;
-    case 6: return norm_warp_kernel<6, WF32>;
-    case 7: return norm_warp_kernel<7, WF32>;
-    case 8: return norm_warp_kernel<8, WF32>;
-    case 9: return norm_warp_kernel<9, WF32>;
-    case 10: return norm_warp_kernel<10, WF32>;
-    case 11: return norm_warp_kernel<11, WF32>;
-    default: return norm_warp_kernel<12, WF32>;
+    case 1: return norm_warp_direct_kernel<1, WF32>;
+    case 2: return norm_warp_direct_kernel<2, WF32>;
+    case 3: return norm_warp_direct_kernel<3, WF32>;
+    case 4: return norm_warp_direct_kernel<4, WF32>;
+    case 5: return norm_warp_direct_kernel<5, WF32>;
+    case 6: return norm_warp_direct_kernel<6, WF32>;
+    case 7: return norm_warp_direct_kernel<7, WF32>;
+    case 8: return norm_warp_direct_kernel<8, WF32>;
+    case 9: return norm_warp_direct_kernel<9, WF32>;
+    case 10: return norm_warp_direct_kernel<10, WF32>;
+    case 11: return norm_warp_direct_kernel<11, WF32>;
+    default: return norm_warp_direct_kernel<12, WF32>;
   }
 }
 
@@ -979,71 +789,11 @@ bool plan_warp(const NormParams& p) {
   return true;
 }
 
-template <bool WF32>
-WarpRingFn pick_warp_ring(int nv) {
-  switch (nv) {
-    case 1: return norm_warp_ring_kernel<1, WF32>;
-    case 2: return norm_warp_ring_kernel<2, WF32>;
-    case 3: return norm_warp_ring_kernel<3, WF32>;
-    case 4: return norm_warp_ring_kernel<4, WF32>;
-    case 5: return norm_warp_ring_kernel<5, WF32>;
-    case 6: return norm_warp_ring_kernel<6, WF32>;
-    case 7: return norm_warp_ring_kernel<7, WF32>;
-    case 8: return norm_warp_ring_kernel<8, WF32>;
-    case 9: return norm_warp_ring_kernel<9, WF32>;
-    case 10: return norm_warp_ring_kernel<10, WF32>;
-    case 11: return norm_warp_ring_kernel<11, WF32>;
-    default: return norm_warp_ring_kernel<12, WF32>;
-  }
-}
-
-// Ring depth for the bulk-copy schedule: as many row slots per warp (2..kRingMaxStages) as
-// fit two CTAs per SM; 0 when two slots do not fit (the register-prefetch kernel then runs).
-int warp_ring_stages(const NormParams& p) {
-  const size_t nvec = p.cols / 8;
-  const bool has_b = p.kind == 1 && p.bias != nullptr;
-  const size_t wbytes = (size_t)p.cols * 4 * (has_b ? 2 : 1);  // f32 gamma (and bias)
-  const size_t budget = 110 * 1024;  // two CTAs per SM, with room for the static barriers
-  if (wbytes >= budget) return 0;
-  const size_t per = (budget - wbytes) / ((size_t)kRingWarps * nvec * 16);
-  return per < 2 ? 0 : (int)std::min<size_t>(per, kRingMaxStages);
-}
-
 int launch_warp(const NormParams& p, cudaStream_t s) {
   const int nvec = p.cols / 8;
-  const bool wf32 = p.w_dtype == kF32;
-  if (const int stages = warp_ring_stages(p)) {
-    const WarpRingFn fn =
-        wf32 ? pick_warp_ring<true>((nvec + 31) / 32) : pick_warp_ring<false>((nvec + 31) / 32);
-    const bool has_b = p.kind == 1 && p.bias != nullptr;
-    const size_t smem = (size_t)p.cols * 4 * (has_b ? 2 : 1) +
-                        (size_t)kRingWarps * stages * nvec * 16;
-    int per_sm = 0;
-    {
-      static std::mutex mu;
-      static std::map<std::pair<int, const void*>, bool> opted;
-      std::lock_guard<std::mutex> g(mu);
-      int dev = 0;
-      cudaGetDevice(&dev);
-      if (!opted[{dev, (const void*)fn}]) {
-        B2F_CUDA_TRY(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          110 * 1024));
-        opted[{dev, (const void*)fn}] = true;
-      }
-    }
-    B2F_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 256, smem));
-    const int grid = std::max(1, std::min((p.rows + kRingWarps - 1) / kRingWarps,
-                                          sm_count() * std::max(per_sm, 1)));
-    fn<<<grid, 256, smem, s>>>(p, stages);
-    B2F_CUDA_TRY(cudaGetLastError());
-    return B2F_OK;
-  }
-  const WarpFn fn = wf32 ? pick_warp<true>((nvec + 31) / 32) : pick_warp<false>((nvec + 31) / 32);
-  const size_t smem = (size_t)2 * nvec * 16 * (wf32 ? 2 : 1);
-  int per_sm = 0;
-  B2F_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 256, smem));
-  const int grid = std::max(1, std::min((p.rows + 7) / 8, sm_count() * std::max(per_sm, 1)));
-  fn<<<grid, 256, smem, s>>>(p);
+  const WarpDirectFn fn = p.w_dtype == kF32 ? pick_warp_direct<true>((nvec + 31) / 32)
+                                            : pick_warp_direct<false>((nvec + 31) / 32);
+  fn<<<(p.rows + 7) / 8, 256, 0, s>>>(p);
   B2F_CUDA_TRY(cudaGetLastError());
   return B2F_OK;
 }

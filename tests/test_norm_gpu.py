@@ -156,8 +156,7 @@ def test_stream_and_rowgroup_schedules_agree(rows, cols, x_dtype, res_dtype, kin
     (257, 2560, "rms", False, 1.0),     # Qwen input RMSNorm (1 + w)
     (1000, 1152, "layer", True, 1.0),   # vision LayerNorm
     (7, 3072, "rms", False, 2.0),       # widest row of the warp schedule
-    (40, 3072, "layer", True, 1.0),     # f32 gamma + bias: ring too deep for two CTAs/SM,
-                                        # rows prefetched into registers instead
+    (40, 3072, "layer", True, 1.0),     # widest LayerNorm row with gamma + bias
     (3, 8, "layer", True, 1.0),
 ])
 def test_warp_schedule_matches_rowgroup(rows, cols, kind, bias, x_scale, wdt):
