@@ -4,6 +4,7 @@
 #include <string>
 #include <vector>
 #include <cstring>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "host_common.h"
@@ -25,6 +26,14 @@ EncodeTiledFn g_encode = nullptr;
 using CtxGetCurrentFn = CUresult (*)(CUcontext*);
 CtxGetCurrentFn g_ctx_get = nullptr;
 }  // namespace
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("B2F_NO_PDL");
+    return !(e != nullptr && e[0] != '\0' && e[0] != '0');
+  }();
+  return on;
+}
 
 unsigned long long context_token() {
   {

@@ -151,6 +151,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // set-up above overlaps the previous kernel; global memory only from here
 
   if (warp == 0) {
     if (lane == 0) {
@@ -588,6 +589,7 @@ __global__ void __launch_bounds__(384, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // set-up above overlaps the previous kernel; global memory only from here
   // Register split (per warpgroup): the producer / MMA warpgroup (warps 0-3, two of them
   // idle) gives up registers to the two softmax warpgroups, which hold a 128-column S row.
   // 128 x 56 + 256 x 224 = 384 x 168, the block's launch allocation.
@@ -1072,9 +1074,11 @@ int launch_attention(const b2f_attn_args* a, cudaStream_t stream) {
     const bool two_heads = p.pair_heads || p.pair_kv;
     dim3 grid(two_heads ? n_qt : (n_qt + 1) / 2, two_heads ? a->hq / 2 : a->hq, a->batch);
     if (a->v_dtype == B2F_DTYPE_F16)
-      attention2_kernel<D, true><<<grid, 384, SMEM, stream>>>(tq, tk, tv, tg, p);
+      B2F_CUDA_TRY(launch_pdl(attention2_kernel<D, true>, grid, dim3(384), SMEM, stream, tq, tk,
+                              tv, tg, p));
     else
-      attention2_kernel<D, false><<<grid, 384, SMEM, stream>>>(tq, tk, tv, tg, p);
+      B2F_CUDA_TRY(launch_pdl(attention2_kernel<D, false>, grid, dim3(384), SMEM, stream, tq,
+                              tk, tv, tg, p));
   } else {
     if (attr_dev[0][slot] != dev) {
       B2F_CUDA_TRY(cudaFuncSetAttribute(attention_kernel<D>,
@@ -1082,7 +1086,7 @@ int launch_attention(const b2f_attn_args* a, cudaStream_t stream) {
       attr_dev[0][slot] = dev;
     }
     dim3 grid(n_qt, a->hq, a->batch);
-    attention_kernel<D><<<grid, 192, SMEM, stream>>>(tq, tk, tv, p);
+    B2F_CUDA_TRY(launch_pdl(attention_kernel<D>, grid, dim3(192), SMEM, stream, tq, tk, tv, p));
   }
   B2F_CUDA_TRY(cudaGetLastError());
   return B2F_OK;

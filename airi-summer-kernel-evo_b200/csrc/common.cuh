@@ -64,6 +64,18 @@ __device__ __forceinline__ bool elect_one() {
   return pred != 0;
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// Kernels of a chain are launched with programmatic stream serialisation (launch_pdl): a
+// kernel may start while its predecessor is still running, so it must execute pdl_wait()
+// before it touches global memory that the predecessor reads or writes (pdl_wait returns
+// once the predecessor grid has completed and its writes are visible; it returns at once
+// for a kernel launched without the attribute).  pdl_trigger() lets the next kernel of
+// the chain be scheduled once every CTA of this grid has triggered or exited.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)

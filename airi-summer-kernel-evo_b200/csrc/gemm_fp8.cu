@@ -172,7 +172,8 @@ int launch_gemm(const b2f_gemm_args* a, EpilogueParams ep, cudaStream_t stream) 
   if ((BN / 2) * (a->out_dtype == B2F_DTYPE_F32 ? 4 : (a->out_dtype == B2F_DTYPE_BF16 ? 2 : 1)) < 64)
     ep.out_vec = 0;
   if (int rc = encode_out_map(a, ep, BN / 2, &to)) return rc;
-  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, to, shape, ep);
+  B2F_CUDA_TRY(launch_pdl(kern, dim3(grid), dim3(Cfg::THREADS), Cfg::SMEM_BYTES, stream, ta, tb,
+                          to, shape, ep));
   B2F_CUDA_TRY(cudaGetLastError());
   return B2F_OK;
 }
@@ -227,7 +228,8 @@ int launch_gemm_pair(const b2f_gemm_args* a, EpilogueParams ep, cudaStream_t str
   const int pairs = num_tiles < cached_pairs ? num_tiles : cached_pairs;
   CUtensorMap to;
   if (int rc = encode_out_map(a, ep, Cfg::BN / 2, &to)) return rc;
-  kern<<<2 * pairs, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(ta, tb, to, shape, ep);
+  B2F_CUDA_TRY(launch_pdl(kern, dim3(2 * pairs), dim3(Cfg::THREADS), Cfg::SMEM_BYTES, stream,
+                          ta, tb, to, shape, ep));
   B2F_CUDA_TRY(cudaGetLastError());
   return B2F_OK;
 }

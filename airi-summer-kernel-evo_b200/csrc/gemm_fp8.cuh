@@ -830,6 +830,7 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // set-up above overlaps the previous kernel; global memory only from here
 
   if (warp == 0) {
     if (lane == 0) {
@@ -1074,6 +1075,7 @@ __global__ void __launch_bounds__(320, 1)
     }
   }
 
+  pdl_trigger();  // this CTA's work is issued: the next kernel may be scheduled
   __syncwarp();
   tc_fence_before();
   __syncthreads();
@@ -1163,6 +1165,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // set-up above overlaps the previous kernel; global memory only from here
 
   if (warp == 0) {
     if (lane == 0) {
@@ -1289,6 +1292,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
     }
   }
 
+  pdl_trigger();  // this CTA's work is issued: the next kernel may be scheduled
   __syncwarp();
   tc_fence_before();
   cluster_sync();

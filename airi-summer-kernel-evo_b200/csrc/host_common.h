@@ -5,6 +5,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <string>
+#include <utility>
 
 #include "../../include/b200fp8.h"
 
@@ -24,6 +25,29 @@ unsigned long long context_token();
 bool encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
                  const unsigned long long* dims, const unsigned long long* strides_bytes,
                  const unsigned int* box, CUtensorMapSwizzle swizzle, std::string* err);
+
+// Launch with programmatic stream serialisation: the kernel may begin (its prologue up to
+// pdl_wait()) while the previous kernel on the stream finishes, which hides the launch
+// gap between the short kernels of a block.  Every kernel launched this way calls
+// pdl_wait() before its first global-memory access.  B2F_NO_PDL=1 in the environment
+// launches them plainly.
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 #define B2F_CUDA_TRY(expr)                                   \
   do {                                                       \

@@ -251,6 +251,7 @@ __device__ __forceinline__ float block_max(float v, float* red) {
 
 // Static scale (one pass), or pass 1 of the dynamic schedule (no q store; amax reduce).
 __global__ void __launch_bounds__(256) norm_pass1_kernel(const NormParams p, int tpr) {
+  pdl_wait();
   __shared__ float red[8];
   const int rpc = blockDim.x / tpr;
   const int t = threadIdx.x % tpr;
@@ -293,6 +294,7 @@ __global__ void __launch_bounds__(256) norm_pass1_kernel(const NormParams p, int
 // Pass 2 of the dynamic schedule: row blocks in reverse order (the most recently written
 // h rows are still in L2), h re-read, statistics recomputed, quantised with amax / 448.
 __global__ void __launch_bounds__(256) norm_pass2_kernel(const NormParams p, int tpr) {
+  pdl_wait();
   __shared__ float red[8];
   const int rpc = blockDim.x / tpr;
   const int t = threadIdx.x % tpr;
@@ -379,6 +381,7 @@ __device__ __forceinline__ void ld8(const uint8_t* base, int rt, long long off, 
 
 template <bool PASS2, int KIND, int DT0, int DT1, int WDT, bool FULL>
 __global__ void __launch_bounds__(256, 3) norm_stream_kernel(const NormParams p, const StreamCfg c) {
+  pdl_wait();
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[kStreamMaxStages];
   __shared__ float red[8];
@@ -639,6 +642,7 @@ constexpr int kWarpMaxNV = 12;
 // kernels' order; outputs in packed f32x2 arithmetic, the same operations per element.
 template <int NV, bool WF32>
 __global__ void __launch_bounds__(256, NV <= 6 ? 4 : 3) norm_warp_direct_kernel(const NormParams p) {
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
   if (row >= p.rows) return;
@@ -793,8 +797,7 @@ int launch_warp(const NormParams& p, cudaStream_t s) {
   const int nvec = p.cols / 8;
   const WarpDirectFn fn = p.w_dtype == kF32 ? pick_warp_direct<true>((nvec + 31) / 32)
                                             : pick_warp_direct<false>((nvec + 31) / 32);
-  fn<<<(p.rows + 7) / 8, 256, 0, s>>>(p);
-  B2F_CUDA_TRY(cudaGetLastError());
+  B2F_CUDA_TRY(launch_pdl(fn, dim3((p.rows + 7) / 8), dim3(256), 0, s, p));
   return B2F_OK;
 }
 
@@ -878,7 +881,7 @@ bool plan_stream(const NormParams& p, bool pass2, StreamLaunch& L) {
 }
 
 int launch_stream(const NormParams& p, const StreamLaunch& L, cudaStream_t s) {
-  L.fn<<<L.grid, L.cfg.tpr, L.smem, s>>>(p, L.cfg);
+  B2F_CUDA_TRY(launch_pdl(L.fn, dim3(L.grid), dim3(L.cfg.tpr), L.smem, s, p, L.cfg));
   B2F_CUDA_TRY(cudaGetLastError());
   return B2F_OK;
 }
@@ -898,7 +901,7 @@ int launch_norm(const NormParams& p, cudaStream_t s) {
     if (p.schedule == B2F_NORM_SCHEDULE_AUTO && plan_stream(p, false, L)) {
       if (int rc = launch_stream(p, L, s)) return rc;
     } else {
-      norm_pass1_kernel<<<grid, threads, 0, s>>>(p, tpr);
+      B2F_CUDA_TRY(launch_pdl(norm_pass1_kernel, dim3(grid), dim3(threads), 0, s, p, tpr));
       B2F_CUDA_TRY(cudaGetLastError());
     }
   }
@@ -906,7 +909,7 @@ int launch_norm(const NormParams& p, cudaStream_t s) {
     if (p.schedule == B2F_NORM_SCHEDULE_AUTO && plan_stream(p, true, L)) {
       if (int rc = launch_stream(p, L, s)) return rc;
     } else {
-      norm_pass2_kernel<<<grid, threads, 0, s>>>(p, tpr);
+      B2F_CUDA_TRY(launch_pdl(norm_pass2_kernel, dim3(grid), dim3(threads), 0, s, p, tpr));
       B2F_CUDA_TRY(cudaGetLastError());
     }
   }

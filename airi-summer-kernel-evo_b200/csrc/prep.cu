@@ -41,6 +41,7 @@ struct RopeParams {
 #endif
 template <int D>
 __global__ void __launch_bounds__(256) head_norm_rope_kernel(const RopeParams p) {
+  pdl_wait();
   constexpr int E = D / 32;  // elements per lane
   constexpr int W = (E + 3) / 4;  // 32-bit words per lane
   // Heads whose loads are in flight together (measured at D = 128, [8192 x 32 heads]:
@@ -229,6 +230,7 @@ __device__ __forceinline__ void head_norm_rope128_token(const RopeParams& p, int
 
 template <int G>
 __global__ void __launch_bounds__(256) head_norm_rope128_kernel(const RopeParams p) {
+  pdl_wait();
   const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (t < p.rows) head_norm_rope128_token<G>(p, t, threadIdx.x & 31);
 }
@@ -365,6 +367,7 @@ __device__ __forceinline__ void fp8_convert8(const uint8_t* in, long long in_ld,
 template <bool F16>
 __global__ void fp8_to_bf16_kernel(const uint8_t* in, long long in_ld, uint16_t* out,
                                    long long out_ld, int rows, int cols, float scale) {
+  pdl_wait();
   fp8_convert8<F16>(in, in_ld, out, out_ld, rows, cols, scale,
                     (long long)blockIdx.x * blockDim.x + threadIdx.x);
 }
@@ -385,6 +388,7 @@ struct VConvertParams {
 template <int GQ, int GK>
 __global__ void __launch_bounds__(256, 2) attn_prep_kernel(const RopeParams q, const RopeParams k,
                                                         const VConvertParams v, int nq) {
+  pdl_wait();
   const int b = blockIdx.x;
   const int lane = threadIdx.x & 31;
   if (b < nq) {
@@ -401,6 +405,7 @@ __global__ void __launch_bounds__(256, 2) attn_prep_kernel(const RopeParams q, c
 __global__ void swiglu_kernel(const uint8_t* gate, long long gate_ld, const uint8_t* up,
                               long long up_ld, uint8_t* out, long long out_ld, int rows, int cols,
                               float in_scale, float out_inv_scale) {
+  pdl_wait();
   const int vec_per_row = cols / 8;
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (long long)rows * vec_per_row) return;
@@ -443,10 +448,11 @@ int b2f_swiglu_fp8(const void* gate, long long gate_ld, const void* up, long lon
     return fail(B2F_ERR_ARG, "swiglu: cols/ld multiples of 8, 8-byte aligned tensors required");
   if (!(out_scale > 0.f)) return fail(B2F_ERR_ARG, "swiglu: out_scale must be > 0");
   const long long n = (long long)rows * (cols / 8);
-  swiglu_kernel<<<(int)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
-      reinterpret_cast<const uint8_t*>(gate), gate_ld, reinterpret_cast<const uint8_t*>(up), up_ld,
-      reinterpret_cast<uint8_t*>(out), out_ld, rows, cols, in_scale, 1.0f / out_scale);
-  B2F_CUDA_TRY(cudaGetLastError());
+  B2F_CUDA_TRY(launch_pdl(swiglu_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0,
+                          (cudaStream_t)stream, reinterpret_cast<const uint8_t*>(gate), gate_ld,
+                          reinterpret_cast<const uint8_t*>(up), up_ld,
+                          reinterpret_cast<uint8_t*>(out), out_ld, rows, cols, in_scale,
+                          1.0f / out_scale));
   return B2F_OK;
 }
 
@@ -517,15 +523,15 @@ int b2f_head_norm_rope(const b2f_rope_args* a, b2f_stream_t stream) {
   const bool fast128 = rope128_ok(a) && a->heads >= 16;
   if (fast128) {
     switch (a->heads / 4) {
-      case 4: head_norm_rope128_kernel<4><<<grid, 256, 0, s>>>(p); break;
-      case 5: head_norm_rope128_kernel<5><<<grid, 256, 0, s>>>(p); break;
-      case 6: head_norm_rope128_kernel<6><<<grid, 256, 0, s>>>(p); break;
-      case 7: head_norm_rope128_kernel<7><<<grid, 256, 0, s>>>(p); break;
-      default: head_norm_rope128_kernel<8><<<grid, 256, 0, s>>>(p); break;
+      case 4: B2F_CUDA_TRY(launch_pdl(head_norm_rope128_kernel<4>, dim3(grid), dim3(256), 0, s, p)); break;
+      case 5: B2F_CUDA_TRY(launch_pdl(head_norm_rope128_kernel<5>, dim3(grid), dim3(256), 0, s, p)); break;
+      case 6: B2F_CUDA_TRY(launch_pdl(head_norm_rope128_kernel<6>, dim3(grid), dim3(256), 0, s, p)); break;
+      case 7: B2F_CUDA_TRY(launch_pdl(head_norm_rope128_kernel<7>, dim3(grid), dim3(256), 0, s, p)); break;
+      default: B2F_CUDA_TRY(launch_pdl(head_norm_rope128_kernel<8>, dim3(grid), dim3(256), 0, s, p)); break;
     }
-  } else if (d == 64) head_norm_rope_kernel<64><<<grid, 256, 0, s>>>(p);
-  else if (d == 128) head_norm_rope_kernel<128><<<grid, 256, 0, s>>>(p);
-  else head_norm_rope_kernel<256><<<grid, 256, 0, s>>>(p);
+  } else if (d == 64) B2F_CUDA_TRY(launch_pdl(head_norm_rope_kernel<64>, dim3(grid), dim3(256), 0, s, p));
+  else if (d == 128) B2F_CUDA_TRY(launch_pdl(head_norm_rope_kernel<128>, dim3(grid), dim3(256), 0, s, p));
+  else B2F_CUDA_TRY(launch_pdl(head_norm_rope_kernel<256>, dim3(grid), dim3(256), 0, s, p));
   B2F_CUDA_TRY(cudaGetLastError());
   return B2F_OK;
 }
@@ -560,7 +566,8 @@ int b2f_attn_prep(const b2f_rope_args* q, const b2f_rope_args* k, const void* v_
   const int gq = q->heads / 4, gk = k->heads / 4;
 #define B2F_PREP(GQ, GK)                                                        \
   if (gq == GQ && gk == GK) {                                                   \
-    attn_prep_kernel<GQ, GK><<<grid, 256, 0, s>>>(pq, pk, pv, nq);              \
+    B2F_CUDA_TRY(launch_pdl(attn_prep_kernel<GQ, GK>, dim3(grid), dim3(256), 0, s, pq, pk, pv, \
+                            nq));                                                   \
     B2F_CUDA_TRY(cudaGetLastError());                                           \
     return B2F_OK;                                                              \
   }
@@ -583,14 +590,13 @@ static int fp8_convert(const void* in, long long in_ld, void* out, long long out
   const long long n = (long long)rows * (cols / 8);
   const int grid = (int)((n + 255) / 256);
   if (f16)
-    fp8_to_bf16_kernel<true><<<grid, 256, 0, (cudaStream_t)stream>>>(
-        reinterpret_cast<const uint8_t*>(in), in_ld, reinterpret_cast<uint16_t*>(out), out_ld,
-        rows, cols, scale);
+    B2F_CUDA_TRY(launch_pdl(fp8_to_bf16_kernel<true>, dim3(grid), dim3(256), 0,
+                            (cudaStream_t)stream, reinterpret_cast<const uint8_t*>(in), in_ld,
+                            reinterpret_cast<uint16_t*>(out), out_ld, rows, cols, scale));
   else
-    fp8_to_bf16_kernel<false><<<grid, 256, 0, (cudaStream_t)stream>>>(
-        reinterpret_cast<const uint8_t*>(in), in_ld, reinterpret_cast<uint16_t*>(out), out_ld,
-        rows, cols, scale);
-  B2F_CUDA_TRY(cudaGetLastError());
+    B2F_CUDA_TRY(launch_pdl(fp8_to_bf16_kernel<false>, dim3(grid), dim3(256), 0,
+                            (cudaStream_t)stream, reinterpret_cast<const uint8_t*>(in), in_ld,
+                            reinterpret_cast<uint16_t*>(out), out_ld, rows, cols, scale));
   return B2F_OK;
 }
 

@@ -833,13 +833,22 @@ class BlockWorkload:
     def roofline(self, per_launch_ms):
         return None  # from the stage breakdown (dominant kernel)
 
+    def snapshot(self):
+        """Keeps the first sequence of the last timed step's output (after the head group's
+        all-reduce): the eager stage timings that follow reuse the output buffer and, with
+        heads parallelism, leave only this rank's partial in it."""
+        out = self.local._g_out if self.tp > 1 else self.blk._g_out
+        self._snap = out[:self.seq].float().cpu()
+
     def parity(self):
         """The timed graph's output for the first sequence of this rank's batch group
         against the CPU oracle block (reference thresholds: 0.05 GPT-2, 0.08 Qwen, plus one
         bf16 rounding of the output)."""
         from oracle import blocks as ob
-        out = self.local._g_out if self.tp > 1 else self.blk._g_out
-        out0 = out[:self.seq].float().cpu()
+        out0 = getattr(self, "_snap", None)
+        if out0 is None:
+            out = self.local._g_out if self.tp > 1 else self.blk._g_out
+            out0 = out[:self.seq].float().cpu()
         x = self.x_cpu[:self.seq].float()
         t0 = time.perf_counter()
         if self.kind == "gpt2":
@@ -1031,6 +1040,8 @@ def measure(wl, args, world, rank, sampler, soak_s, steps, cpu_s):
     scale = 1e12 if wl.unit == "TFLOP/s" else 1e9
     value = wl.work * world / (ms_per_step * 1e-3) / scale  # whole job (all ranks)
 
+    if hasattr(wl, "snapshot"):
+        wl.snapshot()  # the timed output, before the stage timings overwrite its buffer
     stages = wl.stages() if hasattr(wl, "stages") else None
     if stages is not None:
         stages = {k: v for k, v in stages.items()}
