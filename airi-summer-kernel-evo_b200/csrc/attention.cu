@@ -422,6 +422,12 @@ __global__ void __launch_bounds__(192, 1)
 // causal masking the pair is (i, n-1-i), or, for GQA head pairs, the same query rows of
 // two heads sharing K/V.  TMEM: S_A | S_B | O_A | O_B.
 
+__device__ __forceinline__ void sts128(uint32_t addr, const uint32_t (&v)[4]) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v[0]), "r"(v[1]),
+               "r"(v[2]), "r"(v[3])
+               : "memory");
+}
+
 __device__ __forceinline__ float ex2_hw(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -769,6 +775,13 @@ __global__ void __launch_bounds__(384, 1)
     float l = 0.f;
     bool ok = act[x];
     const uint32_t s_col = C::S_COL + x * BKV;
+    // Shared-memory addresses of this row's eight swizzled 16-byte chunks of the P tile
+    // (chunk c of row r at position c ^ (r % 8) of the 128-byte row; the second 64-key
+    // block is a constant offset away).
+    uint32_t p_addr[8];
+#pragma unroll
+    for (int c8 = 0; c8 < 8; ++c8)
+      p_addr[c8] = smem_u32(sp + x * C::P_BYTES + r * 128) + ((c8 ^ (r & 7)) << 4);
     for (int j = 0; j < nkv[x] && ok; ++j) {
       ok = __all_sync(0xffffffffu, mbar_wait(&s_full[x], j & 1, kDevTimeoutEpilogue, abort_flag));
       if (!ok) break;
@@ -857,25 +870,29 @@ __global__ void __launch_bounds__(384, 1)
         // budget.
         const float2 c2 = make_float2(c, c), nm2 = make_float2(-mref, -mref);
         float2 acc2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-        uint8_t* prow = sp + x * C::P_BYTES + r * 128;
 #pragma unroll
         for (int hb = 0; hb < BKV / 64; ++hb) {
 #pragma unroll
-          for (int e = hb * 32; e < hb * 32 + 32; ++e) {
-            const float2 xv = ffma2(make_float2(__uint_as_float(sv(2 * e)),
-                                                __uint_as_float(sv(2 * e + 1))), c2, nm2);
-            // Every exponential on the exponential unit: moving three of eight pairs to
-            // an FMA-pipe polynomial (ex2_poly2) measured slower here (Qwen shape 223 vs
-            // 205 us): the softmax is bound by issue slots, which the polynomial adds.
-            const float e0 = ex2_hw(xv.x), e1 = ex2_hw(xv.y);
-            acc2[e & 1] = fadd2(acc2[e & 1], make_float2(e0, e1));
-            if constexpr (VF16) sv(e) = pack_f16x2(e0, e1);
-            else sv(e) = pack_bf16x2(e0, e1);
-          }
+          for (int c8 = hb * 8; c8 < hb * 8 + 8; ++c8) {
+            // keys [8 c8, 8 c8 + 8): four pairs packed into one fresh 16-byte vector and
+            // stored at once (packing them back into the S registers first cost register
+            // moves: ncu counted about 360 extra FMA / ALU-pipe instructions per warp step)
+            uint32_t q4[4];
 #pragma unroll
-          for (int c8 = hb * 8; c8 < hb * 8 + 8; ++c8)
-            *reinterpret_cast<uint4*>(prow + hb * (BQ * 128) + (((c8 & 7) ^ (r & 7)) << 4)) =
-                make_uint4(sv(4 * c8), sv(4 * c8 + 1), sv(4 * c8 + 2), sv(4 * c8 + 3));
+            for (int t = 0; t < 4; ++t) {
+              const int e = 4 * c8 + t;
+              const float2 xv = ffma2(make_float2(__uint_as_float(sv(2 * e)),
+                                                  __uint_as_float(sv(2 * e + 1))), c2, nm2);
+              // Every exponential on the exponential unit: moving three of eight pairs to
+              // an FMA-pipe polynomial (ex2_poly2) measured slower here (Qwen shape 223 vs
+              // 205 us): the softmax is bound by issue slots, which the polynomial adds.
+              const float e0 = ex2_hw(xv.x), e1 = ex2_hw(xv.y);
+              acc2[t & 1] = fadd2(acc2[t & 1], make_float2(e0, e1));
+              if constexpr (VF16) q4[t] = pack_f16x2(e0, e1);
+              else q4[t] = pack_bf16x2(e0, e1);
+            }
+            sts128(p_addr[c8 & 7] + hb * (BQ * 128), q4);
+          }
         }
         fence_async_shared();  // generic-proxy writes visible to the tensor core
         lt = (acc2[0].x + acc2[0].y) + (acc2[1].x + acc2[1].y);
