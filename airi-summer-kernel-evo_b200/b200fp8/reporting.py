@@ -22,11 +22,11 @@ _ROOT = Path(__file__).resolve().parents[2]
 
 # ncu summaries committed for the kernels behind each task family
 NCU_SUMMARIES = {
-    "gemm": "profiles/gemm_fp8_pair_square8192.md",
+    "gemm": "profiles/gemm_fp8_pair_qwen_square8192.md",
     "gpt2": "profiles/blocks_launch_lists.md",
     "vision": "profiles/blocks_launch_lists.md",
     "qwen": "profiles/blocks_launch_lists.md",
-    "layer_norm": "profiles/layer_norm_rows_16x4194304.md",
+    "layer_norm": "profiles/memory_bound_kernels.md",
 }
 
 

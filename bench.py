@@ -712,7 +712,12 @@ def _stage_model(kind, blk):
         # the weights, writes the gate (e4m3), q and k (e4m3) and V (16-bit)
         "qgkv_gemm_prep": (2.0 * t * hid * nc,
                            t * hid + nc * hid + t * (nc - hk * dh) + 2.0 * t * hk * dh, FP8_PEAK),
+        # projection writing q / gate / k (e4m3) and the 16-bit V image from its epilogue
+        "qgkv_gemm_v": (2.0 * t * hid * nc,
+                        t * hid + nc * hid + t * (nc - hk * dh) + 2.0 * t * hk * dh, FP8_PEAK),
         "qkv_prep": (0.0, 2.0 * t * (h + hk) * dh + 3.0 * t * hk * dh, FP8_PEAK),
+        # q / k head norm + RoPE only (V came from the projection)
+        "qk_prep": (0.0, 2.0 * t * (h + hk) * dh, FP8_PEAK),
         "qk_norm_rope": (0.0, 2.0 * t * (h + hk) * dh, FP8_PEAK),
         "v_convert": (0.0, 3.0 * t * hk * dh, FP8_PEAK),
         "attention": (2.0 * b * h * s * s * dh, t * dh * (3.0 * h + 4.0 * hk), ATTN_PEAK),
