@@ -1012,27 +1012,48 @@ def measure(wl, args, world, rank, sampler, soak_s, steps, cpu_s):
     cev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(steps)]
     has_comm = isinstance(wl, BlockWorkload) and wl.tp > 1
+    # Host time to enqueue one step (no synchronisation): the timed steps are queued behind a
+    # device-side wait at least that long, so the device runs them back to back and the
+    # events time device work, not the Python launch path (which e2e covers).
+    torch.cuda.synchronize()
+    h0 = time.perf_counter()
+    for _ in range(3):
+        if hasattr(wl, "pre_step"):
+            wl.pre_step()
+        wl.step()
+    host_ms = (time.perf_counter() - h0) / 3 * 1e3
+    torch.cuda.synchronize()
+    host_ms = _max_over_ranks(host_ms, world)
     _barrier(world)
     torch.cuda.synchronize()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda._sleep(int((1.5 * steps * host_ms + 0.5) * 2.0e6))  # ~2 GHz clock cycles
     t0.record(stream)
     launches = 0
+    # Per-step events only where the steps are separated by untimed work (the L2 flush of
+    # the GPT-2 block): an event between two launches serialises them and stops the next
+    # kernel's programmatic early launch, which costs the short GEMMs up to a third of a
+    # step.  Otherwise the K steps run back to back between t0 and t1.
+    per_step = getattr(wl, "flush", None) is not None
     for i in range(steps):
         if hasattr(wl, "pre_step"):
             wl.pre_step()
-        ev[i][0].record(stream)
+        if per_step:
+            ev[i][0].record(stream)
         launches += wl.step(cev[i]) if has_comm else wl.step()
-        ev[i][1].record(stream)
+        if per_step:
+            ev[i][1].record(stream)
     t1.record(stream)
     torch.cuda.synchronize()
     t_window1 = time.time()
     _barrier(world)
-    step_ms = [e[0].elapsed_time(e[1]) for e in ev]
-    if getattr(wl, "flush", None) is not None:
+    if per_step:
+        step_ms = [e[0].elapsed_time(e[1]) for e in ev]
         ms_per_step = statistics.mean(step_ms)  # flushes between steps are not timed
     else:
         ms_per_step = t0.elapsed_time(t1) / steps
+        step_ms = [ms_per_step]
     ms_per_step = _max_over_ranks(ms_per_step, world)
     per_launch_ms = _max_over_ranks(statistics.mean(step_ms), world)
     comm = None
