@@ -112,7 +112,8 @@ __device__ __forceinline__ unsigned splitk_state(unsigned int* c, unsigned epoch
 
 struct GemmShape {
   int M, N, K;
-  int splits;  // K slices per output tile (split-K, 1-CTA kernel only); 1 = off
+  int splits;   // K slices per output tile (split-K, 1-CTA kernel only); 1 = off
+  int group_m;  // row blocks per raster group (tile_coords)
 };
 
 // Hardware tanh (MUFU, max relative error ~2^-11); every GELU output is requantised to
@@ -220,9 +221,9 @@ struct GemmCfg {
 };
 
 // Tile order: groups of GROUP_M row-blocks sweep all column blocks, so the CTAs that run
-// concurrently share A rows and B columns in L2.
-__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
-  constexpr int GROUP_M = 16;
+// concurrently share A rows and B columns in L2 (GROUP_M chosen on the host: group_rows).
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int GROUP_M, int& mb,
+                                            int& nb) {
   const int per_group = GROUP_M * num_n;
   const int g = t / per_group;
   const int first_m = g * GROUP_M;
@@ -844,7 +845,7 @@ __global__ void __launch_bounds__(320, 1)
       for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
         const int t = u / splits, sk = u - t * splits;
         int mb, nb;
-        tile_coords(t, num_m, num_n, mb, nb);
+        tile_coords(t, num_m, num_n, shape.group_m, mb, nb);
         const int kb0 = (sk * num_kb) / splits, kb1 = ((sk + 1) * num_kb) / splits;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, kDevTimeoutProducer, abort_flag)) {
@@ -928,7 +929,7 @@ __global__ void __launch_bounds__(320, 1)
     for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++it) {
       const int t = u / splits;
       int mb, nb;
-      tile_coords(t, num_m, num_n, mb, nb);
+      tile_coords(t, num_m, num_n, shape.group_m, mb, nb);
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       float lbv[BN / 64], lcv[BN / 64];
@@ -1177,7 +1178,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
       bool ok = true;
       for (int t = pair; t < num_tiles && ok; t += num_pairs) {
         int mb, nb;
-        tile_coords(t, num_m, num_n, mb, nb);
+        tile_coords(t, num_m, num_n, shape.group_m, mb, nb);
         const int row_a = mb * 2 * Cfg::BM + rank * Cfg::BM;
         const int row_b = nb * BN + rank * (BN / 2);
         for (int kb = 0; kb < num_kb; ++kb) {
@@ -1256,7 +1257,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
     int it = 0;
     for (int t = pair; t < num_tiles; t += num_pairs, ++it) {
       int mb, nb;
-      tile_coords(t, num_m, num_n, mb, nb);
+      tile_coords(t, num_m, num_n, shape.group_m, mb, nb);
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       float lbv[BN / 64], lcv[BN / 64];
