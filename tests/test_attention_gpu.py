@@ -73,6 +73,7 @@ _CASES = [
     (1, 384, 4, 2, 128, True), (2, 128, 16, 4, 256, True), (1, 128, 16, 16, 64, False),
     (1, 200, 2, 1, 128, True), (1, 256, 4, 1, 128, False), (1, 1024, 2, 2, 64, True),
     (1, 512, 2, 1, 256, True), (2, 640, 8, 2, 128, True), (1, 384, 6, 3, 64, False),
+    (2, 200, 4, 4, 64, True),  # head pairs with their own K / V, ragged last query tile
 ]
 
 
