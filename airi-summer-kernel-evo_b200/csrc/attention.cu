@@ -537,10 +537,13 @@ __global__ void __launch_bounds__(384, 1)
   if (p.pair_heads || p.pair_kv) {
     // GQA: query heads 2y and 2y+1 read the same KV head; both tiles take the same query
     // rows, so both stay active for every key tile and share each K / V load.  (pair_kv:
-    // the same for two heads with their own K / V, loaded side by side.)  Longest causal
-    // rows first.
-    qt[0] = qt[1] = n_qt - 1 - blockIdx.x;
-    hx[0] = 2 * blockIdx.y;
+    // the same for two heads with their own K / V, loaded side by side.)  The grid is
+    // (head pairs, batch, query tiles) with the longest causal rows in the first z-slice:
+    // CTAs start in grid order, so every long CTA starts before any shorter one and the
+    // short ones fill the end (longest-first; with the query tile in x, long CTAs that
+    // started late set the kernel's tail).
+    qt[0] = qt[1] = n_qt - 1 - blockIdx.z;
+    hx[0] = 2 * blockIdx.x;
     hx[1] = hx[0] + 1;
     act[0] = true;
   } else {
@@ -561,7 +564,7 @@ __global__ void __launch_bounds__(384, 1)
     const int end = p.causal ? min(p.seq, qt[x] * BQ + BQ) : p.seq;
     nkv[x] = act[x] ? (end + BKV - 1) / BKV : 0;
   }
-  const int b = blockIdx.z;
+  const int b = (p.pair_heads || p.pair_kv) ? blockIdx.y : blockIdx.z;
   const int hk = hx[0] / (p.hq / p.hkv);
   const int kv2 = p.pair_kv ? 2 : 1;     // heads per K / V ring stage
   const int hkv[2] = {hk, p.pair_kv ? hx[1] : hk};
@@ -1110,7 +1113,8 @@ int launch_attention(const b2f_attn_args* a, cudaStream_t stream) {
     // leaves half of the CTA idle for most key tiles.
     p.pair_kv = !p.pair_heads && D == 64 && a->causal && a->hq == a->hkv && a->hq % 2 == 0;
     const bool two_heads = p.pair_heads || p.pair_kv;
-    dim3 grid(two_heads ? n_qt : (n_qt + 1) / 2, two_heads ? a->hq / 2 : a->hq, a->batch);
+    const dim3 grid = two_heads ? dim3(a->hq / 2, a->batch, n_qt)
+                                : dim3((n_qt + 1) / 2, a->hq, a->batch);
     if (a->v_dtype == B2F_DTYPE_F16)
       B2F_CUDA_TRY(launch_pdl(attention2_kernel<D, true>, grid, dim3(384), SMEM, stream, tq, tk,
                               tv, tg, p));
