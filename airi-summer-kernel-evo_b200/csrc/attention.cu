@@ -12,8 +12,8 @@
 // Two kernels:
 //   attention2_kernel<D, VF16> (head_dim 64 / 128): two query tiles per CTA, 128-key
 //     tiles, P through shared memory, S released as soon as the softmax loaded it (384
-//     threads: TMA producer warp, MMA warp, two idle warps, two softmax warpgroups holding
-//     the registers the others give up); the two tiles are GQA head pairs sharing K / V,
+//     threads: TMA producer warp, MMA warp, two idle warps, two softmax warpgroups); the
+//     two tiles are GQA head pairs sharing K / V,
 //     or two heads with their own K / V at the same query rows (causal, head_dim 64), or
 //     causal query tiles (i, n-1-i) of one head; e4m3 gate tiles by TMA.
 //   attention_kernel<256> (head_dim 256): one query tile per CTA (192 threads), S
@@ -602,11 +602,10 @@ __global__ void __launch_bounds__(384, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   pdl_wait();  // set-up above overlaps the previous kernel; global memory only from here
-  // Register split (per warpgroup): the producer / MMA warpgroup (warps 0-3, two of them
-  // idle) gives up registers to the two softmax warpgroups, which hold a 128-column S row.
-  // 128 x 56 + 256 x 224 = 384 x 168, the block's launch allocation.
-  if (warp < 4) setmaxnreg_dec<56>();
-  else setmaxnreg_inc<224>();
+  // Every warp runs at the launch allocation (168 registers).  No `setmaxnreg` split: ptxas
+  // ignores it in relocatable (-rdc) code, and in a whole-program build the MMA issuer's
+  // unrolled loops needed about 150 registers, so the softmax warpgroups could gain at most
+  // 176, which measured slower (170.6 vs 166.5 us at the Qwen shape).
 
   if (warp == 0) {
     // ---------------------------------------------------------------- producers
